@@ -1,0 +1,348 @@
+#!/usr/bin/env python
+"""Benchmark: the wide-MLP data-parallel training step on B200.
+
+Workload: Linear(4096,4096) -> ReLU -> Linear(4096,4096)
+-> ReLU -> Linear(4096,10), cross_entropy, backward, gradient all-reduce
+(mean, NCCL) across ranks, Sgd step lr=0.01; global batch 8192 split evenly
+over the ranks (strong scaling).  Synthetic seeded data, reference init.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line on rank 0.  `value` is global training steps per second
+measured on the device with inputs resident in HBM (CUDA events on the step's
+stream, max over ranks); `e2e` is the same metric through the C-ABI host entry
+point (fg_mlp_step_host) with the batch copied from pinned host memory and the
+loss copied back every step.  `--impl reference` times the reference CPU
+arithmetic (the oracle port: the Rust reference cannot be built here) with all
+host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DIMS = (4096, 4096, 4096, 10)
+GLOBAL_BATCH = 8192
+LR = 0.01
+X_SEED, LABEL_SEED = 13, 14
+METRIC = "MLP train steps/s (wide MLP 4096-4096-4096-10, global batch 8192, fp32)"
+WORKLOAD = "config5: wide MLP data-parallel training step (forward, cross_entropy, backward, allreduce-mean, SGD)"
+GEMM_FLOPS_PER_STEP = 5 * (2 * 8192 * 4096 * 4096) + 3 * (2 * 8192 * 4096 * 10)
+
+
+def env_dist():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def gemm_traffic_per_flop():
+    """DRAM bytes per algorithmic flop of the GEMM, from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "gemm3x_tf32_ncu.md")
+    try:
+        text = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_flop:\s*([0-9.eE+-]+)", text)
+    return float(m.group(1)) if m else None
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle (reference arithmetic) on a bounded sample
+# ---------------------------------------------------------------------------
+def cpu_step_sample(rows: int, threads: int):
+    """Time one C5 step restricted to `rows` batch rows on the oracle; returns seconds."""
+    from oracle import oracle as orc
+    from ferrograd_b200 import data
+    orc.set_threads(threads)
+    x, t = data.mlp_batch(rows, DIMS[0], DIMS[-1], X_SEED, LABEL_SEED)
+    rng = orc.InitRng()
+    ws, bs = [], []
+    for i in range(len(DIMS) - 1):
+        w, b = rng.linear(DIMS[i], DIMS[i + 1])
+        ws.append(w)
+        bs.append(b)
+    t0 = time.perf_counter()
+    orc.mlp_step(ws, bs, x, t, LR, want_grads=False)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(target_s: float = 15.0):
+    threads = os.cpu_count() or 1
+    probe_rows = 128
+    tp = cpu_step_sample(probe_rows, threads)
+    rows = int(min(GLOBAL_BATCH, max(probe_rows, probe_rows * target_s / max(tp, 1e-3))))
+    rows = max(probe_rows, (rows // 128) * 128)
+    ts = cpu_step_sample(rows, threads) if rows != probe_rows else tp
+    step_s = ts * GLOBAL_BATCH / rows
+    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": threads, "kind": "port",
+            "sample": (f"one config-5 training step of the oracle (C restatement of the reference "
+                       f"CPU arithmetic, OpenMP over output rows) on {rows} of {GLOBAL_BATCH} batch "
+                       f"rows ({ts:.2f} s), scaled x{GLOBAL_BATCH / rows:.0f} to the full batch")}
+
+
+def reference_arm(args):
+    rank, world, _ = env_dist()
+    if rank != 0:
+        return 0
+    from oracle import oracle as orc
+    threads = os.cpu_count() or 1
+    # size one sample at ~3 s so K+W samples fit in a few minutes
+    tp = cpu_step_sample(128, threads)
+    rows = int(min(GLOBAL_BATCH, max(128, 128 * 3.0 / max(tp, 1e-3))))
+    rows = max(128, (rows // 128) * 128)
+    for _ in range(args.warmup):
+        cpu_step_sample(rows, threads)
+    times = [cpu_step_sample(rows, threads) for _ in range(args.steps)]
+    step_s = statistics.mean(times) * GLOBAL_BATCH / rows
+    value = 1.0 / step_s
+    sample = (f"oracle port of the reference CPU arithmetic, {threads} threads; each step is "
+              f"{rows} of {GLOBAL_BATCH} batch rows of a config-5 step scaled x{GLOBAL_BATCH / rows:.0f}")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded uniform inputs, one-hot labels)",
+            "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "dims": list(DIMS),
+                       "parallelism": "none (CPU)"},
+            "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "reference_note": "the Rust reference cannot be built here (no rustc/clang); the oracle "
+                              "restates its arithmetic in C"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path).read().splitlines()[1:]:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1].split()[0]))
+                smax = float(parts[2].split()[0])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def our_arm(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ferrograd_b200 import Communicator, CudaDevice, MlpTrainer, data, mlp_init
+
+    rank, world, local = env_dist()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    if GLOBAL_BATCH % world:
+        raise SystemExit("global batch must divide by the number of GPUs")
+    B = GLOBAL_BATCH // world
+
+    x_full, t_full = data.mlp_batch(GLOBAL_BATCH, DIMS[0], DIMS[-1], X_SEED, LABEL_SEED)
+    x = np.ascontiguousarray(x_full[rank * B:(rank + 1) * B])
+    t = np.ascontiguousarray(t_full[rank * B:(rank + 1) * B])
+    del x_full, t_full
+    ws, bs = mlp_init(DIMS)  # seeded: identical on every rank
+
+    comm = None
+    if world > 1:
+        uid = [Communicator.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = Communicator(rank, world, uid[0], timeout_ms=120000)
+    dev = CudaDevice(local)
+    tr = MlpTrainer(dev, DIMS, B, LR, ws, bs, comm=comm, use_graph=True)
+    tr.enable_gemm_timing(True)
+
+    xp = torch.from_numpy(x).pin_memory()
+    tp = torch.from_numpy(t).pin_memory()
+    lossp = torch.zeros(1, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.ExternalStream(dev.stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        tt = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    # warm-up through the host entry point (fills the device input slots too)
+    for _ in range(max(args.warmup, 3)):
+        tr.step_host_ptr(xp.data_ptr(), tp.data_ptr(), lossp.data_ptr())
+    first_loss = float(lossp.item())
+
+    # ---- device-resident timing -------------------------------------------
+    sampler = None
+    if rank == 0:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].isdigit() else local
+        sampler = ClockSampler(phys)
+    barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = int(tr.launches_per_step)
+    e0.record(stream)
+    for _ in range(args.steps):
+        tr.step()
+    e1.record(stream)
+    e1.synchronize()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    gemms = tr.gemm_times()
+
+    # ---- end to end through the C ABI with host buffers --------------------
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tr.step_host_ptr(xp.data_ptr(), tp.data_ptr(), lossp.data_ptr())
+    e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
+    last_loss = float(lossp.item())
+
+    peaks, peak_src = load_peaks()
+    gemm_ms = sum(g[0] for g in gemms)
+    gemm_flops = sum(g[1] for g in gemms)
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    tf32_peak = peaks["bf16_tflops_sustained"] / 2.0
+    peak_3x = tf32_peak / 3.0
+    tpf = gemm_traffic_per_flop()
+    per_launch_flops = gemm_flops / len(gemms) if gemms else 0
+    roofline = {
+        "bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s",
+        "frac": (achieved / peak_3x) if achieved else None,
+        "traffic": (tpf * per_launch_flops) if tpf else None,
+        "kernel": "k_gemm3x (3xTF32 tcgen05, 128x128 tiles)",
+        "achieved_basis": (f"2*M*N*K algorithmic flops / CUDA-event duration, averaged over the "
+                           f"{len(gemms)} GEMM launches of the last timed step ({per_launch_flops:.3e} "
+                           f"flop each)"),
+        "peak_basis": (f"{peak_src} bf16_tflops_sustained {peaks['bf16_tflops_sustained']} / 2 "
+                       f"(dense TF32 = half the bf16 rate) / 3 (3xTF32 issues three MMAs per product)"),
+        "frac_of_tf32_issue": ((3 * achieved) / tf32_peak) if achieved else None,
+    }
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: x uniform[0,1) seed 13, one-hot labels uniform 0..9 seed 14; "
+                    "reference Linear::new init (seed-42 LCG Kaiming normal, zero bias)",
+            "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "dims": list(DIMS),
+                       "per_gpu_batch": B, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (x shard + 2x64 MiB weights + residuals)",
+                       "gemm": "3xTF32 tcgen05 (fp32-accurate)", "graph": "CUDA graph replay"},
+            "roofline": roofline,
+            "e2e": {"value": 1.0 / e2e_s, "unit": "steps/s",
+                    "h2d_bytes_per_step": int(x.nbytes + t.nbytes), "d2h_bytes_per_step": 4},
+            "gpu_launches": launches0 * args.steps,
+            "launches_per_step": launches0,
+            "clocks": clocks,
+            "loss_first_last": [first_loss, last_loss],
+            "gemm_flops_per_step": GEMM_FLOPS_PER_STEP,
+        }
+    if world > 1:
+        barrier()
+    tr.close()
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return reference_arm(args)
+    return our_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

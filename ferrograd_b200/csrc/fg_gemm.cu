@@ -1,0 +1,395 @@
+// 3xTF32 GEMM on the sm_100a tensor cores (tcgen05 + TMEM), operands staged
+// by TMA.  This is the kernel the schedule routes the reduce-of-broadcast-mul
+// pattern to: Tensor::matmul (src/tensor.rs:762-778) and its two backward
+// contractions (src/gradient.rs:100-106,165-176).
+//
+//   C[m,n] = sum_k A(m,k) B(n,k)  ~=  A*B + A*B_lo + A_lo*B
+//
+// The tensor cores read an fp32 operand as TF32 by dropping its low 13
+// mantissa bits, so the raw matrix serves as the high part; *_lo holds the
+// exact residual x - trunc_tf32(x).  The residual-times-residual term is
+// dropped (relative size 2^-22).  Accumulation is fp32 in TMEM.
+//
+// CTA = 6 warps, one output tile of 128 x BN:
+//   warp 0     TMA producer (one elected lane), STAGES-deep smem ring
+//   warp 1     TMEM allocator + MMA issuer (one elected lane)
+//   warps 2-5  epilogue: tcgen05.ld TMEM -> registers -> fused op -> global
+// Operands are K-major ([rows, K], K contiguous) or MN-major ([K, rows]);
+// both are loaded with 128-byte swizzle and described to tcgen05 directly,
+// so no transposed copies are made.  No TMA multicast is used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "fg_gemm.cuh"
+#include "fg_internal.h"
+#include "fg_ptx.cuh"
+
+namespace fg {
+namespace gemm {
+
+using namespace fg::ptx;
+
+constexpr int BM = 128;
+constexpr int BK = 32;      // fp32 elements per k-block: one 128-byte swizzle row
+constexpr int UMMA_K = 8;   // K of one kind::tf32 MMA
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
+  static constexpr int STAGES = (BN <= 128) ? 3 : 2;
+  static constexpr int TMEM_COLS = BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+__device__ __forceinline__ float tf32_residual(float v) {
+  return __fsub_rn(v, __uint_as_float(__float_as_uint(v) & 0xffffe000u));
+}
+
+// Error codes written to the device error word (high 16 bits = role).
+constexpr unsigned kErrProducer = 1u << 16;
+constexpr unsigned kErrMma = 2u << 16;
+constexpr unsigned kErrEpilogue = 3u << 16;
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm3x(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAlo,
+             const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBlo,
+             const GemmParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzle atoms need 1024-byte aligned tiles.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t *empty = full + C::STAGES;
+  uint64_t *accum_full = empty + C::STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum_full + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * BM;
+  const int nk = (p.K + BK - 1) / BK;
+  const bool three = !p.one_pass;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < C::STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum_full, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (three) {
+      prefetch_tmap(&tmAlo);
+      prefetch_tmap(&tmBlo);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      const uint32_t stage_tx = three ? (uint32_t)C::STAGE_BYTES
+                                      : (uint32_t)(C::A_BYTES + C::B_BYTES);
+      int issued_until = 0;  // k-blocks whose loads were issued
+      bool ok = true;
+      for (int kb = 0; kb < nk && ok; kb++) {
+        const int s = kb % C::STAGES;
+        if (kb >= C::STAGES) {
+          ok = mbar_wait(&empty[s], ((kb / C::STAGES) - 1) & 1, p.err, kErrProducer | 1);
+          if (!ok) break;
+        }
+        uint8_t *sa = smem + s * C::STAGE_BYTES;
+        uint8_t *salo = sa + C::A_BYTES;
+        uint8_t *sb = salo + C::A_BYTES;
+        uint8_t *sblo = sb + C::B_BYTES;
+        const int k0 = kb * BK;
+        mbar_arrive_expect_tx(&full[s], stage_tx);
+        if (A_MN) {
+#pragma unroll
+          for (int j = 0; j < BM / 32; j++) {
+            tma_load_2d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, k0);
+            if (three) tma_load_2d(salo + j * 4096, &tmAlo, &full[s], m0 + 32 * j, k0);
+          }
+        } else {
+          tma_load_2d(sa, &tmA, &full[s], k0, m0);
+          if (three) tma_load_2d(salo, &tmAlo, &full[s], k0, m0);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 32; j++) {
+            tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
+            if (three) tma_load_2d(sblo + j * 4096, &tmBlo, &full[s], n0 + 32 * j, k0);
+          }
+        } else {
+          tma_load_2d(sb, &tmB, &full[s], k0, n0);
+          if (three) tma_load_2d(sblo, &tmBlo, &full[s], k0, n0);
+        }
+        issued_until = kb + 1;
+      }
+      if (!ok) {
+        // Let loads already in flight land before the CTA exits.
+        for (int kb = issued_until - C::STAGES < 0 ? 0 : issued_until - C::STAGES;
+             kb < issued_until; kb++)
+          mbar_wait(&full[kb % C::STAGES], (kb / C::STAGES) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+      // K-major: next 8-element K slice is +32 bytes inside the swizzle row;
+      // MN-major: next 8 K rows are the next 1024-byte swizzle atom.
+      constexpr uint32_t a_kstep = A_MN ? 1024 : 32;
+      constexpr uint32_t b_kstep = B_MN ? 1024 : 32;
+      constexpr uint32_t a_lbo = A_MN ? 4096 : 16, a_sbo = 1024;
+      constexpr uint32_t b_lbo = B_MN ? 4096 : 16, b_sbo = 1024;
+      bool ok = true;
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % C::STAGES;
+        ok = mbar_wait(&full[s], (kb / C::STAGES) & 1, p.err, kErrMma | 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+        const uint32_t salo = sa + C::A_BYTES;
+        const uint32_t sb = salo + C::A_BYTES;
+        const uint32_t sblo = sb + C::B_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / UMMA_K; kk++) {
+          const uint64_t da = smem_desc_sw128(sa + kk * a_kstep, a_lbo, a_sbo);
+          const uint64_t db = smem_desc_sw128(sb + kk * b_kstep, b_lbo, b_sbo);
+          const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+          if (three) {
+            const uint64_t dalo = smem_desc_sw128(salo + kk * a_kstep, a_lbo, a_sbo);
+            const uint64_t dblo = smem_desc_sw128(sblo + kk * b_kstep, b_lbo, b_sbo);
+            // small terms first, then the main product
+            mma_tf32(tmem_base, dalo, db, idesc, acc);
+            mma_tf32(tmem_base, da, dblo, idesc, 1u);
+            mma_tf32(tmem_base, da, db, idesc, 1u);
+          } else {
+            mma_tf32(tmem_base, da, db, idesc, acc);
+          }
+        }
+        mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+      }
+      if (ok) mma_commit(accum_full);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = m0 + 32 * q + lane;
+    const bool ok = mbar_wait(accum_full, 0, p.err, kErrEpilogue | 1);
+    tc_fence_after();
+    if (ok) {
+      const bool vec = ((p.ldc & 3) == 0) && ((((uintptr_t)p.C) & 15) == 0) &&
+                       (!p.C_lo || (((uintptr_t)p.C_lo) & 15) == 0) &&
+                       (!p.mask || (((p.ldmask & 3) == 0) && (((uintptr_t)p.mask) & 15) == 0));
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
+        tmem_ld_wait();
+        if (row >= p.M || n0 + c0 >= p.N) continue;
+        float v[32];
+        const int col0 = n0 + c0;
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+        if (p.epilogue == FG_EPI_BIAS || p.epilogue == FG_EPI_BIAS_RELU) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            const float b = (col0 + j < p.N) ? __ldg(p.bias + col0 + j) : 0.f;
+            float z = __fadd_rn(v[j], b);
+            if (p.epilogue == FG_EPI_BIAS_RELU) z = (0.0f < z) ? z : 0.0f;
+            v[j] = z;
+          }
+        } else if (p.epilogue == FG_EPI_RELU_MASK) {
+          const float *mrow = p.mask + (size_t)row * p.ldmask + col0;
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            const float mk = (col0 + j < p.N) ? __ldg(mrow + j) : 0.f;
+            v[j] = (mk > 0.0f) ? v[j] : 0.0f;
+          }
+        }
+        float *crow = p.C + (size_t)row * p.ldc + col0;
+        float *lrow = p.C_lo ? p.C_lo + (size_t)row * p.ldc + col0 : nullptr;
+        if (vec && col0 + 32 <= p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            *reinterpret_cast<float4 *>(crow + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            if (lrow)
+              *reinterpret_cast<float4 *>(lrow + j) =
+                  make_float4(tf32_residual(v[j]), tf32_residual(v[j + 1]),
+                              tf32_residual(v[j + 2]), tf32_residual(v[j + 3]));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            if (col0 + j < p.N) {
+              crow[j] = v[j];
+              if (lrow) lrow[j] = tf32_residual(v[j]);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  });
+  return fn;
+}
+
+// Tensor map over a row-major fp32 matrix of `outer` rows x `inner` columns
+// with row pitch `ld` elements; box = 32 columns x box_rows rows, 128B swizzle.
+static int make_map(CUtensorMap *map, const float *ptr, int inner, int outer, int ld,
+                    int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(FG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)ptr, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FG_ERR_CUDA,
+                     "cuTensorMapEncodeTiled failed (%d): inner=%d outer=%d ld=%d box_rows=%d",
+                     (int)r, inner, outer, ld, box_rows);
+  return FG_OK;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static int launch_t(const GemmPlan &pl, cudaStream_t st) {
+  using C = Cfg<BN>;
+  auto kern = k_gemm3x<BN, A_MN, B_MN>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    FG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::SMEM_BYTES));
+    attr_done[dev] = true;
+  }
+  dim3 grid((pl.p.N + BN - 1) / BN, (pl.p.M + BM - 1) / BM);
+  kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(pl.a, pl.alo, pl.b, pl.blo, pl.p);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, const float *b,
+              const float *b_lo, int ldb, float *c, float *c_lo, int ldc, int flags, int epilogue,
+              const float *bias, const float *mask, int ldmask, GemmPlan *pl) {
+  FG_REQUIRE(M > 0 && N > 0 && K > 0, "gemm: M, N, K must be positive (got %d, %d, %d)", M, N, K);
+  FG_REQUIRE(a && b && c, "gemm: null operand");
+  const bool a_mn = flags & FG_GEMM_A_MN_MAJOR, b_mn = flags & FG_GEMM_B_MN_MAJOR;
+  const bool one = flags & FG_GEMM_1XTF32;
+  FG_REQUIRE(one || (a_lo && b_lo), "gemm: 3xTF32 needs the A and B residuals");
+  FG_REQUIRE(lda % 4 == 0 && ldb % 4 == 0, "gemm: lda/ldb must be multiples of 4 elements");
+  FG_REQUIRE(lda >= (a_mn ? M : K) && ldb >= (b_mn ? N : K) && ldc >= N, "gemm: pitch too small");
+  auto al = [](const void *q) { return q == nullptr || (((uintptr_t)q) & 15) == 0; };
+  FG_REQUIRE(al(a) && al(a_lo) && al(b) && al(b_lo), "gemm: operands must be 16-byte aligned");
+  FG_REQUIRE(epilogue >= FG_EPI_NONE && epilogue <= FG_EPI_RELU_MASK, "gemm: bad epilogue %d",
+             epilogue);
+  FG_REQUIRE(epilogue != FG_EPI_BIAS && epilogue != FG_EPI_BIAS_RELU ? true : bias != nullptr,
+             "gemm: epilogue needs a bias");
+  FG_REQUIRE(epilogue != FG_EPI_RELU_MASK || (mask && ldmask >= N), "gemm: epilogue needs a mask");
+  const int bn = 128;
+  int rc;
+  // A: [M,K] K-major (box 32 x BM rows) or [K,M] MN-major (box 32 x 32)
+  if (a_mn) {
+    if ((rc = make_map(&pl->a, a, M, K, lda, 32))) return rc;
+    if ((rc = make_map(&pl->alo, one ? a : a_lo, M, K, lda, 32))) return rc;
+  } else {
+    if ((rc = make_map(&pl->a, a, K, M, lda, BM))) return rc;
+    if ((rc = make_map(&pl->alo, one ? a : a_lo, K, M, lda, BM))) return rc;
+  }
+  if (b_mn) {
+    if ((rc = make_map(&pl->b, b, N, K, ldb, 32))) return rc;
+    if ((rc = make_map(&pl->blo, one ? b : b_lo, N, K, ldb, 32))) return rc;
+  } else {
+    if ((rc = make_map(&pl->b, b, K, N, ldb, bn))) return rc;
+    if ((rc = make_map(&pl->blo, one ? b : b_lo, K, N, ldb, bn))) return rc;
+  }
+  DevCtx *ctx = ctx_current();
+  if (!ctx) return set_error(FG_ERR_CUDA, "no CUDA device context");
+  GemmParams &p = pl->p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = c;
+  p.C_lo = c_lo;
+  p.ldc = ldc;
+  p.bias = bias;
+  p.mask = mask;
+  p.ldmask = ldmask;
+  p.epilogue = epilogue;
+  p.one_pass = one ? 1 : 0;
+  p.err = ctx->d_err;
+  pl->bn = bn;
+  pl->a_mn = a_mn;
+  pl->b_mn = b_mn;
+  return FG_OK;
+}
+
+int run_plan(const GemmPlan &pl, cudaStream_t st) {
+  if (pl.bn == 128) {
+    if (!pl.a_mn && !pl.b_mn) return launch_t<128, false, false>(pl, st);
+    if (!pl.a_mn && pl.b_mn) return launch_t<128, false, true>(pl, st);
+    if (pl.a_mn && !pl.b_mn) return launch_t<128, true, false>(pl, st);
+    return launch_t<128, true, true>(pl, st);
+  }
+  return set_error(FG_ERR_UNSUPPORTED, "gemm: tile width %d not built", pl.bn);
+}
+
+}  // namespace gemm
+}  // namespace fg
+
+extern "C" int fg_gemm_3xtf32(int M, int N, int K, const float *d_a, const float *d_a_lo, int lda,
+                              const float *d_b, const float *d_b_lo, int ldb, float *d_c,
+                              float *d_c_lo, int ldc, int flags, int epilogue, const float *d_bias,
+                              const float *d_mask, int ldmask, void *stream) {
+  fg::gemm::GemmPlan pl;
+  int rc = fg::gemm::make_plan(M, N, K, d_a, d_a_lo, lda, d_b, d_b_lo, ldb, d_c, d_c_lo, ldc, flags,
+                               epilogue, d_bias, d_mask, ldmask, &pl);
+  if (rc) return rc;
+  return fg::gemm::run_plan(pl, (cudaStream_t)stream);
+}

@@ -1,0 +1,637 @@
+// HBM-bound building blocks: fused elementwise chain, row / column
+// reductions (f32 and bit-exact i32), fused cross-entropy forward+backward,
+// SGD update and the TF32 residual split.
+//
+// All of these stream their operands once: 128-bit loads and stores where
+// the layout allows, grids sized in multiples of the SM count, warp-shuffle
+// reductions with a fixed (deterministic) order.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fg_internal.h"
+#include "fg_kernels.cuh"
+
+namespace fg {
+
+// Reference op semantics (src/codegen/clang.rs:216-229): max is a ternary,
+// every op rounds separately (no FMA contraction).
+__device__ __forceinline__ float ref_max(float a, float b) { return (a > b) ? a : b; }
+__device__ __forceinline__ int32_t ref_max_i(int32_t a, int32_t b) { return (a > b) ? a : b; }
+__device__ __forceinline__ int32_t add_wrap(int32_t a, int32_t b) {
+  return (int32_t)((uint32_t)a + (uint32_t)b);
+}
+
+static int grid_for(size_t work_items, int threads, int per_sm = 8) {
+  DevCtx *c = ctx_current();
+  int sms = (c && c->num_sms) ? c->num_sms : 148;
+  size_t want = (work_items + threads - 1) / threads;
+  size_t cap = (size_t)sms * per_sm;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  return (int)want;
+}
+
+// ---------------------------------------------------------------------------
+// relu(a*b+c)*scale: t = a*b; t = t + c; r = (0 < t) ? t : 0; out = r*scale
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float ew_one(float a, float b, float c, float s) {
+  float t = __fmul_rn(a, b);
+  t = __fadd_rn(t, c);
+  float r = (0.0f < t) ? t : 0.0f;
+  return __fmul_rn(r, s);
+}
+
+__global__ void __launch_bounds__(256) k_ew_fma_relu_scale_v4(const float4 *__restrict__ a,
+                                                              const float4 *__restrict__ b,
+                                                              const float4 *__restrict__ c,
+                                                              float4 *__restrict__ out,
+                                                              size_t n4, float s) {
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  // Two independent 16-byte loads per operand in flight per iteration.
+  for (; i + stride < n4; i += 2 * stride) {
+    float4 a0 = __ldcs(a + i), b0 = __ldcs(b + i), c0 = __ldcs(c + i);
+    float4 a1 = __ldcs(a + i + stride), b1 = __ldcs(b + i + stride), c1 = __ldcs(c + i + stride);
+    float4 r0, r1;
+    r0.x = ew_one(a0.x, b0.x, c0.x, s); r0.y = ew_one(a0.y, b0.y, c0.y, s);
+    r0.z = ew_one(a0.z, b0.z, c0.z, s); r0.w = ew_one(a0.w, b0.w, c0.w, s);
+    r1.x = ew_one(a1.x, b1.x, c1.x, s); r1.y = ew_one(a1.y, b1.y, c1.y, s);
+    r1.z = ew_one(a1.z, b1.z, c1.z, s); r1.w = ew_one(a1.w, b1.w, c1.w, s);
+    __stcs(out + i, r0);
+    __stcs(out + i + stride, r1);
+  }
+  if (i < n4) {
+    float4 a0 = __ldcs(a + i), b0 = __ldcs(b + i), c0 = __ldcs(c + i);
+    float4 r0;
+    r0.x = ew_one(a0.x, b0.x, c0.x, s); r0.y = ew_one(a0.y, b0.y, c0.y, s);
+    r0.z = ew_one(a0.z, b0.z, c0.z, s); r0.w = ew_one(a0.w, b0.w, c0.w, s);
+    __stcs(out + i, r0);
+  }
+}
+
+__global__ void k_ew_fma_relu_scale_tail(const float *__restrict__ a, const float *__restrict__ b,
+                                         const float *__restrict__ c, float *__restrict__ out,
+                                         size_t begin, size_t n, float s) {
+  size_t i = begin + (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i < n; i += (size_t)gridDim.x * blockDim.x) out[i] = ew_one(a[i], b[i], c[i], s);
+}
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+int launch_ew_fma_relu_scale(const float *a, const float *b, const float *c, float *out, size_t n,
+                             float scale, cudaStream_t st) {
+  if (n == 0) return FG_OK;
+  size_t n4 = 0;
+  if (aligned16(a) && aligned16(b) && aligned16(c) && aligned16(out)) n4 = n / 4;
+  if (n4) {
+    k_ew_fma_relu_scale_v4<<<grid_for(n4 / 2 + 1, 256, 16), 256, 0, st>>>(
+        (const float4 *)a, (const float4 *)b, (const float4 *)c, (float4 *)out, n4, scale);
+    FG_LAUNCH_TRY();
+  }
+  if (n4 * 4 < n) {
+    k_ew_fma_relu_scale_tail<<<grid_for(n - n4 * 4, 256), 256, 0, st>>>(a, b, c, out, n4 * 4, n,
+                                                                         scale);
+    FG_LAUNCH_TRY();
+  }
+  return FG_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Row reductions: one warp per row, 16-byte loads, shuffle tree.
+// ---------------------------------------------------------------------------
+template <typename T, int OP>
+__device__ __forceinline__ T red_identity();
+template <> __device__ __forceinline__ float red_identity<float, FG_REDUCE_SUM>() { return 0.0f; }
+template <> __device__ __forceinline__ float red_identity<float, FG_REDUCE_MAX>() { return -INFINITY; }
+template <> __device__ __forceinline__ int32_t red_identity<int32_t, FG_REDUCE_SUM>() { return 0; }
+template <> __device__ __forceinline__ int32_t red_identity<int32_t, FG_REDUCE_MAX>() { return INT32_MIN; }
+
+template <int OP>
+__device__ __forceinline__ float red_op(float a, float b) {
+  return OP == FG_REDUCE_SUM ? __fadd_rn(a, b) : ref_max(a, b);
+}
+template <int OP>
+__device__ __forceinline__ int32_t red_op(int32_t a, int32_t b) {
+  return OP == FG_REDUCE_SUM ? add_wrap(a, b) : ref_max_i(a, b);
+}
+
+template <typename T, int OP>
+__device__ __forceinline__ T warp_reduce(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = red_op<OP>(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <typename T, int OP, bool VEC>
+__global__ void __launch_bounds__(256) k_reduce_rows(const T *__restrict__ x, T *__restrict__ out,
+                                                     size_t rows, size_t cols) {
+  const int lane = threadIdx.x & 31;
+  size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const size_t wstride = (size_t)gridDim.x * (blockDim.x >> 5);
+  for (; row < rows; row += wstride) {
+    const T *p = x + row * cols;
+    T acc0 = red_identity<T, OP>(), acc1 = red_identity<T, OP>();
+    if (VEC) {
+      using V = typename std::conditional<sizeof(T) == 4, uint4, uint4>::type;
+      const size_t nv = cols / 4;
+      const V *pv = reinterpret_cast<const V *>(p);
+      size_t j = lane;
+      for (; j + 32 < nv; j += 64) {
+        V u0 = __ldcs(pv + j), u1 = __ldcs(pv + j + 32);
+        const T *f0 = reinterpret_cast<const T *>(&u0);
+        const T *f1 = reinterpret_cast<const T *>(&u1);
+        acc0 = red_op<OP>(acc0, red_op<OP>(red_op<OP>(f0[0], f0[1]), red_op<OP>(f0[2], f0[3])));
+        acc1 = red_op<OP>(acc1, red_op<OP>(red_op<OP>(f1[0], f1[1]), red_op<OP>(f1[2], f1[3])));
+      }
+      if (j < nv) {
+        V u0 = __ldcs(pv + j);
+        const T *f0 = reinterpret_cast<const T *>(&u0);
+        acc0 = red_op<OP>(acc0, red_op<OP>(red_op<OP>(f0[0], f0[1]), red_op<OP>(f0[2], f0[3])));
+      }
+    } else {
+      for (size_t j = lane; j < cols; j += 32) acc0 = red_op<OP>(acc0, p[j]);
+    }
+    T acc = warp_reduce<T, OP>(red_op<OP>(acc0, acc1));
+    if (lane == 0) out[row] = acc;
+  }
+}
+
+template <typename T, int OP>
+static int launch_rows_t(const void *x, void *out, size_t rows, size_t cols, cudaStream_t st) {
+  const bool vec = (cols % 4 == 0) && aligned16(x);
+  int grid = grid_for(rows * 32, 256, 16);
+  if (vec)
+    k_reduce_rows<T, OP, true><<<grid, 256, 0, st>>>((const T *)x, (T *)out, rows, cols);
+  else
+    k_reduce_rows<T, OP, false><<<grid, 256, 0, st>>>((const T *)x, (T *)out, rows, cols);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+int launch_reduce_rows(int dtype, int op, const void *x, void *out, size_t rows, size_t cols,
+                       cudaStream_t st) {
+  if (rows == 0) return FG_OK;
+  if (dtype == FG_F32)
+    return op == FG_REDUCE_SUM ? launch_rows_t<float, FG_REDUCE_SUM>(x, out, rows, cols, st)
+                               : launch_rows_t<float, FG_REDUCE_MAX>(x, out, rows, cols, st);
+  return op == FG_REDUCE_SUM ? launch_rows_t<int32_t, FG_REDUCE_SUM>(x, out, rows, cols, st)
+                             : launch_rows_t<int32_t, FG_REDUCE_MAX>(x, out, rows, cols, st);
+}
+
+// ---------------------------------------------------------------------------
+// Column reductions (axis 0).  Pass 1: each block owns a 256-column strip and
+// a chunk of rows, threads run down the columns (coalesced), partial results
+// go to scratch [nchunks, cols].  Pass 2 folds the chunks in chunk order.
+// ---------------------------------------------------------------------------
+constexpr int kColTile = 256;
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(256) k_reduce_cols_partial(const T *__restrict__ x,
+                                                             T *__restrict__ part, size_t rows,
+                                                             size_t cols, size_t rows_per_chunk) {
+  size_t col = (size_t)blockIdx.x * kColTile + threadIdx.x;
+  size_t r0 = (size_t)blockIdx.y * rows_per_chunk;
+  size_t r1 = r0 + rows_per_chunk < rows ? r0 + rows_per_chunk : rows;
+  if (col >= cols) return;
+  T a0 = red_identity<T, OP>(), a1 = red_identity<T, OP>();
+  T a2 = red_identity<T, OP>(), a3 = red_identity<T, OP>();
+  size_t r = r0;
+  for (; r + 4 <= r1; r += 4) {
+    a0 = red_op<OP>(a0, __ldcs(x + r * cols + col));
+    a1 = red_op<OP>(a1, __ldcs(x + (r + 1) * cols + col));
+    a2 = red_op<OP>(a2, __ldcs(x + (r + 2) * cols + col));
+    a3 = red_op<OP>(a3, __ldcs(x + (r + 3) * cols + col));
+  }
+  for (; r < r1; r++) a0 = red_op<OP>(a0, __ldcs(x + r * cols + col));
+  part[blockIdx.y * cols + col] = red_op<OP>(red_op<OP>(a0, a1), red_op<OP>(a2, a3));
+}
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(256) k_reduce_cols_final(const T *__restrict__ part,
+                                                           T *__restrict__ out, size_t nchunks,
+                                                           size_t cols) {
+  size_t col = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= cols) return;
+  T acc = red_identity<T, OP>();
+  for (size_t c = 0; c < nchunks; c++) acc = red_op<OP>(acc, part[c * cols + col]);
+  out[col] = acc;
+}
+
+template <typename T, int OP>
+static int launch_cols_t(const void *x, void *out, size_t rows, size_t cols, cudaStream_t st,
+                         void *scratch, size_t scratch_bytes) {
+  if (rows == 0) {  // empty reduction: the identity in every column
+    k_reduce_cols_final<T, OP><<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(nullptr, (T *)out, 0,
+                                                                              cols);
+    FG_LAUNCH_TRY();
+    return FG_OK;
+  }
+  size_t col_tiles = (cols + kColTile - 1) / kColTile;
+  DevCtx *c = ctx_current();
+  size_t sms = (c && c->num_sms) ? c->num_sms : 148;
+  // Enough chunks that col_tiles * nchunks fills every SM ~8 times, each
+  // chunk at least 32 rows.
+  size_t nchunks = (sms * 8 + col_tiles - 1) / col_tiles;
+  size_t max_chunks = (rows + 31) / 32;
+  if (nchunks > max_chunks) nchunks = max_chunks;
+  if (nchunks < 1) nchunks = 1;
+  size_t rpc = (rows + nchunks - 1) / nchunks;
+  nchunks = (rows + rpc - 1) / rpc;
+  size_t need = nchunks * cols * sizeof(T);
+  if (!scratch) {
+    int status = FG_OK;
+    scratch = workspace(need, &status);
+    if (!scratch) return status;
+  } else if (scratch_bytes < need) {
+    return set_error(FG_ERR_INVALID, "column reduce needs %zu scratch bytes, have %zu", need,
+                     scratch_bytes);
+  }
+  dim3 g1((unsigned)col_tiles, (unsigned)nchunks);
+  k_reduce_cols_partial<T, OP><<<g1, kColTile, 0, st>>>((const T *)x, (T *)scratch, rows, cols, rpc);
+  FG_LAUNCH_TRY();
+  k_reduce_cols_final<T, OP><<<(unsigned)((cols + 255) / 256), 256, 0, st>>>((const T *)scratch,
+                                                                            (T *)out, nchunks, cols);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+size_t reduce_cols_scratch_bytes(size_t rows, size_t cols) {
+  // Upper bound used by callers that provide their own scratch.
+  size_t col_tiles = (cols + kColTile - 1) / kColTile;
+  size_t nchunks = (148 * 8 + col_tiles - 1) / col_tiles + 1;
+  size_t max_chunks = (rows + 31) / 32;
+  if (nchunks > max_chunks) nchunks = max_chunks;
+  if (nchunks < 1) nchunks = 1;
+  return nchunks * cols * 4;
+}
+
+int launch_reduce_cols(int dtype, int op, const void *x, void *out, size_t rows, size_t cols,
+                       cudaStream_t st, void *scratch, size_t scratch_bytes) {
+  if (cols == 0) return FG_OK;
+#define FG_COLS(T, OP) launch_cols_t<T, OP>(x, out, rows, cols, st, scratch, scratch_bytes)
+  if (dtype == FG_F32)
+    return op == FG_REDUCE_SUM ? FG_COLS(float, FG_REDUCE_SUM) : FG_COLS(float, FG_REDUCE_MAX);
+  return op == FG_REDUCE_SUM ? FG_COLS(int32_t, FG_REDUCE_SUM) : FG_COLS(int32_t, FG_REDUCE_MAX);
+#undef FG_COLS
+}
+
+// ---------------------------------------------------------------------------
+// Cross-entropy forward + backward (src/tensor.rs:715-752 and the autograd
+// graph of src/gradient.rs:97-205), one warp per row.  Per row:
+//   m = max x; s = x - m; e = exp2(s*log2e); se = sum e; lse = log2(se)*ln2
+//   nps = -sum t*(s - lse)                          (loss term of the row)
+//   g_lp = t*(-1/B); g_se = (ln2*(sum g_lp)) * (1/(se*ln2))
+//   g_s = g_lp + log2e*((e*ln2)*g_se)
+//   dx = g_s + (mask/count) * (-sum g_s),  mask = (x < m) ? 0 : 1
+// The row's loss terms go to scratch and are summed in row order by a
+// second kernel (deterministic).
+// ---------------------------------------------------------------------------
+constexpr float kLog2e = 1.44269504088896340736f;
+constexpr float kLn2 = 0.693147180559945309417f;
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = ref_max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// NV float4 per lane held in registers: cols <= 128 * NV, cols % 4 == 0.
+template <int NV>
+__global__ void __launch_bounds__(256) k_xent_rows_v4(const float *__restrict__ x,
+                                                      const float *__restrict__ t,
+                                                      float *__restrict__ dx,
+                                                      float *__restrict__ row_loss, size_t rows,
+                                                      int cols, float inv_n, float gscale) {
+  const int lane = threadIdx.x & 31;
+  size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const size_t wstride = (size_t)gridDim.x * (blockDim.x >> 5);
+  const int nv = cols / 4;
+  for (; row < rows; row += wstride) {
+    const float4 *xv = reinterpret_cast<const float4 *>(x + row * (size_t)cols);
+    const float4 *tv = reinterpret_cast<const float4 *>(t + row * (size_t)cols);
+    float4 xr[NV], tr[NV];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      int j = lane + 32 * i;
+      if (j < nv) {
+        xr[i] = __ldcs(xv + j);
+        tr[i] = __ldcs(tv + j);
+        m = ref_max(m, ref_max(ref_max(xr[i].x, xr[i].y), ref_max(xr[i].z, xr[i].w)));
+      }
+    }
+    m = warp_max(m);
+    float se = 0.f, st_ = 0.f, sts = 0.f, cnt = 0.f;
+    uint32_t maxbits = 0;  // bit (4i+q) set where x == row max (mask of the max path)
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      int j = lane + 32 * i;
+      if (j < nv) {
+        float *xe = reinterpret_cast<float *>(&xr[i]);
+        const float *te = reinterpret_cast<const float *>(&tr[i]);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          float s = __fsub_rn(xe[q], m);
+          float e = exp2f(__fmul_rn(s, kLog2e));
+          se += e;
+          st_ += te[q];
+          sts += __fmul_rn(te[q], s);
+          if (!(xe[q] < m)) {
+            cnt += 1.0f;
+            maxbits |= 1u << (4 * i + q);
+          }
+          xe[q] = e;  // the register now holds e
+        }
+      }
+    }
+    se = warp_sum(se);
+    st_ = warp_sum(st_);
+    sts = warp_sum(sts);
+    cnt = warp_sum(cnt);
+    const float lse = __fmul_rn(log2f(se), kLn2);
+    // nps = -(sum t*(s - lse)) = -(sum t*s) + lse * sum t
+    const float nps = -(sts - lse * st_);
+    const float g_lp_scale = -inv_n * gscale;
+    const float g_nlse = g_lp_scale * st_;             // sum_c t * (-1/B)
+    const float g_lse = -g_nlse;
+    const float g_se = __fmul_rn(__fmul_rn(kLn2, g_lse), 1.0f / __fmul_rn(se, kLn2));
+    // g_s = t*g_lp_scale + log2e*((e*ln2)*g_se); its row sum feeds the max path.
+    float gsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      int j = lane + 32 * i;
+      if (j < nv) {
+        const float *e = reinterpret_cast<const float *>(&xr[i]);
+        const float *te = reinterpret_cast<const float *>(&tr[i]);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          float gs = __fadd_rn(__fmul_rn(te[q], g_lp_scale),
+                               __fmul_rn(kLog2e, __fmul_rn(__fmul_rn(e[q], kLn2), g_se)));
+          gsum += gs;
+        }
+      }
+    }
+    gsum = warp_sum(gsum);
+    const float g_m = -gsum;
+    const float wmax = __fmul_rn(1.0f / cnt, g_m);
+    if (dx) {
+      float4 *dv = reinterpret_cast<float4 *>(dx + row * (size_t)cols);
+#pragma unroll
+      for (int i = 0; i < NV; i++) {
+        int j = lane + 32 * i;
+        if (j < nv) {
+          const float *e = reinterpret_cast<const float *>(&xr[i]);
+          const float *te = reinterpret_cast<const float *>(&tr[i]);
+          float4 o;
+          float *oe = reinterpret_cast<float *>(&o);
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            float gs = __fadd_rn(__fmul_rn(te[q], g_lp_scale),
+                                 __fmul_rn(kLog2e, __fmul_rn(__fmul_rn(e[q], kLn2), g_se)));
+            float mask = ((maxbits >> (4 * i + q)) & 1u) ? 1.0f : 0.0f;
+            oe[q] = __fadd_rn(gs, __fmul_rn(mask, wmax));
+          }
+          __stcs(dv + j, o);
+        }
+      }
+    }
+    if (lane == 0) row_loss[row] = nps;
+  }
+}
+
+// Generic path (any cols): three sweeps over the row from global memory.
+__global__ void __launch_bounds__(256) k_xent_rows_generic(const float *__restrict__ x,
+                                                           const float *__restrict__ t,
+                                                           float *__restrict__ dx,
+                                                           float *__restrict__ row_loss,
+                                                           size_t rows, int cols, float inv_n,
+                                                           float gscale) {
+  const int lane = threadIdx.x & 31;
+  size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const size_t wstride = (size_t)gridDim.x * (blockDim.x >> 5);
+  for (; row < rows; row += wstride) {
+    const float *xr = x + row * (size_t)cols;
+    const float *tr = t + row * (size_t)cols;
+    float m = -INFINITY;
+    for (int c = lane; c < cols; c += 32) m = ref_max(m, xr[c]);
+    m = warp_max(m);
+    float se = 0.f, st_ = 0.f, sts = 0.f, cnt = 0.f;
+    for (int c = lane; c < cols; c += 32) {
+      float s = __fsub_rn(xr[c], m);
+      se += exp2f(__fmul_rn(s, kLog2e));
+      st_ += tr[c];
+      sts += __fmul_rn(tr[c], s);
+      cnt += (xr[c] < m) ? 0.0f : 1.0f;
+    }
+    se = warp_sum(se);
+    st_ = warp_sum(st_);
+    sts = warp_sum(sts);
+    cnt = warp_sum(cnt);
+    const float lse = __fmul_rn(log2f(se), kLn2);
+    const float nps = -(sts - lse * st_);
+    const float g_lp_scale = -inv_n * gscale;
+    const float g_lse = -(g_lp_scale * st_);
+    const float g_se = __fmul_rn(__fmul_rn(kLn2, g_lse), 1.0f / __fmul_rn(se, kLn2));
+    float gsum = 0.f;
+    for (int c = lane; c < cols; c += 32) {
+      float e = exp2f(__fmul_rn(__fsub_rn(xr[c], m), kLog2e));
+      gsum += __fadd_rn(__fmul_rn(tr[c], g_lp_scale),
+                        __fmul_rn(kLog2e, __fmul_rn(__fmul_rn(e, kLn2), g_se)));
+    }
+    gsum = warp_sum(gsum);
+    const float wmax = __fmul_rn(1.0f / cnt, -gsum);
+    if (dx) {
+      for (int c = lane; c < cols; c += 32) {
+        float e = exp2f(__fmul_rn(__fsub_rn(xr[c], m), kLog2e));
+        float gs = __fadd_rn(__fmul_rn(tr[c], g_lp_scale),
+                             __fmul_rn(kLog2e, __fmul_rn(__fmul_rn(e, kLn2), g_se)));
+        float mask = (xr[c] < m) ? 0.0f : 1.0f;
+        dx[row * (size_t)cols + c] = __fadd_rn(gs, __fmul_rn(mask, wmax));
+      }
+    }
+    if (lane == 0) row_loss[row] = nps;
+  }
+}
+
+// Sum of the row loss terms in a fixed order (one block, strided partials
+// combined by a fixed tree), times 1/B.
+__global__ void __launch_bounds__(1024) k_xent_loss_final(const float *__restrict__ row_loss,
+                                                          size_t rows, float inv_n,
+                                                          float *__restrict__ loss) {
+  __shared__ float sh[32];
+  float acc = 0.f;
+  for (size_t r = threadIdx.x; r < rows; r += blockDim.x) acc += row_loss[r];
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = (threadIdx.x < (blockDim.x >> 5)) ? sh[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) loss[0] = __fmul_rn(v, inv_n);
+  }
+}
+
+int launch_xent(const float *x, const float *t, size_t rows, size_t cols, float *loss, float *dx,
+                float gscale, cudaStream_t st, float *row_scratch) {
+  if (rows == 0 || cols == 0) return set_error(FG_ERR_INVALID, "cross_entropy: empty logits");
+  if (cols > (size_t)INT32_MAX) return set_error(FG_ERR_UNSUPPORTED, "cross_entropy: cols too large");
+  float *scratch = row_scratch;
+  if (!scratch) {
+    int status = FG_OK;
+    scratch = (float *)workspace(rows * sizeof(float), &status);
+    if (!scratch) return status;
+  }
+  const float inv_n = 1.0f / (float)rows;
+  const int c = (int)cols;
+  int grid = grid_for(rows * 32, 256, 16);
+  const bool vec = (cols % 4 == 0) && aligned16(x) && aligned16(t) && (!dx || aligned16(dx));
+  if (vec && cols <= 128)
+    k_xent_rows_v4<1><<<grid, 256, 0, st>>>(x, t, dx, scratch, rows, c, inv_n, gscale);
+  else if (vec && cols <= 256)
+    k_xent_rows_v4<2><<<grid, 256, 0, st>>>(x, t, dx, scratch, rows, c, inv_n, gscale);
+  else if (vec && cols <= 512)
+    k_xent_rows_v4<4><<<grid, 256, 0, st>>>(x, t, dx, scratch, rows, c, inv_n, gscale);
+  else if (vec && cols <= 1024)
+    k_xent_rows_v4<8><<<grid, 256, 0, st>>>(x, t, dx, scratch, rows, c, inv_n, gscale);
+  else
+    k_xent_rows_generic<<<grid, 256, 0, st>>>(x, t, dx, scratch, rows, c, inv_n, gscale);
+  FG_LAUNCH_TRY();
+  k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, rows, inv_n, loss);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+// ---------------------------------------------------------------------------
+// SGD (src/optim.rs:60-71): p = p + (-(g*lr)); optional TF32 residual of p.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float sgd_one(float p, float g, float lr) {
+  return __fadd_rn(p, -__fmul_rn(g, lr));
+}
+__device__ __forceinline__ float tf32_lo(float v) {
+  float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
+  return __fsub_rn(v, hi);
+}
+
+__global__ void __launch_bounds__(256) k_sgd_multi(SgdSegments segs, float lr) {
+  for (int s = 0; s < segs.count; s++) {
+    float *p = segs.p[s];
+    const float *g = segs.g[s];
+    float *lo = segs.lo[s];
+    const size_t n = segs.n[s];
+    const bool vec = ((((uintptr_t)p) | ((uintptr_t)g) | ((uintptr_t)lo)) & 15) == 0;
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    size_t done = 0;
+    if (vec) {
+      const size_t n4 = n / 4;
+      for (size_t j = i; j < n4; j += stride) {
+        float4 pv = reinterpret_cast<float4 *>(p)[j];
+        float4 gv = __ldcs(reinterpret_cast<const float4 *>(g) + j);
+        pv.x = sgd_one(pv.x, gv.x, lr); pv.y = sgd_one(pv.y, gv.y, lr);
+        pv.z = sgd_one(pv.z, gv.z, lr); pv.w = sgd_one(pv.w, gv.w, lr);
+        reinterpret_cast<float4 *>(p)[j] = pv;
+        if (lo) {
+          float4 lv = make_float4(tf32_lo(pv.x), tf32_lo(pv.y), tf32_lo(pv.z), tf32_lo(pv.w));
+          reinterpret_cast<float4 *>(lo)[j] = lv;
+        }
+      }
+      done = n4 * 4;
+    }
+    for (size_t j = done + i; j < n; j += stride) {
+      float v = sgd_one(p[j], g[j], lr);
+      p[j] = v;
+      if (lo) lo[j] = tf32_lo(v);
+    }
+  }
+}
+
+int launch_sgd_multi(const SgdSegments &segs, float lr, cudaStream_t st) {
+  size_t maxn = 0;
+  for (int s = 0; s < segs.count; s++) maxn = segs.n[s] > maxn ? segs.n[s] : maxn;
+  if (!maxn) return FG_OK;
+  k_sgd_multi<<<grid_for(maxn / 4 + 1, 256, 16), 256, 0, st>>>(segs, lr);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+__global__ void __launch_bounds__(256) k_split_lo(const float *__restrict__ x,
+                                                  float *__restrict__ lo, size_t n) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool vec = ((((uintptr_t)x) | ((uintptr_t)lo)) & 15) == 0;
+  size_t done = 0;
+  if (vec) {
+    const size_t n4 = n / 4;
+    for (size_t j = i; j < n4; j += stride) {
+      float4 v = __ldcs(reinterpret_cast<const float4 *>(x) + j);
+      float4 o = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+      __stcs(reinterpret_cast<float4 *>(lo) + j, o);
+    }
+    done = n4 * 4;
+  }
+  for (size_t j = done + i; j < n; j += stride) lo[j] = tf32_lo(x[j]);
+}
+
+int launch_split_lo(const float *x, float *lo, size_t n, cudaStream_t st) {
+  if (!n) return FG_OK;
+  k_split_lo<<<grid_for(n / 4 + 1, 256, 16), 256, 0, st>>>(x, lo, n);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+}  // namespace fg
+
+extern "C" {
+
+int fg_ew_fma_relu_scale(const float *d_a, const float *d_b, const float *d_c, float *d_out,
+                         size_t n, float scale, void *stream) {
+  FG_REQUIRE(n == 0 || (d_a && d_b && d_c && d_out), "fg_ew_fma_relu_scale: null pointer");
+  return fg::launch_ew_fma_relu_scale(d_a, d_b, d_c, d_out, n, scale, (cudaStream_t)stream);
+}
+
+int fg_reduce_rows(int dtype, int op, const void *d_x, void *d_out, size_t rows, size_t cols,
+                   void *stream) {
+  FG_REQUIRE(dtype == FG_F32 || dtype == FG_I32, "fg_reduce_rows: dtype must be F32 or I32");
+  FG_REQUIRE(op == FG_REDUCE_SUM || op == FG_REDUCE_MAX, "fg_reduce_rows: unknown op %d", op);
+  FG_REQUIRE(rows == 0 || (d_out && (cols == 0 || d_x)), "fg_reduce_rows: null pointer");
+  return fg::launch_reduce_rows(dtype, op, d_x, d_out, rows, cols, (cudaStream_t)stream);
+}
+
+int fg_reduce_cols(int dtype, int op, const void *d_x, void *d_out, size_t rows, size_t cols,
+                   void *stream) {
+  FG_REQUIRE(dtype == FG_F32 || dtype == FG_I32, "fg_reduce_cols: dtype must be F32 or I32");
+  FG_REQUIRE(op == FG_REDUCE_SUM || op == FG_REDUCE_MAX, "fg_reduce_cols: unknown op %d", op);
+  FG_REQUIRE(cols == 0 || (d_out && (rows == 0 || d_x)), "fg_reduce_cols: null pointer");
+  return fg::launch_reduce_cols(dtype, op, d_x, d_out, rows, cols, (cudaStream_t)stream, nullptr, 0);
+}
+
+int fg_xent_fwd_bwd(const float *d_logits, const float *d_targets, size_t rows, size_t cols,
+                    float *d_loss, float *d_dx, float grad_scale, void *stream) {
+  FG_REQUIRE(d_logits && d_targets && d_loss, "fg_xent_fwd_bwd: null pointer");
+  return fg::launch_xent(d_logits, d_targets, rows, cols, d_loss, d_dx, grad_scale,
+                         (cudaStream_t)stream, nullptr);
+}
+
+int fg_sgd(float *d_p, const float *d_g, size_t n, float lr, float *d_p_lo, void *stream) {
+  FG_REQUIRE(n == 0 || (d_p && d_g), "fg_sgd: null pointer");
+  fg::SgdSegments s{};
+  s.count = 1;
+  s.p[0] = d_p;
+  s.g[0] = d_g;
+  s.lo[0] = d_p_lo;
+  s.n[0] = n;
+  return fg::launch_sgd_multi(s, lr, (cudaStream_t)stream);
+}
+
+int fg_split_lo(const float *d_x, float *d_lo, size_t n, void *stream) {
+  FG_REQUIRE(n == 0 || (d_x && d_lo), "fg_split_lo: null pointer");
+  return fg::launch_split_lo(d_x, d_lo, n, (cudaStream_t)stream);
+}
+
+}  // extern "C"

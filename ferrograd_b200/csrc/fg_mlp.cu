@@ -1,0 +1,754 @@
+// The MLP training step -- examples/mnist.rs:90-97 (forward, cross_entropy,
+// zero_grad, backward, Sgd::step, loss.to_vec) -- as a fixed schedule of this
+// library's kernels.  It is the schedule ferrograd's scheduler produces for
+// Linear (src/nn.rs:97-104) / relu (src/tensor.rs:519-531) / cross_entropy
+// (src/tensor.rs:738-752) / Sgd (src/optim.rs:60-71) graphs, with every
+// proto-kernel routed to a hand-written building block:
+//
+//   Linear forward / dX / dW   -> 3xTF32 tcgen05 GEMM (fused bias+relu,
+//                                  relu-mask and TF32-residual epilogues)
+//   Linear with <= 16 outputs  -> "skinny" SIMT kernels (one HBM pass)
+//   bias gradient (axis-0 sum) -> deterministic column reduction
+//   cross_entropy fwd+bwd      -> one fused pass
+//   Sgd::step                  -> one multi-tensor pass (+ TF32 residual of W)
+//
+// Data parallel: each rank holds batch rows, gradients of every layer are
+// averaged over ranks by NCCL on a second stream as soon as the layer's
+// backward finishes, overlapping the remaining backward GEMMs.
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "fg_comm.h"
+#include "fg_gemm.cuh"
+#include "fg_internal.h"
+#include "fg_kernels.cuh"
+
+namespace fg {
+
+// ---------------------------------------------------------------------------
+// Skinny layers (out features NJ <= 16): logits = act @ W^T + b and the
+// fused backward pass.
+// ---------------------------------------------------------------------------
+constexpr int kSkinnyMax = 16;
+
+// Each warp computes 4 rows; W is staged in shared memory when it fits.
+template <int NJ, bool WSMEM>
+__global__ void __launch_bounds__(256) k_skinny_fwd(const float *__restrict__ act,
+                                                    const float *__restrict__ W,
+                                                    const float *__restrict__ bias,
+                                                    float *__restrict__ out, int M, int K) {
+  extern __shared__ float4 sW4[];
+  const int K4 = K / 4;
+  const float4 *W4 = WSMEM ? sW4 : reinterpret_cast<const float4 *>(W);
+  if (WSMEM) {
+    const float4 *g = reinterpret_cast<const float4 *>(W);
+    for (int i = threadIdx.x; i < NJ * K4; i += blockDim.x) sW4[i] = g[i];
+    __syncthreads();
+  }
+  const int lane = threadIdx.x & 31;
+  const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int r0 = wid * 4; r0 < M; r0 += nw * 4) {
+    float acc[4][NJ];
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+      for (int j = 0; j < NJ; j++) acc[r][j] = 0.f;
+    for (int k4 = lane; k4 < K4; k4 += 32) {
+      float4 a[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+        a[r] = (r0 + r < M) ? __ldcs(reinterpret_cast<const float4 *>(act + (size_t)(r0 + r) * K) + k4)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        const float4 w = WSMEM ? W4[j * K4 + k4] : __ldg(W4 + j * K4 + k4);
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+          acc[r][j] += a[r].x * w.x + a[r].y * w.y + a[r].z * w.z + a[r].w * w.w;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        float v = acc[r][j];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        acc[r][j] = v;
+      }
+    if (lane < NJ) {
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        if (r0 + r < M) {
+          float v = 0.f;
+#pragma unroll
+          for (int j = 0; j < NJ; j++)
+            if (j == lane) v = acc[r][j];
+          out[(size_t)(r0 + r) * NJ + lane] = __fadd_rn(v, bias[lane]);
+        }
+      }
+    }
+  }
+}
+
+// Backward of a skinny layer.  Thread owns a float4 column slice k4 of the
+// layer input and a chunk of rows:
+//   dW partial[chunk][j][k] += G[m,j] * act[m,k]
+//   Gprev[m,k] = (act[m,k] > 0) ? sum_j G[m,j] * W[j,k] : 0   (+ TF32 residual)
+template <int NJ, bool DX>
+__global__ void __launch_bounds__(256) k_skinny_bwd(const float *__restrict__ G,
+                                                    const float *__restrict__ act,
+                                                    const float *__restrict__ W,
+                                                    float *__restrict__ part,
+                                                    float *__restrict__ gprev,
+                                                    float *__restrict__ gprev_lo, int M, int K,
+                                                    int rows_per_chunk) {
+  __shared__ float sG[64 * kSkinnyMax];
+  const int K4 = K / 4;
+  const int k4 = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r_begin = blockIdx.y * rows_per_chunk;
+  const int r_end = min(M, r_begin + rows_per_chunk);
+  const bool active = k4 < K4;
+  float4 w[NJ];
+  float4 dw[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; j++) {
+    w[j] = (DX && active) ? __ldg(reinterpret_cast<const float4 *>(W + (size_t)j * K) + k4)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    dw[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int rb = r_begin; rb < r_end; rb += 64) {
+    const int nr = min(64, r_end - rb);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nr * NJ; i += blockDim.x) sG[i] = G[(size_t)rb * NJ + i];
+    __syncthreads();
+    if (!active) continue;
+    for (int r = 0; r < nr; r++) {
+      const size_t m = (size_t)(rb + r);
+      const float4 a = __ldcs(reinterpret_cast<const float4 *>(act + m * K) + k4);
+      float4 dx = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        const float g = sG[r * NJ + j];
+        dw[j].x += g * a.x; dw[j].y += g * a.y; dw[j].z += g * a.z; dw[j].w += g * a.w;
+        if (DX) {
+          dx.x += g * w[j].x; dx.y += g * w[j].y; dx.z += g * w[j].z; dx.w += g * w[j].w;
+        }
+      }
+      if (DX) {
+        dx.x = (a.x > 0.f) ? dx.x : 0.f;
+        dx.y = (a.y > 0.f) ? dx.y : 0.f;
+        dx.z = (a.z > 0.f) ? dx.z : 0.f;
+        dx.w = (a.w > 0.f) ? dx.w : 0.f;
+        reinterpret_cast<float4 *>(gprev + m * K)[k4] = dx;
+        if (gprev_lo) {
+          float4 lo;
+          lo.x = __fsub_rn(dx.x, __uint_as_float(__float_as_uint(dx.x) & 0xffffe000u));
+          lo.y = __fsub_rn(dx.y, __uint_as_float(__float_as_uint(dx.y) & 0xffffe000u));
+          lo.z = __fsub_rn(dx.z, __uint_as_float(__float_as_uint(dx.z) & 0xffffe000u));
+          lo.w = __fsub_rn(dx.w, __uint_as_float(__float_as_uint(dx.w) & 0xffffe000u));
+          reinterpret_cast<float4 *>(gprev_lo + m * K)[k4] = lo;
+        }
+      }
+    }
+  }
+  if (active) {
+#pragma unroll
+    for (int j = 0; j < NJ; j++)
+      reinterpret_cast<float4 *>(part + ((size_t)blockIdx.y * NJ + j) * K)[k4] = dw[j];
+  }
+}
+
+// dW[j,k] = sum over chunks (in chunk order) of the partials.
+__global__ void __launch_bounds__(256) k_skinny_dw_final(const float *__restrict__ part,
+                                                         float *__restrict__ dW, int nchunks,
+                                                         size_t jk) {
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= jk) return;
+  float acc = 0.f;
+  for (int c = 0; c < nchunks; c++) acc += part[(size_t)c * jk + i];
+  dW[i] = acc;
+}
+
+template <int NJ>
+static int launch_skinny_fwd_t(const float *act, const float *W, const float *b, float *out, int M,
+                               int K, cudaStream_t st, int sms) {
+  const size_t wbytes = (size_t)NJ * K * 4;
+  const bool smem = wbytes <= 200 * 1024;
+  const int warps_needed = (M + 3) / 4;
+  int grid = (warps_needed + 7) / 8;
+  const int cap = sms * (smem ? 1 : 4);
+  if (grid > cap) grid = cap;
+  if (grid < 1) grid = 1;
+  if (smem) {
+    auto kern = k_skinny_fwd<NJ, true>;
+    static int attr_bytes[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && attr_bytes[dev] < (int)wbytes) {
+      FG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      attr_bytes[dev] = 200 * 1024;
+    }
+    kern<<<grid, 256, wbytes, st>>>(act, W, b, out, M, K);
+  } else {
+    k_skinny_fwd<NJ, false><<<grid, 256, 0, st>>>(act, W, b, out, M, K);
+  }
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+static int launch_skinny_fwd(int nj, const float *act, const float *W, const float *b, float *out,
+                             int M, int K, cudaStream_t st, int sms) {
+  switch (nj) {
+#define FG_NJ(n) \
+  case n: return launch_skinny_fwd_t<n>(act, W, b, out, M, K, st, sms);
+    FG_NJ(1) FG_NJ(2) FG_NJ(3) FG_NJ(4) FG_NJ(5) FG_NJ(6) FG_NJ(7) FG_NJ(8)
+    FG_NJ(9) FG_NJ(10) FG_NJ(11) FG_NJ(12) FG_NJ(13) FG_NJ(14) FG_NJ(15) FG_NJ(16)
+#undef FG_NJ
+    default: return set_error(FG_ERR_UNSUPPORTED, "skinny layer with %d outputs", nj);
+  }
+}
+
+struct SkinnyBwdShape {
+  int threads, colblocks, nchunks, rows_per_chunk;
+};
+
+static SkinnyBwdShape skinny_bwd_shape(int M, int K, int sms) {
+  SkinnyBwdShape s;
+  const int K4 = K / 4;
+  s.threads = K4 >= 256 ? 256 : ((K4 + 31) / 32) * 32;
+  s.colblocks = (K4 + s.threads - 1) / s.threads;
+  int want = (2 * sms + s.colblocks - 1) / s.colblocks;
+  int max_chunks = (M + 15) / 16;
+  if (want > max_chunks) want = max_chunks;
+  if (want < 1) want = 1;
+  s.rows_per_chunk = (M + want - 1) / want;
+  s.nchunks = (M + s.rows_per_chunk - 1) / s.rows_per_chunk;
+  return s;
+}
+
+template <int NJ>
+static int launch_skinny_bwd_t(const float *G, const float *act, const float *W, float *part,
+                               float *dW, float *gprev, float *gprev_lo, int M, int K,
+                               cudaStream_t st, int sms) {
+  SkinnyBwdShape s = skinny_bwd_shape(M, K, sms);
+  dim3 grid(s.colblocks, s.nchunks);
+  if (gprev)
+    k_skinny_bwd<NJ, true><<<grid, s.threads, 0, st>>>(G, act, W, part, gprev, gprev_lo, M, K,
+                                                       s.rows_per_chunk);
+  else
+    k_skinny_bwd<NJ, false><<<grid, s.threads, 0, st>>>(G, act, W, part, nullptr, nullptr, M, K,
+                                                        s.rows_per_chunk);
+  FG_LAUNCH_TRY();
+  size_t jk = (size_t)NJ * K;
+  k_skinny_dw_final<<<(unsigned)((jk + 255) / 256), 256, 0, st>>>(part, dW, s.nchunks, jk);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+static int launch_skinny_bwd(int nj, const float *G, const float *act, const float *W,
+                             float *part, float *dW, float *gprev, float *gprev_lo, int M, int K,
+                             cudaStream_t st, int sms) {
+  switch (nj) {
+#define FG_NJ(n) \
+  case n: return launch_skinny_bwd_t<n>(G, act, W, part, dW, gprev, gprev_lo, M, K, st, sms);
+    FG_NJ(1) FG_NJ(2) FG_NJ(3) FG_NJ(4) FG_NJ(5) FG_NJ(6) FG_NJ(7) FG_NJ(8)
+    FG_NJ(9) FG_NJ(10) FG_NJ(11) FG_NJ(12) FG_NJ(13) FG_NJ(14) FG_NJ(15) FG_NJ(16)
+#undef FG_NJ
+    default: return set_error(FG_ERR_UNSUPPORTED, "skinny layer with %d outputs", nj);
+  }
+}
+
+}  // namespace fg
+
+// ---------------------------------------------------------------------------
+// The plan
+// ---------------------------------------------------------------------------
+namespace {
+
+struct Layer {
+  int in = 0, out = 0;
+  bool tc = false;  // tensor-core layer (out % 16 == 0, out >= 32) vs skinny (out <= 16)
+  float *W = nullptr, *b = nullptr, *W_lo = nullptr;
+  float *dW = nullptr, *db = nullptr;  // inside the flat gradient buffer
+  size_t bucket_off = 0, bucket_len = 0;  // this layer's all-reduce bucket (floats)
+  fg::gemm::GemmPlan fwd, bwd_w, bwd_x;
+};
+
+size_t pad64(size_t n) { return (n + 63) / 64 * 64; }
+
+}  // namespace
+
+struct fg_mlp {
+  fg_device *dev = nullptr;
+  cudaStream_t st = nullptr, comm_st = nullptr;
+  int nl = 0, B = 0;
+  float lr = 0.f;
+  std::vector<int> dims;
+  std::vector<Layer> L;
+  float *x = nullptr, *x_lo = nullptr, *t = nullptr;
+  std::vector<float *> act, act_lo;  // act[l] = output of layer l (post-ReLU; logits for the last)
+  std::vector<float *> G, G_lo;      // G[l] = d loss / d (pre-activation output of layer l)
+  float *grad = nullptr;
+  size_t grad_count = 0;
+  float *loss = nullptr;  // inside the flat gradient buffer (averaged with the layer-0 bucket)
+  float *scratch = nullptr;
+  size_t scratch_bytes = 0;
+  std::vector<void *> allocations;
+  fg_comm *comm = nullptr;
+  std::vector<cudaEvent_t> ev_bucket;
+  cudaEvent_t ev_comm_done = nullptr;
+  bool use_graph = false;
+  cudaGraphExec_t graph = nullptr;
+  bool timing = false;
+  std::vector<cudaEvent_t> ev_t0, ev_t1;  // one pair per GEMM launch of a step
+  std::vector<double> gemm_flops;
+  int gemm_launches = 0;
+  int launches_per_step = 0;
+  int sms = 148;
+};
+
+namespace {
+
+int mlp_alloc(fg_mlp *m, float **p, size_t n) {
+  void *q = nullptr;
+  FG_CUDA_TRY(cudaMalloc(&q, n * sizeof(float) + 256));
+  FG_CUDA_TRY(cudaMemset(q, 0, n * sizeof(float) + 256));
+  m->allocations.push_back(q);
+  *p = (float *)q;
+  return FG_OK;
+}
+
+int build_plans(fg_mlp *m) {
+  const int B = m->B;
+  for (int l = 0; l < m->nl; l++) {
+    Layer &ly = m->L[l];
+    if (!ly.tc) continue;
+    const float *in = (l == 0) ? m->x : m->act[l - 1];
+    const float *in_lo = (l == 0) ? m->x_lo : m->act_lo[l - 1];
+    const bool last = (l == m->nl - 1);
+    int rc = fg::gemm::make_plan(B, ly.out, ly.in, in, in_lo, ly.in, ly.W, ly.W_lo, ly.in,
+                                 m->act[l], last ? nullptr : m->act_lo[l], ly.out, 0,
+                                 last ? FG_EPI_BIAS : FG_EPI_BIAS_RELU, ly.b, nullptr, 0, &ly.fwd);
+    if (rc) return rc;
+    // dW[n,k] = sum_m G[m,n] * in[m,k]: A = G stored [B, out] (MN-major),
+    // B = in stored [B, in] (MN-major), reduction over the batch.
+    rc = fg::gemm::make_plan(ly.out, ly.in, B, m->G[l], m->G_lo[l], ly.out, in, in_lo, ly.in, ly.dW,
+                             nullptr, ly.in, FG_GEMM_A_MN_MAJOR | FG_GEMM_B_MN_MAJOR, FG_EPI_NONE,
+                             nullptr, nullptr, 0, &ly.bwd_w);
+    if (rc) return rc;
+    if (l > 0) {
+      // Gprev[m,k] = (act[m,k] > 0) ? sum_n G[m,n] W[n,k] : 0:
+      // A = G [B, out] K-major, B = W stored [out, in] = [K, N] (MN-major).
+      rc = fg::gemm::make_plan(B, ly.in, ly.out, m->G[l], m->G_lo[l], ly.out, ly.W, ly.W_lo, ly.in,
+                               m->G[l - 1], m->G_lo[l - 1], ly.in, FG_GEMM_B_MN_MAJOR,
+                               FG_EPI_RELU_MASK, nullptr, m->act[l - 1], ly.in, &ly.bwd_x);
+      if (rc) return rc;
+    }
+  }
+  return FG_OK;
+}
+
+int record(cudaEvent_t ev, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  FG_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+  if (cs == cudaStreamCaptureStatusActive)
+    FG_CUDA_TRY(cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal));
+  else
+    FG_CUDA_TRY(cudaEventRecord(ev, st));
+  return FG_OK;
+}
+
+// Launch one GEMM plan, bracketed by timing events when timing is on.
+int run_gemm(fg_mlp *m, const fg::gemm::GemmPlan &pl, cudaStream_t st) {
+  const int i = m->gemm_launches++;
+  const bool t = m->timing && i < (int)m->ev_t0.size();
+  int rc;
+  if (t && (rc = record(m->ev_t0[i], st))) return rc;
+  if ((rc = fg::gemm::run_plan(pl, st))) return rc;
+  if (t) {
+    m->gemm_flops[i] = 2.0 * pl.p.M * (double)pl.p.N * pl.p.K;
+    if ((rc = record(m->ev_t1[i], st))) return rc;
+  }
+  return FG_OK;
+}
+
+// Enqueue one training step on m->st (and m->comm_st).
+int enqueue_step(fg_mlp *m) {
+  cudaStream_t st = m->st;
+  const int B = m->B;
+  int rc;
+  m->gemm_launches = 0;
+  // forward
+  if (m->L[0].tc && (rc = fg::launch_split_lo(m->x, m->x_lo, (size_t)B * m->dims[0], st))) return rc;
+  for (int l = 0; l < m->nl; l++) {
+    Layer &ly = m->L[l];
+    const float *in = (l == 0) ? m->x : m->act[l - 1];
+    if (ly.tc) {
+      if ((rc = run_gemm(m, ly.fwd, st))) return rc;
+    } else {
+      if ((rc = fg::launch_skinny_fwd(ly.out, in, ly.W, ly.b, m->act[l], B, ly.in, st, m->sms)))
+        return rc;
+    }
+  }
+  // cross_entropy forward + backward
+  const int C = m->dims[m->nl];
+  if ((rc = fg::launch_xent(m->act[m->nl - 1], m->t, (size_t)B, (size_t)C, m->loss, m->G[m->nl - 1],
+                            1.0f, st, m->scratch)))
+    return rc;
+  if (m->L[m->nl - 1].tc &&
+      (rc = fg::launch_split_lo(m->G[m->nl - 1], m->G_lo[m->nl - 1], (size_t)B * C, st)))
+    return rc;
+  // backward, last layer first; each layer's bucket is averaged across ranks
+  // on the comm stream while the next layer's backward runs.
+  for (int l = m->nl - 1; l >= 0; l--) {
+    Layer &ly = m->L[l];
+    const float *in = (l == 0) ? m->x : m->act[l - 1];
+    if (ly.tc) {
+      if ((rc = run_gemm(m, ly.bwd_w, st))) return rc;
+      if (l > 0 && (rc = run_gemm(m, ly.bwd_x, st))) return rc;
+    } else {
+      if ((rc = fg::launch_skinny_bwd(ly.out, m->G[l], in, ly.W, m->scratch, ly.dW,
+                                      l > 0 ? m->G[l - 1] : nullptr,
+                                      (l > 0 && m->L[l - 1].tc) ? m->G_lo[l - 1] : nullptr, B,
+                                      ly.in, st, m->sms)))
+        return rc;
+    }
+    if ((rc = fg::launch_reduce_cols(FG_F32, FG_REDUCE_SUM, m->G[l], ly.db, (size_t)B,
+                                     (size_t)ly.out, st, m->scratch, m->scratch_bytes)))
+      return rc;
+    if (m->comm) {
+      FG_CUDA_TRY(cudaEventRecord(m->ev_bucket[l], st));
+      FG_CUDA_TRY(cudaStreamWaitEvent(m->comm_st, m->ev_bucket[l], 0));
+      if ((rc = fg::comm_allreduce_mean(m->comm, m->grad + ly.bucket_off, ly.bucket_len,
+                                        m->comm_st)))
+        return rc;
+    }
+  }
+  if (m->comm) {
+    FG_CUDA_TRY(cudaEventRecord(m->ev_comm_done, m->comm_st));
+    FG_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_comm_done, 0));
+  }
+  // Sgd::step over every parameter (weights of tensor-core layers also get
+  // their TF32 residual for the next step's GEMMs).
+  fg::SgdSegments segs{};
+  for (int l = 0; l < m->nl; l++) {
+    Layer &ly = m->L[l];
+    segs.p[segs.count] = ly.W;
+    segs.g[segs.count] = ly.dW;
+    segs.lo[segs.count] = ly.tc ? ly.W_lo : nullptr;
+    segs.n[segs.count] = (size_t)ly.out * ly.in;
+    segs.count++;
+    segs.p[segs.count] = ly.b;
+    segs.g[segs.count] = ly.db;
+    segs.lo[segs.count] = nullptr;
+    segs.n[segs.count] = (size_t)ly.out;
+    segs.count++;
+    if (segs.count + 2 > fg::kMaxSgdSegments || l == m->nl - 1) {
+      if ((rc = fg::launch_sgd_multi(segs, m->lr, st))) return rc;
+      segs.count = 0;
+    }
+  }
+  return FG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fg_mlp_create(fg_device *dev, int n_layers, const int *dims, int batch, float lr,
+                  fg_mlp **out) {
+  FG_REQUIRE(dev && dims && out, "fg_mlp_create: null argument");
+  FG_REQUIRE(n_layers >= 1 && n_layers <= 3, "fg_mlp_create: 1 to 3 layers supported (got %d)",
+             n_layers);
+  FG_REQUIRE(batch > 0, "fg_mlp_create: batch must be positive");
+  FG_CUDA_TRY(cudaSetDevice(dev->ordinal));
+  fg_mlp *m = new fg_mlp;
+  m->dev = dev;
+  m->st = dev->stream;
+  m->nl = n_layers;
+  m->B = batch;
+  m->lr = lr;
+  m->dims.assign(dims, dims + n_layers + 1);
+  fg::DevCtx *ctx = fg::ctx_current();
+  if (ctx && ctx->num_sms) m->sms = ctx->num_sms;
+  auto fail = [&](int rc) {
+    fg_mlp_destroy(m);
+    return rc;
+  };
+  for (int l = 0; l <= n_layers; l++)
+    if (dims[l] <= 0 || (dims[l] % 4 != 0 && l < n_layers))
+      return fail(fg::set_error(FG_ERR_UNSUPPORTED,
+                                "fg_mlp_create: layer input widths must be multiples of 4 (dims[%d]=%d)",
+                                l, dims[l]));
+  m->L.resize(n_layers);
+  size_t off = 0;
+  int rc;
+  for (int l = 0; l < n_layers; l++) {
+    Layer &ly = m->L[l];
+    ly.in = dims[l];
+    ly.out = dims[l + 1];
+    if (ly.out <= fg::kSkinnyMax) {
+      ly.tc = false;
+      if (l != n_layers - 1)
+        return fail(fg::set_error(FG_ERR_UNSUPPORTED,
+                                  "fg_mlp_create: a layer with <= 16 outputs must be the last"));
+    } else if (ly.out % 16 == 0) {
+      ly.tc = true;
+    } else {
+      return fail(fg::set_error(FG_ERR_UNSUPPORTED,
+                                "fg_mlp_create: layer %d width %d (need <= 16 or a multiple of 16)", l,
+                                ly.out));
+    }
+    ly.bucket_off = off;
+    off += pad64((size_t)ly.out * ly.in) + pad64(ly.out) + (l == 0 ? 64 : 0);
+    ly.bucket_len = off - ly.bucket_off;
+  }
+  m->grad_count = off;
+  if ((rc = mlp_alloc(m, &m->grad, m->grad_count))) return fail(rc);
+  for (int l = 0; l < n_layers; l++) {
+    Layer &ly = m->L[l];
+    ly.dW = m->grad + ly.bucket_off;
+    ly.db = ly.dW + pad64((size_t)ly.out * ly.in);
+    if (l == 0) m->loss = ly.db + pad64(ly.out);
+    if ((rc = mlp_alloc(m, &ly.W, (size_t)ly.out * ly.in))) return fail(rc);
+    if ((rc = mlp_alloc(m, &ly.b, ly.out))) return fail(rc);
+    if (ly.tc && (rc = mlp_alloc(m, &ly.W_lo, (size_t)ly.out * ly.in))) return fail(rc);
+  }
+  if ((rc = mlp_alloc(m, &m->x, (size_t)batch * dims[0]))) return fail(rc);
+  if ((rc = mlp_alloc(m, &m->x_lo, (size_t)batch * dims[0]))) return fail(rc);
+  if ((rc = mlp_alloc(m, &m->t, (size_t)batch * dims[n_layers]))) return fail(rc);
+  m->act.assign(n_layers, nullptr);
+  m->act_lo.assign(n_layers, nullptr);
+  m->G.assign(n_layers, nullptr);
+  m->G_lo.assign(n_layers, nullptr);
+  for (int l = 0; l < n_layers; l++) {
+    size_t n = (size_t)batch * dims[l + 1];
+    if ((rc = mlp_alloc(m, &m->act[l], n))) return fail(rc);
+    if ((rc = mlp_alloc(m, &m->G[l], n))) return fail(rc);
+    if (m->L[l].tc) {
+      if ((rc = mlp_alloc(m, &m->act_lo[l], n))) return fail(rc);
+      if ((rc = mlp_alloc(m, &m->G_lo[l], n))) return fail(rc);
+    }
+  }
+  // scratch: column-reduce partials, skinny dW partials, xent row terms
+  size_t need = (size_t)batch * 4;
+  for (int l = 0; l < n_layers; l++) {
+    size_t r = fg::reduce_cols_scratch_bytes((size_t)batch, (size_t)dims[l + 1]);
+    if (r > need) need = r;
+    if (!m->L[l].tc) {
+      fg::SkinnyBwdShape s = fg::skinny_bwd_shape(batch, dims[l], m->sms);
+      size_t p = (size_t)s.nchunks * dims[l + 1] * dims[l] * 4;
+      if (p > need) need = p;
+    }
+  }
+  m->scratch_bytes = need;
+  if ((rc = mlp_alloc(m, &m->scratch, need / 4 + 1))) return fail(rc);
+  if ((rc = build_plans(m))) return fail(rc);
+  FG_CUDA_TRY(cudaDeviceSynchronize());
+  *out = m;
+  return FG_OK;
+}
+
+int fg_mlp_destroy(fg_mlp *m) {
+  if (!m) return FG_OK;
+  cudaSetDevice(m->dev->ordinal);
+  cudaDeviceSynchronize();
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  for (auto e : m->ev_t0) cudaEventDestroy(e);
+  for (auto e : m->ev_t1) cudaEventDestroy(e);
+  for (auto e : m->ev_bucket) cudaEventDestroy(e);
+  if (m->ev_comm_done) cudaEventDestroy(m->ev_comm_done);
+  if (m->comm_st) cudaStreamDestroy(m->comm_st);
+  for (void *p : m->allocations) cudaFree(p);
+  delete m;
+  return FG_OK;
+}
+
+int fg_mlp_set_params(fg_mlp *m, int layer, const float *h_weight, const float *h_bias) {
+  FG_REQUIRE(m && layer >= 0 && layer < m->nl, "fg_mlp_set_params: bad layer");
+  Layer &ly = m->L[layer];
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  if (h_weight) {
+    FG_CUDA_TRY(cudaMemcpyAsync(ly.W, h_weight, sizeof(float) * ly.out * ly.in,
+                                cudaMemcpyHostToDevice, m->st));
+    if (ly.tc) {
+      int rc = fg::launch_split_lo(ly.W, ly.W_lo, (size_t)ly.out * ly.in, m->st);
+      if (rc) return rc;
+    }
+  }
+  if (h_bias)
+    FG_CUDA_TRY(cudaMemcpyAsync(ly.b, h_bias, sizeof(float) * ly.out, cudaMemcpyHostToDevice, m->st));
+  FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+  return FG_OK;
+}
+
+int fg_mlp_get_params(fg_mlp *m, int layer, float *h_weight, float *h_bias) {
+  FG_REQUIRE(m && layer >= 0 && layer < m->nl, "fg_mlp_get_params: bad layer");
+  Layer &ly = m->L[layer];
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  if (h_weight)
+    FG_CUDA_TRY(cudaMemcpyAsync(h_weight, ly.W, sizeof(float) * ly.out * ly.in,
+                                cudaMemcpyDeviceToHost, m->st));
+  if (h_bias)
+    FG_CUDA_TRY(cudaMemcpyAsync(h_bias, ly.b, sizeof(float) * ly.out, cudaMemcpyDeviceToHost, m->st));
+  FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+  return fg_check_device_error();
+}
+
+int fg_mlp_get_grads(fg_mlp *m, int layer, float *h_dweight, float *h_dbias) {
+  FG_REQUIRE(m && layer >= 0 && layer < m->nl, "fg_mlp_get_grads: bad layer");
+  Layer &ly = m->L[layer];
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  if (h_dweight)
+    FG_CUDA_TRY(cudaMemcpyAsync(h_dweight, ly.dW, sizeof(float) * ly.out * ly.in,
+                                cudaMemcpyDeviceToHost, m->st));
+  if (h_dbias)
+    FG_CUDA_TRY(cudaMemcpyAsync(h_dbias, ly.db, sizeof(float) * ly.out, cudaMemcpyDeviceToHost, m->st));
+  FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+  return fg_check_device_error();
+}
+
+int fg_mlp_attach_comm(fg_mlp *m, fg_comm *comm) {
+  FG_REQUIRE(m, "fg_mlp_attach_comm: null mlp");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  if (m->graph) {
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  m->comm = comm;
+  if (comm && !m->comm_st) {
+    FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->comm_st, cudaStreamNonBlocking));
+    m->ev_bucket.resize(m->nl);
+    for (auto &e : m->ev_bucket) FG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_comm_done, cudaEventDisableTiming));
+  }
+  return FG_OK;
+}
+
+int fg_mlp_input_slots(fg_mlp *m, float **d_x, float **d_targets) {
+  FG_REQUIRE(m, "fg_mlp_input_slots: null mlp");
+  if (d_x) *d_x = m->x;
+  if (d_targets) *d_targets = m->t;
+  return FG_OK;
+}
+
+int fg_mlp_use_graph(fg_mlp *m, int enable) {
+  FG_REQUIRE(m, "fg_mlp_use_graph: null mlp");
+  m->use_graph = enable != 0;
+  if (!m->use_graph && m->graph) {
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  return FG_OK;
+}
+
+int fg_mlp_step(fg_mlp *m, float *d_loss_out) {
+  FG_REQUIRE(m, "fg_mlp_step: null mlp");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  int rc;
+  if (m->use_graph) {
+    if (!m->graph) {
+      // First call: run eagerly once (counts launches, settles lazy init),
+      // then capture the same sequence.
+      uint64_t before = fg_kernel_launches();
+      if ((rc = enqueue_step(m))) return rc;
+      m->launches_per_step = (int)(fg_kernel_launches() - before);
+      FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+      cudaGraph_t g;
+      FG_CUDA_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+      rc = enqueue_step(m);
+      cudaError_t ce = cudaStreamEndCapture(m->st, &g);
+      if (rc) {
+        if (ce == cudaSuccess) cudaGraphDestroy(g);
+        return rc;
+      }
+      FG_CUDA_TRY(ce);
+      cudaError_t ie = cudaGraphInstantiate(&m->graph, g, 0);
+      cudaGraphDestroy(g);
+      FG_CUDA_TRY(ie);
+    } else {
+      FG_CUDA_TRY(cudaGraphLaunch(m->graph, m->st));
+    }
+  } else {
+    uint64_t before = fg_kernel_launches();
+    if ((rc = enqueue_step(m))) return rc;
+    m->launches_per_step = (int)(fg_kernel_launches() - before);
+  }
+  if (d_loss_out)
+    FG_CUDA_TRY(cudaMemcpyAsync(d_loss_out, m->loss, sizeof(float), cudaMemcpyDeviceToDevice, m->st));
+  return FG_OK;
+}
+
+int fg_mlp_step_host(fg_mlp *m, const float *h_x, const float *h_targets, float *h_loss) {
+  FG_REQUIRE(m && h_x && h_targets, "fg_mlp_step_host: null argument");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  FG_CUDA_TRY(cudaMemcpyAsync(m->x, h_x, sizeof(float) * (size_t)m->B * m->dims[0],
+                              cudaMemcpyHostToDevice, m->st));
+  FG_CUDA_TRY(cudaMemcpyAsync(m->t, h_targets, sizeof(float) * (size_t)m->B * m->dims[m->nl],
+                              cudaMemcpyHostToDevice, m->st));
+  int rc = fg_mlp_step(m, nullptr);
+  if (rc) return rc;
+  if (h_loss) {
+    FG_CUDA_TRY(cudaMemcpyAsync(h_loss, m->loss, sizeof(float), cudaMemcpyDeviceToHost, m->st));
+    FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return fg_check_device_error();
+  }
+  return FG_OK;
+}
+
+int fg_mlp_get_logits(fg_mlp *m, float *h_logits) {
+  FG_REQUIRE(m && h_logits, "fg_mlp_get_logits: null argument");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  FG_CUDA_TRY(cudaMemcpyAsync(h_logits, m->act[m->nl - 1],
+                              sizeof(float) * (size_t)m->B * m->dims[m->nl], cudaMemcpyDeviceToHost,
+                              m->st));
+  FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+  return fg_check_device_error();
+}
+
+int fg_mlp_enable_gemm_timing(fg_mlp *m, int enable) {
+  FG_REQUIRE(m, "fg_mlp_enable_gemm_timing: null mlp");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  if (m->graph) {  // the captured sequence changes
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  m->timing = enable != 0;
+  if (m->timing && m->ev_t0.empty()) {
+    const int n = 3 * m->nl;
+    m->ev_t0.resize(n);
+    m->ev_t1.resize(n);
+    m->gemm_flops.assign(n, 0.0);
+    for (int i = 0; i < n; i++) {
+      FG_CUDA_TRY(cudaEventCreate(&m->ev_t0[i]));
+      FG_CUDA_TRY(cudaEventCreate(&m->ev_t1[i]));
+    }
+  }
+  return FG_OK;
+}
+
+int fg_mlp_gemm_times(fg_mlp *m, float *ms, double *flops, int capacity, int *count) {
+  FG_REQUIRE(m && count && (capacity == 0 || (ms && flops)), "fg_mlp_gemm_times: null argument");
+  FG_REQUIRE(m->timing, "fg_mlp_gemm_times: timing is not enabled");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+  int n = m->gemm_launches < (int)m->ev_t0.size() ? m->gemm_launches : (int)m->ev_t0.size();
+  if (n > capacity) n = capacity;
+  for (int i = 0; i < n; i++) {
+    FG_CUDA_TRY(cudaEventElapsedTime(&ms[i], m->ev_t0[i], m->ev_t1[i]));
+    flops[i] = m->gemm_flops[i];
+  }
+  *count = n;
+  return FG_OK;
+}
+
+int fg_mlp_launch_count(fg_mlp *m, int *count) {
+  FG_REQUIRE(m && count, "fg_mlp_launch_count: null argument");
+  *count = m->launches_per_step;
+  return FG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,177 @@
+"""The MLP training path of ferrograd (examples/mnist.rs) on the B200 backend.
+
+* :class:`InitRng` / :func:`linear_init` -- ``Linear::new`` (src/nn.rs:77-85):
+  Kaiming-normal weight from the reference's thread-local LCG (seed 42,
+  continuing across layers), zero bias.  Runs in the C library.
+* :class:`MlpTrainer` -- one ``forward -> cross_entropy -> zero_grad ->
+  backward -> Sgd::step -> loss.to_vec()`` step per call, planned once and
+  replayed (optionally as a CUDA graph), data parallel when given a
+  :class:`Communicator`.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import _lib
+from ._lib import call
+from .device import CudaDevice
+
+
+class InitRng:
+    """The reference's init seed (``INIT_SEED``, src/nn.rs:12-14), starting at 42."""
+
+    def __init__(self, seed: int = 42):
+        self.state = ctypes.c_uint64(seed)
+
+    def kaiming_normal(self, shape: Sequence[int], fan_in: int) -> np.ndarray:
+        out = np.empty(int(np.prod(shape)), dtype=np.float32)
+        call("fg_kaiming_normal", out.ctypes.data, out.size, int(fan_in), ctypes.byref(self.state))
+        return out.reshape(tuple(shape))
+
+
+def linear_init(in_features: int, out_features: int, rng: InitRng) -> Tuple[np.ndarray, np.ndarray]:
+    """``Linear::new(in, out)``: weight [out, in] Kaiming-normal, bias zeros."""
+    w = rng.kaiming_normal((out_features, in_features), in_features)
+    return w, np.zeros(out_features, dtype=np.float32)
+
+
+def mlp_init(dims: Sequence[int], rng: Optional[InitRng] = None):
+    """Parameters of ``Linear(dims[0], dims[1]) ... Linear(dims[-2], dims[-1])``."""
+    rng = InitRng() if rng is None else rng
+    ws, bs = [], []
+    for i in range(len(dims) - 1):
+        w, b = linear_init(dims[i], dims[i + 1], rng)
+        ws.append(w)
+        bs.append(b)
+    return ws, bs
+
+
+class Communicator:
+    """NCCL communicator for the data-parallel step (no reference counterpart)."""
+
+    def __init__(self, rank: int, nranks: int, unique_id: bytes, timeout_ms: int = 60000):
+        h = ctypes.c_void_p()
+        call("fg_comm_init", int(rank), int(nranks), bytes(unique_id), int(timeout_ms), ctypes.byref(h))
+        self._h = h.value
+        self.rank, self.nranks = rank, nranks
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(_lib.UNIQUE_ID_BYTES)
+        call("fg_comm_unique_id", buf)
+        return buf.raw
+
+    def allreduce_mean_(self, ptr: int, count: int, stream: int) -> None:
+        call("fg_allreduce_mean_f32", self._h, ptr, int(count), stream)
+
+    def close(self) -> None:
+        if self._h:
+            call("fg_comm_destroy", self._h)
+            self._h = None
+
+
+class MlpTrainer:
+    """Owns the device parameters and runs training steps through the C ABI."""
+
+    def __init__(self, device: CudaDevice, dims: Sequence[int], batch: int, lr: float,
+                 weights: Sequence[np.ndarray], biases: Sequence[np.ndarray],
+                 comm: Optional[Communicator] = None, use_graph: bool = False):
+        self.device = device
+        self.dims = list(dims)
+        self.batch = int(batch)
+        self.lr = float(lr)
+        self.n_layers = len(dims) - 1
+        d = (ctypes.c_int * len(dims))(*[int(x) for x in dims])
+        h = ctypes.c_void_p()
+        call("fg_mlp_create", device.handle, self.n_layers, d, self.batch, ctypes.c_float(lr),
+             ctypes.byref(h))
+        self._h = h.value
+        for l, (w, b) in enumerate(zip(weights, biases)):
+            w = np.ascontiguousarray(w, dtype=np.float32)
+            b = np.ascontiguousarray(b, dtype=np.float32)
+            assert w.shape == (dims[l + 1], dims[l]) and b.shape == (dims[l + 1],)
+            call("fg_mlp_set_params", self._h, l, w.ctypes.data, b.ctypes.data)
+        self.comm = comm
+        if comm is not None:
+            call("fg_mlp_attach_comm", self._h, comm._h)
+        call("fg_mlp_use_graph", self._h, 1 if use_graph else 0)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            call("fg_mlp_destroy", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def input_slots(self) -> Tuple[int, int]:
+        x = ctypes.c_void_p()
+        t = ctypes.c_void_p()
+        call("fg_mlp_input_slots", self._h, ctypes.byref(x), ctypes.byref(t))
+        return x.value, t.value
+
+    def step_host(self, x: np.ndarray, targets: np.ndarray) -> float:
+        """Copy the batch in, run one step, return the loss (blocking)."""
+        assert x.shape == (self.batch, self.dims[0]) and targets.shape == (self.batch, self.dims[-1])
+        assert x.dtype == np.float32 and targets.dtype == np.float32
+        loss = ctypes.c_float()
+        call("fg_mlp_step_host", self._h, x.ctypes.data, targets.ctypes.data, ctypes.byref(loss))
+        return float(loss.value)
+
+    def step_host_ptr(self, x_ptr: int, t_ptr: int, loss_ptr: int) -> None:
+        """Step from raw (pinned) host pointers; the loss lands in loss_ptr."""
+        call("fg_mlp_step_host", self._h, x_ptr, t_ptr, loss_ptr)
+
+    def step(self, loss_out_ptr: Optional[int] = None) -> None:
+        """Step on inputs already in the device input slots (asynchronous)."""
+        call("fg_mlp_step", self._h, loss_out_ptr)
+
+    def params(self) -> Tuple[List[np.ndarray], List[np.ndarray]]:
+        ws, bs = [], []
+        for l in range(self.n_layers):
+            w = np.empty((self.dims[l + 1], self.dims[l]), np.float32)
+            b = np.empty(self.dims[l + 1], np.float32)
+            call("fg_mlp_get_params", self._h, l, w.ctypes.data, b.ctypes.data)
+            ws.append(w)
+            bs.append(b)
+        return ws, bs
+
+    def grads(self) -> Tuple[List[np.ndarray], List[np.ndarray]]:
+        ws, bs = [], []
+        for l in range(self.n_layers):
+            w = np.empty((self.dims[l + 1], self.dims[l]), np.float32)
+            b = np.empty(self.dims[l + 1], np.float32)
+            call("fg_mlp_get_grads", self._h, l, w.ctypes.data, b.ctypes.data)
+            ws.append(w)
+            bs.append(b)
+        return ws, bs
+
+    def logits(self) -> np.ndarray:
+        out = np.empty((self.batch, self.dims[-1]), np.float32)
+        call("fg_mlp_get_logits", self._h, out.ctypes.data)
+        return out
+
+    def enable_gemm_timing(self, enable: bool = True) -> None:
+        call("fg_mlp_enable_gemm_timing", self._h, 1 if enable else 0)
+
+    def gemm_times(self):
+        """[(ms, flops)] of the tensor-core GEMM launches of the latest step."""
+        cap = 3 * self.n_layers
+        ms = (ctypes.c_float * cap)()
+        fl = (ctypes.c_double * cap)()
+        n = ctypes.c_int()
+        call("fg_mlp_gemm_times", self._h, ms, fl, cap, ctypes.byref(n))
+        return [(ms[i], fl[i]) for i in range(n.value)]
+
+    @property
+    def launches_per_step(self) -> int:
+        n = ctypes.c_int()
+        call("fg_mlp_launch_count", self._h, ctypes.byref(n))
+        return n.value

@@ -1,0 +1,220 @@
+/*
+ * ferro_cuda.h -- C ABI of the B200 (sm_100a) execution backend for
+ * ferrograd's MLP training path.
+ *
+ * Every entry point returns an int status: 0 (FG_OK) on success, otherwise an
+ * FG_ERR_* code, with a human-readable message available from
+ * fg_last_error() on the calling thread.  No entry point aborts the process.
+ * Pointers named d_* are device (HBM) pointers; h_* are host pointers.
+ * Streams are cudaStream_t passed as void* (NULL = the legacy default stream).
+ *
+ * Each declaration cites the reference interface it replaces (file:line in
+ * the ferrograd crate).
+ */
+#ifndef FERRO_CUDA_H
+#define FERRO_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum fg_status {
+  FG_OK = 0,
+  FG_ERR_INVALID = 1,    /* bad argument (size mismatch, null pointer, bad shape) */
+  FG_ERR_CUDA = 2,       /* CUDA runtime / driver call failed */
+  FG_ERR_COMPILE = 3,    /* NVRTC compilation failed (log in fg_last_error) */
+  FG_ERR_NCCL = 4,       /* NCCL call failed or timed out */
+  FG_ERR_DEVICE = 5,     /* a kernel reported an error word (bounded wait expired) */
+  FG_ERR_UNSUPPORTED = 6 /* shape/layout this build does not handle */
+};
+
+/* dtype codes: src/dtype.rs:19-58 (F32, I32, Bool). */
+enum fg_dtype { FG_F32 = 0, FG_I32 = 1, FG_BOOL = 2 };
+
+/* reduce ops: ReduceAxis(Add) / ReduceAxis(Max), src/uop.rs:26-310. */
+enum fg_reduce_op { FG_REDUCE_SUM = 0, FG_REDUCE_MAX = 1 };
+
+typedef struct fg_device fg_device;
+typedef struct fg_buffer fg_buffer;
+typedef struct fg_program fg_program;
+typedef struct fg_comm fg_comm;
+typedef struct fg_mlp fg_mlp;
+
+/* KernelArg (src/device.rs:241-251): tagged union {Buffer, I32, F32, Bool}. */
+enum fg_arg_kind { FG_ARG_BUFFER = 0, FG_ARG_I32 = 1, FG_ARG_F32 = 2, FG_ARG_BOOL = 3 };
+typedef struct fg_kernel_arg {
+  int32_t kind;
+  union {
+    fg_buffer *buffer;
+    int32_t i32;
+    float f32;
+    uint8_t b;
+  } v;
+} fg_kernel_arg;
+
+/* Message of the last failing call on this thread ("" if none). */
+const char *fg_last_error(void);
+
+/* ---- Device trait (src/device.rs:275-332) ------------------------------ */
+
+/* device::get(DeviceId::Cuda(ordinal)) (src/device.rs:338-354): opens the
+ * device context and its stream.  One handle per ordinal per process. */
+int fg_device_open(int ordinal, fg_device **out);
+int fg_device_close(fg_device *dev);
+/* Stream that buffer copies and fg_execute launches are ordered on. */
+int fg_device_stream(fg_device *dev, void **stream);
+int fg_device_sync(fg_device *dev);
+
+/* Device::allocate (src/device.rs:282-283): zero-initialised buffer of
+ * numel elements of dtype.  numel == 0 is allowed (no storage). */
+int fg_alloc(fg_device *dev, int dtype, size_t numel, fg_buffer **out);
+/* Drop of the last Rc<BufferInner> (src/device.rs:95-105). */
+int fg_free(fg_buffer *buf);
+int fg_buffer_info(const fg_buffer *buf, void **d_ptr, int *dtype, size_t *numel);
+/* Device::copy_from_host (src/device.rs:294, src/device/cpu.rs:283-302):
+ * fails with "copy_from_host: expected N bytes, got M" on a size mismatch. */
+int fg_copy_h2d(fg_buffer *buf, const void *h_src, size_t nbytes);
+/* Device::copy_to_host (src/device.rs:302, src/device/cpu.rs:304-316):
+ * synchronous, like the reference's Vec<u8> return. */
+int fg_copy_d2h(const fg_buffer *buf, void *h_dst, size_t nbytes);
+
+/* Device::compile (src/device.rs:309-314): CUDA C source (extern "C"
+ * __global__ func_name) compiled by NVRTC straight to an sm_100a cubin.
+ * block/grid are the launch shape the renderer chose.  Compile errors return
+ * FG_ERR_COMPILE with the NVRTC log in fg_last_error(). */
+int fg_compile(fg_device *dev, const char *source, const char *func_name, int num_args,
+               const uint32_t grid[3], const uint32_t block[3], fg_program **out);
+int fg_program_free(fg_program *prog);
+/* Device::execute (src/device.rs:321, src/device/cpu.rs:328-380): launches
+ * on the device stream; fails if nargs != num_args. */
+int fg_execute(fg_program *prog, const fg_kernel_arg *args, int nargs);
+
+/* ---- Parameter init (src/nn.rs:12-47) ---------------------------------- */
+/* kaiming_normal: the reference's LCG (s = s*6364136223846793005 + 1,
+ * u = (s >> 33) / 2^31) feeding Box-Muller pairs (cos then sin) scaled by
+ * sqrt(2 / fan_in), in f32 on the host.  *state carries the thread-local seed
+ * across layers (42 at start, src/nn.rs:12-14); Linear::new (src/nn.rs:77-85)
+ * draws its weight from it and zero-fills the bias. */
+int fg_kaiming_normal(float *h_out, size_t numel, size_t fan_in, uint64_t *state);
+
+/* ---- Fused building blocks the CUDA pattern router targets -------------- */
+/* Elementwise relu(a*b+c)*scale over n f32 elements: the proto-kernels of
+ * Tensor::mul/add/relu (src/tensor.rs:471-491,519-531) as one pass. */
+int fg_ew_fma_relu_scale(const float *d_a, const float *d_b, const float *d_c, float *d_out,
+                         size_t n, float scale, void *stream);
+
+/* ReduceAxis over the last axis (Tensor::sum / Tensor::max,
+ * src/tensor.rs:665-693): out[r] = op over x[r, 0..cols). */
+int fg_reduce_rows(int dtype, int op, const void *d_x, void *d_out, size_t rows, size_t cols,
+                   void *stream);
+/* ReduceAxis over axis 0: out[c] = op over x[0..rows, c]; deterministic. */
+int fg_reduce_cols(int dtype, int op, const void *d_x, void *d_out, size_t rows, size_t cols,
+                   void *stream);
+
+/* Tensor::cross_entropy (src/tensor.rs:738-752) forward and the gradient
+ * autograd builds for it (src/gradient.rs:97-205), fused in one pass:
+ * d_loss[0] = mean over rows of -sum_c t*log_softmax(x); d_dx (may be NULL)
+ * = d loss / d x scaled by grad_scale (1.0 for the plain loss). */
+int fg_xent_fwd_bwd(const float *d_logits, const float *d_targets, size_t rows, size_t cols,
+                    float *d_loss, float *d_dx, float grad_scale, void *stream);
+
+/* Sgd::step (src/optim.rs:60-71): p <- p + (-(g*lr)).  If d_p_lo is not
+ * NULL it also receives the TF32 residual of the updated p (see fg_split_lo). */
+int fg_sgd(float *d_p, const float *d_g, size_t n, float lr, float *d_p_lo, void *stream);
+
+/* TF32 residual: lo[i] = x[i] - (x[i] with its low 13 mantissa bits cleared).
+ * The tensor cores read x itself as the high part. */
+int fg_split_lo(const float *d_x, float *d_lo, size_t n, void *stream);
+
+/* GEMM epilogues. */
+enum fg_gemm_epilogue {
+  FG_EPI_NONE = 0,      /* C = acc */
+  FG_EPI_BIAS = 1,      /* C = acc + bias[n] */
+  FG_EPI_BIAS_RELU = 2, /* C = relu(acc + bias[n]) */
+  FG_EPI_RELU_MASK = 3  /* C = (mask[m,n] > 0) ? acc : 0 */
+};
+/* Operand layout flags. */
+enum fg_gemm_flags {
+  FG_GEMM_A_MN_MAJOR = 1, /* A stored [K, M] (M contiguous) instead of [M, K] */
+  FG_GEMM_B_MN_MAJOR = 2, /* B stored [K, N] (N contiguous) instead of [N, K] */
+  FG_GEMM_1XTF32 = 4      /* drop the residual products (plain TF32) */
+};
+/* The reduce-of-broadcast-mul behind Tensor::matmul (src/tensor.rs:762-778)
+ * and its two backward contractions (src/gradient.rs:100-106,165-176):
+ *   C[m,n] = sum_k A(m,k) * B(n,k)
+ * on the tcgen05 tensor cores in 3xTF32 (hi*hi + hi*lo + lo*hi), fp32
+ * accumulation in TMEM.  d_a_lo / d_b_lo are the TF32 residuals of A and B
+ * in the same layout (fg_split_lo).  lda/ldb/ldc are row pitches in elements.
+ * d_c_lo (may be NULL) receives the residual of C for a following GEMM.
+ * Requirements: M, N, K > 0, pitches multiples of 4 elements, 16-byte
+ * aligned pointers. */
+int fg_gemm_3xtf32(int M, int N, int K, const float *d_a, const float *d_a_lo, int lda,
+                   const float *d_b, const float *d_b_lo, int ldb, float *d_c, float *d_c_lo,
+                   int ldc, int flags, int epilogue, const float *d_bias, const float *d_mask,
+                   int ldmask, void *stream);
+
+/* ---- MLP training step: forward -> cross_entropy -> backward -> Sgd ----- */
+/* examples/mnist.rs:90-97 on the GPU.  Layers are Linear (src/nn.rs:67-104)
+ * with ReLU between them; dims[0..n_layers] are the widths.  batch is the
+ * rows this rank processes; with a communicator attached the gradients are
+ * averaged across ranks before the update (data parallel). */
+int fg_mlp_create(fg_device *dev, int n_layers, const int *dims, int batch, float lr,
+                  fg_mlp **out);
+int fg_mlp_destroy(fg_mlp *mlp);
+/* Host <-> device parameter transfer; layer l weight is [dims[l+1], dims[l]]. */
+int fg_mlp_set_params(fg_mlp *mlp, int layer, const float *h_weight, const float *h_bias);
+int fg_mlp_get_params(fg_mlp *mlp, int layer, float *h_weight, float *h_bias);
+int fg_mlp_get_grads(fg_mlp *mlp, int layer, float *h_dweight, float *h_dbias);
+int fg_mlp_attach_comm(fg_mlp *mlp, fg_comm *comm);
+/* Device pointers of the step's input slots ([batch, dims[0]] and
+ * [batch, dims[n_layers]]) for callers that fill them on the GPU. */
+int fg_mlp_input_slots(fg_mlp *mlp, float **d_x, float **d_targets);
+/* One step on inputs already in the input slots; d_loss_out (device, may be
+ * NULL) receives this step's loss (mean over the global batch). */
+int fg_mlp_step(fg_mlp *mlp, float *d_loss_out);
+/* One step from host memory: copies h_x / h_targets in, runs the step and
+ * copies the loss out (blocking), the ferrograd call sequence
+ * forward/backward/step/loss.to_vec(). */
+int fg_mlp_step_host(fg_mlp *mlp, const float *h_x, const float *h_targets, float *h_loss);
+/* Capture the device part of fg_mlp_step in a CUDA graph and replay it. */
+int fg_mlp_use_graph(fg_mlp *mlp, int enable);
+/* Pre-update logits of the last step, [batch, dims[n_layers]] (loss.to_vec()
+ * reads pre-update values in the reference, src/tensor.rs:222-252). */
+int fg_mlp_get_logits(fg_mlp *mlp, float *h_logits);
+/* Launches of this library's kernels issued by the last fg_mlp_step. */
+int fg_mlp_launch_count(fg_mlp *mlp, int *count);
+/* GEMM timing: when enabled, each step records a CUDA event pair around every
+ * tensor-core GEMM launch on the step's stream (kept inside the CUDA graph
+ * when graph replay is on).  fg_mlp_gemm_times returns, for the most recent
+ * step, each GEMM's duration in ms and its algorithmic flops (2*M*N*K);
+ * capacity is the length of both arrays, *count the number written. */
+int fg_mlp_enable_gemm_timing(fg_mlp *mlp, int enable);
+int fg_mlp_gemm_times(fg_mlp *mlp, float *ms, double *flops, int capacity, int *count);
+
+/* ---- Data-parallel communicator (no reference counterpart: the reference
+ * is single-device, src/device.rs:37-41) ----------------------------------- */
+#define FG_UNIQUE_ID_BYTES 128
+int fg_comm_unique_id(char out[FG_UNIQUE_ID_BYTES]);
+/* Non-blocking NCCL init polled until timeout_ms; on timeout the
+ * communicator is aborted and FG_ERR_NCCL returned. */
+int fg_comm_init(int rank, int nranks, const char uid[FG_UNIQUE_ID_BYTES], int timeout_ms,
+                 fg_comm **out);
+int fg_comm_destroy(fg_comm *comm);
+int fg_comm_abort(fg_comm *comm);
+/* In-place mean over ranks of count f32 values on stream. */
+int fg_allreduce_mean_f32(fg_comm *comm, float *d_buf, size_t count, void *stream);
+
+/* ---- Diagnostics -------------------------------------------------------- */
+/* Reads and clears the device error word kernels set when a bounded wait
+ * expires; returns FG_ERR_DEVICE with a description if it was set. */
+int fg_check_device_error(void);
+/* Total launches of this library's kernels in this process. */
+uint64_t fg_kernel_launches(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FERRO_CUDA_H */

@@ -1,0 +1,88 @@
+"""One MLP training step (examples/mnist.rs:90-97) on the GPU versus the oracle.
+
+Tolerances (north star): loss relative <= 1e-4; gradients and one-step
+parameter deltas norm-relative <= 1e-4 (max|gpu - ref| / max|ref|); logits
+norm-relative <= 1e-5.
+"""
+import numpy as np
+import pytest
+
+from ferrograd_b200 import CudaDevice, MlpTrainer, data, mlp_init
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4
+
+
+def normrel(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30)
+
+
+def run_both(oracle, dims, batch, lr=0.01, seeds=(1, 2), graph=False, steps=1):
+    x, t = data.mlp_batch(batch, dims[0], dims[-1], *seeds)
+    ws, bs = mlp_init(dims)
+    tr = MlpTrainer(CudaDevice(0), dims, batch, lr, ws, bs, use_graph=graph)
+    ow, ob = [w.copy() for w in ws], [b.copy() for b in bs]
+    for _ in range(steps):
+        loss = tr.step_host(x, t)
+        oloss, ow, ob, odw, odb, ologits = oracle.mlp_step(ow, ob, x, t, lr)
+    return dict(tr=tr, x=x, t=t, ws=ws, bs=bs, loss=loss, oloss=oloss, ow=ow, ob=ob, odw=odw,
+                odb=odb, ologits=ologits)
+
+
+@pytest.mark.parametrize("dims,batch", [((784, 128, 10), 256),       # config 1
+                                        ((512, 256, 256, 10), 384),   # config 5, scaled down
+                                        ((64, 32), 64)])              # single tensor-core layer
+def test_mlp_step_matches_oracle(oracle, dims, batch):
+    r = run_both(oracle, dims, batch)
+    tr = r["tr"]
+    assert abs(r["loss"] - r["oloss"]) <= TOL * abs(r["oloss"])
+    assert normrel(tr.logits(), r["ologits"]) <= 1e-5
+    gw, gb = tr.grads()
+    for l in range(len(dims) - 1):
+        assert normrel(gw[l], r["odw"][l]) <= TOL, ("dW", l)
+        assert normrel(gb[l], r["odb"][l]) <= TOL, ("db", l)
+    pw, pb = tr.params()
+    for l in range(len(dims) - 1):
+        assert normrel(pw[l] - r["ws"][l], r["ow"][l] - r["ws"][l]) <= TOL, ("W delta", l)
+        assert normrel(pb[l] - r["bs"][l], r["ob"][l] - r["bs"][l]) <= TOL, ("b delta", l)
+
+
+def test_mlp_config1_three_steps_track_oracle(oracle):
+    r = run_both(oracle, (784, 128, 10), 256, steps=3)
+    assert abs(r["loss"] - r["oloss"]) <= TOL * abs(r["oloss"])
+    pw, _ = r["tr"].params()
+    assert normrel(pw[0] - r["ws"][0], r["ow"][0] - r["ws"][0]) <= 3 * TOL
+
+
+def test_graph_replay_matches_eager():
+    dims, batch = (512, 256, 256, 10), 256
+    x, t = data.mlp_batch(batch, dims[0], dims[-1], 5, 6)
+    ws, bs = mlp_init(dims)
+    eager = MlpTrainer(CudaDevice(0), dims, batch, 0.01, ws, bs, use_graph=False)
+    graph = MlpTrainer(CudaDevice(0), dims, batch, 0.01, ws, bs, use_graph=True)
+    for _ in range(3):
+        le = eager.step_host(x, t)
+        lg = graph.step_host(x, t)
+        assert le == lg
+    for a, b in zip(eager.params()[0], graph.params()[0]):
+        assert np.array_equal(a, b)
+    assert graph.launches_per_step == eager.launches_per_step > 0
+
+
+def test_loss_decreases_over_steps():
+    """The integration check the reference's MNIST example makes: loss falls."""
+    dims, batch = (784, 128, 10), 256
+    x, t = data.mlp_batch(batch, dims[0], dims[-1], 1, 2)
+    ws, bs = mlp_init(dims)
+    tr = MlpTrainer(CudaDevice(0), dims, batch, 0.1, ws, bs, use_graph=True)
+    losses = [tr.step_host(x, t) for _ in range(20)]
+    assert losses[-1] < losses[0]
+
+
+def test_unsupported_width_is_an_error():
+    from ferrograd_b200 import FerroError
+    with pytest.raises(FerroError):
+        MlpTrainer(CudaDevice(0), (64, 40, 10), 32, 0.01, *mlp_init((64, 40, 10)))
