@@ -193,28 +193,26 @@ def our_arm(args):
     import torch
     import torch.distributed as dist
 
-    from ferrograd_b200 import Communicator, CudaDevice, MlpTrainer, data, mlp_init
+    from ferrograd_b200 import Communicator, CudaDevice, MlpTrainer, data, dp, mlp_init
 
     rank, world, local = env_dist()
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    if GLOBAL_BATCH % world:
-        raise SystemExit("global batch must divide by the number of GPUs")
-    B = GLOBAL_BATCH // world
+    lo, hi = dp.shard_rows(GLOBAL_BATCH, rank, world)
+    B = hi - lo
 
     x_full, t_full = data.mlp_batch(GLOBAL_BATCH, DIMS[0], DIMS[-1], X_SEED, LABEL_SEED)
-    x = np.ascontiguousarray(x_full[rank * B:(rank + 1) * B])
-    t = np.ascontiguousarray(t_full[rank * B:(rank + 1) * B])
+    x = np.ascontiguousarray(x_full[lo:hi])
+    t = np.ascontiguousarray(t_full[lo:hi])
     del x_full, t_full
     ws, bs = mlp_init(DIMS)  # seeded: identical on every rank
 
     comm = None
     if world > 1:
-        uid = [Communicator.unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        comm = Communicator(rank, world, uid[0], timeout_ms=120000)
+        uid = dp.exchange_unique_id(dist, rank, Communicator.unique_id)
+        comm = Communicator(rank, world, uid, timeout_ms=120000)
     dev = CudaDevice(local)
     tr = MlpTrainer(dev, DIMS, B, LR, ws, bs, comm=comm, use_graph=True)
     tr.enable_gemm_timing(True)

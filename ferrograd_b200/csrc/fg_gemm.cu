@@ -155,12 +155,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
-      // K-major: next 8-element K slice is +32 bytes inside the swizzle row;
-      // MN-major: next 8 K rows are the next 1024-byte swizzle atom.
+      // K-major (128B swizzle, 8-row atoms of 128-byte rows): the next
+      // 8-element K slice is +32 bytes inside the swizzle row; SBO = 8 rows.
+      // MN-major (128B swizzle with 32-byte atomicity, 4-row atoms): a K row
+      // is 128 bytes (32 elements of M or N), the next 8 K rows are +1024
+      // bytes, SBO = 4 rows = 512 bytes, LBO = 4096 bytes between the
+      // 32-element MN chunks that TMA wrote as separate boxes.
       constexpr uint32_t a_kstep = A_MN ? 1024 : 32;
       constexpr uint32_t b_kstep = B_MN ? 1024 : 32;
-      constexpr uint32_t a_lbo = A_MN ? 4096 : 16, a_sbo = 1024;
-      constexpr uint32_t b_lbo = B_MN ? 4096 : 16, b_sbo = 1024;
+      constexpr uint32_t a_lbo = A_MN ? 4096 : 16, a_sbo = A_MN ? 512 : 1024;
+      constexpr uint32_t b_lbo = B_MN ? 4096 : 16, b_sbo = B_MN ? 512 : 1024;
+      constexpr uint32_t a_lay = A_MN ? kLayoutSw128Base32 : kLayoutSw128;
+      constexpr uint32_t b_lay = B_MN ? kLayoutSw128Base32 : kLayoutSw128;
       bool ok = true;
       for (int kb = 0; kb < nk; kb++) {
         const int s = kb % C::STAGES;
@@ -173,12 +179,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sblo = sb + C::B_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BK / UMMA_K; kk++) {
-          const uint64_t da = smem_desc_sw128(sa + kk * a_kstep, a_lbo, a_sbo);
-          const uint64_t db = smem_desc_sw128(sb + kk * b_kstep, b_lbo, b_sbo);
+          const uint64_t da = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_lay);
+          const uint64_t db = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_lay);
           const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
           if (three) {
-            const uint64_t dalo = smem_desc_sw128(salo + kk * a_kstep, a_lbo, a_sbo);
-            const uint64_t dblo = smem_desc_sw128(sblo + kk * b_kstep, b_lbo, b_sbo);
+            const uint64_t dalo = smem_desc(salo + kk * a_kstep, a_lbo, a_sbo, a_lay);
+            const uint64_t dblo = smem_desc(sblo + kk * b_kstep, b_lbo, b_sbo, b_lay);
             // small terms first, then the main product
             mma_tf32(tmem_base, dalo, db, idesc, acc);
             mma_tf32(tmem_base, da, dblo, idesc, 1u);
@@ -278,9 +284,11 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // Tensor map over a row-major fp32 matrix of `outer` rows x `inner` columns
-// with row pitch `ld` elements; box = 32 columns x box_rows rows, 128B swizzle.
+// with row pitch `ld` elements; box = 32 columns x box_rows rows.  K-major
+// tiles use the 128-byte swizzle; MN-major tiles the 128-byte swizzle with
+// 32-byte atoms (the layout tcgen05 reads MN-major tf32 operands in).
 static int make_map(CUtensorMap *map, const float *ptr, int inner, int outer, int ld,
-                    int box_rows) {
+                    int box_rows, bool mn_major) {
   auto fn = encode_fn();
   if (!fn) return set_error(FG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
@@ -288,7 +296,8 @@ static int make_map(CUtensorMap *map, const float *ptr, int inner, int outer, in
   cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)ptr, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(FG_ERR_CUDA,
@@ -336,18 +345,18 @@ int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, c
   int rc;
   // A: [M,K] K-major (box 32 x BM rows) or [K,M] MN-major (box 32 x 32)
   if (a_mn) {
-    if ((rc = make_map(&pl->a, a, M, K, lda, 32))) return rc;
-    if ((rc = make_map(&pl->alo, one ? a : a_lo, M, K, lda, 32))) return rc;
+    if ((rc = make_map(&pl->a, a, M, K, lda, 32, true))) return rc;
+    if ((rc = make_map(&pl->alo, one ? a : a_lo, M, K, lda, 32, true))) return rc;
   } else {
-    if ((rc = make_map(&pl->a, a, K, M, lda, BM))) return rc;
-    if ((rc = make_map(&pl->alo, one ? a : a_lo, K, M, lda, BM))) return rc;
+    if ((rc = make_map(&pl->a, a, K, M, lda, BM, false))) return rc;
+    if ((rc = make_map(&pl->alo, one ? a : a_lo, K, M, lda, BM, false))) return rc;
   }
   if (b_mn) {
-    if ((rc = make_map(&pl->b, b, N, K, ldb, 32))) return rc;
-    if ((rc = make_map(&pl->blo, one ? b : b_lo, N, K, ldb, 32))) return rc;
+    if ((rc = make_map(&pl->b, b, N, K, ldb, 32, true))) return rc;
+    if ((rc = make_map(&pl->blo, one ? b : b_lo, N, K, ldb, 32, true))) return rc;
   } else {
-    if ((rc = make_map(&pl->b, b, K, N, ldb, bn))) return rc;
-    if ((rc = make_map(&pl->blo, one ? b : b_lo, K, N, ldb, bn))) return rc;
+    if ((rc = make_map(&pl->b, b, K, N, ldb, bn, false))) return rc;
+    if ((rc = make_map(&pl->blo, one ? b : b_lo, K, N, ldb, bn, false))) return rc;
   }
   DevCtx *ctx = ctx_current();
   if (!ctx) return set_error(FG_ERR_CUDA, "no CUDA device context");

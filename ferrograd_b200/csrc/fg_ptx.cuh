@@ -132,15 +132,24 @@ __device__ __forceinline__ void tmem_ld_wait() {
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"):
 //   [0,14) start address >> 4, [16,30) leading-dimension byte offset >> 4,
 //   [32,46) stride-dimension byte offset >> 4, [46,48) version = 1,
-//   [49,52) base offset = 0, [52] LBO mode = 0, [61,64) layout (2 = 128B swizzle).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+//   [49,52) base offset = 0, [52] LBO mode = 0, [61,64) layout type.
+// Layout types used here:
+//   kLayoutSw128       (2): 128-byte swizzle of 16-byte chunks, 8-row atoms
+//                           (K-major operands)
+//   kLayoutSw128Base32 (1): 128-byte swizzle of 32-byte chunks, 4-row atoms --
+//                           the only layout tcgen05 accepts for MN-major
+//                           32-bit (tf32) operands
+constexpr uint32_t kLayoutSw128 = 2;
+constexpr uint32_t kLayoutSw128Base32 = 1;
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes, uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)(layout & 7u) << 61;
   return d;
 }
 
