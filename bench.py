@@ -152,7 +152,7 @@ class ClockSampler:
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv",
-                                          "-lms", "200", "-i", str(self.gpu)], stdout=self.f,
+                                          "-lms", "100", "-i", str(self.gpu)], stdout=self.f,
                                          stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -326,19 +326,179 @@ def our_arm(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Per-config kernel benchmarks (configs 1-4 of the workload list); the driver's
+# headline line is config 5 above.  Each prints one JSON line.
+# ---------------------------------------------------------------------------
+def _event_time(fn, iters, flush=None):
+    """Average ms of fn() over iters, each call bracketed by CUDA events on the
+    current stream; `flush` (if given) runs untimed before every call."""
+    import torch
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return statistics.mean(times)
+
+
+def _hbm_roofline(nbytes, ms, peaks, src, kernel):
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": gbs / peaks["hbm_gbs"], "traffic": None, "kernel": kernel,
+            "peak_basis": f"{src} hbm_gbs (copy bandwidth, burst)"}
+
+
+def config_bench(args):
+    import torch
+
+    from ferrograd_b200 import CudaDevice, MlpTrainer, data, kernels, mlp_init
+    from ferrograd_b200._lib import REDUCE_MAX, REDUCE_SUM
+
+    peaks, src = load_peaks()
+    iters, warm = args.steps, max(args.warmup, 3)
+    flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MiB > L2
+
+    def flush():
+        flush_buf.zero_()
+
+    if args.config == "c1":
+        dims, B = (784, 128, 10), 256
+        x, t = data.mlp_batch(B, dims[0], dims[-1], 1, 2)
+        tr = MlpTrainer(CudaDevice(0), dims, B, 0.01, *mlp_init(dims), use_graph=True)
+        xp, tp = torch.from_numpy(x).pin_memory(), torch.from_numpy(t).pin_memory()
+        lossp = torch.zeros(1).pin_memory()
+        for _ in range(warm):
+            tr.step_host_ptr(xp.data_ptr(), tp.data_ptr(), lossp.data_ptr())
+        stream = torch.cuda.ExternalStream(tr.device.stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(iters):
+            tr.step()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        t0 = time.perf_counter()
+        for _ in range(iters):
+            tr.step_host_ptr(xp.data_ptr(), tp.data_ptr(), lossp.data_ptr())
+        e2e_ms = (time.perf_counter() - t0) / iters * 1e3
+        flops = 2 * B * (784 * 128 + 128 * 10) * 3 - 2 * B * 784 * 128  # no dX for the input
+        line = {"metric": "config1 MLP train steps/s (784-128-10, batch 256)", "value": 1e3 / ms,
+                "unit": "steps/s", "ms_per_step": ms, "launches_per_step": tr.launches_per_step,
+                "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s",
+                        "h2d_bytes_per_step": int(x.nbytes + t.nbytes), "d2h_bytes_per_step": 4},
+                "flop_per_step": flops, "bound": "latency (launch-bound; CUDA graph replay)"}
+    elif args.config == "c2":
+        n = data.C2_N
+        g = torch.Generator(device="cuda").manual_seed(3)
+        a, b, c = (torch.randn(n, device="cuda", generator=g) for _ in range(3))
+        out = torch.empty_like(a)
+        fn = lambda: kernels.ew_fma_relu_scale(a, b, c, 0.5, out=out)  # noqa: E731
+        for _ in range(warm):
+            fn()
+        ms = _event_time(fn, iters)
+        ew = _hbm_roofline(16 * n, ms, peaks, src, "k_ew_fma_relu_scale_v4")
+        ew.update(ms=ms)
+        X = torch.randn(data.C2_X, device="cuda", generator=g)
+        Xi = torch.randint(-1000, 1001, data.C2_X, device="cuda", dtype=torch.int32, generator=g)
+        reds = {}
+        for name, f in (("f32 sum last axis", lambda: kernels.reduce_rows(X, REDUCE_SUM)),
+                        ("f32 max last axis", lambda: kernels.reduce_rows(X, REDUCE_MAX)),
+                        ("f32 sum axis 0", lambda: kernels.reduce_cols(X, REDUCE_SUM)),
+                        ("i32 sum last axis", lambda: kernels.reduce_rows(Xi, REDUCE_SUM)),
+                        ("i32 max last axis", lambda: kernels.reduce_rows(Xi, REDUCE_MAX))):
+            for _ in range(warm):
+                f()
+            rms = _event_time(f, iters, flush)
+            r = _hbm_roofline(X.numel() * 4, rms, peaks, src, name)
+            r.update(ms=rms)
+            reds[name] = r
+        line = {"metric": "config2 fused elementwise relu(a*b+c)*0.5 over 64M f32 (GB/s)",
+                "value": ew["achieved"], "unit": "GB/s", "roofline": ew, "reductions": reds,
+                "config": {"workload": "config2", "n": n, "X": list(data.C2_X),
+                           "l2": "elementwise inputs 768 MiB > L2; reductions flush L2 (256 MiB "
+                                 "write) before every timed call"}}
+    elif args.config == "c3":
+        nn_ = data.C3_N
+        g = torch.Generator(device="cuda").manual_seed(8)
+        A = (torch.rand((nn_, nn_), device="cuda", generator=g) * 2 - 1) / 64
+        Bm = (torch.rand((nn_, nn_), device="cuda", generator=g) * 2 - 1) / 64
+        G = torch.randn((nn_, nn_), device="cuda", generator=g) * 1e-2
+        A_lo, B_lo, G_lo = kernels.split_lo(A), kernels.split_lo(Bm), kernels.split_lo(G)
+        out = torch.empty((nn_, nn_), device="cuda")
+        cases = {
+            "C = A.B (K-major x MN-major)": lambda: kernels.gemm(A, Bm, a_lo=A_lo, b_lo=B_lo,
+                                                                 b_mn_major=True, out=out),
+            "dA = G.B^T (K-major x K-major)": lambda: kernels.gemm(G, Bm, a_lo=G_lo, b_lo=B_lo,
+                                                                   out=out),
+            "dB = A^T.G (MN-major x MN-major)": lambda: kernels.gemm(A, G, a_lo=A_lo, b_lo=G_lo,
+                                                                     a_mn_major=True,
+                                                                     b_mn_major=True, out=out),
+        }
+        flops = 2 * nn_ ** 3
+        peak = peaks["bf16_tflops"] / 2 / 3
+        res = {}
+        for name, f in cases.items():
+            for _ in range(warm):
+                f()
+            ms = _event_time(f, iters)
+            tf = flops / (ms * 1e-3) / 1e12
+            res[name] = {"ms": ms, "tflops": tf, "frac": tf / peak}
+        avg = statistics.mean(r["tflops"] for r in res.values())
+        line = {"metric": "config3 GEMM 4096^3 fp32 via 3xTF32 tcgen05 (algorithmic TFLOP/s)",
+                "value": avg, "unit": "TFLOP/s",
+                "roofline": {"bound": "tensor", "achieved": avg, "peak": peak, "unit": "TFLOP/s",
+                             "frac": avg / peak, "traffic": None, "kernel": "k_gemm3x",
+                             "peak_basis": f"{src} bf16_tflops (burst) / 2 (TF32) / 3 (3 MMAs)"},
+                "contractions": res,
+                "config": {"workload": "config3", "M": nn_, "N": nn_, "K": nn_,
+                           "l2": "operands + residuals 256 MiB > L2"}}
+    elif args.config == "c4":
+        Bx, C = data.C4
+        g = torch.Generator(device="cuda").manual_seed(11)
+        x = torch.randn((Bx, C), device="cuda", generator=g) * 2
+        lab = torch.randint(0, C, (Bx,), device="cuda", generator=g)
+        t = torch.nn.functional.one_hot(lab, C).float()
+        fn = lambda: kernels.xent_fwd_bwd(x, t)  # noqa: E731
+        for _ in range(warm):
+            fn()
+        ms = _event_time(fn, iters)
+        r = _hbm_roofline(3 * Bx * C * 4, ms, peaks, src, "k_xent_rows_v4<8> + k_xent_loss_final")
+        r.update(ms=ms)
+        line = {"metric": "config4 cross-entropy fwd+bwd [65536,1000] f32 (GB/s)",
+                "value": r["achieved"], "unit": "GB/s", "roofline": r,
+                "config": {"workload": "config4", "shape": [Bx, C],
+                           "l2": "logits + targets + dlogits 786 MB > L2"}}
+    else:
+        raise SystemExit(f"unknown config {args.config}")
+    line.update({"n_gpus": 1, "steps": iters, "warmup": warm, "dtype": "f32", "data": "synthetic"})
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5"], default="c5",
+                    help="c5 (default) is the headline training step; c1-c4 time one config")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return reference_arm(args)
+    if args.config != "c5":
+        return config_bench(args)
     return our_arm(args)
 
 

@@ -341,7 +341,10 @@ int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, c
   FG_REQUIRE(epilogue != FG_EPI_BIAS && epilogue != FG_EPI_BIAS_RELU ? true : bias != nullptr,
              "gemm: epilogue needs a bias");
   FG_REQUIRE(epilogue != FG_EPI_RELU_MASK || (mask && ldmask >= N), "gemm: epilogue needs a mask");
-  const int bn = 128;
+  // 128 x 256 tiles need ~25% less shared-memory operand traffic per flop
+  // than 128 x 128 (the tensor cores re-read A for every 8-deep K slice);
+  // narrow outputs keep the 128-wide tile.
+  const int bn = (N >= 256) ? 256 : 128;
   int rc;
   // A: [M,K] K-major (box 32 x BM rows) or [K,M] MN-major (box 32 x 32)
   if (a_mn) {
@@ -385,6 +388,12 @@ int run_plan(const GemmPlan &pl, cudaStream_t st) {
     if (!pl.a_mn && pl.b_mn) return launch_t<128, false, true>(pl, st);
     if (pl.a_mn && !pl.b_mn) return launch_t<128, true, false>(pl, st);
     return launch_t<128, true, true>(pl, st);
+  }
+  if (pl.bn == 256) {
+    if (!pl.a_mn && !pl.b_mn) return launch_t<256, false, false>(pl, st);
+    if (!pl.a_mn && pl.b_mn) return launch_t<256, false, true>(pl, st);
+    if (pl.a_mn && !pl.b_mn) return launch_t<256, true, false>(pl, st);
+    return launch_t<256, true, true>(pl, st);
   }
   return set_error(FG_ERR_UNSUPPORTED, "gemm: tile width %d not built", pl.bn);
 }
