@@ -459,6 +459,43 @@ def config_bench(args):
                 "contractions": res,
                 "config": {"workload": "config3", "M": nn_, "N": nn_, "K": nn_,
                            "l2": "operands + residuals 256 MiB > L2"}}
+    elif args.config == "c5gemm":
+        # the three GEMM shapes of the config-5 step at one GPU, with the step's epilogues
+        M, N = GLOBAL_BATCH, 4096
+        g = torch.Generator(device="cuda").manual_seed(13)
+        act = torch.rand((M, N), device="cuda", generator=g)
+        W = torch.randn((N, N), device="cuda", generator=g) * (2.0 / N) ** 0.5
+        Gm = torch.randn((M, N), device="cuda", generator=g) * 1e-4
+        bias = torch.zeros(N, device="cuda")
+        act_lo, W_lo, G_lo = kernels.split_lo(act), kernels.split_lo(W), kernels.split_lo(Gm)
+        out, out_lo = torch.empty((M, N), device="cuda"), torch.empty((M, N), device="cuda")
+        dW = torch.empty((N, N), device="cuda")
+        from ferrograd_b200._lib import EPI_BIAS_RELU, EPI_RELU_MASK
+        cases = {
+            "forward act.W^T + b, relu (K x K)": (2 * M * N * N, lambda: kernels.gemm(
+                act, W, a_lo=act_lo, b_lo=W_lo, epilogue=EPI_BIAS_RELU, bias=bias, out=out,
+                out_lo=out_lo)),
+            "dW = G^T.act (MN x MN)": (2 * M * N * N, lambda: kernels.gemm(
+                Gm, act, a_lo=G_lo, b_lo=act_lo, a_mn_major=True, b_mn_major=True, out=dW)),
+            "dX = mask(G.W) (K x MN)": (2 * M * N * N, lambda: kernels.gemm(
+                Gm, W, a_lo=G_lo, b_lo=W_lo, b_mn_major=True, epilogue=EPI_RELU_MASK, mask=act,
+                out=out, out_lo=out_lo)),
+        }
+        peak = peaks["bf16_tflops"] / 2 / 3
+        res = {}
+        for name, (fl, f) in cases.items():
+            for _ in range(warm):
+                f()
+            ms = _event_time(f, iters)
+            tf = fl / (ms * 1e-3) / 1e12
+            res[name] = {"ms": ms, "tflops": tf, "frac": tf / peak}
+        avg = statistics.mean(r["tflops"] for r in res.values())
+        line = {"metric": "config5 GEMMs 8192x4096x4096 (3xTF32 tcgen05, algorithmic TFLOP/s)",
+                "value": avg, "unit": "TFLOP/s",
+                "roofline": {"bound": "tensor", "achieved": avg, "peak": peak, "unit": "TFLOP/s",
+                             "frac": avg / peak, "traffic": None, "kernel": "k_gemm3x",
+                             "peak_basis": f"{src} bf16_tflops (burst) / 2 (TF32) / 3 (3 MMAs)"},
+                "contractions": res, "config": {"workload": "config5 GEMM shapes"}}
     elif args.config == "c4":
         Bx, C = data.C4
         g = torch.Generator(device="cuda").manual_seed(11)
@@ -490,7 +527,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5"], default="c5",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c5gemm"], default="c5",
                     help="c5 (default) is the headline training step; c1-c4 time one config")
     args = ap.parse_args()
     if args.warmup < 3:
