@@ -64,6 +64,7 @@ SIGNATURES = [
     ("fg_reduce_rows", _i, [_i, _i, _vp, _vp, _sz, _sz, _vp]),
     ("fg_reduce_cols", _i, [_i, _i, _vp, _vp, _sz, _sz, _vp]),
     ("fg_xent_fwd_bwd", _i, [_vp, _vp, _sz, _sz, _vp, _vp, _f, _vp]),
+    ("fg_xent_fwd_bwd_noalloc", _i, [_vp, _vp, _sz, _sz, _vp, _vp, _f, _vp]),
     ("fg_sgd", _i, [_vp, _vp, _sz, _f, _vp, _vp]),
     ("fg_split_lo", _i, [_vp, _vp, _sz, _vp]),
     ("fg_gemm_3xtf32", _i, [_i, _i, _i, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp, _vp,

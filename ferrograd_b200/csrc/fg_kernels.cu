@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "fg_internal.h"
 #include "fg_kernels.cuh"
 
@@ -616,6 +618,106 @@ int fg_xent_fwd_bwd(const float *d_logits, const float *d_targets, size_t rows, 
   FG_REQUIRE(d_logits && d_targets && d_loss, "fg_xent_fwd_bwd: null pointer");
   return fg::launch_xent(d_logits, d_targets, rows, cols, d_loss, d_dx, grad_scale,
                          (cudaStream_t)stream, nullptr);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Cross-entropy without any device allocation.
+//
+// Some callers cannot allocate device memory once they are running: a host
+// that reserves its whole device-memory budget at start-up (a serving
+// process, or a runtime with its own pool) and must not call cudaMalloc later,
+// because cudaMalloc / cudaFree can synchronise the device, can fail under
+// fragmentation in the middle of a job, and bypass the caller's accounting.
+// fg_xent_fwd_bwd_noalloc gives them the cross-entropy kernel with its
+// per-row scratch in this file-scope array instead of the library's growable
+// workspace.  The array is part of the library's device image, so every GPU
+// that loads the library holds it (kFgXentNoallocMaxRows floats, 1 MiB)
+// until the process exits.
+//
+// In host code the array's name is only a host-side stand-in, not a device
+// address: the launcher passes the address that cudaGetSymbolAddress returned
+// for the current device.  All calls share the array and each call
+// overwrites every row it uses before reading it (nothing needs to start at
+// zero), so calls that overlap on the GPU -- two streams, or two threads --
+// race on it and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_xent_noalloc_scratch[kFgXentNoallocMaxRows];
+
+namespace fg {
+namespace {
+
+struct NoallocDevice {
+  float *scratch = nullptr;  // device address of g_xent_noalloc_scratch
+  int sms = 0;
+  bool ready = false;
+};
+std::mutex g_noalloc_mu;
+NoallocDevice g_noalloc[64];
+
+// Once per device, with that device current: resolve the array's device
+// address and the SM count.  Neither call allocates.
+int noalloc_setup(NoallocDevice **out) {
+  int dev = 0;
+  FG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(FG_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoallocDevice &d = g_noalloc[dev];
+  if (!d.ready) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_xent_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(FG_ERR_CUDA, "cudaGetSymbolAddress(g_xent_noalloc_scratch) failed: %s",
+                       cudaGetErrorString(e));
+    FG_CUDA_TRY(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    d.scratch = (float *)p;
+    d.ready = true;
+  }
+  *out = &d;
+  return FG_OK;
+}
+
+}  // namespace
+}  // namespace fg
+
+extern "C" {
+
+int fg_xent_fwd_bwd_noalloc(const float *d_logits, const float *d_targets, size_t rows,
+                            size_t cols, float *d_loss, float *d_dx, float grad_scale,
+                            void *stream) {
+  FG_REQUIRE(d_logits && d_targets && d_loss, "fg_xent_fwd_bwd_noalloc: null pointer");
+  FG_REQUIRE(rows > 0 && cols > 0, "fg_xent_fwd_bwd_noalloc: empty logits");
+  FG_REQUIRE(rows <= (size_t)kFgXentNoallocMaxRows,
+             "fg_xent_fwd_bwd_noalloc: %zu rows exceed the static scratch limit of %d rows", rows,
+             kFgXentNoallocMaxRows);
+  FG_REQUIRE(cols <= (size_t)INT32_MAX, "fg_xent_fwd_bwd_noalloc: cols too large");
+  fg::NoallocDevice *nd = nullptr;
+  int rc = fg::noalloc_setup(&nd);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const float inv_n = 1.0f / (float)rows;
+  const int c = (int)cols;
+  size_t want = (rows * 32 + 255) / 256;
+  size_t cap = (size_t)nd->sms * 16;
+  const int grid = (int)(want < cap ? (want ? want : 1) : cap);
+  const bool vec = (cols % 4 == 0) && fg::aligned16(d_logits) && fg::aligned16(d_targets) &&
+                   (!d_dx || fg::aligned16(d_dx));
+  float *scratch = nd->scratch;
+  if (vec && cols <= 128)
+    fg::k_xent_rows_v4<1><<<grid, 256, 0, st>>>(d_logits, d_targets, d_dx, scratch, rows, c, inv_n, grad_scale);
+  else if (vec && cols <= 256)
+    fg::k_xent_rows_v4<2><<<grid, 256, 0, st>>>(d_logits, d_targets, d_dx, scratch, rows, c, inv_n, grad_scale);
+  else if (vec && cols <= 512)
+    fg::k_xent_rows_v4<4><<<grid, 256, 0, st>>>(d_logits, d_targets, d_dx, scratch, rows, c, inv_n, grad_scale);
+  else if (vec && cols <= 1024)
+    fg::k_xent_rows_v4<8><<<grid, 256, 0, st>>>(d_logits, d_targets, d_dx, scratch, rows, c, inv_n, grad_scale);
+  else
+    fg::k_xent_rows_generic<<<grid, 256, 0, st>>>(d_logits, d_targets, d_dx, scratch, rows, c, inv_n, grad_scale);
+  FG_LAUNCH_TRY();
+  fg::k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, rows, inv_n, d_loss);
+  FG_LAUNCH_TRY();
+  return FG_OK;
 }
 
 int fg_sgd(float *d_p, const float *d_g, size_t n, float lr, float *d_p_lo, void *stream) {

@@ -3,6 +3,12 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include "../../include/ferro_cuda.h"
+
+// Rows of per-row scratch held in the library's static device array for
+// fg_xent_fwd_bwd_noalloc (262144 floats = 1 MiB per GPU).
+constexpr int kFgXentNoallocMaxRows = FG_XENT_NOALLOC_MAX_ROWS;
+
 namespace fg {
 
 constexpr int kMaxSgdSegments = 8;

@@ -121,6 +121,20 @@ int fg_reduce_cols(int dtype, int op, const void *d_x, void *d_out, size_t rows,
 int fg_xent_fwd_bwd(const float *d_logits, const float *d_targets, size_t rows, size_t cols,
                     float *d_loss, float *d_dx, float grad_scale, void *stream);
 
+/* No counterpart in the reference.  fg_xent_fwd_bwd without any device
+ * allocation, for callers that may not allocate device memory after start-up
+ * (a process that reserves its whole memory budget up front: cudaMalloc can
+ * synchronise the device and fail under fragmentation mid-run).  The per-row
+ * scratch is a static array inside the library, 1 MiB on every GPU that
+ * loads it, so rows is limited to FG_XENT_NOALLOC_MAX_ROWS; larger inputs
+ * return FG_ERR_INVALID.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) and should come before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race. */
+#define FG_XENT_NOALLOC_MAX_ROWS 262144
+int fg_xent_fwd_bwd_noalloc(const float *d_logits, const float *d_targets, size_t rows,
+                            size_t cols, float *d_loss, float *d_dx, float grad_scale,
+                            void *stream);
+
 /* Sgd::step (src/optim.rs:60-71): p <- p + (-(g*lr)).  If d_p_lo is not
  * NULL it also receives the TF32 residual of the updated p (see fg_split_lo). */
 int fg_sgd(float *d_p, const float *d_g, size_t n, float lr, float *d_p_lo, void *stream);
