@@ -244,11 +244,11 @@ def our_arm(args):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
         phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].isdigit() else local
         sampler = ClockSampler(phys)
-    barrier()
-    torch.cuda.synchronize()
-    if sampler:
+    if sampler:  # start sampling before the barrier so every rank enters the timed region together
         sampler.start()
         time.sleep(0.4)
+    barrier()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = int(tr.launches_per_step)
     e0.record(stream)
@@ -257,8 +257,8 @@ def our_arm(args):
     e1.record(stream)
     e1.synchronize()
     torch.cuda.synchronize()
-    clocks = sampler.stop() if sampler else None
     barrier()
+    clocks = sampler.stop() if sampler else None
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     gemms = tr.gemm_times()
 

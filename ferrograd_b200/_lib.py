@@ -80,6 +80,7 @@ SIGNATURES = [
     ("fg_mlp_step_host", _i, [_vp, _vp, _vp, _vp]),
     ("fg_mlp_use_graph", _i, [_vp, _i]),
     ("fg_mlp_get_logits", _i, [_vp, _vp]),
+    ("fg_mlp_get_activations", _i, [_vp, _i, _vp]),
     ("fg_mlp_launch_count", _i, [_vp, ctypes.POINTER(_i)]),
     ("fg_mlp_enable_gemm_timing", _i, [_vp, _i]),
     ("fg_mlp_gemm_times", _i, [_vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double),

@@ -16,7 +16,8 @@
 //   warps 2-5  epilogue: tcgen05.ld TMEM -> registers -> fused op -> global
 // Operands are K-major ([rows, K], K contiguous) or MN-major ([K, rows]);
 // both are loaded with 128-byte swizzle and described to tcgen05 directly,
-// so no transposed copies are made.  No TMA multicast is used anywhere.
+// so no transposed copies are made.  Every TMA load fills only this CTA's own
+// shared memory from this GPU's memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>

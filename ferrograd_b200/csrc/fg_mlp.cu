@@ -699,6 +699,15 @@ int fg_mlp_step_host(fg_mlp *m, const float *h_x, const float *h_targets, float 
   return FG_OK;
 }
 
+int fg_mlp_get_activations(fg_mlp *m, int layer, float *h_out) {
+  FG_REQUIRE(m && h_out && layer >= 0 && layer < m->nl, "fg_mlp_get_activations: bad argument");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  FG_CUDA_TRY(cudaMemcpyAsync(h_out, m->act[layer], sizeof(float) * (size_t)m->B * m->dims[layer + 1],
+                              cudaMemcpyDeviceToHost, m->st));
+  FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+  return fg_check_device_error();
+}
+
 int fg_mlp_get_logits(fg_mlp *m, float *h_logits) {
   FG_REQUIRE(m && h_logits, "fg_mlp_get_logits: null argument");
   FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));

@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for sm_100a: mbarriers (with bounded waits), TMA
-// tile loads (never with .multicast::cluster), tcgen05 TMEM allocation, MMA,
+// tile loads (plain, this CTA only), tcgen05 TMEM allocation, MMA,
 // commit and TMEM loads.
 #pragma once
 #include <cuda.h>

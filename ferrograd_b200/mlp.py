@@ -153,6 +153,12 @@ class MlpTrainer:
             bs.append(b)
         return ws, bs
 
+    def activations(self, layer: int) -> np.ndarray:
+        """Output of `layer` in the last forward pass (post-ReLU, or logits)."""
+        out = np.empty((self.batch, self.dims[layer + 1]), np.float32)
+        call("fg_mlp_get_activations", self._h, int(layer), out.ctypes.data)
+        return out
+
     def logits(self) -> np.ndarray:
         out = np.empty((self.batch, self.dims[-1]), np.float32)
         call("fg_mlp_get_logits", self._h, out.ctypes.data)

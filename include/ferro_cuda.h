@@ -198,6 +198,10 @@ int fg_mlp_use_graph(fg_mlp *mlp, int enable);
 /* Pre-update logits of the last step, [batch, dims[n_layers]] (loss.to_vec()
  * reads pre-update values in the reference, src/tensor.rs:222-252). */
 int fg_mlp_get_logits(fg_mlp *mlp, float *h_logits);
+/* Output of layer `layer` in the last step's forward pass, [batch,
+ * dims[layer+1]]: post-ReLU activations for hidden layers, logits for the
+ * last (the intermediates ferrograd materializes, src/schedule.rs:289-335). */
+int fg_mlp_get_activations(fg_mlp *mlp, int layer, float *h_out);
 /* Launches of this library's kernels issued by the last fg_mlp_step. */
 int fg_mlp_launch_count(fg_mlp *mlp, int *count);
 /* GEMM timing: when enabled, each step records a CUDA event pair around every

@@ -532,8 +532,20 @@ void orc_sgd(float *p, const float *g, long n, float lr) {
  * in place; dW / db (optional, may be NULL) receive the gradients; logits_out
  * (optional) the pre-update logits.  Returns the loss.
  * ------------------------------------------------------------------------- */
+float orc_mlp_step_acts(int nl, const long *dims, long B, float lr, float **W, float **bias,
+                        const float *x, const float *t, float **dW, float **db, float *logits_out,
+                        float **acts_out);
+
 float orc_mlp_step(int nl, const long *dims, long B, float lr, float **W, float **bias,
                    const float *x, const float *t, float **dW, float **db, float *logits_out) {
+  return orc_mlp_step_acts(nl, dims, B, lr, W, bias, x, t, dW, db, logits_out, NULL);
+}
+
+/* As orc_mlp_step; acts_out (optional) receives each hidden layer's post-ReLU
+ * activations [B, dims[l+1]] for l < nl-1. */
+float orc_mlp_step_acts(int nl, const long *dims, long B, float lr, float **W, float **bias,
+                        const float *x, const float *t, float **dW, float **db, float *logits_out,
+                        float **acts_out) {
   float **z = (float **)calloc((size_t)nl, sizeof(float *)); /* pre-activations */
   float **a = (float **)calloc((size_t)nl, sizeof(float *)); /* post-ReLU acts */
   for (int l = 0; l < nl; l++) {
@@ -544,6 +556,7 @@ float orc_mlp_step(int nl, const long *dims, long B, float lr, float **W, float 
     if (l < nl - 1) {
       a[l] = (float *)malloc(sizeof(float) * (size_t)(B * out));
       orc_relu(z[l], a[l], B * out);
+      if (acts_out && acts_out[l]) memcpy(acts_out[l], a[l], sizeof(float) * (size_t)(B * out));
     }
   }
   long C = dims[nl];

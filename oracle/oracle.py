@@ -60,6 +60,8 @@ def lib():
                                _f32p, _f32p, ctypes.POINTER(ctypes.c_void_p),
                                ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
     L.orc_mlp_step.restype = ctypes.c_float
+    L.orc_mlp_step_acts.argtypes = L.orc_mlp_step.argtypes + [ctypes.POINTER(ctypes.c_void_p)]
+    L.orc_mlp_step_acts.restype = ctypes.c_float
     _lib = L
     return L
 
@@ -184,10 +186,11 @@ def sgd(p, g, lr: float):
     return p
 
 
-def mlp_step(weights, biases, x, t, lr: float, want_grads: bool = True):
+def mlp_step(weights, biases, x, t, lr: float, want_grads: bool = True, acts=None):
     """One training step; returns (loss, new_weights, new_biases, dW, db, logits).
 
     Inputs are not modified: parameters are copied before the in-place update.
+    If `acts` is a list, it receives the hidden layers' post-ReLU activations.
     """
     nl = len(weights)
     dims = [weights[0].shape[1]] + [w.shape[0] for w in weights]
@@ -202,6 +205,10 @@ def mlp_step(weights, biases, x, t, lr: float, want_grads: bool = True):
     bp = (ctypes.c_void_p * nl)(*[b.ctypes.data for b in bs])
     dWp = (ctypes.c_void_p * nl)(*[w.ctypes.data for w in dWs]) if want_grads else None
     dbp = (ctypes.c_void_p * nl)(*[b.ctypes.data for b in dbs]) if want_grads else None
-    loss = lib().orc_mlp_step(nl, dims_c, B, ctypes.c_float(lr), Wp, bp, _c(x), _c(t),
-                              dWp, dbp, logits.ctypes.data)
+    hidden = [np.empty((B, dims[l + 1]), np.float32) for l in range(nl - 1)]
+    ap = (ctypes.c_void_p * max(1, nl - 1))(*[h.ctypes.data for h in hidden])
+    loss = lib().orc_mlp_step_acts(nl, dims_c, B, ctypes.c_float(lr), Wp, bp, _c(x), _c(t),
+                                   dWp, dbp, logits.ctypes.data, ap)
+    if acts is not None:
+        acts.extend(hidden)
     return float(np.float32(loss)), Ws, bs, dWs, dbs, logits
