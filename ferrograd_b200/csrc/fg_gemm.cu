@@ -10,9 +10,10 @@
 // exact residual x - trunc_tf32(x).  The residual-times-residual term is
 // dropped (relative size 2^-22).  Accumulation is fp32 in TMEM.
 //
-// CTA = 6 warps, one output tile of 128 x BN:
+// Persistent CTA (one per SM, 6 warps) looping over 128 x BN output tiles:
 //   warp 0     TMA producer (one elected lane), STAGES-deep smem ring
-//   warp 1     TMEM allocator + MMA issuer (one elected lane)
+//   warp 1     TMEM allocator + MMA issuer (one elected lane); two TMEM
+//              accumulators so tile i+1 accumulates while tile i drains
 //   warps 2-5  epilogue: tcgen05.ld TMEM -> registers -> fused op -> global
 // Operands are K-major ([rows, K], K contiguous) or MN-major ([K, rows]);
 // both are loaded with 128-byte swizzle and described to tcgen05 directly,
@@ -44,7 +45,7 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
   static constexpr int STAGES = (BN <= 128) ? 3 : 2;
-  static constexpr int TMEM_COLS = BN;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -59,6 +60,28 @@ constexpr unsigned kErrProducer = 1u << 16;
 constexpr unsigned kErrMma = 2u << 16;
 constexpr unsigned kErrEpilogue = 3u << 16;
 
+// Tile index -> (m block, n block).  Tiles are walked in groups of kGroupM
+// row blocks, row block fastest, so the ~148 tiles in flight at any time
+// share a few B panels and a few A panels (L2 reuse of both operands).
+constexpr int kGroupM = 16;
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int &mb, int &nb) {
+  const int per_group = kGroupM * num_n;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gm = min(kGroupM, num_m - first_m);
+  const int r = tile - group * per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Persistent: one CTA per SM loops over output tiles.  The accumulator lives
+// in one of two TMEM buffers (2 x BN columns): while the epilogue warps drain
+// tile i from one buffer, the MMA warp already accumulates tile i+1 in the
+// other.
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm3x(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAlo,
@@ -71,13 +94,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
   uint64_t *empty = full + C::STAGES;
-  uint64_t *accum_full = empty + C::STAGES;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum_full + 1);
+  uint64_t *tmem_full = empty + C::STAGES;  // [2]: accumulator ready for the epilogue
+  uint64_t *tmem_empty = tmem_full + 2;     // [2]: epilogue drained the accumulator
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tmem_empty + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * BM;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int ntiles = num_m * num_n;
   const int nk = (p.K + BK - 1) / BK;
   const bool three = !p.one_pass;
 
@@ -86,7 +111,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum_full, 1);
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 128);  // every epilogue thread arrives
+    }
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -109,47 +137,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer ----------------
       const uint32_t stage_tx = three ? (uint32_t)C::STAGE_BYTES
                                       : (uint32_t)(C::A_BYTES + C::B_BYTES);
-      int issued_until = 0;  // k-blocks whose loads were issued
+      int it = 0;  // k-blocks issued so far, across tiles
       bool ok = true;
-      for (int kb = 0; kb < nk && ok; kb++) {
-        const int s = kb % C::STAGES;
-        if (kb >= C::STAGES) {
-          ok = mbar_wait(&empty[s], ((kb / C::STAGES) - 1) & 1, p.err, kErrProducer | 1);
-          if (!ok) break;
-        }
-        uint8_t *sa = smem + s * C::STAGE_BYTES;
-        uint8_t *salo = sa + C::A_BYTES;
-        uint8_t *sb = salo + C::A_BYTES;
-        uint8_t *sblo = sb + C::B_BYTES;
-        const int k0 = kb * BK;
-        mbar_arrive_expect_tx(&full[s], stage_tx);
-        if (A_MN) {
-#pragma unroll
-          for (int j = 0; j < BM / 32; j++) {
-            tma_load_2d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, k0);
-            if (three) tma_load_2d(salo + j * 4096, &tmAlo, &full[s], m0 + 32 * j, k0);
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < nk; kb++, it++) {
+          const int s = it % C::STAGES;
+          if (it >= C::STAGES) {
+            ok = mbar_wait(&empty[s], ((it / C::STAGES) - 1) & 1, p.err, kErrProducer | 1);
+            if (!ok) break;
           }
-        } else {
-          tma_load_2d(sa, &tmA, &full[s], k0, m0);
-          if (three) tma_load_2d(salo, &tmAlo, &full[s], k0, m0);
-        }
-        if (B_MN) {
+          uint8_t *sa = smem + s * C::STAGE_BYTES;
+          uint8_t *salo = sa + C::A_BYTES;
+          uint8_t *sb = salo + C::A_BYTES;
+          uint8_t *sblo = sb + C::B_BYTES;
+          const int k0 = kb * BK;
+          mbar_arrive_expect_tx(&full[s], stage_tx);
+          if (A_MN) {
 #pragma unroll
-          for (int j = 0; j < BN / 32; j++) {
-            tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
-            if (three) tma_load_2d(sblo + j * 4096, &tmBlo, &full[s], n0 + 32 * j, k0);
+            for (int j = 0; j < BM / 32; j++) {
+              tma_load_2d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, k0);
+              if (three) tma_load_2d(salo + j * 4096, &tmAlo, &full[s], m0 + 32 * j, k0);
+            }
+          } else {
+            tma_load_2d(sa, &tmA, &full[s], k0, m0);
+            if (three) tma_load_2d(salo, &tmAlo, &full[s], k0, m0);
           }
-        } else {
-          tma_load_2d(sb, &tmB, &full[s], k0, n0);
-          if (three) tma_load_2d(sblo, &tmBlo, &full[s], k0, n0);
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 32; j++) {
+              tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
+              if (three) tma_load_2d(sblo + j * 4096, &tmBlo, &full[s], n0 + 32 * j, k0);
+            }
+          } else {
+            tma_load_2d(sb, &tmB, &full[s], k0, n0);
+            if (three) tma_load_2d(sblo, &tmBlo, &full[s], k0, n0);
+          }
         }
-        issued_until = kb + 1;
       }
       if (!ok) {
         // Let loads already in flight land before the CTA exits.
-        for (int kb = issued_until - C::STAGES < 0 ? 0 : issued_until - C::STAGES;
-             kb < issued_until; kb++)
-          mbar_wait(&full[kb % C::STAGES], (kb / C::STAGES) & 1, nullptr, 0);
+        for (int i = it - C::STAGES < 0 ? 0 : it - C::STAGES; i < it; i++)
+          mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1, nullptr, 0);
       }
     }
   } else if (warp == 1) {
@@ -169,50 +200,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t a_lay = A_MN ? kLayoutSw128Base32 : kLayoutSw128;
       constexpr uint32_t b_lay = B_MN ? kLayoutSw128Base32 : kLayoutSw128;
       bool ok = true;
-      for (int kb = 0; kb < nk; kb++) {
-        const int s = kb % C::STAGES;
-        ok = mbar_wait(&full[s], (kb / C::STAGES) & 1, p.err, kErrMma | 1);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
-        const uint32_t salo = sa + C::A_BYTES;
-        const uint32_t sb = salo + C::A_BYTES;
-        const uint32_t sblo = sb + C::B_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BK / UMMA_K; kk++) {
-          const uint64_t da = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_lay);
-          const uint64_t db = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_lay);
-          const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-          if (three) {
-            const uint64_t dalo = smem_desc(salo + kk * a_kstep, a_lbo, a_sbo, a_lay);
-            const uint64_t dblo = smem_desc(sblo + kk * b_kstep, b_lbo, b_sbo, b_lay);
-            // small terms first, then the main product
-            mma_tf32(tmem_base, dalo, db, idesc, acc);
-            mma_tf32(tmem_base, da, dblo, idesc, 1u);
-            mma_tf32(tmem_base, da, db, idesc, 1u);
-          } else {
-            mma_tf32(tmem_base, da, db, idesc, acc);
-          }
+      int it = 0, local = 0;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, local++) {
+        const int acc_buf = local & 1;
+        if (local >= 2) {
+          ok = mbar_wait(&tmem_empty[acc_buf], ((local >> 1) - 1) & 1, p.err, kErrMma | 2);
+          if (!ok) break;
         }
-        mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc_buf * BN);
+        for (int kb = 0; kb < nk; kb++, it++) {
+          const int s = it % C::STAGES;
+          ok = mbar_wait(&full[s], (it / C::STAGES) & 1, p.err, kErrMma | 1);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t salo = sa + C::A_BYTES;
+          const uint32_t sb = salo + C::A_BYTES;
+          const uint32_t sblo = sb + C::B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; kk++) {
+            const uint64_t da = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_lay);
+            const uint64_t db = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_lay);
+            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            if (three) {
+              const uint64_t dalo = smem_desc(salo + kk * a_kstep, a_lbo, a_sbo, a_lay);
+              const uint64_t dblo = smem_desc(sblo + kk * b_kstep, b_lbo, b_sbo, b_lay);
+              // small terms first, then the main product
+              mma_tf32(d_tmem, dalo, db, idesc, acc);
+              mma_tf32(d_tmem, da, dblo, idesc, 1u);
+              mma_tf32(d_tmem, da, db, idesc, 1u);
+            } else {
+              mma_tf32(d_tmem, da, db, idesc, acc);
+            }
+          }
+          mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+        }
+        if (ok) mma_commit(&tmem_full[acc_buf]);
       }
-      if (ok) mma_commit(accum_full);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = m0 + 32 * q + lane;
-    const bool ok = mbar_wait(accum_full, 0, p.err, kErrEpilogue | 1);
-    tc_fence_after();
-    if (ok) {
-      const bool vec = ((p.ldc & 3) == 0) && ((((uintptr_t)p.C) & 15) == 0) &&
-                       (!p.C_lo || (((uintptr_t)p.C_lo) & 15) == 0) &&
-                       (!p.mask || (((p.ldmask & 3) == 0) && (((uintptr_t)p.mask) & 15) == 0));
+    const bool vec = ((p.ldc & 3) == 0) && ((((uintptr_t)p.C) & 15) == 0) &&
+                     (!p.C_lo || (((uintptr_t)p.C_lo) & 15) == 0) &&
+                     (!p.mask || (((p.ldmask & 3) == 0) && (((uintptr_t)p.mask) & 15) == 0));
+    int local = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, local++) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int m0 = mb * BM, n0 = nb * BN;
+      const int acc_buf = local & 1;
+      const int row = m0 + 32 * q + lane;
+      if (!mbar_wait(&tmem_full[acc_buf], (local >> 1) & 1, p.err, kErrEpilogue | 1)) break;
+      tc_fence_after();
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         __syncwarp();
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc_buf * BN + c0),
+                           r);
         tmem_ld_wait();
         if (row >= p.M || n0 + c0 >= p.N) continue;
         float v[32];
@@ -256,6 +303,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      // every TMEM load of this buffer has completed (tcgen05.wait::ld above)
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[acc_buf]);
     }
   }
 
@@ -319,7 +369,10 @@ static int launch_t(const GemmPlan &pl, cudaStream_t st) {
                                      C::SMEM_BYTES));
     attr_done[dev] = true;
   }
-  dim3 grid((pl.p.N + BN - 1) / BN, (pl.p.M + BM - 1) / BM);
+  const int ntiles = ((pl.p.N + BN - 1) / BN) * ((pl.p.M + BM - 1) / BM);
+  DevCtx *ctx = ctx_current();
+  const int sms = (ctx && ctx->num_sms) ? ctx->num_sms : 148;
+  const int grid = ntiles < sms ? ntiles : sms;  // persistent: one CTA per SM
   kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(pl.a, pl.alo, pl.b, pl.blo, pl.p);
   FG_LAUNCH_TRY();
   return FG_OK;

@@ -138,14 +138,22 @@ __global__ void __launch_bounds__(256) k_reduce_rows(const T *__restrict__ x, T 
       const size_t nv = cols / 4;
       const V *pv = reinterpret_cast<const V *>(p);
       size_t j = lane;
-      for (; j + 32 < nv; j += 64) {
-        V u0 = __ldcs(pv + j), u1 = __ldcs(pv + j + 32);
-        const T *f0 = reinterpret_cast<const T *>(&u0);
-        const T *f1 = reinterpret_cast<const T *>(&u1);
-        acc0 = red_op<OP>(acc0, red_op<OP>(red_op<OP>(f0[0], f0[1]), red_op<OP>(f0[2], f0[3])));
-        acc1 = red_op<OP>(acc1, red_op<OP>(red_op<OP>(f1[0], f1[1]), red_op<OP>(f1[2], f1[3])));
+      // eight independent 16-byte loads in flight per lane
+      for (; j + 7 * 32 < nv; j += 8 * 32) {
+        V u[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) u[k] = __ldcs(pv + j + 32 * k);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          const T *f = reinterpret_cast<const T *>(&u[k]);
+          T g = red_op<OP>(red_op<OP>(f[0], f[1]), red_op<OP>(f[2], f[3]));
+          if (k & 1)
+            acc1 = red_op<OP>(acc1, g);
+          else
+            acc0 = red_op<OP>(acc0, g);
+        }
       }
-      if (j < nv) {
+      for (; j < nv; j += 32) {
         V u0 = __ldcs(pv + j);
         const T *f0 = reinterpret_cast<const T *>(&u0);
         acc0 = red_op<OP>(acc0, red_op<OP>(red_op<OP>(f0[0], f0[1]), red_op<OP>(f0[2], f0[3])));
@@ -208,6 +216,49 @@ __global__ void __launch_bounds__(256) k_reduce_cols_partial(const T *__restrict
   part[blockIdx.y * cols + col] = red_op<OP>(red_op<OP>(a0, a1), red_op<OP>(a2, a3));
 }
 
+// 16-byte variant: a thread owns 4 adjacent columns, 8 rows in flight.
+template <typename T, int OP>
+__global__ void __launch_bounds__(64) k_reduce_cols_partial_v4(const T *__restrict__ x,
+                                                               T *__restrict__ part, size_t rows,
+                                                               size_t cols,
+                                                               size_t rows_per_chunk) {
+  const size_t col = ((size_t)blockIdx.x * 64 + threadIdx.x) * 4;
+  const size_t r0 = (size_t)blockIdx.y * rows_per_chunk;
+  const size_t r1 = r0 + rows_per_chunk < rows ? r0 + rows_per_chunk : rows;
+  if (col >= cols) return;
+  T a[4], b[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) a[q] = b[q] = red_identity<T, OP>();
+  size_t r = r0;
+  for (; r + 8 <= r1; r += 8) {
+    uint4 u[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) u[k] = __ldcs(reinterpret_cast<const uint4 *>(x + (r + k) * cols + col));
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const T *f = reinterpret_cast<const T *>(&u[k]);
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        if (k & 1)
+          b[q] = red_op<OP>(b[q], f[q]);
+        else
+          a[q] = red_op<OP>(a[q], f[q]);
+      }
+    }
+  }
+  for (; r < r1; r++) {
+    uint4 u = __ldcs(reinterpret_cast<const uint4 *>(x + r * cols + col));
+    const T *f = reinterpret_cast<const T *>(&u);
+#pragma unroll
+    for (int q = 0; q < 4; q++) a[q] = red_op<OP>(a[q], f[q]);
+  }
+  uint4 o;
+  T *oe = reinterpret_cast<T *>(&o);
+#pragma unroll
+  for (int q = 0; q < 4; q++) oe[q] = red_op<OP>(a[q], b[q]);
+  *reinterpret_cast<uint4 *>(part + blockIdx.y * cols + col) = o;
+}
+
 template <typename T, int OP>
 __global__ void __launch_bounds__(256) k_reduce_cols_final(const T *__restrict__ part,
                                                            T *__restrict__ out, size_t nchunks,
@@ -249,7 +300,11 @@ static int launch_cols_t(const void *x, void *out, size_t rows, size_t cols, cud
                      scratch_bytes);
   }
   dim3 g1((unsigned)col_tiles, (unsigned)nchunks);
-  k_reduce_cols_partial<T, OP><<<g1, kColTile, 0, st>>>((const T *)x, (T *)scratch, rows, cols, rpc);
+  if (cols % 4 == 0 && aligned16(x) && aligned16(scratch))
+    k_reduce_cols_partial_v4<T, OP><<<g1, 64, 0, st>>>((const T *)x, (T *)scratch, rows, cols, rpc);
+  else
+    k_reduce_cols_partial<T, OP><<<g1, kColTile, 0, st>>>((const T *)x, (T *)scratch, rows, cols,
+                                                          rpc);
   FG_LAUNCH_TRY();
   k_reduce_cols_final<T, OP><<<(unsigned)((cols + 255) / 256), 256, 0, st>>>((const T *)scratch,
                                                                             (T *)out, nchunks, cols);
@@ -303,7 +358,11 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// NV float4 per lane held in registers: cols <= 128 * NV, cols % 4 == 0.
+// NV float4 of logits per lane held in registers: cols <= 128 * NV,
+// cols % 4 == 0.  Targets are not kept: their row sums (sum t, sum t*x) are
+// folded in as they arrive, and the gradient pass re-reads them, which hits
+// L1 (the row was read moments before with L1 caching).  That keeps the
+// kernel at ~60 registers, 4 blocks (32 warps) per SM.
 template <int NV>
 __global__ void __launch_bounds__(256) k_xent_rows_v4(const float *__restrict__ x,
                                                       const float *__restrict__ t,
@@ -317,33 +376,36 @@ __global__ void __launch_bounds__(256) k_xent_rows_v4(const float *__restrict__ 
   for (; row < rows; row += wstride) {
     const float4 *xv = reinterpret_cast<const float4 *>(x + row * (size_t)cols);
     const float4 *tv = reinterpret_cast<const float4 *>(t + row * (size_t)cols);
-    float4 xr[NV], tr[NV];
-    float m = -INFINITY;
+    float4 xr[NV];
+    float m = -INFINITY, st_ = 0.f, stx = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      int j = lane + 32 * i;
+      if (j < nv) xr[i] = __ldcs(xv + j);
+    }
 #pragma unroll
     for (int i = 0; i < NV; i++) {
       int j = lane + 32 * i;
       if (j < nv) {
-        xr[i] = __ldcs(xv + j);
-        tr[i] = __ldcs(tv + j);
+        const float4 tt = __ldg(tv + j);
         m = ref_max(m, ref_max(ref_max(xr[i].x, xr[i].y), ref_max(xr[i].z, xr[i].w)));
+        st_ += (tt.x + tt.y) + (tt.z + tt.w);
+        stx += __fmul_rn(tt.x, xr[i].x) + __fmul_rn(tt.y, xr[i].y) + __fmul_rn(tt.z, xr[i].z) +
+               __fmul_rn(tt.w, xr[i].w);
       }
     }
     m = warp_max(m);
-    float se = 0.f, st_ = 0.f, sts = 0.f, cnt = 0.f;
+    float se = 0.f, cnt = 0.f;
     uint32_t maxbits = 0;  // bit (4i+q) set where x == row max (mask of the max path)
 #pragma unroll
     for (int i = 0; i < NV; i++) {
       int j = lane + 32 * i;
       if (j < nv) {
         float *xe = reinterpret_cast<float *>(&xr[i]);
-        const float *te = reinterpret_cast<const float *>(&tr[i]);
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-          float s = __fsub_rn(xe[q], m);
-          float e = exp2f(__fmul_rn(s, kLog2e));
+          const float e = exp2f(__fmul_rn(__fsub_rn(xe[q], m), kLog2e));
           se += e;
-          st_ += te[q];
-          sts += __fmul_rn(te[q], s);
           if (!(xe[q] < m)) {
             cnt += 1.0f;
             maxbits |= 1u << (4 * i + q);
@@ -354,14 +416,13 @@ __global__ void __launch_bounds__(256) k_xent_rows_v4(const float *__restrict__ 
     }
     se = warp_sum(se);
     st_ = warp_sum(st_);
-    sts = warp_sum(sts);
+    stx = warp_sum(stx);
     cnt = warp_sum(cnt);
     const float lse = __fmul_rn(log2f(se), kLn2);
-    // nps = -(sum t*(s - lse)) = -(sum t*s) + lse * sum t
-    const float nps = -(sts - lse * st_);
+    // nps = -sum_c t*(s - lse), s = x - m: -(sum t*x - m*sum t) + lse*sum t
+    const float nps = -((stx - m * st_) - lse * st_);
     const float g_lp_scale = -inv_n * gscale;
-    const float g_nlse = g_lp_scale * st_;             // sum_c t * (-1/B)
-    const float g_lse = -g_nlse;
+    const float g_lse = -(g_lp_scale * st_);  // -(sum_c t * (-1/B))
     const float g_se = __fmul_rn(__fmul_rn(kLn2, g_lse), 1.0f / __fmul_rn(se, kLn2));
     // g_s = t*g_lp_scale + log2e*((e*ln2)*g_se); its row sum feeds the max path.
     float gsum = 0.f;
@@ -369,34 +430,33 @@ __global__ void __launch_bounds__(256) k_xent_rows_v4(const float *__restrict__ 
     for (int i = 0; i < NV; i++) {
       int j = lane + 32 * i;
       if (j < nv) {
+        const float4 tt = __ldg(tv + j);
+        const float *te = reinterpret_cast<const float *>(&tt);
         const float *e = reinterpret_cast<const float *>(&xr[i]);
-        const float *te = reinterpret_cast<const float *>(&tr[i]);
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-          float gs = __fadd_rn(__fmul_rn(te[q], g_lp_scale),
-                               __fmul_rn(kLog2e, __fmul_rn(__fmul_rn(e[q], kLn2), g_se)));
-          gsum += gs;
-        }
+        for (int q = 0; q < 4; q++)
+          gsum += __fadd_rn(__fmul_rn(te[q], g_lp_scale),
+                            __fmul_rn(kLog2e, __fmul_rn(__fmul_rn(e[q], kLn2), g_se)));
       }
     }
     gsum = warp_sum(gsum);
-    const float g_m = -gsum;
-    const float wmax = __fmul_rn(1.0f / cnt, g_m);
+    const float wmax = __fmul_rn(1.0f / cnt, -gsum);
     if (dx) {
       float4 *dv = reinterpret_cast<float4 *>(dx + row * (size_t)cols);
 #pragma unroll
       for (int i = 0; i < NV; i++) {
         int j = lane + 32 * i;
         if (j < nv) {
+          const float4 tt = __ldg(tv + j);
+          const float *te = reinterpret_cast<const float *>(&tt);
           const float *e = reinterpret_cast<const float *>(&xr[i]);
-          const float *te = reinterpret_cast<const float *>(&tr[i]);
           float4 o;
           float *oe = reinterpret_cast<float *>(&o);
 #pragma unroll
           for (int q = 0; q < 4; q++) {
-            float gs = __fadd_rn(__fmul_rn(te[q], g_lp_scale),
-                                 __fmul_rn(kLog2e, __fmul_rn(__fmul_rn(e[q], kLn2), g_se)));
-            float mask = ((maxbits >> (4 * i + q)) & 1u) ? 1.0f : 0.0f;
+            const float gs = __fadd_rn(__fmul_rn(te[q], g_lp_scale),
+                                       __fmul_rn(kLog2e, __fmul_rn(__fmul_rn(e[q], kLn2), g_se)));
+            const float mask = ((maxbits >> (4 * i + q)) & 1u) ? 1.0f : 0.0f;
             oe[q] = __fadd_rn(gs, __fmul_rn(mask, wmax));
           }
           __stcs(dv + j, o);
