@@ -155,7 +155,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t *sblo = sb + C::B_BYTES;
           const int k0 = kb * BK;
           mbar_arrive_expect_tx(&full[s], stage_tx);
-          if (A_MN) {
+          if (A_MN && p.a3d) {
+            tma_load_3d(sa, &tmA, &full[s], 0, k0, m0 / 32);
+            if (three) tma_load_3d(salo, &tmAlo, &full[s], 0, k0, m0 / 32);
+          } else if (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / 32; j++) {
               tma_load_2d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, k0);
@@ -165,7 +168,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sa, &tmA, &full[s], k0, m0);
             if (three) tma_load_2d(salo, &tmAlo, &full[s], k0, m0);
           }
-          if (B_MN) {
+          if (B_MN && p.b3d) {
+            tma_load_3d(sb, &tmB, &full[s], 0, k0, n0 / 32);
+            if (three) tma_load_3d(sblo, &tmBlo, &full[s], 0, k0, n0 / 32);
+          } else if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 32; j++) {
               tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
@@ -357,6 +363,24 @@ static int make_map(CUtensorMap *map, const float *ptr, int inner, int outer, in
   return FG_OK;
 }
 
+// MN-major operand [K, mn] (pitch ld) viewed as 3-D {32, K, mn/32} with the
+// 32-element chunks 128 bytes apart, so one box {32, 32, rows/32} lands in
+// shared memory as rows/32 chunks of 32 K-rows x 128 bytes -- the same layout
+// the per-chunk 2-D loads produce.  Only valid when mn % 32 == 0 (the last
+// chunk then ends exactly at the end of the row).
+static int make_map_mn3d(CUtensorMap *map, const float *ptr, int mn, int K, int ld, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(FG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {32, (cuuint64_t)K, (cuuint64_t)(mn / 32)};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, 128};
+  cuuint32_t box[3] = {32, 32, (cuuint32_t)(box_rows / 32)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)ptr, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FG_OK : FG_ERR_UNSUPPORTED;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 static int launch_t(const GemmPlan &pl, cudaStream_t st) {
   using C = Cfg<BN>;
@@ -415,6 +439,28 @@ int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, c
     if ((rc = make_map(&pl->b, b, K, N, ldb, bn, false))) return rc;
     if ((rc = make_map(&pl->blo, one ? b : b_lo, K, N, ldb, bn, false))) return rc;
   }
+  // single 3-D boxes for MN-major operands whose extent is a multiple of 32
+  pl->p.a3d = 0;
+  pl->p.b3d = 0;
+  if (a_mn && M % 32 == 0) {
+    CUtensorMap t0, t1;
+    if (make_map_mn3d(&t0, a, M, K, lda, BM) == FG_OK &&
+        make_map_mn3d(&t1, one ? a : a_lo, M, K, lda, BM) == FG_OK) {
+      pl->a = t0;
+      pl->alo = t1;
+      pl->p.a3d = 1;
+    }
+  }
+  if (b_mn && N % 32 == 0) {
+    CUtensorMap t0, t1;
+    if (make_map_mn3d(&t0, b, N, K, ldb, bn) == FG_OK &&
+        make_map_mn3d(&t1, one ? b : b_lo, N, K, ldb, bn) == FG_OK) {
+      pl->b = t0;
+      pl->blo = t1;
+      pl->p.b3d = 1;
+    }
+  }
+  fg::clear_error();
   DevCtx *ctx = ctx_current();
   if (!ctx) return set_error(FG_ERR_CUDA, "no CUDA device context");
   GemmParams &p = pl->p;

@@ -16,6 +16,7 @@ struct GemmParams {
   int ldmask;
   int epilogue;
   int one_pass;
+  int a3d, b3d;  // MN-major operand loaded as one 3-D box (MN % 32 == 0)
   unsigned int *err;
 };
 
