@@ -169,11 +169,13 @@ __global__ void __launch_bounds__(256) k_reduce_rows(const T *__restrict__ x, T 
 template <typename T, int OP>
 static int launch_rows_t(const void *x, void *out, size_t rows, size_t cols, cudaStream_t st) {
   const bool vec = (cols % 4 == 0) && aligned16(x);
-  int grid = grid_for(rows * 32, 256, 16);
+  // 4 warps per block: blocks are the unit the scheduler balances across
+  // SMs, and small blocks keep the per-SM row count within ~1% of the mean.
+  int grid = grid_for(rows * 32, 128, 64);
   if (vec)
-    k_reduce_rows<T, OP, true><<<grid, 256, 0, st>>>((const T *)x, (T *)out, rows, cols);
+    k_reduce_rows<T, OP, true><<<grid, 128, 0, st>>>((const T *)x, (T *)out, rows, cols);
   else
-    k_reduce_rows<T, OP, false><<<grid, 256, 0, st>>>((const T *)x, (T *)out, rows, cols);
+    k_reduce_rows<T, OP, false><<<grid, 128, 0, st>>>((const T *)x, (T *)out, rows, cols);
   FG_LAUNCH_TRY();
   return FG_OK;
 }
@@ -541,8 +543,21 @@ int launch_xent(const float *x, const float *t, size_t rows, size_t cols, float 
   }
   const float inv_n = 1.0f / (float)rows;
   const int c = (int)cols;
-  int grid = grid_for(rows * 32, 256, 16);
   const bool vec = (cols % 4 == 0) && aligned16(x) && aligned16(t) && (!dx || aligned16(dx));
+  // One resident wave: blocks per SM from the kernel's occupancy, so every
+  // warp strides over (almost) the same number of rows.
+  int per_sm = 4;
+  {
+    const void *kern = (vec && cols <= 128)    ? (const void *)k_xent_rows_v4<1>
+                       : (vec && cols <= 256)  ? (const void *)k_xent_rows_v4<2>
+                       : (vec && cols <= 512)  ? (const void *)k_xent_rows_v4<4>
+                       : (vec && cols <= 1024) ? (const void *)k_xent_rows_v4<8>
+                                               : (const void *)k_xent_rows_generic;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, 0) == cudaSuccess && occ > 0)
+      per_sm = occ;
+  }
+  int grid = grid_for(rows * 32, 256, per_sm);
   if (vec && cols <= 128)
     k_xent_rows_v4<1><<<grid, 256, 0, st>>>(x, t, dx, scratch, rows, c, inv_n, gscale);
   else if (vec && cols <= 256)
