@@ -261,6 +261,7 @@ def our_arm(args):
     clocks = sampler.stop() if sampler else None
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     gemms = tr.gemm_times()
+    comms = tr.comm_times() if comm is not None else []
 
     # ---- end to end through the C ABI with host buffers --------------------
     barrier()
@@ -306,6 +307,8 @@ def our_arm(args):
             "roofline": roofline,
             "e2e": {"value": 1.0 / e2e_s, "unit": "steps/s",
                     "h2d_bytes_per_step": int(x.nbytes + t.nbytes), "d2h_bytes_per_step": 4},
+            "gemm_ms_last_step": [round(g[0], 4) for g in gemms],
+            "allreduce_ms_mb_last_step": [[round(c[0], 4), round(c[1] / 2**20, 2)] for c in comms],
             "gpu_launches": launches0 * args.steps,
             "launches_per_step": launches0,
             "clocks": clocks,

@@ -85,6 +85,8 @@ SIGNATURES = [
     ("fg_mlp_enable_gemm_timing", _i, [_vp, _i]),
     ("fg_mlp_gemm_times", _i, [_vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double),
                                _i, ctypes.POINTER(_i)]),
+    ("fg_mlp_comm_times", _i, [_vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double),
+                               _i, ctypes.POINTER(_i)]),
     ("fg_comm_unique_id", _i, [ctypes.c_char_p]),
     ("fg_comm_init", _i, [_i, _i, ctypes.c_char_p, _i, _pp]),
     ("fg_comm_destroy", _i, [_vp]),

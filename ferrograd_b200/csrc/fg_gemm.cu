@@ -396,7 +396,9 @@ static int launch_t(const GemmPlan &pl, cudaStream_t st) {
   const int ntiles = ((pl.p.N + BN - 1) / BN) * ((pl.p.M + BM - 1) / BM);
   DevCtx *ctx = ctx_current();
   const int sms = (ctx && ctx->num_sms) ? ctx->num_sms : 148;
-  const int grid = ntiles < sms ? ntiles : sms;  // persistent: one CTA per SM
+  int cap = sms;  // persistent: one CTA per SM
+  if (pl.max_ctas > 0 && pl.max_ctas < cap) cap = pl.max_ctas;
+  const int grid = ntiles < cap ? ntiles : cap;
   kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(pl.a, pl.alo, pl.b, pl.blo, pl.p);
   FG_LAUNCH_TRY();
   return FG_OK;
@@ -479,6 +481,7 @@ int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, c
   pl->bn = bn;
   pl->a_mn = a_mn;
   pl->b_mn = b_mn;
+  pl->max_ctas = 0;
   return FG_OK;
 }
 

@@ -26,6 +26,7 @@ struct GemmPlan {
   GemmParams p;
   int bn;
   bool a_mn, b_mn;
+  int max_ctas;  // persistent grid cap (0: one CTA per SM); leaves SMs to a concurrent collective
 };
 
 int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, const float *b,

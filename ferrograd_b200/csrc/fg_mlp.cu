@@ -16,6 +16,7 @@
 // averaged over ranks by NCCL on a second stream as soon as the layer's
 // backward finishes, overlapping the remaining backward GEMMs.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 
 #include <vector>
 
@@ -275,6 +276,11 @@ struct Layer {
   float *dW = nullptr, *db = nullptr;  // inside the flat gradient buffer
   size_t bucket_off = 0, bucket_len = 0;  // this layer's all-reduce bucket (floats)
   fg::gemm::GemmPlan fwd, bwd_w, bwd_x;
+  // dW as two launches over the halves of its output rows, so that with a
+  // communicator the first half's all-reduce overlaps the second half's GEMM
+  // (used for layer 0, whose bucket is the last one of the backward pass)
+  bool can_split_w = false;
+  fg::gemm::GemmPlan bwd_w_half[2];
 };
 
 size_t pad64(size_t n) { return (n + 63) / 64 * 64; }
@@ -298,7 +304,8 @@ struct fg_mlp {
   size_t scratch_bytes = 0;
   std::vector<void *> allocations;
   fg_comm *comm = nullptr;
-  std::vector<cudaEvent_t> ev_bucket;
+  std::vector<cudaEvent_t> ev_bucket, ev_wread;
+  cudaEvent_t ev_half = nullptr;
   cudaEvent_t ev_comm_done = nullptr;
   bool use_graph = false;
   cudaGraphExec_t graph = nullptr;
@@ -306,6 +313,9 @@ struct fg_mlp {
   std::vector<cudaEvent_t> ev_t0, ev_t1;  // one pair per GEMM launch of a step
   std::vector<double> gemm_flops;
   int gemm_launches = 0;
+  std::vector<cudaEvent_t> ev_c0, ev_c1;  // one pair per all-reduce of a step
+  std::vector<double> comm_bytes;
+  int comm_launches = 0;
   int launches_per_step = 0;
   int sms = 148;
 };
@@ -339,6 +349,17 @@ int build_plans(fg_mlp *m) {
                              nullptr, ly.in, FG_GEMM_A_MN_MAJOR | FG_GEMM_B_MN_MAJOR, FG_EPI_NONE,
                              nullptr, nullptr, 0, &ly.bwd_w);
     if (rc) return rc;
+    if (l == 0 && ly.out % 64 == 0) {
+      const int half = ly.out / 2;
+      for (int h = 0; h < 2; h++) {
+        rc = fg::gemm::make_plan(half, ly.in, B, m->G[l] + h * half, m->G_lo[l] + h * half, ly.out,
+                                 in, in_lo, ly.in, ly.dW + (size_t)h * half * ly.in, nullptr, ly.in,
+                                 FG_GEMM_A_MN_MAJOR | FG_GEMM_B_MN_MAJOR, FG_EPI_NONE, nullptr,
+                                 nullptr, 0, &ly.bwd_w_half[h]);
+        if (rc) return rc;
+      }
+      ly.can_split_w = true;
+    }
     if (l > 0) {
       // Gprev[m,k] = (act[m,k] > 0) ? sum_n G[m,n] W[n,k] : 0:
       // A = G [B, out] K-major, B = W stored [out, in] = [K, N] (MN-major).
@@ -375,12 +396,54 @@ int run_gemm(fg_mlp *m, const fg::gemm::GemmPlan &pl, cudaStream_t st) {
   return FG_OK;
 }
 
+// SMs the overlapped backward GEMMs leave free for the collective
+// (FG_COMM_SM_RESERVE, default 16).
+int comm_sm_reserve() {
+  const char *e = getenv("FG_COMM_SM_RESERVE");
+  int v = e ? atoi(e) : 16;
+  return v < 0 ? 0 : (v > 64 ? 64 : v);
+}
+
+// Sgd::step for layer l's weight and bias on `st`.
+int sgd_layer(fg_mlp *m, int l, cudaStream_t st) {
+  Layer &ly = m->L[l];
+  fg::SgdSegments segs{};
+  segs.count = 2;
+  segs.p[0] = ly.W;
+  segs.g[0] = ly.dW;
+  segs.lo[0] = ly.tc ? ly.W_lo : nullptr;
+  segs.n[0] = (size_t)ly.out * ly.in;
+  segs.p[1] = ly.b;
+  segs.g[1] = ly.db;
+  segs.lo[1] = nullptr;
+  segs.n[1] = (size_t)ly.out;
+  return fg::launch_sgd_multi(segs, m->lr, st);
+}
+
+// Average [off, off+len) of the gradient buffer across ranks on the comm
+// stream once everything enqueued on st so far has run.
+int bucket_allreduce(fg_mlp *m, cudaEvent_t ev, size_t off, size_t len) {
+  FG_CUDA_TRY(cudaEventRecord(ev, m->st));
+  FG_CUDA_TRY(cudaStreamWaitEvent(m->comm_st, ev, 0));
+  const int i = m->comm_launches++;
+  const bool t = m->timing && i < (int)m->ev_c0.size();
+  int rc;
+  if (t && (rc = record(m->ev_c0[i], m->comm_st))) return rc;
+  if ((rc = fg::comm_allreduce_mean(m->comm, m->grad + off, len, m->comm_st))) return rc;
+  if (t) {
+    m->comm_bytes[i] = (double)len * sizeof(float);
+    if ((rc = record(m->ev_c1[i], m->comm_st))) return rc;
+  }
+  return FG_OK;
+}
+
 // Enqueue one training step on m->st (and m->comm_st).
 int enqueue_step(fg_mlp *m) {
   cudaStream_t st = m->st;
   const int B = m->B;
   int rc;
   m->gemm_launches = 0;
+  m->comm_launches = 0;
   // forward
   if (m->L[0].tc && (rc = fg::launch_split_lo(m->x, m->x_lo, (size_t)B * m->dims[0], st))) return rc;
   for (int l = 0; l < m->nl; l++) {
@@ -401,14 +464,31 @@ int enqueue_step(fg_mlp *m) {
   if (m->L[m->nl - 1].tc &&
       (rc = fg::launch_split_lo(m->G[m->nl - 1], m->G_lo[m->nl - 1], (size_t)B * C, st)))
     return rc;
-  // backward, last layer first; each layer's bucket is averaged across ranks
-  // on the comm stream while the next layer's backward runs.
+  // backward, last layer first.  With a communicator each layer's bucket
+  // [dW | db] is averaged across ranks on the comm stream as soon as it is
+  // complete -- before this layer's dX GEMM, which does not contribute to it
+  // -- and the layer's SGD follows on the comm stream once the dX GEMM (the
+  // last reader of W) has run, overlapping the layers below.
   for (int l = m->nl - 1; l >= 0; l--) {
     Layer &ly = m->L[l];
     const float *in = (l == 0) ? m->x : m->act[l - 1];
-    if (ly.tc) {
+    const bool split = m->comm && ly.tc && ly.can_split_w;
+    const size_t half_elems = (size_t)(ly.out / 2) * ly.in;
+    if (split) {
+      // first half of dW's rows: average and apply it while the second half
+      // is computed (layer 0 has no dX GEMM, nothing reads W afterwards)
+      if ((rc = run_gemm(m, ly.bwd_w_half[0], st))) return rc;
+      if ((rc = bucket_allreduce(m, m->ev_half, ly.bucket_off, half_elems))) return rc;
+      fg::SgdSegments segs{};
+      segs.count = 1;
+      segs.p[0] = ly.W;
+      segs.g[0] = ly.dW;
+      segs.lo[0] = ly.W_lo;
+      segs.n[0] = half_elems;
+      if ((rc = fg::launch_sgd_multi(segs, m->lr, m->comm_st))) return rc;
+      if ((rc = run_gemm(m, ly.bwd_w_half[1], st))) return rc;
+    } else if (ly.tc) {
       if ((rc = run_gemm(m, ly.bwd_w, st))) return rc;
-      if (l > 0 && (rc = run_gemm(m, ly.bwd_x, st))) return rc;
     } else {
       if ((rc = fg::launch_skinny_bwd(ly.out, m->G[l], in, ly.W, m->scratch, ly.dW,
                                       l > 0 ? m->G[l - 1] : nullptr,
@@ -419,17 +499,37 @@ int enqueue_step(fg_mlp *m) {
     if ((rc = fg::launch_reduce_cols(FG_F32, FG_REDUCE_SUM, m->G[l], ly.db, (size_t)B,
                                      (size_t)ly.out, st, m->scratch, m->scratch_bytes)))
       return rc;
+    const size_t done = split ? half_elems : 0;
+    if (m->comm &&
+        (rc = bucket_allreduce(m, m->ev_bucket[l], ly.bucket_off + done, ly.bucket_len - done)))
+      return rc;
+    if (ly.tc && l > 0 && (rc = run_gemm(m, ly.bwd_x, st))) return rc;
     if (m->comm) {
-      FG_CUDA_TRY(cudaEventRecord(m->ev_bucket[l], st));
-      FG_CUDA_TRY(cudaStreamWaitEvent(m->comm_st, m->ev_bucket[l], 0));
-      if ((rc = fg::comm_allreduce_mean(m->comm, m->grad + ly.bucket_off, ly.bucket_len,
-                                        m->comm_st)))
+      if (ly.tc && l > 0) {  // SGD must not overtake the dX GEMM reading W
+        FG_CUDA_TRY(cudaEventRecord(m->ev_wread[l], st));
+        FG_CUDA_TRY(cudaStreamWaitEvent(m->comm_st, m->ev_wread[l], 0));
+      }
+      if (split) {
+        fg::SgdSegments segs{};
+        segs.count = 2;
+        segs.p[0] = ly.W + half_elems;
+        segs.g[0] = ly.dW + half_elems;
+        segs.lo[0] = ly.W_lo + half_elems;
+        segs.n[0] = (size_t)ly.out * ly.in - half_elems;
+        segs.p[1] = ly.b;
+        segs.g[1] = ly.db;
+        segs.lo[1] = nullptr;
+        segs.n[1] = (size_t)ly.out;
+        if ((rc = fg::launch_sgd_multi(segs, m->lr, m->comm_st))) return rc;
+      } else if ((rc = sgd_layer(m, l, m->comm_st))) {
         return rc;
+      }
     }
   }
   if (m->comm) {
     FG_CUDA_TRY(cudaEventRecord(m->ev_comm_done, m->comm_st));
     FG_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_comm_done, 0));
+    return FG_OK;
   }
   // Sgd::step over every parameter (weights of tensor-core layers also get
   // their TF32 residual for the next step's GEMMs).
@@ -559,8 +659,12 @@ int fg_mlp_destroy(fg_mlp *m) {
   if (m->graph) cudaGraphExecDestroy(m->graph);
   for (auto e : m->ev_t0) cudaEventDestroy(e);
   for (auto e : m->ev_t1) cudaEventDestroy(e);
+  for (auto e : m->ev_c0) cudaEventDestroy(e);
+  for (auto e : m->ev_c1) cudaEventDestroy(e);
   for (auto e : m->ev_bucket) cudaEventDestroy(e);
+  for (auto e : m->ev_wread) cudaEventDestroy(e);
   if (m->ev_comm_done) cudaEventDestroy(m->ev_comm_done);
+  if (m->ev_half) cudaEventDestroy(m->ev_half);
   if (m->comm_st) cudaStreamDestroy(m->comm_st);
   for (void *p : m->allocations) cudaFree(p);
   delete m;
@@ -619,11 +723,26 @@ int fg_mlp_attach_comm(fg_mlp *m, fg_comm *comm) {
     m->graph = nullptr;
   }
   m->comm = comm;
+  // The backward GEMMs that run while gradient all-reduces are in flight
+  // leave SMs to the collective's kernels; a persistent grid over every SM
+  // would keep them from starting until the GEMM ends.
+  const int reserve = comm ? comm_sm_reserve() : 0;
+  for (int l = 0; l < m->nl; l++) {
+    Layer &ly = m->L[l];
+    const int cap = reserve ? m->sms - reserve : 0;
+    if (l < m->nl - 1) ly.bwd_x.max_ctas = cap;
+    ly.bwd_w.max_ctas = (l < m->nl - 1) ? cap : 0;
+    ly.bwd_w_half[0].max_ctas = cap;
+    ly.bwd_w_half[1].max_ctas = cap;
+  }
   if (comm && !m->comm_st) {
     FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->comm_st, cudaStreamNonBlocking));
     m->ev_bucket.resize(m->nl);
     for (auto &e : m->ev_bucket) FG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    m->ev_wread.resize(m->nl);
+    for (auto &e : m->ev_wread) FG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_comm_done, cudaEventDisableTiming));
+    FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_half, cudaEventDisableTiming));
   }
   return FG_OK;
 }
@@ -735,6 +854,14 @@ int fg_mlp_enable_gemm_timing(fg_mlp *m, int enable) {
       FG_CUDA_TRY(cudaEventCreate(&m->ev_t0[i]));
       FG_CUDA_TRY(cudaEventCreate(&m->ev_t1[i]));
     }
+    const int nc = m->nl + 1;
+    m->ev_c0.resize(nc);
+    m->ev_c1.resize(nc);
+    m->comm_bytes.assign(nc, 0.0);
+    for (int i = 0; i < nc; i++) {
+      FG_CUDA_TRY(cudaEventCreate(&m->ev_c0[i]));
+      FG_CUDA_TRY(cudaEventCreate(&m->ev_c1[i]));
+    }
   }
   return FG_OK;
 }
@@ -749,6 +876,21 @@ int fg_mlp_gemm_times(fg_mlp *m, float *ms, double *flops, int capacity, int *co
   for (int i = 0; i < n; i++) {
     FG_CUDA_TRY(cudaEventElapsedTime(&ms[i], m->ev_t0[i], m->ev_t1[i]));
     flops[i] = m->gemm_flops[i];
+  }
+  *count = n;
+  return FG_OK;
+}
+
+int fg_mlp_comm_times(fg_mlp *m, float *ms, double *bytes, int capacity, int *count) {
+  FG_REQUIRE(m && count && (capacity == 0 || (ms && bytes)), "fg_mlp_comm_times: null argument");
+  FG_REQUIRE(m->timing, "fg_mlp_comm_times: timing is not enabled");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+  int n = m->comm_launches < (int)m->ev_c0.size() ? m->comm_launches : (int)m->ev_c0.size();
+  if (n > capacity) n = capacity;
+  for (int i = 0; i < n; i++) {
+    FG_CUDA_TRY(cudaEventElapsedTime(&ms[i], m->ev_c0[i], m->ev_c1[i]));
+    bytes[i] = m->comm_bytes[i];
   }
   *count = n;
   return FG_OK;

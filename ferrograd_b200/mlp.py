@@ -176,6 +176,15 @@ class MlpTrainer:
         call("fg_mlp_gemm_times", self._h, ms, fl, cap, ctypes.byref(n))
         return [(ms[i], fl[i]) for i in range(n.value)]
 
+    def comm_times(self):
+        """[(ms, bytes)] of the gradient all-reduces of the latest step."""
+        cap = self.n_layers + 1
+        ms = (ctypes.c_float * cap)()
+        by = (ctypes.c_double * cap)()
+        n = ctypes.c_int()
+        call("fg_mlp_comm_times", self._h, ms, by, cap, ctypes.byref(n))
+        return [(ms[i], by[i]) for i in range(n.value)]
+
     @property
     def launches_per_step(self) -> int:
         n = ctypes.c_int()

@@ -211,6 +211,10 @@ int fg_mlp_launch_count(fg_mlp *mlp, int *count);
  * capacity is the length of both arrays, *count the number written. */
 int fg_mlp_enable_gemm_timing(fg_mlp *mlp, int enable);
 int fg_mlp_gemm_times(fg_mlp *mlp, float *ms, double *flops, int capacity, int *count);
+/* With GEMM timing enabled and a communicator attached: duration (ms, from
+ * enqueue on the comm stream to completion) and size of each gradient
+ * all-reduce of the most recent step. */
+int fg_mlp_comm_times(fg_mlp *mlp, float *ms, double *bytes, int capacity, int *count);
 
 /* ---- Data-parallel communicator (no reference counterpart: the reference
  * is single-device, src/device.rs:37-41) ----------------------------------- */
