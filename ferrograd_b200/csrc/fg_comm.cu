@@ -102,6 +102,14 @@ int comm_allreduce_mean(fg_comm *c, float *buf, size_t count, cudaStream_t st) {
   return nccl_settle(c, r, "ncclAllReduce");
 }
 
+// Plain sum (callers pre-scale by 1/nranks): unlike ncclAvg it is eligible
+// for NVLS, the in-switch reduction over NVSwitch multicast.
+int comm_allreduce_sum(fg_comm *c, float *buf, size_t count, cudaStream_t st) {
+  if (!count) return FG_OK;
+  ncclResult_t r = nccl()->allReduce(buf, buf, count, ncclFloat32, ncclSum, c->comm, st);
+  return nccl_settle(c, r, "ncclAllReduce");
+}
+
 int comm_nranks(const fg_comm *c) { return c ? c->nranks : 1; }
 
 }  // namespace fg

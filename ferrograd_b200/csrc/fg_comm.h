@@ -7,5 +7,6 @@
 
 namespace fg {
 int comm_allreduce_mean(fg_comm *c, float *buf, size_t count, cudaStream_t st);
+int comm_allreduce_sum(fg_comm *c, float *buf, size_t count, cudaStream_t st);
 int comm_nranks(const fg_comm *c);
 }  // namespace fg

@@ -517,7 +517,8 @@ __global__ void __launch_bounds__(256) k_xent_rows_generic(const float *__restri
 // combined by a fixed tree), times 1/B.
 __global__ void __launch_bounds__(1024) k_xent_loss_final(const float *__restrict__ row_loss,
                                                           size_t rows, float inv_n,
-                                                          float *__restrict__ loss) {
+                                                          float *__restrict__ loss,
+                                                          float loss_scale) {
   __shared__ float sh[32];
   float acc = 0.f;
   for (size_t r = threadIdx.x; r < rows; r += blockDim.x) acc += row_loss[r];
@@ -527,12 +528,12 @@ __global__ void __launch_bounds__(1024) k_xent_loss_final(const float *__restric
   if (threadIdx.x < 32) {
     float v = (threadIdx.x < (blockDim.x >> 5)) ? sh[threadIdx.x] : 0.f;
     v = warp_sum(v);
-    if (threadIdx.x == 0) loss[0] = __fmul_rn(v, inv_n);
+    if (threadIdx.x == 0) loss[0] = __fmul_rn(__fmul_rn(v, inv_n), loss_scale);
   }
 }
 
 int launch_xent(const float *x, const float *t, size_t rows, size_t cols, float *loss, float *dx,
-                float gscale, cudaStream_t st, float *row_scratch) {
+                float gscale, cudaStream_t st, float *row_scratch, float loss_scale) {
   if (rows == 0 || cols == 0) return set_error(FG_ERR_INVALID, "cross_entropy: empty logits");
   if (cols > (size_t)INT32_MAX) return set_error(FG_ERR_UNSUPPORTED, "cross_entropy: cols too large");
   float *scratch = row_scratch;
@@ -569,7 +570,7 @@ int launch_xent(const float *x, const float *t, size_t rows, size_t cols, float 
   else
     k_xent_rows_generic<<<grid, 256, 0, st>>>(x, t, dx, scratch, rows, c, inv_n, gscale);
   FG_LAUNCH_TRY();
-  k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, rows, inv_n, loss);
+  k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, rows, inv_n, loss, loss_scale);
   FG_LAUNCH_TRY();
   return FG_OK;
 }
@@ -682,7 +683,7 @@ int fg_xent_fwd_bwd(const float *d_logits, const float *d_targets, size_t rows, 
                     float *d_loss, float *d_dx, float grad_scale, void *stream) {
   FG_REQUIRE(d_logits && d_targets && d_loss, "fg_xent_fwd_bwd: null pointer");
   return fg::launch_xent(d_logits, d_targets, rows, cols, d_loss, d_dx, grad_scale,
-                         (cudaStream_t)stream, nullptr);
+                         (cudaStream_t)stream, nullptr, 1.0f);
 }
 
 }  // extern "C"
@@ -780,7 +781,7 @@ int fg_xent_fwd_bwd_noalloc(const float *d_logits, const float *d_targets, size_
   else
     fg::k_xent_rows_generic<<<grid, 256, 0, st>>>(d_logits, d_targets, d_dx, scratch, rows, c, inv_n, grad_scale);
   FG_LAUNCH_TRY();
-  fg::k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, rows, inv_n, d_loss);
+  fg::k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, rows, inv_n, d_loss, 1.0f);
   FG_LAUNCH_TRY();
   return FG_OK;
 }

@@ -29,8 +29,9 @@ int launch_reduce_cols(int dtype, int op, const void *x, void *out, size_t rows,
                        cudaStream_t st, void *scratch, size_t scratch_bytes);
 size_t reduce_cols_scratch_bytes(size_t rows, size_t cols);
 // row_scratch == nullptr: use the per-device workspace (rows floats).
+// loss = loss_scale * mean over the rows; dx scaled by gscale.
 int launch_xent(const float *x, const float *t, size_t rows, size_t cols, float *loss, float *dx,
-                float gscale, cudaStream_t st, float *row_scratch);
+                float gscale, cudaStream_t st, float *row_scratch, float loss_scale = 1.0f);
 int launch_sgd_multi(const SgdSegments &segs, float lr, cudaStream_t st);
 int launch_split_lo(const float *x, float *lo, size_t n, cudaStream_t st);
 

@@ -397,10 +397,11 @@ int run_gemm(fg_mlp *m, const fg::gemm::GemmPlan &pl, cudaStream_t st) {
 }
 
 // SMs the overlapped backward GEMMs leave free for the collective
-// (FG_COMM_SM_RESERVE, default 16).
+// (FG_COMM_SM_RESERVE, default 0: on this box reserving SMs slowed the
+// GEMMs more than it sped up the all-reduce).
 int comm_sm_reserve() {
   const char *e = getenv("FG_COMM_SM_RESERVE");
-  int v = e ? atoi(e) : 16;
+  int v = e ? atoi(e) : 0;
   return v < 0 ? 0 : (v > 64 ? 64 : v);
 }
 
@@ -429,7 +430,7 @@ int bucket_allreduce(fg_mlp *m, cudaEvent_t ev, size_t off, size_t len) {
   const bool t = m->timing && i < (int)m->ev_c0.size();
   int rc;
   if (t && (rc = record(m->ev_c0[i], m->comm_st))) return rc;
-  if ((rc = fg::comm_allreduce_mean(m->comm, m->grad + off, len, m->comm_st))) return rc;
+  if ((rc = fg::comm_allreduce_sum(m->comm, m->grad + off, len, m->comm_st))) return rc;
   if (t) {
     m->comm_bytes[i] = (double)len * sizeof(float);
     if ((rc = record(m->ev_c1[i], m->comm_st))) return rc;
@@ -458,8 +459,11 @@ int enqueue_step(fg_mlp *m) {
   }
   // cross_entropy forward + backward
   const int C = m->dims[m->nl];
+  // With N ranks the local loss and its gradient are pre-scaled by 1/N so
+  // that a plain sum across ranks (NVLS-eligible) yields the global mean.
+  const float rank_scale = 1.0f / (float)fg::comm_nranks(m->comm);
   if ((rc = fg::launch_xent(m->act[m->nl - 1], m->t, (size_t)B, (size_t)C, m->loss, m->G[m->nl - 1],
-                            1.0f, st, m->scratch)))
+                            rank_scale, st, m->scratch, rank_scale)))
     return rc;
   if (m->L[m->nl - 1].tc &&
       (rc = fg::launch_split_lo(m->G[m->nl - 1], m->G_lo[m->nl - 1], (size_t)B * C, st)))
