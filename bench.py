@@ -59,7 +59,7 @@ def load_peaks():
 
 def gemm_traffic_per_flop():
     """DRAM bytes per algorithmic flop of the GEMM, from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "gemm3x_tf32_ncu.md")
+    path = os.path.join(ROOT, "profiles", "gemm3x_c5_shapes_ncu.md")
     try:
         text = open(path).read()
     except OSError:
@@ -284,7 +284,7 @@ def our_arm(args):
         "bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s",
         "frac": (achieved / peak_3x) if achieved else None,
         "traffic": (tpf * per_launch_flops) if tpf else None,
-        "kernel": "k_gemm3x (3xTF32 tcgen05, 128x128 tiles)",
+        "kernel": "k_gemm3x (3xTF32 tcgen05, persistent, 128x256 tiles)",
         "achieved_basis": (f"2*M*N*K algorithmic flops / CUDA-event duration, averaged over the "
                            f"{len(gemms)} GEMM launches of the last timed step ({per_launch_flops:.3e} "
                            f"flop each)"),
