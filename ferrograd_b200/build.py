@@ -8,6 +8,7 @@ from __future__ import annotations
 import os
 import subprocess
 import sys
+import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
@@ -32,6 +33,13 @@ def _stale(obj: str, deps: list[str]) -> bool:
 
 
 def build(verbose: bool = False) -> str:
+    """Build the CUDA library, then the front end on top of it."""
+    lib = build_cuda(verbose)
+    build_front(verbose)
+    return lib
+
+
+def build_cuda(verbose: bool = False) -> str:
     os.makedirs(OBJDIR, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     headers.append(os.path.join(ROOT, "include", "ferro_cuda.h"))
@@ -51,6 +59,54 @@ def build(verbose: bool = False) -> str:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
     return LIB
+
+
+FRONT = os.path.join(CSRC, "front")
+FRONT_SOURCES = ["graph.cpp", "render.cpp", "exec.cpp", "tensor.cpp"]
+FRONT_LIB = os.path.join(HERE, "libferro_front.so")
+CXX = os.environ.get("CXX_FRONT", "g++")
+CXXFLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter",
+            f"-I{os.path.join(ROOT, 'include')}"]
+
+
+def _front_module_path() -> str:
+    return os.path.join(HERE, "_front" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_front(verbose: bool = False) -> str:
+    """Build ``libferro_front.so`` (the C++ lazy-graph front end, linked to
+    ``libferro_cuda.so``) and its Python module ``_front`` with g++."""
+    import pybind11
+
+    os.makedirs(OBJDIR, exist_ok=True)
+    headers = [os.path.join(FRONT, f) for f in os.listdir(FRONT) if f.endswith(".h")]
+    headers.append(os.path.join(ROOT, "include", "ferro_cuda.h"))
+    objs = []
+    for src in FRONT_SOURCES:
+        s = os.path.join(FRONT, src)
+        o = os.path.join(OBJDIR, "front_" + src.replace(".cpp", ".o"))
+        objs.append(o)
+        if _stale(o, [s] + headers):
+            cmd = [CXX, *CXXFLAGS, "-c", s, "-o", o]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            subprocess.run(cmd, check=True)
+    link = ["-L" + HERE, "-lferro_cuda", "-Wl,-rpath,$ORIGIN"]
+    if _stale(FRONT_LIB, objs + [LIB]):
+        cmd = [CXX, "-shared", "-o", FRONT_LIB, *objs, *link]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+    mod = _front_module_path()
+    py_src = os.path.join(FRONT, "front_py.cpp")
+    if _stale(mod, [py_src, FRONT_LIB] + headers):
+        cmd = [CXX, *CXXFLAGS, "-shared", f"-I{pybind11.get_include()}",
+               f"-I{sysconfig.get_paths()['include']}", py_src, "-o", mod,
+               "-L" + HERE, "-lferro_front", "-lferro_cuda", "-Wl,-rpath,$ORIGIN"]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+    return mod
 
 
 if __name__ == "__main__":

@@ -44,6 +44,17 @@ DevCtx *ctx_current() {
     if (cudaMalloc(&c.d_err, sizeof(unsigned int)) != cudaSuccess) return nullptr;
     if (cudaMemset(c.d_err, 0, sizeof(unsigned int)) != cudaSuccess) return nullptr;
     cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    // fg_alloc/fg_free are stream-ordered (cudaMallocAsync/cudaFreeAsync)
+    // from the device's default pool; keep freed blocks in the pool instead
+    // of returning them to the driver at every synchronisation, so a
+    // training loop reuses its per-step buffers.  This is a property of this
+    // process's pool, not of the GPU.
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+      uint64_t keep = UINT64_MAX;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    cudaGetLastError();
     c.ordinal = dev;
   }
   return &c;
@@ -254,10 +265,16 @@ int fg_copy_h2d(fg_buffer *buf, const void *h_src, size_t nbytes) {
   if (!nbytes) return FG_OK;
   FG_REQUIRE(h_src, "copy_from_host: null source");
   FG_CUDA_TRY(cudaSetDevice(buf->dev->ordinal));
+  // The reference copies synchronously from a borrowed slice, so the source
+  // may be released as soon as this returns.  From pageable memory
+  // cudaMemcpyAsync returns once the bytes are staged, which already gives
+  // that; only a page-locked source needs the stream drained.
+  cudaPointerAttributes attr;
+  bool pinned = cudaPointerGetAttributes(&attr, h_src) == cudaSuccess &&
+                attr.type == cudaMemoryTypeHost;
+  cudaGetLastError();
   FG_CUDA_TRY(cudaMemcpyAsync(buf->dptr, h_src, nbytes, cudaMemcpyHostToDevice, buf->dev->stream));
-  // The reference copies synchronously from a borrowed slice; the host
-  // memory may be released right after the call returns.
-  FG_CUDA_TRY(cudaStreamSynchronize(buf->dev->stream));
+  if (pinned) FG_CUDA_TRY(cudaStreamSynchronize(buf->dev->stream));
   return FG_OK;
 }
 

@@ -1,0 +1,635 @@
+// exec.cpp -- runs scheduled proto-kernels on the B200 through the C ABI.
+//
+// Replaces Tensor::execute_item / run_kernel (src/tensor.rs:813-898,
+// 1018-1028) and CpuDevice::{compile,execute} (src/device/cpu.rs:151-208,
+// 318-380).  Per item the router
+//   1. extracts every reduce-of-broadcast-mul contraction (Tensor::matmul,
+//      src/tensor.rs:762-778, and the two contractions its gradient builds,
+//      src/gradient.rs:100-106,165-176) large enough for the tensor cores and
+//      runs it on fg_gemm_3xtf32, operands passed in place when they are
+//      strided views of a buffer and staged into a K-major copy otherwise;
+//   2. extracts large f32 ReduceAxis over a contiguous view and runs it on
+//      the HBM reduction kernels (fg_reduce_rows / fg_reduce_cols);
+//   3. renders what is left (render.cpp) and launches it with fg_execute,
+//      compiling with fg_compile on a program-cache miss.
+// Steps 1-2 change the summation order of those reductions (fp32 tree /
+// tensor-core order instead of the reference's sequential one); with
+// FG_FRONT_EXACT=1 every kernel is rendered and the arithmetic is the
+// reference's.
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <optional>
+#include <unordered_map>
+
+#include "front_internal.h"
+
+namespace ferro {
+
+namespace {
+
+fg_device *g_dev = nullptr;
+int g_ordinal = -1;
+uint64_t g_buffer_ids = 0;
+Stats g_stats;
+std::string g_last_source;
+uint64_t g_kernel_count = 0;
+
+void check(int rc, const char *what) {
+  if (rc != FG_OK) throw Panic(std::string(what) + ": " + fg_last_error());
+}
+
+int env_ordinal() {
+  const char *e = std::getenv("FG_DEVICE");
+  if (!e || !*e) return 0;
+  const char *p = std::strncmp(e, "cuda:", 5) == 0 ? e + 5 : e;
+  return std::atoi(p);
+}
+
+std::unordered_map<std::string, fg_program *> &program_cache() {
+  static std::unordered_map<std::string, fg_program *> c;
+  return c;
+}
+
+}  // namespace
+
+bool exact_mode() {
+  const char *e = std::getenv("FG_FRONT_EXACT");
+  return e && *e && std::strcmp(e, "0") != 0;
+}
+
+int debug_level() {
+  const char *e = std::getenv("DEBUG");
+  return e ? std::atoi(e) : 0;
+}
+
+Stats &stats() { return g_stats; }
+void reset_stats() { g_stats = Stats{}; }
+const std::string &last_source() { return g_last_source; }
+
+void set_device(int ordinal) {
+  if (g_dev && ordinal == g_ordinal) return;
+  if (g_dev) throw Panic("set_device: the front end's device is already open");
+  g_ordinal = ordinal;
+}
+
+fg_device *device() {
+  if (!g_dev) {
+    int ord = g_ordinal >= 0 ? g_ordinal : env_ordinal();
+    check(fg_device_open(ord, &g_dev), "open CUDA device");
+    g_ordinal = ord;
+  }
+  return g_dev;
+}
+
+void synchronize() {
+  if (g_dev) check(fg_device_sync(g_dev), "synchronize");
+}
+
+// ---- DeviceBuffer (src/device.rs:95-214) ----------------------------------
+DeviceBuffer::DeviceBuffer(DType dt, size_t n) : dtype(dt), count(n), id(g_buffer_ids++) {}
+
+DeviceBuffer::~DeviceBuffer() {
+  if (h) fg_free(h);
+}
+
+void DeviceBuffer::ensure_allocated() {
+  if (h) return;
+  check(fg_alloc(device(), (int)dtype, count, &h), "allocate");
+  if (!pending.empty()) {
+    int rc = fg_copy_h2d(h, pending.data(), pending.size());
+    check(rc, "copy_from_host");
+    std::vector<uint8_t>().swap(pending);
+  }
+}
+
+void *DeviceBuffer::ptr() {
+  ensure_allocated();
+  void *p = nullptr;
+  check(fg_buffer_info(h, &p, nullptr, nullptr), "buffer_info");
+  return p;
+}
+
+std::vector<uint8_t> DeviceBuffer::to_host() {
+  ensure_allocated();
+  std::vector<uint8_t> out(count * dtype_size(dtype));
+  check(fg_copy_d2h(h, out.data(), out.size()), "copy_to_host");
+  return out;
+}
+
+namespace {
+
+void *stream() {
+  void *s = nullptr;
+  check(fg_device_stream(device(), &s), "device stream");
+  return s;
+}
+
+float *fptr(const BufferP &b, int64_t offset = 0) {
+  return static_cast<float *>(b->ptr()) + offset;
+}
+
+// ---- strided views --------------------------------------------------------
+struct View {
+  BufferP buf;
+  int64_t offset = 0;
+  Shape shape;
+  std::vector<int64_t> strides;
+};
+
+// Strides of `nd` over the same memory as (od, os), or nothing when the
+// reshape is not expressible as a strided view.
+std::optional<std::vector<int64_t>> reshape_strides(const Shape &od, const std::vector<int64_t> &os,
+                                                    const Shape &nd) {
+  std::vector<int64_t> ns(nd.size(), 0);
+  if (numel(od) == 0 || od.empty()) {
+    int64_t s = 1;
+    for (size_t a = nd.size(); a-- > 0;) {
+      ns[a] = s;
+      s *= nd[a];
+    }
+    return ns;
+  }
+  // Walk old dimensions from the innermost, grouping runs that are
+  // contiguous with each other; each run must be covered exactly by a run
+  // of new dimensions.
+  long vd = (long)nd.size() - 1;
+  int64_t base = os.back(), run = 1, vrun = 1;
+  for (long td = (long)od.size() - 1; td >= 0; td--) {
+    run *= od[(size_t)td];
+    bool run_ends = td == 0 || (od[(size_t)td - 1] != 1 && os[(size_t)td - 1] != run * base);
+    if (!run_ends) continue;
+    while (vd >= 0 && (vrun < run || nd[(size_t)vd] == 1)) {
+      ns[(size_t)vd] = vrun * base;
+      vrun *= nd[(size_t)vd];
+      vd--;
+    }
+    if (vrun != run) return std::nullopt;
+    if (td > 0) {
+      base = os[(size_t)td - 1];
+      run = 1;
+      vrun = 1;
+    }
+  }
+  if (vd != -1) return std::nullopt;
+  return ns;
+}
+
+std::optional<View> try_view(const UOp *n) {
+  switch (n->op) {
+    case Op::Buffer: {
+      View v;
+      v.buf = n->buf;
+      v.shape = {(int64_t)n->buf->count};
+      v.strides = {1};
+      return v;
+    }
+    case Op::Reshape: {
+      auto v = try_view(n->src[0].get());
+      if (!v) return std::nullopt;
+      auto ns = reshape_strides(v->shape, v->strides, n->shape);
+      if (!ns) return std::nullopt;
+      v->shape = n->shape;
+      v->strides = *ns;
+      return v;
+    }
+    case Op::Permute: {
+      auto v = try_view(n->src[0].get());
+      if (!v) return std::nullopt;
+      View o = *v;
+      for (size_t i = 0; i < n->arg.size(); i++) {
+        o.shape[i] = v->shape[(size_t)n->arg[i]];
+        o.strides[i] = v->strides[(size_t)n->arg[i]];
+      }
+      return o;
+    }
+    case Op::Expand: {
+      auto v = try_view(n->src[0].get());
+      if (!v) return std::nullopt;
+      for (size_t a = 0; a < n->shape.size(); a++)
+        if (v->shape[a] == 1 && n->shape[a] != 1) v->strides[a] = 0;
+      v->shape = n->shape;
+      return v;
+    }
+    case Op::Shrink: {
+      auto v = try_view(n->src[0].get());
+      if (!v) return std::nullopt;
+      for (size_t a = 0; a < n->arg.size(); a++) {
+        const UOp *s = n->src[a + 1].get();
+        if (s->op != Op::Const) return std::nullopt;
+        v->offset += (int64_t)s->value * v->strides[a];
+      }
+      v->shape = n->shape;
+      return v;
+    }
+    default:
+      return std::nullopt;
+  }
+}
+
+// Which axes of a node's value vary (used to classify contraction operands).
+std::vector<bool> deps(const UOp *n) {
+  const size_t r = n->has_shape ? n->shape.size() : 0;
+  std::vector<bool> d(r, false);
+  switch (n->op) {
+    case Op::Const:
+      return d;
+    case Op::Buffer:
+      if (r && n->buf->count > 1) d[0] = true;
+      return d;
+    case Op::Reshape: {
+      auto sd = deps(n->src[0].get());
+      const Shape &ss = n->src[0]->shape, &ds = n->shape;
+      std::vector<size_t> dn, sn;
+      for (size_t a = 0; a < ds.size(); a++)
+        if (ds[a] != 1) dn.push_back(a);
+      for (size_t a = 0; a < ss.size(); a++)
+        if (ss[a] != 1) sn.push_back(a);
+      bool same = dn.size() == sn.size();
+      for (size_t i = 0; same && i < dn.size(); i++) same = ds[dn[i]] == ss[sn[i]];
+      if (same) {
+        for (size_t i = 0; i < dn.size(); i++) d[dn[i]] = sd[sn[i]];
+      } else if (std::any_of(sd.begin(), sd.end(), [](bool b) { return b; })) {
+        for (size_t i : dn) d[i] = true;
+      }
+      return d;
+    }
+    case Op::Permute: {
+      auto sd = deps(n->src[0].get());
+      for (size_t i = 0; i < r; i++) d[i] = sd[(size_t)n->arg[i]];
+      return d;
+    }
+    case Op::Expand:
+    case Op::Shrink: {
+      auto sd = deps(n->src[0].get());
+      for (size_t a = 0; a < r && a < sd.size(); a++) d[a] = sd[a] && n->shape[a] != 1;
+      return d;
+    }
+    case Op::ReduceAxis: {
+      auto sd = deps(n->src[0].get());
+      for (size_t a = 0; a < r; a++) d[a] = sd[a];
+      for (int64_t a : n->arg) d[(size_t)a] = false;
+      return d;
+    }
+    default: {
+      for (auto &s : n->src) {
+        if (s->op == Op::Const) continue;
+        auto sd = deps(s.get());
+        if (sd.size() != r) return std::vector<bool>(r, true);
+        for (size_t a = 0; a < r; a++) d[a] = d[a] || sd[a];
+      }
+      return d;
+    }
+  }
+}
+
+// ---- program cache and generic launches -----------------------------------
+void launch_rendered(const RenderedKernel &rk, const BufferP &out) {
+  auto &cache = program_cache();
+  fg_program *prog = nullptr;
+  auto it = cache.find(rk.source);
+  int nargs = (int)rk.params.size() + (rk.has_out_slot ? 1 : 0);
+  const uint64_t kid = g_kernel_count++;
+  if (it != cache.end()) {
+    prog = it->second;
+    g_stats.cache_hits++;
+    if (debug_level() >= 1) fprintf(stderr, "*** CUDA %4llu  (cached)         arg %2d\n",
+                                    (unsigned long long)kid, nargs);
+  } else {
+    uint32_t grid[3] = {rk.grid, 1, 1}, block[3] = {rk.block, 1, 1};
+    check(fg_compile(device(), rk.source.c_str(), "fg_kernel", nargs, grid, block, &prog),
+          "compile");
+    cache.emplace(rk.source, prog);
+    g_stats.compiled++;
+    if (debug_level() >= 4) fprintf(stderr, "%s\n", rk.source.c_str());
+    if (debug_level() >= 1) fprintf(stderr, "*** CUDA %4llu  kernel_%-9llu arg %2d  (compiled)\n",
+                                    (unsigned long long)kid, (unsigned long long)kid, nargs);
+  }
+  g_last_source = rk.source;
+  std::vector<fg_kernel_arg> args;
+  args.reserve((size_t)nargs);
+  if (rk.has_out_slot) {
+    out->ensure_allocated();
+    fg_kernel_arg a{};
+    a.kind = FG_ARG_BUFFER;
+    a.v.buffer = out->h;
+    args.push_back(a);
+  }
+  for (const KernelInput &in : rk.params) {
+    fg_kernel_arg a{};
+    switch (in.kind) {
+      case KernelInput::Buffer:
+        in.buffer->ensure_allocated();
+        a.kind = FG_ARG_BUFFER;
+        a.v.buffer = in.buffer->h;
+        break;
+      case KernelInput::I32:
+        a.kind = FG_ARG_I32;
+        a.v.i32 = (int32_t)in.i;
+        break;
+      case KernelInput::F32:
+        a.kind = FG_ARG_F32;
+        a.v.f32 = (float)in.f;
+        break;
+      case KernelInput::Bool:
+        a.kind = FG_ARG_BOOL;
+        a.v.b = (uint8_t)in.i;
+        break;
+    }
+    args.push_back(a);
+  }
+  check(fg_execute(prog, args.data(), nargs), "execute");
+  g_stats.rendered++;
+}
+
+BufferP temp_buffer(DType dt, int64_t n) {
+  auto b = std::make_shared<DeviceBuffer>(dt, (size_t)n);
+  b->ensure_allocated();
+  return b;
+}
+
+// ---- contraction matching ---------------------------------------------------
+struct Contraction {
+  const UOp *reduce;
+  UOpP a, b;           // operand expressions over the 3-D domain
+  size_t ai, bj, r;    // row axis (A), column axis (B), reduced axis
+  int64_t M, N, K;
+};
+
+constexpr int64_t kGemmMinWork = int64_t(1) << 22;
+constexpr int64_t kHandReduceMin = int64_t(1) << 20;
+
+std::optional<Contraction> match_contraction(const UOp *n) {
+  if (n->op != Op::ReduceAxis || n->reduce_op != Op::Add || n->dtype != DType::F32) return {};
+  if (n->arg.size() != 1) return {};
+  const UOp *m = n->src[0].get();
+  if (m->op != Op::Mul || !m->has_shape || m->shape.size() != 3) return {};
+  const size_t r = (size_t)n->arg[0];
+  size_t i = r == 0 ? 1 : 0, j = r == 2 ? 1 : 2;
+  auto dp = deps(m->src[0].get()), dq = deps(m->src[1].get());
+  if (dp.size() != 3 || dq.size() != 3) return {};
+  Contraction c;
+  c.reduce = n;
+  c.r = r;
+  if (!dp[j] && !dq[i] && (dp[i] || dq[j])) {
+    c.a = m->src[0];
+    c.b = m->src[1];
+    c.ai = i;
+    c.bj = j;
+  } else if (!dq[j] && !dp[i] && (dq[i] || dp[j])) {
+    c.a = m->src[1];
+    c.b = m->src[0];
+    c.ai = i;
+    c.bj = j;
+  } else {
+    return {};
+  }
+  const Shape &s = m->shape;
+  c.M = s[i];
+  c.N = s[j];
+  c.K = s[r];
+  if (c.M * c.N * c.K < kGemmMinWork) return {};
+  return c;
+}
+
+struct Operand {
+  BufferP hold;  // staged copy (if any)
+  BufferP lo;    // TF32 residual
+  const float *ptr = nullptr;
+  const float *lo_ptr = nullptr;
+  int ld = 0;
+  bool mn_major = false;
+};
+
+Operand prepare_operand(const UOpP &x, size_t row_axis, size_t red_axis, size_t bcast_axis,
+                        int64_t rows, int64_t K) {
+  Operand op;
+  auto v = x->dtype == DType::F32 ? try_view(x.get()) : std::nullopt;
+  if (v && (v->strides[bcast_axis] == 0 || v->shape[bcast_axis] == 1) &&
+      (v->offset * 4) % 16 == 0) {
+    const int64_t sr = v->strides[row_axis], sk = v->strides[red_axis];
+    const int64_t extent = (rows - 1) * sr + (K - 1) * sk + 1;
+    bool kmaj = (sk == 1 || K == 1) && sr % 4 == 0 && sr >= K && sr <= INT32_MAX;
+    bool mnmaj = !kmaj && (sr == 1 || rows == 1) && sk % 4 == 0 && sk >= rows && sk <= INT32_MAX;
+    if (rows == 1 && (sk == 1 || K == 1)) {
+      kmaj = true;
+    }
+    if (kmaj || mnmaj) {
+      op.ptr = fptr(v->buf, v->offset);
+      op.ld = kmaj ? (int)std::max<int64_t>(sr, (K + 3) / 4 * 4) : (int)sk;
+      if (kmaj && rows == 1) op.ld = (int)((K + 3) / 4 * 4);
+      op.mn_major = mnmaj;
+      const int64_t span = kmaj ? (rows - 1) * op.ld + K : (K - 1) * op.ld + rows;
+      (void)extent;
+      op.lo = temp_buffer(DType::F32, span);
+      check(fg_split_lo(op.ptr, fptr(op.lo), (size_t)span, stream()), "split_lo");
+      op.lo_ptr = fptr(op.lo);
+      return op;
+    }
+  }
+  // Stage a copy whose contiguous axis is the operand's higher-numbered one
+  // (its natural row-major order, so the staging pass reads coalesced):
+  // K-major out[row][k] when the reduced axis is inner, else MN-major
+  // out[k][row].  The broadcast axis is read at 0.
+  const bool kmaj = red_axis > row_axis;
+  const int64_t outer = kmaj ? rows : K, inner = kmaj ? K : rows;
+  const int64_t ld = (inner + 3) / 4 * 4;
+  op.hold = temp_buffer(DType::F32, outer * ld);
+  RenderSpec spec;
+  spec.value = x;
+  spec.domain = {outer, inner};
+  spec.value_ctx.assign(3, "0");
+  spec.value_ctx[row_axis] = kmaj ? "c0" : "c1";
+  spec.value_ctx[red_axis] = kmaj ? "c1" : "c0";
+  spec.store = RenderSpec::Pitched;
+  spec.pitch = ld;
+  spec.out_dtype = DType::F32;
+  spec.unroll = 4;
+  launch_rendered(render_kernel(spec), op.hold);
+  op.ptr = fptr(op.hold);
+  op.ld = (int)ld;
+  op.mn_major = !kmaj;
+  op.lo = temp_buffer(DType::F32, outer * ld);
+  check(fg_split_lo(op.ptr, fptr(op.lo), (size_t)(outer * ld), stream()), "split_lo");
+  op.lo_ptr = fptr(op.lo);
+  return op;
+}
+
+void run_contraction(const Contraction &c, const UOpP &a, const UOpP &b, const BufferP &out) {
+  const size_t bc_a = c.bj, bc_b = c.ai;
+  Operand A = prepare_operand(a, c.ai, c.r, bc_a, c.M, c.K);
+  Operand B = prepare_operand(b, c.bj, c.r, bc_b, c.N, c.K);
+  int flags = (A.mn_major ? FG_GEMM_A_MN_MAJOR : 0) | (B.mn_major ? FG_GEMM_B_MN_MAJOR : 0);
+  check(fg_gemm_3xtf32((int)c.M, (int)c.N, (int)c.K, A.ptr, A.lo_ptr, A.ld, B.ptr, B.lo_ptr, B.ld,
+                       fptr(out), nullptr, (int)c.N, flags, FG_EPI_NONE, nullptr, nullptr, 0,
+                       stream()),
+        "gemm");
+  g_stats.gemm++;
+  if (debug_level() >= 1)
+    fprintf(stderr, "*** CUDA %4llu  gemm3xtf32 %lldx%lldx%lld%s%s\n",
+            (unsigned long long)g_kernel_count++, (long long)c.M, (long long)c.N,
+            (long long)c.K, A.mn_major ? " A:mn" : "", B.mn_major ? " B:mn" : "");
+}
+
+// ---- hand-written reductions ------------------------------------------------
+struct HandReduce {
+  const UOp *reduce;
+  View v;
+  bool rows;  // reduce over the innermost extent (else over the outer one)
+  int64_t outer, extent, inner;
+};
+
+std::optional<HandReduce> match_hand_reduce(const UOp *n) {
+  if (n->op != Op::ReduceAxis || n->dtype != DType::F32) return {};
+  auto v = try_view(n->src[0].get());
+  if (!v || numel(v->shape) < kHandReduceMin) return {};
+  // The view must be contiguous row-major.
+  int64_t s = 1;
+  for (size_t a = v->shape.size(); a-- > 0;) {
+    if (v->shape[a] != 1 && v->strides[a] != s) return {};
+    s *= v->shape[a];
+  }
+  if ((v->offset * 4) % 16 != 0) return {};
+  std::vector<int64_t> axes = n->arg;
+  std::sort(axes.begin(), axes.end());
+  const Shape &sh = v->shape;
+  // Reduced axes (ignoring size-1 ones) must form one contiguous block.
+  std::vector<int64_t> red;
+  for (int64_t a : axes)
+    if (sh[(size_t)a] != 1) red.push_back(a);
+  if (red.empty()) return {};
+  for (size_t i = 1; i < red.size(); i++)
+    if (red[i] != red[i - 1] + 1) return {};
+  HandReduce h;
+  h.reduce = n;
+  h.v = *v;
+  h.outer = h.extent = h.inner = 1;
+  for (size_t a = 0; a < sh.size(); a++) {
+    if ((int64_t)a < red.front())
+      h.outer *= sh[a];
+    else if ((int64_t)a <= red.back())
+      h.extent *= sh[a];
+    else
+      h.inner *= sh[a];
+  }
+  if (h.inner == 1) {
+    h.rows = true;
+  } else if (h.outer == 1) {
+    h.rows = false;
+  } else {
+    return {};
+  }
+  return h;
+}
+
+void run_hand_reduce(const HandReduce &h, const BufferP &out) {
+  int op = h.reduce->reduce_op == Op::Add ? FG_REDUCE_SUM : FG_REDUCE_MAX;
+  const float *x = fptr(h.v.buf, h.v.offset);
+  if (h.rows)
+    check(fg_reduce_rows(FG_F32, op, x, fptr(out), (size_t)h.outer, (size_t)h.extent, stream()),
+          "reduce_rows");
+  else
+    check(fg_reduce_cols(FG_F32, op, x, fptr(out), (size_t)h.extent, (size_t)h.inner, stream()),
+          "reduce_cols");
+  g_stats.hand_reduce++;
+  if (debug_level() >= 1)
+    fprintf(stderr, "*** CUDA %4llu  reduce_%s %lldx%lld\n", (unsigned long long)g_kernel_count++,
+            h.rows ? "rows" : "cols", (long long)(h.rows ? h.outer : h.extent),
+            (long long)(h.rows ? h.extent : h.inner));
+}
+
+// Root of an allocating item, looking through a same-size Reshape.
+const UOp *root_reduce(const UOpP &value) {
+  const UOp *v = value.get();
+  while (v->op == Op::Reshape) v = v->src[0].get();
+  return v;
+}
+
+}  // namespace
+
+RoutePlan plan_route(const ScheduleItem &item) {
+  RoutePlan p;
+  p.route = "rendered";
+  if (exact_mode()) return p;
+  bool root_handled = false;
+  for (auto &n : toposort(item.value)) {
+    if (auto c = match_contraction(n.get())) {
+      char buf[128];
+      snprintf(buf, sizeof(buf), "gemm %lldx%lldx%lld", (long long)c->M, (long long)c->N,
+               (long long)c->K);
+      p.steps.push_back(buf);
+      if (!item.store_dest && root_reduce(item.value) == n.get()) root_handled = true;
+    } else if (auto h = match_hand_reduce(n.get())) {
+      p.steps.push_back(h->rows ? "reduce_rows" : "reduce_cols");
+      if (!item.store_dest && root_reduce(item.value) == n.get()) root_handled = true;
+    }
+  }
+  if (root_handled && p.steps.size() == 1)
+    p.route = p.steps[0].substr(0, p.steps[0].find(' '));
+  else if (!p.steps.empty())
+    p.route = "mixed";
+  return p;
+}
+
+std::string render_item_source(const ScheduleItem &item) {
+  RenderSpec spec;
+  spec.value = item.value;
+  spec.domain = item.out_shape;
+  spec.unroll = 4;
+  if (item.store_dest) {
+    spec.store = RenderSpec::View;
+    spec.dest = item.store_dest;
+  } else {
+    spec.out_dtype = item.value->dtype;
+  }
+  return render_kernel(spec).source;
+}
+
+void run_item(const ScheduleItem &item) {
+  g_stats.kernels++;
+  UOpP value = item.value;
+  if (!exact_mode()) {
+    // Extract routed reductions bottom-up, substituting each result.
+    std::unordered_map<const UOp *, UOpP> repl;
+    std::vector<UOpP> hold;
+    for (auto &n : toposort(item.value)) {
+      if (n->op != Op::ReduceAxis) continue;
+      auto c = match_contraction(n.get());
+      std::optional<HandReduce> h;
+      if (!c) h = match_hand_reduce(n.get());
+      if (!c && !h) continue;
+      const bool is_root = !item.store_dest && root_reduce(item.value) == n.get();
+      BufferP out = is_root ? item.output : temp_buffer(DType::F32, numel(n->shape));
+      if (c) {
+        std::unordered_map<const UOp *, UOpP> memo_a, memo_b;
+        UOpP a = repl.empty() ? c->a : substitute_with_map(c->a, repl, memo_a);
+        UOpP b = repl.empty() ? c->b : substitute_with_map(c->b, repl, memo_b);
+        run_contraction(*c, a, b, out);
+      } else {
+        run_hand_reduce(*h, out);
+      }
+      if (is_root) return;
+      UOpP sub = make_reshape(make_buffer(out), n->shape);
+      hold.push_back(sub);
+      repl[n.get()] = sub;
+    }
+    if (!repl.empty()) {
+      std::unordered_map<const UOp *, UOpP> memo;
+      value = substitute_with_map(item.value, repl, memo);
+    }
+  }
+  RenderSpec spec;
+  spec.value = value;
+  spec.domain = item.out_shape;
+  spec.unroll = 4;
+  if (item.store_dest) {
+    spec.store = RenderSpec::View;
+    spec.dest = item.store_dest;
+  } else {
+    spec.out_dtype = item.value->dtype;
+  }
+  launch_rendered(render_kernel(spec), item.output);
+}
+
+}  // namespace ferro

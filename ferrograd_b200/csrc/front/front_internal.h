@@ -1,0 +1,66 @@
+// front_internal.h -- declarations shared by the front end's translation units.
+#pragma once
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "ferro_front.h"
+
+namespace ferro {
+
+// The reference panics on misuse (assert!/expect); the front end throws.
+struct Panic : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+// Slot assignment of a kernel's inputs (src/schedule.rs:176-245).
+struct ParamSlots {
+  std::vector<KernelInput> inputs;  // in slot order, starting at slot_offset
+  std::unordered_map<const DeviceBuffer *, int> buffer_slot;
+  // For each Shrink node: per-axis scalar slot of its start, or -1 when the
+  // start stays a literal (full-length axis).
+  std::unordered_map<const UOp *, std::vector<int>> shrink_slots;
+};
+ParamSlots collect_params(const UOpP &root, int slot_offset);
+
+UOpP substitute_materialized(const UOpP &root, const std::map<const UOp *, UOpP> &repl);
+UOpP substitute_with_map(const UOpP &root, const std::unordered_map<const UOp *, UOpP> &repl,
+                         std::unordered_map<const UOp *, UOpP> &memo);
+
+// ---- CUDA C renderer (render.cpp) -----------------------------------------
+// One rendered kernel: thread t of the grid evaluates `value` at the domain
+// coordinates of element(s) t and stores the result.
+struct RenderSpec {
+  UOpP value;
+  Shape domain;                    // iteration shape (row-major element order)
+  // Index expression per axis of value's shape in terms of the domain
+  // coordinates c0..c{n-1}; empty means value's shape == domain.
+  std::vector<std::string> value_ctx;
+  enum Store { Contig, Pitched, View } store = Contig;
+  int64_t pitch = 0;  // Pitched: out[c0 * pitch + c1] over a 2-D domain
+  UOpP dest;          // View: movement chain over the destination buffer
+  DType out_dtype = DType::F32;
+  int unroll = 1;     // elements per thread
+};
+
+struct RenderedKernel {
+  std::string source;
+  uint32_t grid = 1, block = 256;
+  // Arguments in slot order: slot 0 is the output for Contig/Pitched stores.
+  bool has_out_slot = true;
+  std::vector<KernelInput> params;  // slots after the output slot
+};
+RenderedKernel render_kernel(const RenderSpec &spec);
+
+// Float literal as the reference prints constants: from the f64 value with
+// an f suffix (src/codegen/clang.rs).
+std::string float_literal(double v);
+
+// Environment flag: FG_FRONT_EXACT=1 renders every kernel (no GEMM or
+// hand-written reductions), reproducing the reference's arithmetic order.
+bool exact_mode();
+int debug_level();
+
+}  // namespace ferro

@@ -1,0 +1,628 @@
+// graph.cpp -- interned UOp graph nodes (src/uop.rs), reverse-mode gradient
+// rules (src/gradient.rs) and the kernel scheduler (src/schedule.rs).
+#include <algorithm>
+#include <cstring>
+#include <functional>
+#include <sstream>
+#include <stdexcept>
+#include <unordered_map>
+#include <unordered_set>
+
+#include "ferro_front.h"
+#include "front_internal.h"
+
+namespace ferro {
+
+int64_t numel(const Shape &s) {
+  int64_t n = 1;
+  for (int64_t d : s) n *= d;
+  return n;
+}
+
+std::string shape_str(const Shape &s) {
+  std::ostringstream o;
+  o << "[";
+  for (size_t i = 0; i < s.size(); i++) o << (i ? ", " : "") << s[i];
+  o << "]";
+  return o.str();
+}
+
+size_t dtype_size(DType d) { return d == DType::Bool ? 1 : 4; }
+
+const char *dtype_name(DType d) {
+  switch (d) {
+    case DType::F32: return "f32";
+    case DType::I32: return "i32";
+    case DType::Bool: return "bool";
+  }
+  return "?";
+}
+
+const char *op_name(Op op) {
+  static const char *names[] = {"Buffer", "Const", "Reshape", "Permute", "Expand", "Shrink",
+                                "Contiguous", "Add", "Mul", "Neg", "Reciprocal", "Exp2", "Log2",
+                                "Sqrt", "Max", "CmpLt", "Where", "ReduceAxis", "Store", "After",
+                                "Sink"};
+  return names[(int)op];
+}
+
+bool is_alu(Op op) {
+  switch (op) {
+    case Op::Add: case Op::Mul: case Op::Max: case Op::CmpLt: case Op::Where: case Op::Neg:
+    case Op::Exp2: case Op::Log2: case Op::Sqrt: case Op::Reciprocal:
+      return true;
+    default:
+      return false;
+  }
+}
+
+bool is_movement(Op op) {
+  return op == Op::Shrink || op == Op::Reshape || op == Op::Permute || op == Op::Expand;
+}
+
+// ---------------------------------------------------------------------------
+// Interning (src/uop.rs:536-570): a node is looked up by (op, dtype, source
+// identities, arg, literal, buffer identity).  Entries hold weak references;
+// an expired entry is overwritten, and sources of a live entry are alive
+// (the node owns them), so a live key never carries a dangling pointer.
+namespace {
+
+struct Key {
+  int op;
+  int dtype;
+  int rop;
+  uint64_t vbits;
+  const void *buf;
+  std::vector<const UOp *> src;
+  std::vector<int64_t> arg;
+  bool operator==(const Key &o) const {
+    return op == o.op && dtype == o.dtype && rop == o.rop && vbits == o.vbits && buf == o.buf &&
+           src == o.src && arg == o.arg;
+  }
+};
+
+struct KeyHash {
+  size_t operator()(const Key &k) const {
+    uint64_t h = 1469598103934665603ULL;
+    auto mix = [&h](uint64_t v) { h = (h ^ v) * 1099511628211ULL; };
+    mix((uint64_t)k.op);
+    mix((uint64_t)k.dtype);
+    mix((uint64_t)k.rop);
+    mix(k.vbits);
+    mix((uint64_t)(uintptr_t)k.buf);
+    for (auto *p : k.src) mix((uint64_t)(uintptr_t)p);
+    for (auto a : k.arg) mix((uint64_t)a);
+    return (size_t)h;
+  }
+};
+
+std::unordered_map<Key, std::weak_ptr<const UOp>, KeyHash> &interner() {
+  static std::unordered_map<Key, std::weak_ptr<const UOp>, KeyHash> m;
+  return m;
+}
+size_t g_sweep_at = 4096;
+uint64_t g_uid = 0;
+
+void sweep_interner() {
+  auto &m = interner();
+  for (auto it = m.begin(); it != m.end();) {
+    if (it->second.expired())
+      it = m.erase(it);
+    else
+      ++it;
+  }
+  g_sweep_at = std::max<size_t>(4096, m.size() * 2);
+}
+
+void infer_shape(UOp &u) {
+  switch (u.op) {
+    case Op::Buffer:
+      u.has_shape = true;
+      u.shape = {(int64_t)u.buf->count};
+      return;
+    case Op::Shrink:
+    case Op::Reshape:
+    case Op::Expand:
+      u.has_shape = true;
+      u.shape = u.arg;
+      return;
+    case Op::Permute: {
+      const UOp &s = *u.src[0];
+      if (!s.has_shape) return;
+      u.has_shape = true;
+      for (int64_t a : u.arg) u.shape.push_back(s.shape[(size_t)a]);
+      return;
+    }
+    case Op::ReduceAxis: {
+      const UOp &s = *u.src[0];
+      if (!s.has_shape) return;
+      u.has_shape = true;
+      u.shape = s.shape;
+      for (int64_t a : u.arg) u.shape[(size_t)a] = 1;
+      return;
+    }
+    case Op::Const:
+      u.has_shape = true;
+      u.shape = {1};
+      return;
+    case Op::Contiguous:
+    case Op::After:
+      u.has_shape = u.src[0]->has_shape;
+      u.shape = u.src[0]->shape;
+      return;
+    case Op::Store:
+    case Op::Sink:
+      return;
+    default:
+      if (is_alu(u.op)) {
+        u.has_shape = u.src[0]->has_shape;
+        u.shape = u.src[0]->shape;
+      }
+      return;
+  }
+}
+
+UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, std::vector<int64_t> arg = {},
+            Op rop = Op::Add, double value = 0.0, const BufferP &buf = nullptr) {
+  Key k;
+  k.op = (int)op;
+  k.dtype = (int)dt;
+  k.rop = op == Op::ReduceAxis ? (int)rop : 0;
+  std::memcpy(&k.vbits, &value, sizeof(double));
+  k.buf = buf.get();
+  k.src.reserve(srcs.size());
+  for (auto &s : srcs) k.src.push_back(s.get());
+  k.arg = arg;
+  auto &m = interner();
+  auto it = m.find(k);
+  if (it != m.end()) {
+    if (auto live = it->second.lock()) return live;
+  }
+  auto u = std::make_shared<UOp>();
+  u->op = op;
+  u->dtype = dt;
+  u->src = std::move(srcs);
+  u->arg = std::move(arg);
+  u->reduce_op = k.rop ? rop : Op::Add;
+  if (op == Op::ReduceAxis) u->reduce_op = rop;
+  u->value = value;
+  u->buf = buf;
+  u->uid = g_uid++;
+  infer_shape(*u);
+  UOpP out = u;
+  m[k] = out;
+  if (m.size() > g_sweep_at) sweep_interner();
+  return out;
+}
+
+}  // namespace
+
+size_t interner_size() {
+  sweep_interner();
+  return interner().size();
+}
+
+UOpP make_buffer(const BufferP &b) { return intern(Op::Buffer, b->dtype, {}, {}, Op::Add, 0.0, b); }
+UOpP make_const(double v, DType dt) { return intern(Op::Const, dt, {}, {}, Op::Add, v); }
+UOpP make_reshape(const UOpP &s, const Shape &shape) {
+  return intern(Op::Reshape, s->dtype, {s}, shape);
+}
+UOpP make_permute(const UOpP &s, const std::vector<int64_t> &order) {
+  return intern(Op::Permute, s->dtype, {s}, order);
+}
+UOpP make_expand(const UOpP &s, const Shape &shape) {
+  return intern(Op::Expand, s->dtype, {s}, shape);
+}
+UOpP make_shrink(const UOpP &s, const std::vector<UOpP> &starts, const Shape &lengths) {
+  std::vector<UOpP> srcs{s};
+  srcs.insert(srcs.end(), starts.begin(), starts.end());
+  return intern(Op::Shrink, s->dtype, std::move(srcs), lengths);
+}
+UOpP make_contiguous(const UOpP &s) { return intern(Op::Contiguous, s->dtype, {s}); }
+UOpP make_alu(Op op, DType dt, std::vector<UOpP> srcs) { return intern(op, dt, std::move(srcs)); }
+UOpP make_add(const UOpP &a, const UOpP &b) { return intern(Op::Add, a->dtype, {a, b}); }
+UOpP make_mul(const UOpP &a, const UOpP &b) { return intern(Op::Mul, a->dtype, {a, b}); }
+UOpP make_neg(const UOpP &a) { return intern(Op::Neg, a->dtype, {a}); }
+UOpP make_reciprocal(const UOpP &a) { return intern(Op::Reciprocal, a->dtype, {a}); }
+UOpP make_cmplt(const UOpP &a, const UOpP &b) { return intern(Op::CmpLt, DType::Bool, {a, b}); }
+UOpP make_where(const UOpP &c, const UOpP &t, const UOpP &f) {
+  return intern(Op::Where, t->dtype, {c, t, f});
+}
+UOpP make_reduce(const UOpP &s, Op rop, const std::vector<int64_t> &axes) {
+  return intern(Op::ReduceAxis, s->dtype, {s}, axes, rop);
+}
+UOpP make_store(const UOpP &dest, const UOpP &value) {
+  return intern(Op::Store, dest->dtype, {dest, value});
+}
+UOpP make_after(const UOpP &value, const UOpP &effect) {
+  return intern(Op::After, value->dtype, {value, effect});
+}
+UOpP make_sink(const std::vector<UOpP> &srcs) { return intern(Op::Sink, DType::F32, srcs); }
+
+UOpP make_full(const Shape &shape, DType dt, double value) {
+  Shape base(shape.size(), 1);
+  UOpP b = make_reshape(make_const(value, dt), base);
+  bool all_one = std::all_of(shape.begin(), shape.end(), [](int64_t d) { return d == 1; });
+  return all_one ? b : make_expand(b, shape);
+}
+
+bool has_buffer_identity(const UOp *u) {
+  if (u->op == Op::Buffer) return true;
+  if (u->op == Op::After || is_movement(u->op)) return has_buffer_identity(u->src[0].get());
+  return false;
+}
+
+std::vector<UOpP> toposort(const UOpP &root) {
+  // Iterative post-order DFS.  Sources are pushed in reverse so the first
+  // source is finished first; After walks its effect last-pushed-first
+  // (src/uop.rs:1044-1074).
+  std::vector<UOpP> out;
+  std::unordered_set<const UOp *> visited;
+  std::vector<std::pair<UOpP, bool>> stack{{root, false}};
+  while (!stack.empty()) {
+    auto [node, processed] = stack.back();
+    stack.pop_back();
+    if (visited.count(node.get())) continue;
+    if (processed) {
+      visited.insert(node.get());
+      out.push_back(node);
+      continue;
+    }
+    stack.push_back({node, true});
+    if (node->op == Op::After) {
+      for (auto &s : node->src)
+        if (!visited.count(s.get())) stack.push_back({s, false});
+    } else {
+      for (auto it = node->src.rbegin(); it != node->src.rend(); ++it)
+        if (!visited.count(it->get())) stack.push_back({*it, false});
+    }
+  }
+  return out;
+}
+
+std::string dump(const UOpP &root) {
+  auto order = toposort(root);
+  std::unordered_map<const UOp *, size_t> idx;
+  std::ostringstream o;
+  for (size_t i = 0; i < order.size(); i++) {
+    const UOp *u = order[i].get();
+    idx[u] = i;
+    o << "%" << i << " = " << op_name(u->op) << " " << dtype_name(u->dtype);
+    if (u->has_shape) o << " " << shape_str(u->shape);
+    if (!u->src.empty()) {
+      o << " (";
+      for (size_t j = 0; j < u->src.size(); j++) o << (j ? ", " : "") << "%" << idx[u->src[j].get()];
+      o << ")";
+    }
+    if (u->op == Op::Const) o << " value=" << u->value;
+    if (u->op == Op::Buffer) o << " buf#" << u->buf->id << "[" << u->buf->count << "]";
+    if (u->op == Op::ReduceAxis) o << " " << op_name(u->reduce_op) << shape_str(u->arg);
+    if (u->op == Op::Permute || u->op == Op::Reshape || u->op == Op::Expand ||
+        u->op == Op::Shrink)
+      o << " arg=" << shape_str(u->arg);
+    o << "\n";
+  }
+  return o.str();
+}
+
+// ---------------------------------------------------------------------------
+// Gradient rules (src/gradient.rs:97-205).
+namespace {
+
+std::unordered_map<const UOp *, std::vector<UOpP>> consumer_map(const std::vector<UOpP> &order) {
+  std::unordered_map<const UOp *, std::vector<UOpP>> m;
+  for (auto &n : order)
+    for (auto &s : n->src) m[s.get()].push_back(n);
+  return m;
+}
+
+UOpP const_like(const UOp *node, double v) { return make_const(v, node->dtype); }
+
+UOpP zero_like(const UOp *node) {
+  Shape s = node->has_shape ? node->shape : Shape{1};
+  return make_full(s, node->dtype, 0.0);
+}
+
+std::vector<UOpP> gradient_for_op(const UOpP &nodep, const UOpP &grad) {
+  const UOp *node = nodep.get();
+  switch (node->op) {
+    case Op::Add:
+      return {grad, grad};
+    case Op::Mul:
+      return {make_mul(node->src[1], grad), make_mul(node->src[0], grad)};
+    case Op::Neg:
+      return {make_neg(grad)};
+    case Op::Reciprocal:
+      return {make_mul(make_neg(grad), make_mul(nodep, nodep))};
+    case Op::Exp2:
+      return {make_mul(make_mul(nodep, const_like(node, 0.6931471805599453)), grad)};
+    case Op::Log2:
+      return {make_mul(grad, make_reciprocal(make_mul(node->src[0],
+                                                      const_like(node, 0.6931471805599453))))};
+    case Op::Sqrt:
+      return {make_mul(grad, make_reciprocal(make_mul(const_like(node, 2.0), nodep)))};
+    case Op::Max: {
+      const UOpP &x = node->src[0], &y = node->src[1];
+      UOpP zero = const_like(node, 0.0);
+      UOpP half = make_mul(grad, const_like(node, 0.5));
+      UOpP x_wins = make_cmplt(y, x), y_wins = make_cmplt(x, y);
+      UOpP x_grad = make_where(x_wins, grad, make_where(y_wins, zero, half));
+      UOpP y_grad = make_where(y_wins, grad, make_where(x_wins, zero, half));
+      return {x_grad, y_grad};
+    }
+    case Op::CmpLt:
+      return {nullptr, nullptr};
+    case Op::Where: {
+      UOpP zero = const_like(node, 0.0);
+      return {nullptr, make_where(node->src[0], grad, zero), make_where(node->src[0], zero, grad)};
+    }
+    case Op::Reshape:
+      return {make_reshape(grad, node->src[0]->shape)};
+    case Op::Permute: {
+      std::vector<int64_t> inv(node->arg.size());
+      for (size_t i = 0; i < node->arg.size(); i++) inv[(size_t)node->arg[i]] = (int64_t)i;
+      return {make_permute(grad, inv)};
+    }
+    case Op::Expand: {
+      const Shape &src = node->src[0]->shape;
+      std::vector<int64_t> axes;
+      for (size_t a = 0; a < src.size(); a++)
+        if (src[a] == 1 && node->arg[a] > 1) axes.push_back((int64_t)a);
+      if (axes.empty()) return {grad};
+      return {make_reduce(grad, Op::Add, axes)};
+    }
+    case Op::Contiguous:
+      return {grad};
+    case Op::ReduceAxis: {
+      const UOpP &src = node->src[0];
+      const Shape &ss = src->shape;
+      if (node->reduce_op == Op::Add) return {make_expand(grad, ss)};
+      UOpP max_e = make_expand(nodep, ss);
+      UOpP grad_e = make_expand(grad, ss);
+      UOpP is_not_max = make_cmplt(src, max_e);
+      UOpP mask = make_where(is_not_max, make_const(0.0, grad->dtype), make_const(1.0, grad->dtype));
+      UOpP count = make_reduce(mask, Op::Add, node->arg);
+      UOpP weighted = make_mul(mask, make_reciprocal(make_expand(count, ss)));
+      return {make_mul(weighted, grad_e)};
+    }
+    case Op::Buffer:
+    case Op::Const:
+      return {};
+    default:
+      throw Panic(std::string("gradient not implemented for ") + op_name(node->op));
+  }
+}
+
+}  // namespace
+
+std::map<const UOp *, UOpP> compute_gradient(const UOpP &root, const UOpP &root_grad,
+                                             const std::vector<UOpP> &targets) {
+  auto order = toposort(root);
+  auto consumers = consumer_map(order);
+  // needed_nodes (src/gradient.rs:64-81): nodes on a path from a target up
+  // to the root, found by walking consumers.
+  std::unordered_set<const UOp *> needed;
+  std::vector<const UOp *> stack;
+  for (auto &t : targets) stack.push_back(t.get());
+  while (!stack.empty()) {
+    const UOp *n = stack.back();
+    stack.pop_back();
+    if (!needed.insert(n).second) continue;
+    auto it = consumers.find(n);
+    if (it != consumers.end())
+      for (auto &c : it->second) stack.push_back(c.get());
+  }
+  needed.insert(root.get());
+
+  std::unordered_map<const UOp *, UOpP> grads;
+  grads[root.get()] = root_grad;
+  for (auto it = order.rbegin(); it != order.rend(); ++it) {
+    const UOpP &node = *it;
+    if (!needed.count(node.get())) continue;
+    auto g = grads.find(node.get());
+    if (g == grads.end()) continue;
+    UOpP grad = g->second;
+    auto local = gradient_for_op(node, grad);
+    for (size_t i = 0; i < node->src.size() && i < local.size(); i++) {
+      if (!local[i]) continue;
+      const UOp *s = node->src[i].get();
+      if (!needed.count(s)) continue;
+      auto e = grads.find(s);
+      if (e == grads.end())
+        grads[s] = local[i];
+      else
+        e->second = make_add(e->second, local[i]);
+    }
+  }
+  std::map<const UOp *, UOpP> result;
+  for (auto &t : targets) {
+    auto g = grads.find(t.get());
+    result[t.get()] = g != grads.end() ? g->second : zero_like(t.get());
+  }
+  return result;
+}
+
+// ---------------------------------------------------------------------------
+// Scheduling (src/schedule.rs:64-365).
+namespace {
+
+using ReplMap = std::map<const UOp *, UOpP>;
+
+// Chained reductions: every node below a ReduceAxis (src/schedule.rs:264-272).
+std::unordered_set<const UOp *> nested_reduce_inputs(const std::vector<UOpP> &order) {
+  std::unordered_set<const UOp *> feeds;
+  for (auto it = order.rbegin(); it != order.rend(); ++it) {
+    const UOp *n = it->get();
+    if (n->op == Op::ReduceAxis || feeds.count(n))
+      for (auto &s : n->src) feeds.insert(s.get());
+  }
+  return feeds;
+}
+
+bool should_materialize(const UOp *node, const std::unordered_set<const UOp *> &roots,
+                        const std::unordered_map<const UOp *, std::vector<UOpP>> &consumers,
+                        const std::unordered_set<const UOp *> &nested) {
+  if (roots.count(node) || !node->has_shape) return false;
+  switch (node->op) {
+    case Op::Sink: case Op::Store: case Op::After: case Op::Buffer: case Op::Const:
+      return false;
+    default:
+      break;
+  }
+  if (node->op == Op::Contiguous) return true;
+  if (is_movement(node->op)) return false;
+  if (has_buffer_identity(node)) return false;
+  auto it = consumers.find(node);
+  if (it != consumers.end() && it->second.size() > 1) return true;
+  if (node->op == Op::ReduceAxis && it != consumers.end() &&
+      std::any_of(it->second.begin(), it->second.end(),
+                  [](const UOpP &c) { return is_alu(c->op); }))
+    return true;
+  return node->op == Op::ReduceAxis && nested.count(node);
+}
+
+}  // namespace
+
+UOpP substitute_materialized(const UOpP &root, const ReplMap &repl) {
+  auto order = toposort(root);
+  std::unordered_map<const UOp *, UOpP> sub;
+  for (auto &node : order) {
+    if (node != root) {
+      auto r = repl.find(node.get());
+      if (r != repl.end()) {
+        sub[node.get()] = r->second;
+        continue;
+      }
+    }
+    bool changed = false;
+    std::vector<UOpP> srcs;
+    srcs.reserve(node->src.size());
+    for (auto &s : node->src) {
+      auto f = sub.find(s.get());
+      UOpP ns = f != sub.end() ? f->second : s;
+      changed |= ns != s;
+      srcs.push_back(ns);
+    }
+    sub[node.get()] =
+        changed ? intern(node->op, node->dtype, std::move(srcs), node->arg, node->reduce_op,
+                         node->value, node->buf)
+                : node;
+  }
+  return sub[root.get()];
+}
+
+UOpP substitute_with_map(const UOpP &root, const std::unordered_map<const UOp *, UOpP> &repl,
+                         std::unordered_map<const UOp *, UOpP> &memo) {
+  auto order = toposort(root);
+  for (auto &node : order) {
+    if (memo.count(node.get())) continue;
+    auto r = repl.find(node.get());
+    if (r != repl.end()) {
+      memo[node.get()] = r->second;
+      continue;
+    }
+    bool changed = false;
+    std::vector<UOpP> srcs;
+    srcs.reserve(node->src.size());
+    for (auto &s : node->src) {
+      UOpP ns = memo.at(s.get());
+      changed |= ns != s;
+      srcs.push_back(ns);
+    }
+    memo[node.get()] =
+        changed ? intern(node->op, node->dtype, std::move(srcs), node->arg, node->reduce_op,
+                         node->value, node->buf)
+                : node;
+  }
+  return memo.at(root.get());
+}
+
+ParamSlots collect_params(const UOpP &root, int slot_offset) {
+  // parameterize_inputs (src/schedule.rs:176-245): buffers by first
+  // appearance, one scalar per parameterised Shrink start.
+  ParamSlots ps;
+  for (auto &node : toposort(root)) {
+    if (node->op == Op::Buffer) {
+      if (!ps.buffer_slot.count(node->buf.get())) {
+        ps.buffer_slot[node->buf.get()] = (int)ps.inputs.size() + slot_offset;
+        KernelInput in{KernelInput::Buffer, node->buf};
+        ps.inputs.push_back(in);
+      }
+    } else if (node->op == Op::Shrink) {
+      const Shape &ss = node->src[0]->shape;
+      std::vector<int> slots(node->arg.size(), -1);
+      for (size_t a = 0; a < node->arg.size(); a++) {
+        const UOpP &start = node->src[a + 1];
+        if (node->arg[a] != ss[a] && start->op == Op::Const) {
+          slots[a] = (int)ps.inputs.size() + slot_offset;
+          KernelInput in{KernelInput::I32, nullptr};
+          in.i = (int64_t)start->value;
+          ps.inputs.push_back(in);
+        }
+      }
+      ps.shrink_slots[node.get()] = slots;
+    }
+  }
+  return ps;
+}
+
+namespace {
+
+ScheduleItem parameterize(const UOpP &expr) {
+  ScheduleItem it;
+  it.value = expr;
+  it.out_shape = expr->has_shape ? expr->shape : Shape{1};
+  it.output = std::make_shared<DeviceBuffer>(expr->dtype, (size_t)numel(it.out_shape));
+  it.inputs = collect_params(expr, 1).inputs;
+  return it;
+}
+
+ScheduleItem parameterize_store(const UOpP &store) {
+  ScheduleItem it;
+  it.store_dest = store->src[0];
+  it.value = store->src[1];
+  it.out_shape = it.value->has_shape ? it.value->shape : Shape{1};
+  it.inputs = collect_params(store, 0).inputs;
+  return it;
+}
+
+UOpP buffer_replacement(const ScheduleItem &it) {
+  return make_reshape(make_buffer(it.output), it.out_shape);
+}
+
+}  // namespace
+
+SchedulePlan schedule_many(const std::vector<UOpP> &exprs) {
+  if (exprs.empty()) throw Panic("schedule_many requires at least one root");
+  UOpP uni = make_sink(exprs);
+  auto order = toposort(uni);
+  auto consumers = consumer_map(order);
+  auto nested = nested_reduce_inputs(order);
+  std::unordered_set<const UOp *> roots;
+  for (auto &e : exprs) roots.insert(e.get());
+
+  SchedulePlan plan;
+  for (auto &node : order) {
+    if (!should_materialize(node.get(), roots, consumers, nested)) continue;
+    UOpP k = substitute_materialized(node, plan.replacements);
+    ScheduleItem item = parameterize(k);
+    plan.replacements[node.get()] = buffer_replacement(item);
+    plan.keep.push_back(node);
+    plan.items.push_back(std::move(item));
+  }
+  for (auto &e : exprs) {
+    UOpP fin = substitute_materialized(e, plan.replacements);
+    if (fin->op == Op::After && fin->src.size() == 2 && fin->src[1]->op == Op::Store) {
+      plan.items.push_back(parameterize_store(fin->src[1]));
+      plan.replacements[e.get()] = fin->src[0];
+    } else {
+      ScheduleItem item = parameterize(fin);
+      plan.replacements[e.get()] = buffer_replacement(item);
+      plan.items.push_back(std::move(item));
+    }
+    plan.keep.push_back(e);
+  }
+  return plan;
+}
+
+}  // namespace ferro

@@ -1,0 +1,553 @@
+// render.cpp -- CUDA C renderer for scheduled proto-kernels.
+//
+// Replaces the reference's rangeify -> optimize -> late_expand ->
+// devectorize -> linearize -> ClangRenderer chain (src/schedule/rangeify.rs,
+// src/optimize/*.rs, src/expand.rs, src/devectorize.rs, src/linearize.rs,
+// src/codegen/clang.rs) with a direct walk of the tensor-level expression.
+// The arithmetic is the reference's, op for op:
+//   * every ALU op is one correctly rounded operation; Add/Mul use
+//     __fadd_rn/__fmul_rn so nvcc never contracts them into an FMA (the
+//     reference emits one op per C statement, clang.rs:216-229);
+//   * exp2/log2 are double-precision calls on the float argument, rounded to
+//     float; sqrt and reciprocal are correctly rounded; max is (a>b)?a:b;
+//   * a reduction walks its axes in order with one accumulator; when the
+//     last reduced axis has size R > 4 and R % 4 == 0 it is split into
+//     blocks of four lanes folded left to right, acc = acc op (((v0 op v1)
+//     op v2) op v3) (src/optimize/unroll.rs:41-113,
+//     src/devectorize.rs:206-347); the identity is 0 or -inf (INT_MIN for
+//     i32);
+//   * symbolic_simple (src/optimize/symbolic.rs:42-56) folds ALU ops on
+//     literal constants: const op const in f64, x+0, 0+x, x*1, 1*x -> x,
+//     x*0, 0*x -> 0.
+// The thread mapping is the B200's: one thread per output element (or
+// `unroll` elements, loads of all of them issued before the stores), 256
+// threads per block, a grid covering the domain.
+#include <algorithm>
+#include <charconv>
+#include <cmath>
+#include <cstring>
+#include <sstream>
+
+#include "front_internal.h"
+
+namespace ferro {
+
+std::string float_literal(double v) {
+  if (std::isinf(v)) return v > 0 ? "INFINITY" : "(-INFINITY)";
+  if (std::isnan(v)) return "NAN";
+  char buf[64];
+  auto r = std::to_chars(buf, buf + sizeof(buf), v);
+  std::string s(buf, r.ptr);
+  if (s.find_first_of(".eEn") == std::string::npos) s += ".0";
+  return s + "f";
+}
+
+namespace {
+
+const char *ctype(DType d) {
+  switch (d) {
+    case DType::F32: return "float";
+    case DType::I32: return "int";
+    case DType::Bool: return "bool";
+  }
+  return "float";
+}
+const char *storage_type(DType d) {
+  switch (d) {
+    case DType::F32: return "float";
+    case DType::I32: return "int";
+    case DType::Bool: return "unsigned char";
+  }
+  return "float";
+}
+
+bool is_int_literal(const std::string &s) {
+  if (s.empty()) return false;
+  size_t i = s[0] == '-' ? 1 : 0;
+  if (i == s.size()) return false;
+  for (; i < s.size(); i++)
+    if (s[i] < '0' || s[i] > '9') return false;
+  return true;
+}
+
+struct Val {
+  std::string expr;
+  DType dt = DType::F32;
+  bool is_const = false;
+  double c = 0.0;
+};
+
+std::string literal_of(double v, DType dt) {
+  if (dt == DType::F32) return float_literal(v);
+  if (dt == DType::Bool) return v != 0.0 ? "true" : "false";
+  if (std::isinf(v)) return v > 0 ? "2147483647" : "(-2147483647 - 1)";
+  char buf[32];
+  snprintf(buf, sizeof(buf), "%lld", (long long)v);
+  return buf;
+}
+
+bool bits_equal(double a, double b) {
+  uint64_t x, y;
+  std::memcpy(&x, &a, 8);
+  std::memcpy(&y, &b, 8);
+  return x == y;
+}
+
+class Emitter {
+ public:
+  explicit Emitter(const ParamSlots &ps) : ps_(ps) { scopes_.emplace_back(); }
+
+  std::ostringstream body;
+  int indent = 2;
+
+  void line(const std::string &s) { body << std::string((size_t)indent, ' ') << s << "\n"; }
+  std::string fresh(const char *p) { return std::string(p) + std::to_string(tmp_++); }
+  void open(const std::string &head) {
+    line(head + " {");
+    indent += 2;
+    scopes_.emplace_back();
+  }
+  void close() {
+    indent -= 2;
+    line("}");
+    scopes_.pop_back();
+  }
+  // A brace block that starts a fresh memo scope.
+  void open_block() { open(""); }
+
+  // Index expression variables: literals stay literal, others get a name.
+  std::string idx(const std::string &expr) {
+    if (is_int_literal(expr)) return expr;
+    for (auto s = scopes_.rbegin(); s != scopes_.rend(); ++s) {
+      auto f = s->idx.find(expr);
+      if (f != s->idx.end()) return f->second;
+    }
+    std::string v = fresh("i");
+    line("const long long " + v + " = " + expr + ";");
+    scopes_.back().idx[expr] = v;
+    return v;
+  }
+
+  Val value(const UOp *n, const std::vector<std::string> &ctx);
+
+  // Index into the buffer at the bottom of a movement chain.
+  std::string view_index(const UOp *n, const std::vector<std::string> &ctx,
+                         const DeviceBuffer **buf);
+
+ private:
+  struct Scope {
+    std::unordered_map<std::string, Val> vals;
+    std::unordered_map<std::string, std::string> idx;
+  };
+
+  Val lookup(const std::string &key) {
+    for (auto s = scopes_.rbegin(); s != scopes_.rend(); ++s) {
+      auto f = s->vals.find(key);
+      if (f != s->vals.end()) return f->second;
+    }
+    return Val{};
+  }
+
+  std::vector<std::string> src_ctx(const UOp *n, const std::vector<std::string> &ctx);
+  Val emit_alu(Op op, DType dt, const std::vector<Val> &a);
+  Val emit_reduce(const UOp *n, const std::vector<std::string> &ctx);
+  Val bind(const std::string &expr, DType dt) {
+    std::string v = fresh("v");
+    line(std::string("const ") + ctype(dt) + " " + v + " = " + expr + ";");
+    return Val{v, dt};
+  }
+
+  const ParamSlots &ps_;
+  std::vector<Scope> scopes_;
+  int tmp_ = 0;
+};
+
+std::string mul_idx(const std::string &a, int64_t k) {
+  if (a == "0" || k == 0) return "0";
+  if (k == 1) return a;
+  return a + " * " + std::to_string(k) + "LL";
+}
+
+std::vector<std::string> Emitter::src_ctx(const UOp *n, const std::vector<std::string> &ctx) {
+  const UOp *s = n->src[0].get();
+  const Shape &ss = s->shape;
+  std::vector<std::string> out(ss.size(), "0");
+  switch (n->op) {
+    case Op::Reshape: {
+      const Shape &ds = n->shape;
+      if (numel(ss) == 1) return out;
+      if (ctx.size() != ds.size())
+        throw Panic("render: reshape index rank " + std::to_string(ctx.size()) + " != shape " +
+                    shape_str(ds));
+      std::vector<size_t> dn, sn;
+      for (size_t a = 0; a < ds.size(); a++)
+        if (ds[a] != 1) dn.push_back(a);
+      for (size_t a = 0; a < ss.size(); a++)
+        if (ss[a] != 1) sn.push_back(a);
+      bool same = dn.size() == sn.size();
+      for (size_t i = 0; same && i < dn.size(); i++) same = ds[dn[i]] == ss[sn[i]];
+      if (same) {
+        for (size_t i = 0; i < dn.size(); i++) out[sn[i]] = ctx[dn[i]];
+        return out;
+      }
+      // General reshape: row-major linear index, unflattened into the source.
+      std::string lin;
+      int64_t stride = 1;
+      for (size_t a = ds.size(); a-- > 0;) {
+        if (ds[a] != 1 && ctx[a] != "0") {
+          std::string t = mul_idx(ctx[a], stride);
+          lin = lin.empty() ? t : t + " + " + lin;
+        }
+        stride *= ds[a];
+      }
+      if (lin.empty()) return out;
+      std::string l = idx(lin);
+      int64_t sstride = 1;
+      std::vector<int64_t> strides(ss.size());
+      for (size_t a = ss.size(); a-- > 0;) {
+        strides[a] = sstride;
+        sstride *= ss[a];
+      }
+      bool first = true;
+      for (size_t a = 0; a < ss.size(); a++) {
+        if (ss[a] == 1) continue;
+        std::string e = strides[a] == 1 ? l : "(" + l + " / " + std::to_string(strides[a]) + "LL)";
+        if (!first) e = "(" + e + " % " + std::to_string(ss[a]) + "LL)";
+        first = false;
+        out[a] = idx(e);
+      }
+      return out;
+    }
+    case Op::Permute:
+      for (size_t i = 0; i < n->arg.size(); i++) out[(size_t)n->arg[i]] = ctx.at(i);
+      return out;
+    case Op::Expand:
+      for (size_t a = 0; a < ss.size(); a++) out[a] = ss[a] == 1 ? "0" : ctx.at(a);
+      return out;
+    case Op::Shrink: {
+      auto it = ps_.shrink_slots.find(n);
+      for (size_t a = 0; a < ss.size(); a++) {
+        int slot = it != ps_.shrink_slots.end() ? it->second[a] : -1;
+        std::string start;
+        if (slot >= 0)
+          start = "(long long)s" + std::to_string(slot);
+        else
+          start = std::to_string((long long)n->src[a + 1]->value);
+        if (start == "0")
+          out[a] = ctx.at(a);
+        else if (ctx.at(a) == "0")
+          out[a] = idx(start);
+        else
+          out[a] = idx(ctx.at(a) + " + " + start);
+      }
+      return out;
+    }
+    default:
+      return ctx;
+  }
+}
+
+std::string Emitter::view_index(const UOp *n, const std::vector<std::string> &ctx,
+                                const DeviceBuffer **buf) {
+  if (n->op == Op::Buffer) {
+    *buf = n->buf.get();
+    return ctx.empty() ? "0" : ctx[0];
+  }
+  if (is_movement(n->op) || n->op == Op::After || n->op == Op::Contiguous) {
+    if (n->op == Op::After || n->op == Op::Contiguous) return view_index(n->src[0].get(), ctx, buf);
+    return view_index(n->src[0].get(), src_ctx(n, ctx), buf);
+  }
+  throw Panic(std::string("render: store destination must be a view of a buffer, got ") +
+              op_name(n->op));
+}
+
+Val Emitter::emit_alu(Op op, DType dt, const std::vector<Val> &a) {
+  // symbolic_simple folds (src/optimize/symbolic.rs:42-56).
+  if ((op == Op::Add || op == Op::Mul) && a.size() == 2) {
+    const Val &x = a[0], &y = a[1];
+    if (x.is_const && y.is_const) {
+      double r = op == Op::Add ? x.c + y.c : x.c * y.c;
+      if (dt == DType::I32) r = (double)(op == Op::Add ? (long long)x.c + (long long)y.c
+                                                       : (long long)x.c * (long long)y.c);
+      return Val{literal_of(r, dt), dt, true, r};
+    }
+    if (op == Op::Add && y.is_const && bits_equal(y.c, 0.0)) return x;
+    if (op == Op::Add && x.is_const && bits_equal(x.c, 0.0)) return y;
+    if (op == Op::Mul && y.is_const && bits_equal(y.c, 1.0)) return x;
+    if (op == Op::Mul && x.is_const && bits_equal(x.c, 1.0)) return y;
+    if (op == Op::Mul && y.is_const && bits_equal(y.c, 0.0)) return y;
+    if (op == Op::Mul && x.is_const && bits_equal(x.c, 0.0)) return x;
+  }
+  const bool f = dt == DType::F32;
+  std::string e;
+  switch (op) {
+    case Op::Add:
+      e = f ? "__fadd_rn(" + a[0].expr + ", " + a[1].expr + ")"
+            : "(int)((unsigned)(" + a[0].expr + ") + (unsigned)(" + a[1].expr + "))";
+      break;
+    case Op::Mul:
+      e = f ? "__fmul_rn(" + a[0].expr + ", " + a[1].expr + ")"
+            : "(int)((unsigned)(" + a[0].expr + ") * (unsigned)(" + a[1].expr + "))";
+      break;
+    case Op::Neg:
+      e = f ? "(-" + a[0].expr + ")" : "(int)(0u - (unsigned)(" + a[0].expr + "))";
+      break;
+    case Op::Reciprocal:
+      e = f ? "__frcp_rn(" + a[0].expr + ")" : "(1 / (" + a[0].expr + "))";
+      break;
+    case Op::Exp2:
+      e = "(float)exp2((double)" + a[0].expr + ")";
+      break;
+    case Op::Log2:
+      e = "(float)log2((double)" + a[0].expr + ")";
+      break;
+    case Op::Sqrt:
+      e = "__fsqrt_rn(" + a[0].expr + ")";
+      break;
+    case Op::Max:
+      e = "((" + a[0].expr + " > " + a[1].expr + ") ? " + a[0].expr + " : " + a[1].expr + ")";
+      break;
+    case Op::CmpLt:
+      e = "(" + a[0].expr + " < " + a[1].expr + ")";
+      break;
+    case Op::Where:
+      e = "(" + a[0].expr + " ? " + a[1].expr + " : " + a[2].expr + ")";
+      break;
+    default:
+      throw Panic(std::string("render: not an ALU op: ") + op_name(op));
+  }
+  return bind(e, dt);
+}
+
+Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
+  const UOp *s = n->src[0].get();
+  const Shape &ss = s->shape;
+  std::vector<int64_t> axes = n->arg;
+  std::sort(axes.begin(), axes.end());
+  axes.erase(std::unique(axes.begin(), axes.end()), axes.end());
+  const DType dt = n->dtype;
+  const Op rop = n->reduce_op;
+  std::string init = rop == Op::Add ? literal_of(0.0, dt) : literal_of(-INFINITY, dt);
+  std::string acc = fresh("acc");
+  line(std::string(ctype(dt)) + " " + acc + " = " + init + ";");
+  std::vector<std::string> sc = ctx;
+  sc.resize(ss.size(), "0");
+  size_t opened = 0;
+  for (size_t i = 0; i + 1 < axes.size(); i++) {
+    size_t a = (size_t)axes[i];
+    std::string r = fresh("r");
+    open("for (long long " + r + " = 0; " + r + " < " + std::to_string(ss[a]) + "LL; ++" + r +
+         ")");
+    opened++;
+    sc[a] = r;
+  }
+  auto combine = [&](const Val &x, const Val &y) {
+    // Reduce combination is built after symbolic folding in the reference,
+    // so it is never folded.
+    Val nx = x, ny = y;
+    nx.is_const = ny.is_const = false;
+    return emit_alu(rop, dt, {nx, ny});
+  };
+  size_t last = axes.empty() ? 0 : (size_t)axes.back();
+  int64_t R = axes.empty() ? 1 : ss[last];
+  if (!axes.empty() && R > 4 && R % 4 == 0) {
+    std::string r = fresh("r");
+    if (R / 4 > 8) line("#pragma unroll 4");
+    open("for (long long " + r + " = 0; " + r + " < " + std::to_string(R / 4) + "LL; ++" + r + ")");
+    opened++;
+    Val lanes[4];
+    for (int u = 0; u < 4; u++) {
+      sc[last] = idx(r + " * 4LL + " + std::to_string(u));
+      lanes[u] = value(s, sc);
+    }
+    Val h = combine(combine(combine(lanes[0], lanes[1]), lanes[2]), lanes[3]);
+    Val acc_v{acc, dt};
+    Val upd = combine(acc_v, h);
+    line(acc + " = " + upd.expr + ";");
+  } else if (!axes.empty() && R > 1) {
+    std::string r = fresh("r");
+    if (R > 8) line("#pragma unroll 4");
+    open("for (long long " + r + " = 0; " + r + " < " + std::to_string(R) + "LL; ++" + r + ")");
+    opened++;
+    sc[last] = r;
+    Val v = value(s, sc);
+    Val upd = combine(Val{acc, dt}, v);
+    line(acc + " = " + upd.expr + ";");
+  } else {
+    if (!axes.empty()) sc[last] = "0";
+    open_block();
+    opened++;
+    Val v = value(s, sc);
+    Val upd = combine(Val{acc, dt}, v);
+    line(acc + " = " + upd.expr + ";");
+  }
+  while (opened--) close();
+  return Val{acc, dt};
+}
+
+Val Emitter::value(const UOp *n, const std::vector<std::string> &ctx) {
+  if (n->op == Op::Const) return Val{literal_of(n->value, n->dtype), n->dtype, true, n->value};
+  std::string key = std::to_string((uintptr_t)n);
+  for (auto &c : ctx) key += "," + c;
+  Val m = lookup(key);
+  if (!m.expr.empty()) return m;
+  Val out;
+  switch (n->op) {
+    case Op::Buffer: {
+      int slot = ps_.buffer_slot.at(n->buf.get());
+      std::string i = ctx.empty() ? "0" : ctx[0];
+      std::string ld = "p" + std::to_string(slot) + "[" + i + "]";
+      if (n->dtype == DType::Bool) ld = "(" + ld + " != 0)";
+      out = bind(ld, n->dtype);
+      break;
+    }
+    case Op::Reshape:
+    case Op::Permute:
+    case Op::Expand:
+    case Op::Shrink:
+      out = value(n->src[0].get(), src_ctx(n, ctx));
+      break;
+    case Op::Contiguous:
+    case Op::After:
+      out = value(n->src[0].get(), ctx);
+      break;
+    case Op::ReduceAxis:
+      out = emit_reduce(n, ctx);
+      break;
+    default: {
+      if (!is_alu(n->op)) throw Panic(std::string("render: unsupported op ") + op_name(n->op));
+      std::vector<Val> a;
+      for (auto &s : n->src) a.push_back(value(s.get(), ctx));
+      out = emit_alu(n->op, n->dtype, a);
+      break;
+    }
+  }
+  if (!out.is_const) scopes_.back().vals[key] = out;
+  return out;
+}
+
+bool contains_reduce(const UOpP &root) {
+  for (auto &n : toposort(root))
+    if (n->op == Op::ReduceAxis) return true;
+  return false;
+}
+
+}  // namespace
+
+RenderedKernel render_kernel(const RenderSpec &spec) {
+  const bool store_view = spec.store == RenderSpec::View;
+  // Slot assignment as the reference parameterises (slot 0 = output for
+  // allocating kernels; the destination is a regular input for stores).
+  ParamSlots ps = store_view ? collect_params(make_store(spec.dest, spec.value), 0)
+                             : collect_params(spec.value, 1);
+  Emitter em(ps);
+  const Shape &D = spec.domain;
+  const int64_t N = numel(D);
+  const bool has_reduce = contains_reduce(spec.value);
+  const int U = has_reduce ? 1 : std::max(1, spec.unroll);
+  int dest_slot = -1;
+  if (store_view) {
+    const DeviceBuffer *db = nullptr;
+    std::vector<std::string> dummy(spec.dest->shape.size(), "0");
+    Emitter probe(ps);
+    probe.view_index(spec.dest.get(), dummy, &db);
+    dest_slot = ps.buffer_slot.at(db);
+  }
+
+  std::vector<int64_t> strides(D.size());
+  int64_t st = 1;
+  for (size_t a = D.size(); a-- > 0;) {
+    strides[a] = st;
+    st *= D[a];
+  }
+  const DType odt = store_view ? spec.dest->dtype : spec.out_dtype;
+  em.line("const long long e0 = (long long)blockIdx.x * " + std::to_string(256 * U) +
+          "LL + threadIdx.x;");
+  std::vector<std::string> res(U), sidx(U);
+  for (int u = 0; u < U; u++) {
+    res[u] = "res" + std::to_string(u);
+    sidx[u] = "st" + std::to_string(u);
+    em.line(std::string(ctype(store_view ? spec.value->dtype : spec.value->dtype)) + " " + res[u] +
+            " = " + literal_of(0.0, spec.value->dtype) + ";");
+    em.line("long long " + sidx[u] + " = -1;");
+  }
+  for (int u = 0; u < U; u++) {
+    std::string e = u == 0 ? "e0" : "(e0 + " + std::to_string(256 * u) + "LL)";
+    em.open("if (" + e + " < " + std::to_string(N) + "LL)");
+    std::string ev = em.idx(e);
+    std::vector<std::string> c(D.size(), "0");
+    bool first = true;
+    for (size_t a = 0; a < D.size(); a++) {
+      if (D[a] == 1) continue;
+      std::string x = strides[a] == 1 ? ev : "(" + ev + " / " + std::to_string(strides[a]) + "LL)";
+      if (!first) x = "(" + x + " % " + std::to_string(D[a]) + "LL)";
+      first = false;
+      c[a] = em.idx(x);
+    }
+    std::vector<std::string> vctx = c;
+    if (!spec.value_ctx.empty()) {
+      vctx.clear();
+      for (const std::string &t : spec.value_ctx) {
+        std::string x = t;
+        for (size_t a = D.size(); a-- > 0;) {
+          std::string name = "c" + std::to_string(a);
+          size_t pos;
+          while ((pos = x.find(name)) != std::string::npos) x.replace(pos, name.size(), c[a]);
+        }
+        vctx.push_back(em.idx(x));
+      }
+    }
+    Val v = em.value(spec.value.get(), vctx);
+    em.line(res[u] + " = " + v.expr + ";");
+    std::string s;
+    if (store_view) {
+      const DeviceBuffer *db = nullptr;
+      s = em.view_index(spec.dest.get(), c, &db);
+    } else if (spec.store == RenderSpec::Pitched) {
+      s = c.size() == 2 ? em.idx(mul_idx(c[0], spec.pitch) + " + " + c[1]) : ev;
+    } else {
+      s = ev;
+    }
+    em.line(sidx[u] + " = " + s + ";");
+    em.close();
+  }
+  const int out_slot = store_view ? dest_slot : 0;
+  for (int u = 0; u < U; u++) {
+    std::string val = odt == DType::Bool ? "(unsigned char)(" + res[u] + ")" : res[u];
+    em.line("if (" + sidx[u] + " >= 0) p" + std::to_string(out_slot) + "[" + sidx[u] + "] = " +
+            val + ";");
+  }
+
+  std::ostringstream src;
+  src << "// rendered by the ferrograd_b200 front end\n";
+  src << "#ifndef INFINITY\n#define INFINITY __int_as_float(0x7f800000)\n#endif\n"
+         "#ifndef NAN\n#define NAN __int_as_float(0x7fffffff)\n#endif\n";
+  src << "extern \"C\" __global__ void __launch_bounds__(256) fg_kernel(";
+  std::vector<std::string> params;
+  if (!store_view) params.push_back(std::string(storage_type(spec.out_dtype)) + "* __restrict__ p0");
+  const int off = store_view ? 0 : 1;
+  for (size_t i = 0; i < ps.inputs.size(); i++) {
+    const KernelInput &in = ps.inputs[i];
+    int slot = (int)i + off;
+    if (in.kind == KernelInput::Buffer) {
+      bool written = slot == out_slot;
+      params.push_back(std::string(written ? "" : "const ") + storage_type(in.buffer->dtype) +
+                       "* __restrict__ p" + std::to_string(slot));
+    } else {
+      params.push_back("int s" + std::to_string(slot));
+    }
+  }
+  for (size_t i = 0; i < params.size(); i++) src << (i ? ", " : "") << params[i];
+  src << ") {\n" << em.body.str() << "}\n";
+
+  RenderedKernel rk;
+  rk.source = src.str();
+  rk.block = 256;
+  int64_t blocks = (N + 256LL * U - 1) / (256LL * U);
+  rk.grid = (uint32_t)std::max<int64_t>(1, blocks);
+  rk.has_out_slot = !store_view;
+  rk.params = ps.inputs;
+  return rk;
+}
+
+}  // namespace ferro

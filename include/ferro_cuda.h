@@ -75,7 +75,9 @@ int fg_alloc(fg_device *dev, int dtype, size_t numel, fg_buffer **out);
 int fg_free(fg_buffer *buf);
 int fg_buffer_info(const fg_buffer *buf, void **d_ptr, int *dtype, size_t *numel);
 /* Device::copy_from_host (src/device.rs:294, src/device/cpu.rs:283-302):
- * fails with "copy_from_host: expected N bytes, got M" on a size mismatch. */
+ * fails with "copy_from_host: expected N bytes, got M" on a size mismatch.
+ * The copy is ordered on the device stream; h_src may be reused as soon as
+ * the call returns. */
 int fg_copy_h2d(fg_buffer *buf, const void *h_src, size_t nbytes);
 /* Device::copy_to_host (src/device.rs:302, src/device/cpu.rs:304-316):
  * synchronous, like the reference's Vec<u8> return. */

@@ -1,0 +1,247 @@
+"""The C++ lazy-Tensor front end on the GPU.
+
+* The reference's own tensor tests (src/tensor.rs:1128-1314,
+  src/optim.rs:73-95, src/nn.rs:106-162) with their known answers.
+* One MNIST-style training step (examples/mnist.rs:90-97) against the
+  oracle: with FG_FRONT_EXACT=1 every kernel is rendered with the reference's
+  arithmetic and the step must match the oracle bit for bit; in the default
+  mode contractions run on the 3xTF32 tensor cores and large sums on the HBM
+  reduction kernels, within the north star's 1e-4 (tests/mlp_check.py).
+"""
+import numpy as np
+import pytest
+
+from ferrograd_b200 import data, mlp_init
+from ferrograd_b200 import front as F
+from mlp_check import check_step
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4
+
+
+def normrel(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+# ------------------------------------------------- reference tensor tests
+def test_new_roundtrip():
+    t = F.tensor([1.0, 2.0, 3.0])
+    assert t.shape == (3,) and t.dtype == "f32" and t.is_realized()
+    assert t.to_vec() == [1.0, 2.0, 3.0]
+
+
+def test_add_mul_relu_realize():
+    a, b = F.tensor([1.0, 2.0, 3.0]), F.tensor([4.0, 5.0, 6.0])
+    assert a.add(b).to_vec() == [5.0, 7.0, 9.0]
+    assert F.tensor([2.0, 3.0, 4.0]).mul(F.tensor([5.0, 6.0, 7.0])).to_vec() == [10.0, 18.0, 28.0]
+    assert F.tensor([1.0, -2.0, 3.0, -4.0]).relu().to_vec() == [1.0, 0.0, 3.0, 0.0]
+
+
+def test_log_softmax_matches_known_values():
+    r = F.tensor(np.array([[0.0, 1.0]], np.float32)).log_softmax(1).realize().to_vec()
+    for a, e in zip(r, [-1.3132616, -0.31326166]):
+        assert abs(a - e) < 1e-5
+
+
+def test_cross_entropy_matches_one_hot_mean_loss():
+    logits = F.tensor(np.array([[2.0, 0.0], [0.0, 2.0]], np.float32))
+    targets = F.tensor(np.array([[1.0, 0.0], [0.0, 1.0]], np.float32))
+    loss = logits.cross_entropy(targets).realize().to_vec()[0]
+    assert abs(loss - 0.12692805) < 1e-5
+
+
+def test_sum_over_axis_zero_and_narrow_and_contiguous():
+    x = F.tensor(np.arange(1, 7, dtype=np.float32).reshape(2, 3))
+    assert x.sum([0]).realize().to_vec() == [5.0, 7.0, 9.0]
+    n = x.narrow(0, 1, 1)
+    assert n.shape == (1, 3) and n.to_vec() == [4.0, 5.0, 6.0]
+    c = x.permute([1, 0]).contiguous()
+    assert c.shape == (3, 2) and c.to_vec() == [1.0, 4.0, 2.0, 5.0, 3.0, 6.0]
+
+
+def test_gradients_skip_untracked_narrow_inputs():
+    x = F.tensor(np.array([[1.0, 2.0], [3.0, 4.0]], np.float32)).narrow(0, 1, 1)
+    w = F.tensor(np.array([[10.0], [20.0]], np.float32)).with_requires_grad(True)
+    (g,) = x.matmul(w).sum([0, 1]).gradient([w])
+    assert g.to_vec() == [3.0, 4.0] and not g.requires_grad()
+
+
+def test_gradients_flow_through_contiguous():
+    x = F.tensor(np.arange(1, 7, dtype=np.float32).reshape(2, 3)).with_requires_grad(True)
+    (g,) = x.permute([1, 0]).contiguous().sum([0, 1]).gradient([x])
+    assert g.to_vec() == [1.0] * 6
+
+
+def test_realize_idempotent_clone_shares_and_assign_in_place():
+    b = F.tensor([1.0, 2.0]).add(F.tensor([3.0, 4.0]))
+    assert b.realize().realize().to_vec() == [4.0, 6.0]
+    left = F.Tensor.zeros([2])
+    alias = left
+    left.replace(F.tensor([5.0, 7.0]))
+    assert alias.to_vec() == [5.0, 7.0]
+    t = F.tensor([1.0, 2.0])
+    t.assign(F.tensor([8.0, 9.0]))
+    F.Tensor.realize_many([t])
+    assert t.to_vec() == [8.0, 9.0]
+
+
+def test_backward_stores_gradients():
+    x = F.tensor([3.0]).with_requires_grad(True)
+    y = F.tensor([5.0]).with_requires_grad(True)
+    x.mul(y).sum([0]).backward()
+    assert x.grad().to_vec() == [5.0] and y.grad().to_vec() == [3.0]
+
+
+def test_new_infers_i32_and_bool():
+    assert F.tensor(np.array([1, 2, 3], np.int32)).realize().numpy().tolist() == [1, 2, 3]
+    assert F.tensor(np.array([True, False, True])).realize().numpy().tolist() == [True, False, True]
+
+
+def test_sgd_step_updates_parameter():
+    param = F.tensor([3.0]).with_requires_grad(True)
+    target = F.tensor([2.0])
+    d = param.sub(target)
+    loss = d.mul(param.sub(target)).sum([0])
+    opt = F.Sgd([param], 0.1)
+    opt.zero_grad()
+    loss.backward()
+    opt.step()
+    assert param.to_vec()[0] < 3.0
+
+
+def test_linear_forward_and_zero_bias():
+    layer = F.Linear(3, 2)
+    out = layer.forward(F.tensor(np.arange(1, 7, dtype=np.float32).reshape(2, 3)))
+    assert out.shape == (2, 2) and out.requires_grad()
+    assert F.Linear(4, 5).parameters()[1].to_vec() == [0.0] * 5
+
+
+def test_i32_reductions_are_exact():
+    x = np.random.default_rng(3).integers(-1000, 1000, size=(33, 40), dtype=np.int32)
+    t = F.tensor(x)
+    assert t.sum([1]).numpy().ravel().tolist() == x.sum(1).tolist()
+    assert t.max([0]).numpy().ravel().tolist() == x.max(0).tolist()
+
+
+# ---------------------------------------------------- the MNIST training step
+def front_step(dims, batch, lr, seeds, keep_acts=False):
+    x, t = data.mlp_batch(batch, dims[0], dims[-1], *seeds)
+    F.reset_init_seed(42)
+    model = F.Mlp(dims)
+    ws = [layer.weight.numpy() for layer in model.layers]
+    bs = [layer.bias.numpy() for layer in model.layers]
+    opt = F.Sgd(model.parameters(), lr)
+    xt, tt = F.tensor(x), F.tensor(t)
+    hs = []
+    h = xt
+    for i, layer in enumerate(model.layers):  # Mlp.forward, keeping activations
+        h = layer.forward(h)
+        if i + 1 < len(model.layers):
+            h = h.relu()
+            hs.append(h)
+    loss = h.cross_entropy(tt)
+    opt.zero_grad()
+    loss.backward()
+    grads = ([layer.weight.grad() for layer in model.layers],
+             [layer.bias.grad() for layer in model.layers])
+    opt.step()
+    lv = loss.to_vec()[0]
+    gw = [g.numpy() for g in grads[0]]
+    gb = [g.numpy().ravel() for g in grads[1]]
+    pw = [layer.weight.numpy() for layer in model.layers]
+    pb = [layer.bias.numpy() for layer in model.layers]
+    acts = [a.numpy() for a in hs]
+    return dict(x=x, t=t, ws=ws, bs=bs, loss=lv, grads=(gw, gb), params=(pw, pb), acts=acts)
+
+
+def test_front_init_matches_linear_init():
+    F.reset_init_seed(42)
+    model = F.Mlp((64, 32, 10))
+    ws, _ = mlp_init((64, 32, 10))
+    for layer, w in zip(model.layers, ws):
+        assert np.array_equal(layer.weight.numpy(), w)
+
+
+@pytest.mark.parametrize("dims,batch", [((784, 128, 10), 256), ((96, 64, 48, 10), 64)])
+def test_front_step_exact_mode_matches_oracle_bitwise(oracle, monkeypatch, dims, batch):
+    monkeypatch.setenv("FG_FRONT_EXACT", "1")
+    F.reset_stats()
+    r = front_step(dims, batch, 0.01, (1, 2))
+    assert F.stats()["gemm"] == 0 and F.stats()["hand_reduce"] == 0
+    oloss, ow, ob, odw, odb, _ = oracle.mlp_step(r["ws"], r["bs"], r["x"], r["t"], 0.01)
+    assert np.float32(r["loss"]) == np.float32(oloss)
+    gw, gb = r["grads"]
+    pw, pb = r["params"]
+    for l in range(len(dims) - 1):
+        assert np.array_equal(gw[l], odw[l]), (l, normrel(gw[l], odw[l]))
+        assert np.array_equal(gb[l], odb[l]), (l, normrel(gb[l], odb[l]))
+        assert np.array_equal(pw[l], ow[l]) and np.array_equal(pb[l], ob[l])
+
+
+@pytest.mark.parametrize("dims,batch", [((784, 128, 10), 256), ((512, 256, 256, 10), 384)])
+def test_front_step_default_mode_matches_oracle(oracle, monkeypatch, dims, batch):
+    monkeypatch.delenv("FG_FRONT_EXACT", raising=False)
+    F.reset_stats()
+    r = front_step(dims, batch, 0.01, (1, 2))
+    assert F.stats()["gemm"] > 0
+    oacts = []
+    out = oracle.mlp_step(r["ws"], r["bs"], r["x"], r["t"], 0.01, acts=oacts)
+    assert abs(r["loss"] - out[0]) <= TOL * abs(out[0])
+    check_step(r["ws"], r["bs"], r["x"], r["t"], 0.01, r["acts"], r["grads"], r["params"], out,
+               oacts, tol=TOL)
+
+
+def test_front_matmul_routes_and_transposes():
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal((384, 256), dtype=np.float32)
+    b = rng.standard_normal((256, 320), dtype=np.float32)
+    F.reset_stats()
+    c = F.tensor(a).matmul(F.tensor(b)).numpy()
+    assert F.stats()["gemm"] == 1
+    assert normrel(c, a.astype(np.float64) @ b) <= 1e-5
+
+
+def test_front_big_reductions_route_to_hand_kernels(oracle):
+    x = data.normal((2048, 1024), 6)
+    t = F.tensor(x)
+    F.reset_stats()
+    s_rows = t.sum([1]).numpy().ravel()
+    m_rows = t.max([1]).numpy().ravel()
+    s_cols = t.sum([0]).numpy().ravel()
+    assert F.stats()["hand_reduce"] == 3
+    assert normrel(s_rows, oracle.reduce_last(x, oracle.SUM)) <= TOL
+    assert np.array_equal(m_rows, oracle.reduce_last(x, oracle.MAX))
+    assert normrel(s_cols, oracle.reduce_axis0(x, oracle.SUM)) <= TOL
+
+
+def test_narrow_batches_reuse_compiled_kernels(monkeypatch):
+    """examples/mnist.rs slices batches with narrow(0, start, batch): the
+    start is a kernel argument, so later batches hit the program cache."""
+    monkeypatch.setenv("FG_FRONT_EXACT", "1")
+    rng = np.random.default_rng(9)
+    X = F.tensor(rng.random((512, 64), np.float32))
+    T = F.one_hot(rng.integers(0, 10, 512), 10)
+    F.reset_init_seed(42)
+    model = F.Mlp((64, 32, 10))
+    opt = F.Sgd(model.parameters(), 0.1)
+    losses = []
+    compiled = []
+    for i in range(4):
+        xb, tb = X.narrow(0, 128 * i, 128), T.narrow(0, 128 * i, 128)
+        losses.append(F.train_step(model, opt, xb, tb))
+        compiled.append(F.stats()["compiled"])
+    assert compiled[1] == compiled[2] == compiled[3]
+    assert all(np.isfinite(losses))
+
+
+def test_front_training_reduces_loss():
+    x, t = data.mlp_batch(256, 784, 10, 1, 2)
+    F.reset_init_seed(42)
+    model = F.Mlp((784, 128, 10))
+    opt = F.Sgd(model.parameters(), 0.1)
+    xt, tt = F.tensor(x), F.tensor(t)
+    losses = [F.train_step(model, opt, xt, tt) for _ in range(10)]
+    assert losses[-1] < losses[0]
