@@ -8,12 +8,15 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cooperative_groups.h>
 #include <mutex>
 
 #include "fg_internal.h"
 #include "fg_kernels.cuh"
 
 namespace fg {
+
+namespace cg = cooperative_groups;
 
 // Reference op semantics (src/codegen/clang.rs:216-229): max is a ternary,
 // every op rounds separately (no FMA contraction).
@@ -124,44 +127,82 @@ __device__ __forceinline__ T warp_reduce(T v) {
   return v;
 }
 
-template <typename T, int OP, bool VEC>
-__global__ void __launch_bounds__(256) k_reduce_rows(const T *__restrict__ x, T *__restrict__ out,
-                                                     size_t rows, size_t cols) {
+template <typename T, int OP>
+__device__ __forceinline__ T red4(const uint4 &u) {
+  const T *f = reinterpret_cast<const T *>(&u);
+  return red_op<OP>(red_op<OP>(f[0], f[1]), red_op<OP>(f[2], f[3]));
+}
+
+// One warp per row, 16-byte loads.  The row is walked in batches of kRowBatch
+// loads per lane, and the next batch is in flight while the current one is
+// folded, so each warp keeps its loads outstanding for the whole row instead
+// of draining at every batch; the grid is a fixed multiple of the SM count
+// and warps stride over the rows.
+constexpr int kRowBatch = 8;
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(128) k_reduce_rows_v4(const T *__restrict__ x, T *__restrict__ out,
+                                                        size_t rows, size_t cols) {
+  const int lane = threadIdx.x & 31;
+  size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const size_t wstride = (size_t)gridDim.x * (blockDim.x >> 5);
+  const size_t nv = cols / 4;  // 16-byte vectors per row
+  const T id = red_identity<T, OP>();
+  const uint4 idv = [&] {
+    uint4 v;
+    T *f = reinterpret_cast<T *>(&v);
+    f[0] = f[1] = f[2] = f[3] = id;
+    return v;
+  }();
+  for (; row < rows; row += wstride) {
+    const uint4 *pv = reinterpret_cast<const uint4 *>(x + row * cols);
+    T acc0 = id, acc1 = id;
+    uint4 cur[kRowBatch];
+#pragma unroll
+    for (int k = 0; k < kRowBatch; k++) {
+      const size_t j = lane + 32 * (size_t)k;
+      cur[k] = j < nv ? __ldcs(pv + j) : idv;
+    }
+    for (size_t base = 32 * kRowBatch; base < nv + 32 * kRowBatch; base += 32 * kRowBatch) {
+      uint4 nxt[kRowBatch];
+      const bool more = base < nv;
+      if (more) {
+#pragma unroll
+        for (int k = 0; k < kRowBatch; k++) {
+          const size_t j = base + lane + 32 * (size_t)k;
+          nxt[k] = j < nv ? __ldcs(pv + j) : idv;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kRowBatch; k++) {
+        const T g = red4<T, OP>(cur[k]);
+        if (k & 1)
+          acc1 = red_op<OP>(acc1, g);
+        else
+          acc0 = red_op<OP>(acc0, g);
+      }
+      if (!more) break;
+#pragma unroll
+      for (int k = 0; k < kRowBatch; k++) cur[k] = nxt[k];
+    }
+    T acc = warp_reduce<T, OP>(red_op<OP>(acc0, acc1));
+    if (lane == 0) out[row] = acc;
+  }
+}
+
+// Rows whose length is not a multiple of 4 (or unaligned): scalar loads.
+template <typename T, int OP>
+__global__ void __launch_bounds__(128) k_reduce_rows_scalar(const T *__restrict__ x,
+                                                            T *__restrict__ out, size_t rows,
+                                                            size_t cols) {
   const int lane = threadIdx.x & 31;
   size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const size_t wstride = (size_t)gridDim.x * (blockDim.x >> 5);
   for (; row < rows; row += wstride) {
     const T *p = x + row * cols;
-    T acc0 = red_identity<T, OP>(), acc1 = red_identity<T, OP>();
-    if (VEC) {
-      using V = typename std::conditional<sizeof(T) == 4, uint4, uint4>::type;
-      const size_t nv = cols / 4;
-      const V *pv = reinterpret_cast<const V *>(p);
-      size_t j = lane;
-      // sixteen independent 16-byte loads in flight per lane
-      for (; j + 15 * 32 < nv; j += 16 * 32) {
-        V u[16];
-#pragma unroll
-        for (int k = 0; k < 16; k++) u[k] = __ldcs(pv + j + 32 * k);
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-          const T *f = reinterpret_cast<const T *>(&u[k]);
-          T g = red_op<OP>(red_op<OP>(f[0], f[1]), red_op<OP>(f[2], f[3]));
-          if (k & 1)
-            acc1 = red_op<OP>(acc1, g);
-          else
-            acc0 = red_op<OP>(acc0, g);
-        }
-      }
-      for (; j < nv; j += 32) {
-        V u0 = __ldcs(pv + j);
-        const T *f0 = reinterpret_cast<const T *>(&u0);
-        acc0 = red_op<OP>(acc0, red_op<OP>(red_op<OP>(f0[0], f0[1]), red_op<OP>(f0[2], f0[3])));
-      }
-    } else {
-      for (size_t j = lane; j < cols; j += 32) acc0 = red_op<OP>(acc0, p[j]);
-    }
-    T acc = warp_reduce<T, OP>(red_op<OP>(acc0, acc1));
+    T acc = red_identity<T, OP>();
+    for (size_t j = lane; j < cols; j += 32) acc = red_op<OP>(acc, p[j]);
+    acc = warp_reduce<T, OP>(acc);
     if (lane == 0) out[row] = acc;
   }
 }
@@ -169,13 +210,12 @@ __global__ void __launch_bounds__(256) k_reduce_rows(const T *__restrict__ x, T 
 template <typename T, int OP>
 static int launch_rows_t(const void *x, void *out, size_t rows, size_t cols, cudaStream_t st) {
   const bool vec = (cols % 4 == 0) && aligned16(x);
-  // 4 warps per block: blocks are the unit the scheduler balances across
-  // SMs, and small blocks keep the per-SM row count within ~1% of the mean.
-  int grid = grid_for(rows * 32, 128, 64);
+  // 4 warps per block, 8 blocks per SM: every warp strides over rows.
+  int grid = grid_for(rows * 32, 128, 8);
   if (vec)
-    k_reduce_rows<T, OP, true><<<grid, 128, 0, st>>>((const T *)x, (T *)out, rows, cols);
+    k_reduce_rows_v4<T, OP><<<grid, 128, 0, st>>>((const T *)x, (T *)out, rows, cols);
   else
-    k_reduce_rows<T, OP, false><<<grid, 128, 0, st>>>((const T *)x, (T *)out, rows, cols);
+    k_reduce_rows_scalar<T, OP><<<grid, 128, 0, st>>>((const T *)x, (T *)out, rows, cols);
   FG_LAUNCH_TRY();
   return FG_OK;
 }
@@ -272,6 +312,88 @@ __global__ void __launch_bounds__(256) k_reduce_cols_final(const T *__restrict__
   out[col] = acc;
 }
 
+// Wide column reductions in one kernel: a CTA owns a strip of 128 columns
+// (a warp row of 16-byte loads) and one of kColChunks row chunks; the
+// chunks of a strip form a thread-block cluster and fold their partial sums
+// through distributed shared memory, rank 0 adding them in chunk order
+// (deterministic).  No scratch, no second launch.
+constexpr int kColChunks = 8;
+constexpr int kColWarps = 16;
+
+template <typename T, int OP>
+__global__ void __cluster_dims__(1, kColChunks, 1) __launch_bounds__(kColWarps * 32)
+    k_reduce_cols_cluster(const T *__restrict__ x, T *__restrict__ out, size_t rows, size_t cols) {
+  __shared__ uint4 wpart[kColWarps][32];
+  __shared__ uint4 cpart[32];
+  cg::cluster_group cl = cg::this_cluster();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t col = (size_t)blockIdx.x * 128 + (size_t)lane * 4;
+  const bool active = col < cols;
+  const size_t chunk = (rows + kColChunks - 1) / kColChunks;
+  const size_t r0 = (size_t)blockIdx.y * chunk;
+  const size_t r1 = r0 + chunk < rows ? r0 + chunk : rows;
+  const T id = red_identity<T, OP>();
+  T a[4] = {id, id, id, id}, b[4] = {id, id, id, id};
+  size_t r = r0 + warp;
+  if (active) {
+    for (; r + 7 * kColWarps < r1; r += 8 * kColWarps) {
+      uint4 u[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++)
+        u[k] = __ldcs(reinterpret_cast<const uint4 *>(x + (r + k * kColWarps) * cols + col));
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const T *f = reinterpret_cast<const T *>(&u[k]);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          if (k & 1)
+            b[q] = red_op<OP>(b[q], f[q]);
+          else
+            a[q] = red_op<OP>(a[q], f[q]);
+        }
+      }
+    }
+    for (; r < r1; r += kColWarps) {
+      uint4 u = __ldcs(reinterpret_cast<const uint4 *>(x + r * cols + col));
+      const T *f = reinterpret_cast<const T *>(&u);
+#pragma unroll
+      for (int q = 0; q < 4; q++) a[q] = red_op<OP>(a[q], f[q]);
+    }
+  }
+  {
+    uint4 v;
+    T *f = reinterpret_cast<T *>(&v);
+#pragma unroll
+    for (int q = 0; q < 4; q++) f[q] = red_op<OP>(a[q], b[q]);
+    wpart[warp][lane] = v;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint4 v = wpart[0][lane];
+    T *s = reinterpret_cast<T *>(&v);
+    for (int w = 1; w < kColWarps; w++) {
+      const T *f = reinterpret_cast<const T *>(&wpart[w][lane]);
+#pragma unroll
+      for (int q = 0; q < 4; q++) s[q] = red_op<OP>(s[q], f[q]);
+    }
+    cpart[lane] = v;
+  }
+  cl.sync();
+  if (cl.block_rank() == 0 && warp == 0) {
+    uint4 v = cpart[lane];
+    T *s = reinterpret_cast<T *>(&v);
+    for (unsigned q = 1; q < (unsigned)kColChunks; q++) {
+      const uint4 *rp = cl.map_shared_rank(cpart, q);
+      uint4 w = rp[lane];
+      const T *f = reinterpret_cast<const T *>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; e++) s[e] = red_op<OP>(s[e], f[e]);
+    }
+    if (active) *reinterpret_cast<uint4 *>(out + col) = v;
+  }
+  cl.sync();  // keep every CTA's shared memory alive until rank 0 has read it
+}
+
 template <typename T, int OP>
 static int launch_cols_t(const void *x, void *out, size_t rows, size_t cols, cudaStream_t st,
                          void *scratch, size_t scratch_bytes) {
@@ -284,6 +406,16 @@ static int launch_cols_t(const void *x, void *out, size_t rows, size_t cols, cud
   size_t col_tiles = (cols + kColTile - 1) / kColTile;
   DevCtx *c = ctx_current();
   size_t sms = (c && c->num_sms) ? c->num_sms : 148;
+  // Wide inputs: the single-kernel cluster reduction, once its strips x
+  // chunks cover every SM and each chunk has rows to stream.
+  const size_t strips = (cols + 127) / 128;
+  if (cols % 4 == 0 && aligned16(x) && aligned16(out) && strips * kColChunks >= sms &&
+      rows >= (size_t)kColChunks * kColWarps) {
+    dim3 g((unsigned)strips, kColChunks);
+    k_reduce_cols_cluster<T, OP><<<g, kColWarps * 32, 0, st>>>((const T *)x, (T *)out, rows, cols);
+    FG_LAUNCH_TRY();
+    return FG_OK;
+  }
   // Enough chunks that col_tiles * nchunks fills every SM ~16 times, each
   // chunk at least 32 rows.
   size_t nchunks = (sms * 16 + col_tiles - 1) / col_tiles;
@@ -366,30 +498,58 @@ __device__ __forceinline__ float warp_max(float v) {
 // L1 (the row was read moments before with L1 caching).  That keeps the
 // kernel at ~60 registers, 4 blocks (32 warps) per SM.
 template <int NV>
-__global__ void __launch_bounds__(256) k_xent_rows_v4(const float *__restrict__ x,
+__global__ void __launch_bounds__(256, 1) k_xent_rows_v4(const float *__restrict__ x,
                                                       const float *__restrict__ t,
                                                       float *__restrict__ dx,
-                                                      float *__restrict__ row_loss, size_t rows,
+                                                      float *__restrict__ warp_loss, size_t rows,
                                                       int cols, float inv_n, float gscale) {
   const int lane = threadIdx.x & 31;
   size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const size_t wstride = (size_t)gridDim.x * (blockDim.x >> 5);
   const int nv = cols / 4;
-  for (; row < rows; row += wstride) {
+  const size_t gwarp = row;
+  float wloss = 0.f;  // this warp's rows' losses, summed in row order
+  // Software pipeline: the next row's logits and targets are loaded while
+  // the current row is reduced and its gradient written.
+  float4 xn[NV], tn[NV];
+  if (row < rows) {
     const float4 *xv = reinterpret_cast<const float4 *>(x + row * (size_t)cols);
     const float4 *tv = reinterpret_cast<const float4 *>(t + row * (size_t)cols);
-    float4 xr[NV];
-    float m = -INFINITY, st_ = 0.f, stx = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV; i++) {
-      int j = lane + 32 * i;
-      if (j < nv) xr[i] = __ldcs(xv + j);
-    }
 #pragma unroll
     for (int i = 0; i < NV; i++) {
       int j = lane + 32 * i;
       if (j < nv) {
-        const float4 tt = __ldg(tv + j);
+        xn[i] = __ldcs(xv + j);
+        tn[i] = __ldcs(tv + j);
+      }
+    }
+  }
+  for (; row < rows; row += wstride) {
+    float4 xr[NV], tr[NV];
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      xr[i] = xn[i];
+      tr[i] = tn[i];
+    }
+    const size_t nrow = row + wstride;
+    if (nrow < rows) {
+      const float4 *xv = reinterpret_cast<const float4 *>(x + nrow * (size_t)cols);
+      const float4 *tv = reinterpret_cast<const float4 *>(t + nrow * (size_t)cols);
+#pragma unroll
+      for (int i = 0; i < NV; i++) {
+        int j = lane + 32 * i;
+        if (j < nv) {
+          xn[i] = __ldcs(xv + j);
+          tn[i] = __ldcs(tv + j);
+        }
+      }
+    }
+    float m = -INFINITY, st_ = 0.f, stx = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      int j = lane + 32 * i;
+      if (j < nv) {
+        const float4 tt = tr[i];
         m = ref_max(m, ref_max(ref_max(xr[i].x, xr[i].y), ref_max(xr[i].z, xr[i].w)));
         st_ += (tt.x + tt.y) + (tt.z + tt.w);
         stx += __fmul_rn(tt.x, xr[i].x) + __fmul_rn(tt.y, xr[i].y) + __fmul_rn(tt.z, xr[i].z) +
@@ -439,7 +599,7 @@ __global__ void __launch_bounds__(256) k_xent_rows_v4(const float *__restrict__ 
       for (int i = 0; i < NV; i++) {
         int j = lane + 32 * i;
         if (j < nv) {
-          const float4 tt = __ldg(tv + j);
+          const float4 tt = tr[i];
           const float *te = reinterpret_cast<const float *>(&tt);
           const float *e = reinterpret_cast<const float *>(&xr[i]);
           float4 o;
@@ -455,20 +615,23 @@ __global__ void __launch_bounds__(256) k_xent_rows_v4(const float *__restrict__ 
         }
       }
     }
-    if (lane == 0) row_loss[row] = nps;
+    wloss += nps;
   }
+  if (lane == 0 && gwarp < rows) warp_loss[gwarp] = wloss;
 }
 
 // Generic path (any cols): three sweeps over the row from global memory.
 __global__ void __launch_bounds__(256) k_xent_rows_generic(const float *__restrict__ x,
                                                            const float *__restrict__ t,
                                                            float *__restrict__ dx,
-                                                           float *__restrict__ row_loss,
+                                                           float *__restrict__ warp_loss,
                                                            size_t rows, int cols, float inv_n,
                                                            float gscale) {
   const int lane = threadIdx.x & 31;
   size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const size_t wstride = (size_t)gridDim.x * (blockDim.x >> 5);
+  const size_t gwarp = row;
+  float wloss = 0.f;
   for (; row < rows; row += wstride) {
     const float *xr = x + row * (size_t)cols;
     const float *tr = t + row * (size_t)cols;
@@ -509,19 +672,21 @@ __global__ void __launch_bounds__(256) k_xent_rows_generic(const float *__restri
         dx[row * (size_t)cols + c] = __fadd_rn(gs, __fmul_rn(mask, wmax));
       }
     }
-    if (lane == 0) row_loss[row] = nps;
+    wloss += nps;
   }
+  if (lane == 0 && gwarp < rows) warp_loss[gwarp] = wloss;
 }
 
 // Sum of the row loss terms in a fixed order (one block, strided partials
 // combined by a fixed tree), times 1/B.
-__global__ void __launch_bounds__(1024) k_xent_loss_final(const float *__restrict__ row_loss,
-                                                          size_t rows, float inv_n,
+// Sums the per-warp loss partials (count of them, in warp order).
+__global__ void __launch_bounds__(1024) k_xent_loss_final(const float *__restrict__ warp_loss,
+                                                          size_t count, float inv_n,
                                                           float *__restrict__ loss,
                                                           float loss_scale) {
   __shared__ float sh[32];
   float acc = 0.f;
-  for (size_t r = threadIdx.x; r < rows; r += blockDim.x) acc += row_loss[r];
+  for (size_t r = threadIdx.x; r < count; r += blockDim.x) acc += warp_loss[r];
   acc = warp_sum(acc);
   if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
   __syncthreads();
@@ -530,6 +695,12 @@ __global__ void __launch_bounds__(1024) k_xent_loss_final(const float *__restric
     v = warp_sum(v);
     if (threadIdx.x == 0) loss[0] = __fmul_rn(__fmul_rn(v, inv_n), loss_scale);
   }
+}
+
+// Number of per-warp partials a row kernel of `grid` 256-thread blocks writes.
+static size_t xent_partials(int grid, size_t rows) {
+  size_t w = (size_t)grid * 8;
+  return w < rows ? w : rows;
 }
 
 int launch_xent(const float *x, const float *t, size_t rows, size_t cols, float *loss, float *dx,
@@ -570,7 +741,8 @@ int launch_xent(const float *x, const float *t, size_t rows, size_t cols, float 
   else
     k_xent_rows_generic<<<grid, 256, 0, st>>>(x, t, dx, scratch, rows, c, inv_n, gscale);
   FG_LAUNCH_TRY();
-  k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, rows, inv_n, loss, loss_scale);
+  k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, xent_partials(grid, rows), inv_n, loss,
+                                        loss_scale);
   FG_LAUNCH_TRY();
   return FG_OK;
 }
@@ -781,7 +953,8 @@ int fg_xent_fwd_bwd_noalloc(const float *d_logits, const float *d_targets, size_
   else
     fg::k_xent_rows_generic<<<grid, 256, 0, st>>>(d_logits, d_targets, d_dx, scratch, rows, c, inv_n, grad_scale);
   FG_LAUNCH_TRY();
-  fg::k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, rows, inv_n, d_loss, 1.0f);
+  fg::k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, fg::xent_partials(grid, rows), inv_n,
+                                            d_loss, 1.0f);
   FG_LAUNCH_TRY();
   return FG_OK;
 }

@@ -207,6 +207,14 @@ PYBIND11_MODULE(_front, m) {
   m.def("init_seed", &init_seed);
   m.def("set_device", &set_device);
   m.def("synchronize", &synchronize);
+  m.def(
+      "stream",
+      []() {
+        void *st = nullptr;
+        if (fg_device_stream(device(), &st) != FG_OK) throw Panic(fg_last_error());
+        return (uintptr_t)st;
+      },
+      "CUDA stream (as an integer handle) the front end launches on.");
   m.def("exact_mode", &exact_mode);
   m.def("last_source", []() { return last_source(); });
   m.def("reset_stats", &reset_stats);

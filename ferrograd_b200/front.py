@@ -34,6 +34,7 @@ reset_init_seed = _front.reset_init_seed
 init_seed = _front.init_seed
 set_device = _front.set_device
 synchronize = _front.synchronize
+stream = _front.stream
 schedule = _front.schedule
 schedule_uops = _front.schedule_uops
 stats = _front.stats
@@ -42,7 +43,7 @@ last_source = _front.last_source
 exact_mode = _front.exact_mode
 
 __all__ = ["Tensor", "Linear", "Sgd", "UOp", "Mlp", "reset_init_seed", "init_seed",
-           "set_device", "synchronize", "schedule", "schedule_uops", "stats", "reset_stats",
+           "set_device", "synchronize", "stream", "schedule", "schedule_uops", "stats", "reset_stats",
            "last_source", "exact_mode", "tensor", "one_hot"]
 
 
