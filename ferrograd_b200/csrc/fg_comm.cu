@@ -112,6 +112,18 @@ int comm_allreduce_sum(fg_comm *c, float *buf, size_t count, cudaStream_t st) {
 
 int comm_nranks(const fg_comm *c) { return c ? c->nranks : 1; }
 
+// The backward GEMMs of config 5 have 128 x (a power of two) output tiles
+// at every rank count, so a persistent grid of num_SMs - 20 = 128 CTAs on a
+// B200 loses nothing to tile quantisation, and the 20 SMs it leaves free
+// run the all-reduce beside it.  The collective must then fit in those SMs:
+// a wider one would take SMs the GEMM's 128 CTAs need and push some of its
+// tiles into a second wave.
+int comm_sm_reserve() {
+  const char *e = getenv("FG_COMM_SM_RESERVE");
+  int v = e && *e ? atoi(e) : kCommSmReserve;
+  return v < 0 ? 0 : (v > 64 ? 64 : v);
+}
+
 }  // namespace fg
 
 extern "C" {
@@ -138,6 +150,7 @@ int fg_comm_init(int rank, int nranks, const char uid[FG_UNIQUE_ID_BYTES], int t
   memcpy(&id, uid, sizeof(id));
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
+  if (fg::comm_sm_reserve() > 0) cfg.maxCTAs = fg::comm_sm_reserve();
   fg_comm *c = new fg_comm{nullptr, rank, nranks, timeout_ms > 0 ? timeout_ms : 60000};
   ncclResult_t r = fg::nccl()->commInitRankConfig(&c->comm, nranks, id, rank, &cfg);
   int rc = (r == ncclSuccess || r == ncclInProgress) && c->comm

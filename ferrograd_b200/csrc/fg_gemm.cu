@@ -24,6 +24,8 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "fg_gemm.cuh"
 #include "fg_internal.h"
@@ -78,6 +80,67 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// A CTA's work: its whole tiles (data-parallel waves), then its contiguous
+// share of the stream-K units (k-blocks of the tail tiles in (tile, k)
+// order), walked from its end to its start.  All three warp roles walk the
+// same sequence of segments.
+//
+// Walking backwards makes every dependency short: the segment a CTA takes
+// first is the head of a tile whose last k-block lies in a later CTA's
+// range, and it leaves a partial; the segment it takes last is the tail of
+// the tile its range starts in, and it finishes that tile, adding the
+// partials that earlier CTAs produced at the start of their own walks.
+struct Seg {
+  int tile, k0, k1;
+};
+
+__device__ __forceinline__ long long sk_begin(const GemmParams &p, int c) {
+  return p.sk_units * (long long)c / (long long)gridDim.x;
+}
+
+struct SegIter {
+  int next_dp, dp_tiles, nk;
+  long long lo, hi;  // SK units still to walk: [lo, hi), taken from hi down
+  __device__ SegIter(const GemmParams &p, int nk_)
+      : next_dp(blockIdx.x), dp_tiles(p.dp_tiles), nk(nk_), lo(sk_begin(p, blockIdx.x)),
+        hi(sk_begin(p, blockIdx.x + 1)) {}
+  __device__ bool next(Seg &s) {
+    if (next_dp < dp_tiles) {
+      s.tile = next_dp;
+      s.k0 = 0;
+      s.k1 = nk;
+      next_dp += gridDim.x;
+      return true;
+    }
+    if (hi <= lo) return false;
+    const long long t = (hi - 1) / nk;
+    const long long t0 = t * nk;
+    const long long b = lo > t0 ? lo : t0;
+    s.tile = dp_tiles + (int)t;
+    s.k0 = (int)(b - t0);
+    s.k1 = (int)(hi - t0);
+    hi = b;
+    return true;
+  }
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Bounded wait (~1 s of SM clocks) for a stream-K partial's flag.
+__device__ __forceinline__ bool wait_flag(const unsigned int *flag, unsigned int *err) {
+  const long long t0 = clock64();
+  for (;;) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v) return true;
+    if (clock64() - t0 > 2000000000LL) {
+      if (err) atomicOr(err, kErrEpilogue | 3u);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
 // Persistent: one CTA per SM loops over output tiles.  The accumulator lives
 // in one of two TMEM buffers (2 x BN columns): while the epilogue warps drain
 // tile i from one buffer, the MMA warp already accumulates tile i+1 in the
@@ -102,7 +165,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = (p.N + BN - 1) / BN;
-  const int ntiles = num_m * num_n;
   const int nk = (p.K + BK - 1) / BK;
   const bool three = !p.one_pass;
 
@@ -137,13 +199,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer ----------------
       const uint32_t stage_tx = three ? (uint32_t)C::STAGE_BYTES
                                       : (uint32_t)(C::A_BYTES + C::B_BYTES);
-      int it = 0;  // k-blocks issued so far, across tiles
+      int it = 0;  // k-blocks issued so far, across segments
       bool ok = true;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+      SegIter segs(p, nk);
+      Seg sg;
+      while (ok && segs.next(sg)) {
         int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
+        tile_coords(sg.tile, num_m, num_n, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
-        for (int kb = 0; kb < nk; kb++, it++) {
+        for (int kb = sg.k0; kb < sg.k1; kb++, it++) {
           const int s = it % C::STAGES;
           if (it >= C::STAGES) {
             ok = mbar_wait(&empty[s], ((it / C::STAGES) - 1) & 1, p.err, kErrProducer | 1);
@@ -207,7 +271,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t b_lay = B_MN ? kLayoutSw128Base32 : kLayoutSw128;
       bool ok = true;
       int it = 0, local = 0;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, local++) {
+      SegIter segs(p, nk);
+      Seg sg;
+      for (; ok && segs.next(sg); local++) {
         const int acc_buf = local & 1;
         if (local >= 2) {
           ok = mbar_wait(&tmem_empty[acc_buf], ((local >> 1) - 1) & 1, p.err, kErrMma | 2);
@@ -215,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc_buf * BN);
-        for (int kb = 0; kb < nk; kb++, it++) {
+        for (int kb = sg.k0; kb < sg.k1; kb++, it++) {
           const int s = it % C::STAGES;
           ok = mbar_wait(&full[s], (it / C::STAGES) & 1, p.err, kErrMma | 1);
           if (!ok) break;
@@ -228,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < BK / UMMA_K; kk++) {
             const uint64_t da = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_lay);
             const uint64_t db = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_lay);
-            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > sg.k0 || kk > 0) ? 1u : 0u;
             if (three) {
               const uint64_t dalo = smem_desc(salo + kk * a_kstep, a_lbo, a_sbo, a_lay);
               const uint64_t dblo = smem_desc(sblo + kk * b_kstep, b_lbo, b_sbo, b_lay);
@@ -252,26 +318,75 @@ __global__ void __launch_bounds__(kThreads, 1)
                      (!p.C_lo || (((uintptr_t)p.C_lo) & 15) == 0) &&
                      (!p.mask || (((p.ldmask & 3) == 0) && (((uintptr_t)p.mask) & 15) == 0));
     int local = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, local++) {
+    const int trow = 32 * q + lane;  // this thread's row within the tile
+    // After a timed-out wait the warp stops touching TMEM and memory but
+    // still takes every named barrier, so the other epilogue warps never
+    // wait on a barrier this warp skipped.
+    bool dead = false;
+    SegIter segs(p, nk);
+    Seg sg;
+    for (; segs.next(sg); local++) {
       int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+      tile_coords(sg.tile, num_m, num_n, mb, nb);
       const int m0 = mb * BM, n0 = nb * BN;
       const int acc_buf = local & 1;
       const int row = m0 + 32 * q + lane;
-      if (!mbar_wait(&tmem_full[acc_buf], (local >> 1) & 1, p.err, kErrEpilogue | 1)) break;
+      // Stream-K roles: a segment without the tile's last k-block leaves a
+      // partial (it is the first segment its CTA walks); one with the last
+      // k-block but not the first finishes the tile, adding the partials of
+      // the CTAs below it that cover the tile's earlier k-blocks (the last
+      // segment its CTA walks, so they are ready).
+      const bool partial_out = sg.k1 < nk;
+      const bool finisher = sg.k1 == nk && sg.k0 > 0;
+      int c_lo = 0;  // contributors c_lo .. blockIdx.x-1, added from the top down
+      if (finisher) {
+        const long long tile_start = (long long)(sg.tile - p.dp_tiles) * nk;
+        c_lo = blockIdx.x - 1;
+        while (c_lo > 0 && sk_begin(p, c_lo) > tile_start) c_lo--;
+        if (threadIdx.x == 64 && !dead)
+          for (int c = (int)blockIdx.x - 1; c >= c_lo; c--)
+            if (!wait_flag(p.sk_flags + c, p.err)) break;
+        epi_bar();
+        __threadfence();  // the partial loads below stay after the acquire
+      }
+      if (!dead && !mbar_wait(&tmem_full[acc_buf], (local >> 1) & 1, p.err, kErrEpilogue | 1))
+        dead = true;
       tc_fence_after();
+      float *my_ws = partial_out ? p.sk_ws + (size_t)blockIdx.x * (BM * BN) + (size_t)trow * BN
+                                 : nullptr;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = 0; c0 < BN && !dead; c0 += 32) {
         uint32_t r[32];
         __syncwarp();
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc_buf * BN + c0),
                            r);
         tmem_ld_wait();
+        if (partial_out) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            __stcg(reinterpret_cast<float4 *>(my_ws + c0 + j),
+                   make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                               __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])));
+          continue;
+        }
         if (row >= p.M || n0 + c0 >= p.N) continue;
         float v[32];
         const int col0 = n0 + c0;
 #pragma unroll
         for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+        if (finisher) {
+          for (int c = (int)blockIdx.x - 1; c >= c_lo; c--) {
+            const float *w = p.sk_ws + (size_t)c * (BM * BN) + (size_t)trow * BN + c0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 u = __ldcg(reinterpret_cast<const float4 *>(w + j));
+              v[j] = __fadd_rn(v[j], u.x);
+              v[j + 1] = __fadd_rn(v[j + 1], u.y);
+              v[j + 2] = __fadd_rn(v[j + 2], u.z);
+              v[j + 3] = __fadd_rn(v[j + 3], u.w);
+            }
+          }
+        }
         if (p.epilogue == FG_EPI_BIAS || p.epilogue == FG_EPI_BIAS_RELU) {
 #pragma unroll
           for (int j = 0; j < 32; j++) {
@@ -311,7 +426,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // every TMEM load of this buffer has completed (tcgen05.wait::ld above)
       tc_fence_before();
-      mbar_arrive(&tmem_empty[acc_buf]);
+      if (!dead) mbar_arrive(&tmem_empty[acc_buf]);
+      if (partial_out) {
+        // publish: every thread's stores, then one release of the flag
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          __threadfence();
+          asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.sk_flags + blockIdx.x),
+                       "r"(1u)
+                       : "memory");
+        }
+      } else if (finisher) {
+        epi_bar();  // all partials read
+        if (threadIdx.x == 64)
+          for (int c = (int)blockIdx.x - 1; c >= c_lo; c--) p.sk_flags[c] = 0u;
+      }
     }
   }
 
@@ -381,6 +511,64 @@ static int make_map_mn3d(CUtensorMap *map, const float *ptr, int mn, int K, int 
   return r == CUDA_SUCCESS ? FG_OK : FG_ERR_UNSUPPORTED;
 }
 
+// Splits a launch into whole-tile waves and a stream-K tail; returns the
+// grid.  Whole waves keep the grouped tile order (operand panels shared in
+// L2); only the last, partial wave's tiles are cut into k-ranges, so every
+// CTA ends at the same k-block count instead of a fraction of the SMs
+// running one more tile.  Used only when whole waves would waste >= 5% (a
+// 1024-tile grid on 148 SMs wastes 1%: measured slower with the split).  A
+// tail share under 1/4 tile per CTA borrows the previous whole wave; the
+// grid shrinks so that every CTA gets >= max(nk/8, 24) k-blocks, and below
+// one CTA per tail tile the split is not used.
+static int plan_stream_k(GemmParams &p, int ntiles, int nk, int cap, float *ws,
+                         unsigned int *flags) {
+  p.dp_tiles = ntiles;
+  p.sk_units = 0;
+  p.sk_ws = ws;
+  p.sk_flags = flags;
+  int grid = ntiles < cap ? ntiles : cap;
+  static const int mode = [] {
+    const char *e = getenv("FG_GEMM_STREAM_K");
+    return e && *e ? atoi(e) : 1;
+  }();
+  if (mode == 0 || !ws || !flags || nk < 8 || ntiles % cap == 0) return grid;
+  // Only when whole-tile waves would leave enough of the last wave idle.
+  static const double min_gain = [] {
+    const char *e = getenv("FG_GEMM_STREAM_K_MIN_GAIN");
+    return e && *e ? atof(e) : 0.05;
+  }();
+  const double waves = (double)ntiles / cap;
+  const double whole = (double)((ntiles + cap - 1) / cap);
+  if (whole / waves - 1.0 < min_gain) return grid;
+  long long full = ntiles / cap;
+  long long units = (long long)(ntiles - full * cap) * nk;
+  if (full >= 1 && units < (long long)cap * (nk / 4)) {
+    full -= 1;
+    units += (long long)cap * nk;
+  }
+  // Each partial costs about one epilogue pass (~2-3 k-blocks of MMA time),
+  // so a CTA's share must be long enough to amortise it.
+  const long long min_share = nk / 8 > 24 ? nk / 8 : 24;
+  long long g = units / min_share;
+  if (g > cap) g = cap;
+  if (full > 0 && g < cap) return grid;  // waves need the whole grid
+  if (g <= ntiles - full * cap) return grid;  // no better than whole tiles
+  p.dp_tiles = (int)(full * cap);
+  p.sk_units = units;
+  return (int)g;
+}
+
+size_t stream_k_ws_bytes(int ctas) {
+  return (size_t)ctas * BM * 256 * sizeof(float) + (size_t)ctas * sizeof(unsigned int) + 256;
+}
+
+void stream_k_attach(GemmPlan *pl, void *ws, int ctas) {
+  pl->sk_ws = static_cast<float *>(ws);
+  pl->sk_flags = ws ? reinterpret_cast<unsigned int *>(static_cast<char *>(ws) +
+                                                        (size_t)ctas * BM * 256 * sizeof(float))
+                    : nullptr;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 static int launch_t(const GemmPlan &pl, cudaStream_t st) {
   using C = Cfg<BN>;
@@ -394,12 +582,14 @@ static int launch_t(const GemmPlan &pl, cudaStream_t st) {
     attr_done[dev] = true;
   }
   const int ntiles = ((pl.p.N + BN - 1) / BN) * ((pl.p.M + BM - 1) / BM);
+  const int nk = (pl.p.K + BK - 1) / BK;
   DevCtx *ctx = ctx_current();
   const int sms = (ctx && ctx->num_sms) ? ctx->num_sms : 148;
   int cap = sms;  // persistent: one CTA per SM
   if (pl.max_ctas > 0 && pl.max_ctas < cap) cap = pl.max_ctas;
-  const int grid = ntiles < cap ? ntiles : cap;
-  kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(pl.a, pl.alo, pl.b, pl.blo, pl.p);
+  GemmParams p = pl.p;
+  const int grid = plan_stream_k(p, ntiles, nk, cap, pl.sk_ws, pl.sk_flags);
+  kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(pl.a, pl.alo, pl.b, pl.blo, p);
   FG_LAUNCH_TRY();
   return FG_OK;
 }
@@ -482,7 +672,42 @@ int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, c
   pl->a_mn = a_mn;
   pl->b_mn = b_mn;
   pl->max_ctas = 0;
+  pl->sk_ws = nullptr;
+  pl->sk_flags = nullptr;
   return FG_OK;
+}
+
+// One stream-K workspace per (device, stream) for the one-shot entry point:
+// launches on one stream are ordered, so they can share it; launches on
+// different streams get their own.  Allocated (zeroed) on first use outside
+// stream capture; a capturing stream without one runs whole tiles only.
+void attach_stream_ws(GemmPlan *pl, cudaStream_t st) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, cudaStream_t>, void *>> pool;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  DevCtx *ctx = ctx_current();
+  const int sms = (ctx && ctx->num_sms) ? ctx->num_sms : 148;
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto &e : pool)
+    if (e.first.first == dev && e.first.second == st) {
+      stream_k_attach(pl, e.second, sms);
+      return;
+    }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return;
+  }
+  void *ws = nullptr;
+  const size_t bytes = stream_k_ws_bytes(sms);
+  if (cudaMalloc(&ws, bytes) != cudaSuccess || cudaMemset(ws, 0, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    if (ws) cudaFree(ws);
+    return;
+  }
+  pool.push_back({{dev, st}, ws});
+  stream_k_attach(pl, ws, sms);
 }
 
 int run_plan(const GemmPlan &pl, cudaStream_t st) {
@@ -512,5 +737,6 @@ extern "C" int fg_gemm_3xtf32(int M, int N, int K, const float *d_a, const float
   int rc = fg::gemm::make_plan(M, N, K, d_a, d_a_lo, lda, d_b, d_b_lo, ldb, d_c, d_c_lo, ldc, flags,
                                epilogue, d_bias, d_mask, ldmask, &pl);
   if (rc) return rc;
+  fg::gemm::attach_stream_ws(&pl, (cudaStream_t)stream);
   return fg::gemm::run_plan(pl, (cudaStream_t)stream);
 }

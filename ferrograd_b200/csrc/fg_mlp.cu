@@ -396,15 +396,6 @@ int run_gemm(fg_mlp *m, const fg::gemm::GemmPlan &pl, cudaStream_t st) {
   return FG_OK;
 }
 
-// SMs the overlapped backward GEMMs leave free for the collective
-// (FG_COMM_SM_RESERVE, default 0: on this box reserving SMs slowed the
-// GEMMs more than it sped up the all-reduce).
-int comm_sm_reserve() {
-  const char *e = getenv("FG_COMM_SM_RESERVE");
-  int v = e ? atoi(e) : 0;
-  return v < 0 ? 0 : (v > 64 ? 64 : v);
-}
-
 // Sgd::step for layer l's weight and bias on `st`.
 int sgd_layer(fg_mlp *m, int l, cudaStream_t st) {
   Layer &ly = m->L[l];
@@ -651,6 +642,19 @@ int fg_mlp_create(fg_device *dev, int n_layers, const int *dims, int batch, floa
   m->scratch_bytes = need;
   if ((rc = mlp_alloc(m, &m->scratch, need / 4 + 1))) return fail(rc);
   if ((rc = build_plans(m))) return fail(rc);
+  // One stream-K workspace for every GEMM of the step: they all run in
+  // order on the step's compute stream.
+  {
+    float *ws = nullptr;
+    if ((rc = mlp_alloc(m, &ws, fg::gemm::stream_k_ws_bytes(m->sms) / 4 + 1))) return fail(rc);
+    for (int l = 0; l < m->nl; l++) {
+      Layer &ly = m->L[l];
+      if (!ly.tc) continue;
+      for (fg::gemm::GemmPlan *pl : {&ly.fwd, &ly.bwd_w, &ly.bwd_x, &ly.bwd_w_half[0],
+                                     &ly.bwd_w_half[1]})
+        fg::gemm::stream_k_attach(pl, ws, m->sms);
+    }
+  }
   FG_CUDA_TRY(cudaDeviceSynchronize());
   *out = m;
   return FG_OK;
@@ -730,7 +734,7 @@ int fg_mlp_attach_comm(fg_mlp *m, fg_comm *comm) {
   // The backward GEMMs that run while gradient all-reduces are in flight
   // leave SMs to the collective's kernels; a persistent grid over every SM
   // would keep them from starting until the GEMM ends.
-  const int reserve = comm ? comm_sm_reserve() : 0;
+  const int reserve = comm && fg::comm_nranks(comm) > 1 ? fg::comm_sm_reserve() : 0;
   for (int l = 0; l < m->nl; l++) {
     Layer &ly = m->L[l];
     const int cap = reserve ? m->sms - reserve : 0;

@@ -126,3 +126,32 @@ def test_gemm_full_size_precision():
     one = kernels.gemm(A, Bm, b_mn_major=True, one_pass=True)
     assert nrel(one, A.double() @ Bm.double()) > 2 * err_c
     kernels.check_device_error()
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 2048), (128, 128, 8192), (1000, 300, 1000)])
+def test_gemm_stream_k_tail_with_epilogues(M, N, K):
+    """Few output tiles and a long K: the persistent grid splits the tiles'
+    k-blocks over many CTAs (stream-K), and the CTA holding each tile's
+    first k-block adds the others' partials before the fused epilogue.  The
+    result must match float64 per element, keep the epilogue semantics and
+    be bitwise reproducible run to run (partials are added in CTA order)."""
+    A = data.uniform((M, K), 11, -1, 1)
+    B = data.uniform((N, K), 12, -1, 1)
+    bias = data.normal(N, 13)
+    base = A.astype(np.float64) @ B.astype(np.float64).T
+    bound = elemwise_bound(A, B) + 1e-3
+    ta, tb, tbias = cuda(A), cuda(B), cuda(bias)
+    plain = kernels.gemm(ta, tb).cpu().numpy()
+    check_close(plain, base, bound)
+    out_lo = torch.empty((M, N), device="cuda")
+    r = kernels.gemm(ta, tb, epilogue=EPI_BIAS_RELU, bias=tbias, out_lo=out_lo)
+    rn = r.cpu().numpy()
+    check_close(rn, np.maximum(base + bias, 0), bound)
+    hi = (r.view(torch.int32) & -8192).view(torch.float32)
+    assert torch.equal(hi + out_lo, r)
+    mask = cuda(data.normal((M, N), 14))
+    mz = kernels.gemm(ta, tb, epilogue=EPI_RELU_MASK, mask=mask).cpu().numpy()
+    check_close(mz, np.where(mask.cpu().numpy() > 0, base, 0), bound)
+    for _ in range(3):
+        assert np.array_equal(kernels.gemm(ta, tb).cpu().numpy(), plain)
+    kernels.check_device_error()
