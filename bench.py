@@ -292,6 +292,12 @@ def our_arm(args):
                        f"(dense TF32 = half the bf16 rate) / 3 (3xTF32 issues three MMAs per product)"),
         "frac_of_tf32_issue": ((3 * achieved) / tf32_peak) if achieved else None,
     }
+    # Parameters must stay identical across ranks (config 5): every rank hashes
+    # its weights and biases after the last step; the digests are compared.
+    from ferrograd_b200.dp import digests_agree, params_digest
+    pw, pb = tr.params()
+    digest = params_digest(list(pw) + list(pb))
+    identical = digests_agree(dist, digest, world) if world > 1 else True
     line = None
     if rank == 0:
         line = {
@@ -314,6 +320,8 @@ def our_arm(args):
             "clocks": clocks,
             "loss_first_last": [first_loss, last_loss],
             "gemm_flops_per_step": GEMM_FLOPS_PER_STEP,
+            "params_identical_across_ranks": bool(identical),
+            "params_sha256_rank0": digest[:16],
         }
     if world > 1:
         barrier()

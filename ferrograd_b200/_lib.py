@@ -67,6 +67,8 @@ SIGNATURES = [
     ("fg_xent_fwd_bwd_noalloc", _i, [_vp, _vp, _sz, _sz, _vp, _vp, _f, _vp]),
     ("fg_sgd", _i, [_vp, _vp, _sz, _f, _vp, _vp]),
     ("fg_split_lo", _i, [_vp, _vp, _sz, _vp]),
+    ("fg_u8_to_f32_div", _i, [_vp, _vp, _sz, _f, _vp]),
+    ("fg_one_hot_u8", _i, [_vp, _vp, _sz, _i, _vp]),
     ("fg_gemm_3xtf32", _i, [_i, _i, _i, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp, _vp,
                             _i, _vp]),
     ("fg_mlp_create", _i, [_vp, _i, ctypes.POINTER(_i), _i, _f, _pp]),

@@ -748,6 +748,42 @@ int launch_xent(const float *x, const float *t, size_t rows, size_t cols, float 
 }
 
 // ---------------------------------------------------------------------------
+// Dataset path: IDX pixels (u8) -> f32 / divisor on the device, and dense
+// one-hot targets, so a dataset is uploaded once as bytes and stays resident.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_u8_to_f32_div(const uint8_t *__restrict__ src,
+                                                       float *__restrict__ dst, size_t n,
+                                                       float divisor) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t n16 = (((uintptr_t)src | (uintptr_t)dst) & 15) == 0 ? n / 16 : 0;
+  for (size_t v = i; v < n16; v += stride) {
+    const uint4 u = __ldcs(reinterpret_cast<const uint4 *>(src) + v);
+    const uint8_t *b = reinterpret_cast<const uint8_t *>(&u);
+    float4 *o = reinterpret_cast<float4 *>(dst + v * 16);
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      __stcs(o + q, make_float4(__fdiv_rn((float)b[4 * q], divisor),
+                                __fdiv_rn((float)b[4 * q + 1], divisor),
+                                __fdiv_rn((float)b[4 * q + 2], divisor),
+                                __fdiv_rn((float)b[4 * q + 3], divisor)));
+  }
+  for (size_t j = n16 * 16 + i; j < n; j += stride) dst[j] = __fdiv_rn((float)src[j], divisor);
+}
+
+__global__ void __launch_bounds__(256) k_one_hot_u8(const uint8_t *__restrict__ labels,
+                                                    float *__restrict__ out, size_t n,
+                                                    int classes) {
+  const size_t total = n * (size_t)classes;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t j = (size_t)blockIdx.x * blockDim.x + threadIdx.x; j < total; j += stride) {
+    const size_t row = j / (size_t)classes;
+    const int c = (int)(j - row * (size_t)classes);
+    out[j] = (int)labels[row] == c ? 1.0f : 0.0f;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // SGD (src/optim.rs:60-71): p = p + (-(g*lr)); optional TF32 residual of p.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float sgd_one(float p, float g, float lr) {
@@ -955,6 +991,26 @@ int fg_xent_fwd_bwd_noalloc(const float *d_logits, const float *d_targets, size_
   FG_LAUNCH_TRY();
   fg::k_xent_loss_final<<<1, 1024, 0, st>>>(scratch, fg::xent_partials(grid, rows), inv_n,
                                             d_loss, 1.0f);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+int fg_u8_to_f32_div(const uint8_t *d_src, float *d_dst, size_t n, float divisor, void *stream) {
+  FG_REQUIRE(n == 0 || (d_src && d_dst), "fg_u8_to_f32_div: null pointer");
+  FG_REQUIRE(divisor != 0.0f, "fg_u8_to_f32_div: zero divisor");
+  if (n == 0) return FG_OK;
+  fg::k_u8_to_f32_div<<<fg::grid_for(n / 16 + 1, 256, 16), 256, 0, (cudaStream_t)stream>>>(
+      d_src, d_dst, n, divisor);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
+int fg_one_hot_u8(const uint8_t *d_labels, float *d_out, size_t n, int classes, void *stream) {
+  FG_REQUIRE(classes > 0 && classes <= 256, "fg_one_hot_u8: classes must be in 1..256");
+  FG_REQUIRE(n == 0 || (d_labels && d_out), "fg_one_hot_u8: null pointer");
+  if (n == 0) return FG_OK;
+  fg::k_one_hot_u8<<<fg::grid_for(n * (size_t)classes, 256, 16), 256, 0, (cudaStream_t)stream>>>(
+      d_labels, d_out, n, classes);
   FG_LAUNCH_TRY();
   return FG_OK;
 }

@@ -111,6 +111,34 @@ void *DeviceBuffer::ptr() {
   return p;
 }
 
+BufferP device_u8_to_f32(const uint8_t *data, size_t n, float divisor) {
+  auto src = std::make_shared<DeviceBuffer>(DType::Bool, n);
+  if (n) src->pending.assign(data, data + n);
+  auto dst = std::make_shared<DeviceBuffer>(DType::F32, n);
+  void *st = nullptr;
+  check(fg_device_stream(device(), &st), "device stream");
+  check(fg_u8_to_f32_div(static_cast<const uint8_t *>(src->ptr()), static_cast<float *>(dst->ptr()),
+                         n, divisor, st),
+        "u8_to_f32_div");
+  return dst;  // src is released stream-ordered after the conversion
+}
+
+BufferP device_one_hot_u8(const uint8_t *labels, size_t n, int classes) {
+  for (size_t i = 0; i < n; i++)
+    if (labels[i] >= classes)
+      throw Panic("one_hot: label " + std::to_string(labels[i]) + " out of range for " +
+                  std::to_string(classes) + " classes");
+  auto src = std::make_shared<DeviceBuffer>(DType::Bool, n);
+  if (n) src->pending.assign(labels, labels + n);
+  auto dst = std::make_shared<DeviceBuffer>(DType::F32, n * (size_t)classes);
+  void *st = nullptr;
+  check(fg_device_stream(device(), &st), "device stream");
+  check(fg_one_hot_u8(static_cast<const uint8_t *>(src->ptr()), static_cast<float *>(dst->ptr()), n,
+                      classes, st),
+        "one_hot_u8");
+  return dst;
+}
+
 std::vector<uint8_t> DeviceBuffer::to_host() {
   ensure_allocated();
   std::vector<uint8_t> out(count * dtype_size(dtype));

@@ -175,6 +175,11 @@ class Tensor {
   // A tensor over a reserved (not yet written) buffer, for graph building and
   // scheduling tests; reading it before a kernel writes it gives zeros.
   static Tensor empty(const Shape &shape, DType dt = DType::F32);
+  // Dataset path (src/dataset.rs:116-140, examples/mnist.rs:7-14): bytes
+  // uploaded once and converted on the device into realized f32 tensors --
+  // pixels as (float)b / divisor, labels as dense one-hot rows.
+  static Tensor from_u8_div(const uint8_t *data, const Shape &shape, float divisor);
+  static Tensor one_hot_u8(const uint8_t *labels, int64_t n, int classes);
 
   bool defined() const { return (bool)p_; }
   Shape shape() const;

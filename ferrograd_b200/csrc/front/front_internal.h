@@ -63,4 +63,8 @@ std::string float_literal(double v);
 bool exact_mode();
 int debug_level();
 
+// Device-side conversions behind Tensor::from_u8_div / one_hot_u8.
+BufferP device_u8_to_f32(const uint8_t *data, size_t n, float divisor);
+BufferP device_one_hot_u8(const uint8_t *labels, size_t n, int classes);
+
 }  // namespace ferro

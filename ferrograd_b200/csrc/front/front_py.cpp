@@ -128,6 +128,19 @@ PYBIND11_MODULE(_front, m) {
                     return Tensor::empty(to_shape(s), parse_dtype(dt));
                   },
                   py::arg("shape"), py::arg("dtype") = "f32")
+      .def_static("from_u8",
+                  [](const py::array_t<uint8_t, py::array::c_style | py::array::forcecast> &a,
+                     float divisor) {
+                    Shape shape;
+                    for (py::ssize_t i = 0; i < a.ndim(); i++) shape.push_back((int64_t)a.shape(i));
+                    return Tensor::from_u8_div(a.data(), shape, divisor);
+                  },
+                  py::arg("data"), py::arg("divisor") = 255.0f,
+                  "Bytes uploaded once, converted on the device to (float)b / divisor.")
+      .def_static("one_hot_u8",
+                  [](const py::array_t<uint8_t, py::array::c_style | py::array::forcecast> &a,
+                     int classes) { return Tensor::one_hot_u8(a.data(), (int64_t)a.size(), classes); },
+                  py::arg("labels"), py::arg("classes"))
       .def_property_readonly("shape", [](const Tensor &t) { return shape_tuple(t.shape()); })
       .def_property_readonly("dtype", [](const Tensor &t) { return std::string(dtype_name(t.dtype())); })
       .def("numel", &Tensor::numel)

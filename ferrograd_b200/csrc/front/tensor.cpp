@@ -147,6 +147,18 @@ Tensor Tensor::zeros(const Shape &shape, DType dt) {
 
 Tensor Tensor::empty(const Shape &shape, DType dt) { return zeros(shape, dt); }
 
+Tensor Tensor::from_u8_div(const uint8_t *data, const Shape &shape, float divisor) {
+  for (int64_t d : shape) require(d >= 0, "negative dimension in " + shape_str(shape));
+  BufferP b = device_u8_to_f32(data, (size_t)ferro::numel(shape), divisor);
+  return from_uop(make_reshape(make_buffer(b), shape), false);
+}
+
+Tensor Tensor::one_hot_u8(const uint8_t *labels, int64_t n, int classes) {
+  require(n >= 0 && classes > 0, "one_hot: bad size");
+  BufferP b = device_one_hot_u8(labels, (size_t)n, classes);
+  return from_uop(make_reshape(make_buffer(b), {n, (int64_t)classes}), false);
+}
+
 Tensor Tensor::full(const Shape &shape, float value) {
   std::vector<float> v((size_t)ferro::numel(shape), value);
   return from_f32(v.data(), shape);

@@ -141,6 +141,15 @@ int fg_xent_fwd_bwd_noalloc(const float *d_logits, const float *d_targets, size_
  * NULL it also receives the TF32 residual of the updated p (see fg_split_lo). */
 int fg_sgd(float *d_p, const float *d_g, size_t n, float lr, float *d_p_lo, void *stream);
 
+/* Dataset path.  parse_images (src/dataset.rs:116-140) maps each IDX pixel
+ * to f32::from(b) / 255.0; here the bytes are uploaded once and converted on
+ * the device: d_dst[i] = (float)d_src[i] / divisor, correctly rounded (the
+ * same value).  one_hot (examples/mnist.rs:7-14): d_out[i, c] = 1.0 when
+ * d_labels[i] == c, else 0.0 ([n, classes], row-major); a label >= classes
+ * leaves its row all zero (the host loader rejects such labels first). */
+int fg_u8_to_f32_div(const uint8_t *d_src, float *d_dst, size_t n, float divisor, void *stream);
+int fg_one_hot_u8(const uint8_t *d_labels, float *d_out, size_t n, int classes, void *stream);
+
 /* TF32 residual: lo[i] = x[i] - (x[i] with its low 13 mantissa bits cleared).
  * The tensor cores read x itself as the high part. */
 int fg_split_lo(const float *d_x, float *d_lo, size_t n, void *stream);
