@@ -330,6 +330,9 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
   std::string init = rop == Op::Add ? literal_of(0.0, dt) : literal_of(-INFINITY, dt);
   std::string acc = fresh("acc");
   line(std::string(ctype(dt)) + " " + acc + " = " + init + ";");
+  // An empty reduced axis leaves the identity: no element is read.
+  for (int64_t a : axes)
+    if (ss[(size_t)a] == 0) return Val{acc, dt};
   std::vector<std::string> sc = ctx;
   sc.resize(ss.size(), "0");
   size_t opened = 0;

@@ -283,3 +283,13 @@ def test_const_folding_follows_symbolic_simple():
     # The gradient is expand(full(1.0)) -- a constant kernel: no loads.
     src = F.schedule([g], with_source=True)[0]["source"]
     assert "1.0f" in src and "p1[" not in src
+
+
+def test_reduction_over_an_empty_axis_reads_nothing():
+    """sum/max over a zero-length axis is the identity (0 / -inf); the
+    rendered kernel must not load from the empty buffer."""
+    z = F.Tensor.empty([0, 3])
+    for red, ident in ((z.sum([0]), "0.0f"), (z.max([0]), "(-INFINITY)")):
+        src = F.schedule([red], with_source=True)[0]["source"]
+        body = src.split("{", 1)[1]
+        assert "p1[" not in body and ident in body
