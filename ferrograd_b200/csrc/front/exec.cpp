@@ -87,21 +87,60 @@ void synchronize() {
   if (g_dev) check(fg_device_sync(g_dev), "synchronize");
 }
 
+bool device_is_open() { return g_dev != nullptr; }
+
 // ---- DeviceBuffer (src/device.rs:95-214) ----------------------------------
+// Storage of dropped buffers is kept, per (dtype, count), and handed to the
+// next buffer of the same size that a kernel or an upload will overwrite, so
+// a training loop's per-step intermediates and temporaries are neither
+// reallocated nor zero-filled.  Reuse is safe in stream order: every launch
+// and copy of the front end is on its device's stream.  Buffers that must
+// read as zeros (Tensor::zeros) still get fresh zero-filled storage.
+namespace {
+std::unordered_multimap<uint64_t, fg_buffer *> &storage_pool() {
+  static std::unordered_multimap<uint64_t, fg_buffer *> p;
+  return p;
+}
+size_t g_pooled_bytes = 0;
+constexpr size_t kPoolCapBytes = size_t(16) << 30;
+uint64_t pool_key(DType dt, size_t n) { return ((uint64_t)n << 2) | (uint64_t)dt; }
+}  // namespace
+
 DeviceBuffer::DeviceBuffer(DType dt, size_t n) : dtype(dt), count(n), id(g_buffer_ids++) {}
 
 DeviceBuffer::~DeviceBuffer() {
-  if (h) fg_free(h);
+  if (!h) return;
+  const size_t bytes = count * dtype_size(dtype);
+  if (count && g_pooled_bytes + bytes <= kPoolCapBytes) {
+    storage_pool().emplace(pool_key(dtype, count), h);
+    g_pooled_bytes += bytes;
+  } else {
+    fg_free(h);
+  }
 }
 
 void DeviceBuffer::ensure_allocated() {
   if (h) return;
-  check(fg_alloc(device(), (int)dtype, count, &h), "allocate");
+  const bool must_zero = zero_init && pending.empty();
+  auto &pool = storage_pool();
+  auto it = must_zero || !count ? pool.end() : pool.find(pool_key(dtype, count));
+  if (it != pool.end()) {
+    h = it->second;
+    pool.erase(it);
+    g_pooled_bytes -= count * dtype_size(dtype);
+  } else {
+    check(fg_alloc(device(), (int)dtype, count, &h), "allocate");
+  }
   if (!pending.empty()) {
     int rc = fg_copy_h2d(h, pending.data(), pending.size());
     check(rc, "copy_from_host");
     std::vector<uint8_t>().swap(pending);
   }
+}
+
+void DeviceBuffer::upload(const void *data, size_t bytes) {
+  ensure_allocated();
+  check(fg_copy_h2d(h, data, bytes), "copy_from_host");
 }
 
 void *DeviceBuffer::ptr() {
@@ -313,6 +352,16 @@ std::vector<bool> deps(const UOp *n) {
 }
 
 // ---- program cache and generic launches -----------------------------------
+void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelInput> &params,
+                 const BufferP &out);
+
+// A one-element buffer passed in the slot of a known-zero input.
+fg_buffer *placeholder_buffer() {
+  static fg_buffer *b = nullptr;
+  if (!b) check(fg_alloc(device(), FG_F32, 1, &b), "allocate");
+  return b;
+}
+
 void launch_rendered(const RenderedKernel &rk, const BufferP &out) {
   auto &cache = program_cache();
   fg_program *prog = nullptr;
@@ -335,22 +384,32 @@ void launch_rendered(const RenderedKernel &rk, const BufferP &out) {
                                     (unsigned long long)kid, (unsigned long long)kid, nargs);
   }
   g_last_source = rk.source;
+  launch_args(prog, rk.has_out_slot, rk.params, out);
+}
+
+void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelInput> &params,
+                 const BufferP &out) {
+  const int nargs = (int)params.size() + (has_out_slot ? 1 : 0);
   std::vector<fg_kernel_arg> args;
   args.reserve((size_t)nargs);
-  if (rk.has_out_slot) {
+  if (has_out_slot) {
     out->ensure_allocated();
     fg_kernel_arg a{};
     a.kind = FG_ARG_BUFFER;
     a.v.buffer = out->h;
     args.push_back(a);
   }
-  for (const KernelInput &in : rk.params) {
+  for (const KernelInput &in : params) {
     fg_kernel_arg a{};
     switch (in.kind) {
       case KernelInput::Buffer:
-        in.buffer->ensure_allocated();
         a.kind = FG_ARG_BUFFER;
-        a.v.buffer = in.buffer->h;
+        if (in.buffer->known_zero() && !in.buffer->is_allocated()) {
+          a.v.buffer = placeholder_buffer();  // the kernel never reads it
+        } else {
+          in.buffer->ensure_allocated();
+          a.v.buffer = in.buffer->h;
+        }
         break;
       case KernelInput::I32:
         a.kind = FG_ARG_I32;
@@ -369,6 +428,92 @@ void launch_rendered(const RenderedKernel &rk, const BufferP &out) {
   }
   check(fg_execute(prog, args.data(), nargs), "execute");
   g_stats.rendered++;
+}
+
+// Structural key of a render request: everything the rendered source
+// depends on (ops, dtypes, shapes, args, literals, reduce ops, the graph's
+// shape, buffer slots and Shrink parameter slots, the domain and the store),
+// but not which buffers fill the slots.  Encoding it costs a walk of the
+// expression; rendering costs ~60 us per kernel, so steady-state steps look
+// programs up by this key and render only on a miss.
+struct KeyBuf {
+  std::string s;
+  void put(int64_t v) { s.append(reinterpret_cast<const char *>(&v), sizeof(v)); }
+  void put_str(const std::string &t) {
+    put((int64_t)t.size());
+    s.append(t);
+  }
+};
+
+std::string spec_key(const RenderSpec &spec, const ParamSlots &ps) {
+  KeyBuf k;
+  k.put((int64_t)spec.store);
+  k.put(spec.pitch);
+  k.put((int64_t)spec.out_dtype);
+  k.put(spec.unroll);
+  k.put((int64_t)spec.domain.size());
+  for (int64_t d : spec.domain) k.put(d);
+  k.put((int64_t)spec.value_ctx.size());
+  for (auto &c : spec.value_ctx) k.put_str(c);
+  UOpP root = spec.store == RenderSpec::View ? make_store(spec.dest, spec.value) : spec.value;
+  std::unordered_map<const UOp *, int64_t> pos;
+  for (auto &n : toposort(root)) {
+    pos[n.get()] = (int64_t)pos.size();
+    k.put((int64_t)n->op);
+    k.put((int64_t)n->dtype);
+    k.put((int64_t)n->reduce_op);
+    int64_t vb;
+    std::memcpy(&vb, &n->value, sizeof(vb));
+    k.put(vb);
+    k.put((int64_t)n->shape.size());
+    for (int64_t d : n->shape) k.put(d);
+    k.put((int64_t)n->arg.size());
+    for (int64_t a : n->arg) k.put(a);
+    k.put((int64_t)n->src.size());
+    for (auto &src : n->src) k.put(pos.at(src.get()));
+    if (n->op == Op::Buffer) {
+      k.put(ps.buffer_slot.at(n->buf.get()));
+      k.put((int64_t)n->buf->count);
+      k.put(n->buf->known_zero() ? 1 : 0);
+    } else if (n->op == Op::Shrink) {
+      for (int sl : ps.shrink_slots.at(n.get())) k.put(sl);
+    }
+  }
+  k.put(spec.store == RenderSpec::View ? 1 : 0);
+  return k.s;
+}
+
+struct CachedKernel {
+  fg_program *prog;
+  bool has_out_slot;
+};
+
+std::unordered_map<std::string, CachedKernel> &spec_cache() {
+  static std::unordered_map<std::string, CachedKernel> c;
+  return c;
+}
+
+// Render (on a miss) and launch one generic kernel.
+void launch_spec(const RenderSpec &spec, const BufferP &out) {
+  const bool view = spec.store == RenderSpec::View;
+  ParamSlots ps = view ? collect_params(make_store(spec.dest, spec.value), 0)
+                       : collect_params(spec.value, 1);
+  std::string key = spec_key(spec, ps);
+  auto &cache = spec_cache();
+  auto it = cache.find(key);
+  if (it == cache.end()) {
+    RenderedKernel rk = render_kernel(spec);
+    launch_rendered(rk, out);
+    auto pit = program_cache().find(rk.source);
+    if (pit != program_cache().end()) cache.emplace(key, CachedKernel{pit->second, rk.has_out_slot});
+    return;
+  }
+  g_stats.cache_hits++;
+  if (debug_level() >= 1)
+    fprintf(stderr, "*** CUDA %4llu  (cached)         arg %2d\n",
+            (unsigned long long)g_kernel_count++,
+            (int)ps.inputs.size() + (it->second.has_out_slot ? 1 : 0));
+  launch_args(it->second.prog, it->second.has_out_slot, ps.inputs, out);
 }
 
 BufferP temp_buffer(DType dt, int64_t n) {
@@ -430,6 +575,37 @@ struct Operand {
   bool mn_major = false;
 };
 
+struct StageKey {
+  const UOp *x;
+  bool kmaj;
+  int64_t rows, K;
+  size_t row_axis, red_axis;
+  bool operator==(const StageKey &o) const {
+    return x == o.x && kmaj == o.kmaj && rows == o.rows && K == o.K && row_axis == o.row_axis &&
+           red_axis == o.red_axis;
+  }
+};
+struct StageKeyHash {
+  size_t operator()(const StageKey &k) const {
+    return std::hash<const void *>()(k.x) ^ (size_t)(k.rows * 1000003 + k.K * 31 + k.kmaj) ^
+           (k.row_axis << 7) ^ (k.red_axis << 11);
+  }
+};
+struct Staged {
+  Operand op;
+  std::vector<std::pair<BufferP, uint64_t>> reads;  // buffers read, at their versions
+  UOpP keep;
+  bool valid() const {
+    for (auto &r : reads)
+      if (r.first->version != r.second) return false;
+    return true;
+  }
+};
+std::unordered_map<StageKey, Staged, StageKeyHash> &staged_cache() {
+  static std::unordered_map<StageKey, Staged, StageKeyHash> c;
+  return c;
+}
+
 Operand prepare_operand(const UOpP &x, size_t row_axis, size_t red_axis, size_t bcast_axis,
                         int64_t rows, int64_t K) {
   Operand op;
@@ -448,13 +624,31 @@ Operand prepare_operand(const UOpP &x, size_t row_axis, size_t red_axis, size_t 
       op.ld = kmaj ? (int)std::max<int64_t>(sr, (K + 3) / 4 * 4) : (int)sk;
       if (kmaj && rows == 1) op.ld = (int)((K + 3) / 4 * 4);
       op.mn_major = mnmaj;
-      const int64_t span = kmaj ? (rows - 1) * op.ld + K : (K - 1) * op.ld + rows;
       (void)extent;
-      op.lo = temp_buffer(DType::F32, span);
-      check(fg_split_lo(op.ptr, fptr(op.lo), (size_t)span, stream()), "split_lo");
-      op.lo_ptr = fptr(op.lo);
+      // The residual of the whole buffer, made once per version of its
+      // contents (a weight read by the forward and the dX GEMM, an input
+      // read by the forward and the dW GEMM).
+      DeviceBuffer &b = *v->buf;
+      if (!b.lo || b.lo_version != b.version) {
+        b.lo = temp_buffer(DType::F32, (int64_t)b.count);
+        check(fg_split_lo(fptr(v->buf), fptr(b.lo), b.count, stream()), "split_lo");
+        b.lo_version = b.version;
+      }
+      op.lo = b.lo;
+      op.lo_ptr = fptr(b.lo, v->offset);
       return op;
     }
+  }
+  // A lazy operand staged earlier in this realize (the ReLU output read by
+  // the forward GEMM and again by the dW GEMM) is reused while the buffers
+  // it reads are unchanged.
+  const bool kmaj0 = red_axis > row_axis;
+  StageKey sk0{x.get(), kmaj0, rows, K, row_axis, red_axis};
+  auto &stage = staged_cache();
+  auto sit = stage.find(sk0);
+  if (sit != stage.end() && sit->second.valid()) {
+    op = sit->second.op;
+    return op;
   }
   // Stage a copy whose contiguous axis is the operand's higher-numbered one
   // (its natural row-major order, so the staging pass reads coalesced):
@@ -474,13 +668,19 @@ Operand prepare_operand(const UOpP &x, size_t row_axis, size_t red_axis, size_t 
   spec.pitch = ld;
   spec.out_dtype = DType::F32;
   spec.unroll = 4;
-  launch_rendered(render_kernel(spec), op.hold);
+  launch_spec(spec, op.hold);
   op.ptr = fptr(op.hold);
   op.ld = (int)ld;
   op.mn_major = !kmaj;
   op.lo = temp_buffer(DType::F32, outer * ld);
   check(fg_split_lo(op.ptr, fptr(op.lo), (size_t)(outer * ld), stream()), "split_lo");
   op.lo_ptr = fptr(op.lo);
+  Staged st;
+  st.op = op;
+  st.keep = x;
+  for (auto &n : toposort(x))
+    if (n->op == Op::Buffer) st.reads.emplace_back(n->buf, n->buf->version);
+  stage[sk0] = st;
   return op;
 }
 
@@ -614,6 +814,8 @@ std::string render_item_source(const ScheduleItem &item) {
   return render_kernel(spec).source;
 }
 
+void end_realize() { staged_cache().clear(); }
+
 void run_item(const ScheduleItem &item) {
   g_stats.kernels++;
   UOpP value = item.value;
@@ -657,7 +859,14 @@ void run_item(const ScheduleItem &item) {
   } else {
     spec.out_dtype = item.value->dtype;
   }
-  launch_rendered(render_kernel(spec), item.output);
+  launch_spec(spec, item.output);
+  if (item.store_dest) {
+    // the destination's contents changed: cached residuals and staged
+    // operands that read it are stale
+    const UOp *d = item.store_dest.get();
+    while (d->op != Op::Buffer && !d->src.empty()) d = d->src[0].get();
+    if (d->op == Op::Buffer) d->buf->version++;
+  }
 }
 
 }  // namespace ferro

@@ -74,13 +74,23 @@ struct DeviceBuffer {
   uint64_t id;
   fg_buffer *h = nullptr;
   std::vector<uint8_t> pending;  // host bytes to upload on allocation
-  bool zero_init = false;        // Device::allocate semantics when no data
+  bool zero_init = false;        // Tensor::zeros: must read as zeros (no data given)
+  // Writes into an existing buffer (in-place stores) bump the version; the
+  // TF32 residual of the contents is cached for the version it was made for.
+  uint64_t version = 0;
+  std::shared_ptr<DeviceBuffer> lo;
+  uint64_t lo_version = ~0ull;
   DeviceBuffer(DType dt, size_t n);
   ~DeviceBuffer();
   DeviceBuffer(const DeviceBuffer &) = delete;
   DeviceBuffer &operator=(const DeviceBuffer &) = delete;
   bool is_allocated() const { return h != nullptr; }
+  // Zero-filled at creation and never written since (Tensor::zeros): kernels
+  // may use the value 0 instead of reading it.
+  bool known_zero() const { return zero_init && pending.empty() && version == 0; }
   void ensure_allocated();
+  // Allocates and copies `bytes` from host memory now (Device::copy_from_host).
+  void upload(const void *data, size_t bytes);
   void *ptr();
   std::vector<uint8_t> to_host();
 };
@@ -266,7 +276,10 @@ struct Sgd {
 // Device the front end runs on: cuda:0, or FG_DEVICE=cuda:N, or set_device.
 void set_device(int ordinal);
 fg_device *device();
+bool device_is_open();
 void synchronize();
+// Drops per-realize caches (staged GEMM operands); called after a realize.
+void end_realize();
 
 // Per-kernel routing decision for an item, without running it.
 struct RoutePlan {

@@ -397,6 +397,12 @@ Val Emitter::value(const UOp *n, const std::vector<std::string> &ctx) {
   Val out;
   switch (n->op) {
     case Op::Buffer: {
+      if (n->buf->known_zero()) {
+        // a never-written zeros buffer: the loaded value is 0 (not folded
+        // as a literal: the reference loads it)
+        out = Val{literal_of(0.0, n->dtype), n->dtype};
+        break;
+      }
       int slot = ps_.buffer_slot.at(n->buf.get());
       std::string i = ctx.empty() ? "0" : ctx[0];
       std::string ld = "p" + std::to_string(slot) + "[" + i + "]";

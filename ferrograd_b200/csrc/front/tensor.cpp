@@ -122,8 +122,12 @@ Tensor Tensor::from_host(DType dt, const void *data, size_t bytes, const Shape &
   require(bytes == n * dtype_size(dt), "data length " + std::to_string(bytes / dtype_size(dt)) +
                                            " doesn't match shape " + shape_str(shape));
   auto buf = std::make_shared<DeviceBuffer>(dt, n);
-  if (bytes) buf->pending.assign((const uint8_t *)data, (const uint8_t *)data + bytes);
-  buf->zero_init = true;
+  if (bytes) {
+    if (device_is_open())
+      buf->upload(data, bytes);  // straight from the caller's memory
+    else
+      buf->pending.assign((const uint8_t *)data, (const uint8_t *)data + bytes);
+  }
   return from_uop(make_reshape(make_buffer(buf), shape), false);
 }
 
@@ -367,6 +371,7 @@ void Tensor::realize_many(const std::vector<Tensor> &ts) {
   if (roots.empty()) return;
   SchedulePlan plan = schedule_many(roots);
   for (const ScheduleItem &item : plan.items) run_item(item);
+  end_realize();
   apply_map_to_tensors(plan.replacements);
 }
 

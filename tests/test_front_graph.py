@@ -293,3 +293,13 @@ def test_reduction_over_an_empty_axis_reads_nothing():
         src = F.schedule([red], with_source=True)[0]["source"]
         body = src.split("{", 1)[1]
         assert "p1[" not in body and ident in body
+
+
+def test_only_zeros_tensors_render_as_known_zero():
+    """Tensor::zeros buffers that nothing has written may be used as the
+    value 0; uploaded data never is."""
+    z = F.Tensor.zeros([4])
+    d = F.tensor([1.0, 2.0, 3.0, 4.0])
+    src = F.schedule([z.add(d)], with_source=True)[0]["source"]
+    body = src.split("{", 1)[1]
+    assert body.count("p1[") == 0 and body.count("p2[") > 0  # only the data tensor is loaded
