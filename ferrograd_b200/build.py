@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libferro_cuda.so")
 OBJDIR = os.path.join(HERE, "_build")
 
-SOURCES = ["fg_runtime.cu", "fg_kernels.cu", "fg_gemm.cu", "fg_mlp.cu", "fg_comm.cu"]
+SOURCES = ["fg_runtime.cu", "fg_kernels.cu", "fg_gemm.cu", "fg_mlp.cu", "fg_comm.cu", "fg_init.cpp"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -46,7 +46,7 @@ def build_cuda(verbose: bool = False) -> str:
     objs = []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
-        o = os.path.join(OBJDIR, src.replace(".cu", ".o"))
+        o = os.path.join(OBJDIR, os.path.splitext(src)[0] + ".o")
         objs.append(o)
         if _stale(o, [s] + headers):
             cmd = [NVCC, *ARCH, *FLAGS, "-c", s, "-o", o]

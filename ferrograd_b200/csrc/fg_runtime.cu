@@ -143,28 +143,6 @@ static size_t dtype_size(int dtype) {
 
 extern "C" {
 
-int fg_kaiming_normal(float *h_out, size_t numel, size_t fan_in, uint64_t *state) {
-  FG_REQUIRE(state && (numel == 0 || h_out), "fg_kaiming_normal: null argument");
-  FG_REQUIRE(fan_in > 0, "fg_kaiming_normal: fan_in must be positive");
-  const float stdv = sqrtf(2.0f / (float)fan_in);
-  auto next_unit = [state]() {
-    const uint64_t next = *state * 6364136223846793005ULL + 1ULL;
-    *state = next;
-    return (float)(next >> 33) / (float)(1ULL << 31);
-  };
-  size_t n = 0;
-  while (n < numel) {
-    float u1 = next_unit();
-    if (!(u1 >= 1.17549435e-38f)) u1 = 1.17549435e-38f;  // max(u1, f32::MIN_POSITIVE)
-    const float u2 = next_unit();
-    const float radius = sqrtf(-2.0f * logf(u1)) * stdv;
-    const float theta = (2.0f * 3.14159265358979323846f) * u2;
-    h_out[n++] = radius * cosf(theta);
-    if (n < numel) h_out[n++] = radius * sinf(theta);
-  }
-  return FG_OK;
-}
-
 const char *fg_last_error(void) { return fg::g_last_error.c_str(); }
 
 uint64_t fg_kernel_launches(void) { return fg::g_launches.load(); }

@@ -1,0 +1,268 @@
+// hostdev.cpp -- TEST INFRASTRUCTURE ONLY: a host implementation of the
+// device part of include/ferro_cuda.h, so the C++ front end can be linked
+// against it and run on a machine without a GPU.
+//
+// fg_compile takes the CUDA C the front end renders, compiles it with g++
+// (-ffp-contract=off, one rounding per op like the reference's clang C)
+// behind a small prelude that maps the CUDA spellings to C++ (blockIdx /
+// threadIdx become globals the launcher sets, __fadd_rn is a float add,
+// exp2((double)x) is libm's), and fg_execute runs the kernel over its grid.
+// That makes an independent CPU execution of the front end's schedule and
+// rendered arithmetic -- a second oracle for exact mode (FG_FRONT_EXACT=1).
+// The tensor-core GEMM, the HBM reductions and the TF32 split are not
+// emulated: they report FG_ERR_UNSUPPORTED, so only exact mode runs here.
+// Nothing in the product loads this library.
+#include <dlfcn.h>
+#include <stdarg.h>
+#include <unistd.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <functional>
+#include <regex>
+#include <string>
+#include <vector>
+
+#include "ferro_cuda.h"
+
+namespace fg {
+static thread_local std::string g_err;
+int set_error(int code, const char *fmt, ...) {
+  char buf[4096];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+}  // namespace fg
+
+struct fg_device {
+  int ordinal;
+};
+struct fg_buffer {
+  void *p;
+  int dtype;
+  size_t numel;
+};
+struct fg_program {
+  void *so;
+  void (*launch)(void **args, unsigned grid, unsigned block);
+  int num_args;
+  unsigned grid, block;
+};
+
+static size_t esize(int dt) { return dt == FG_BOOL ? 1 : 4; }
+
+// Prelude that lets the rendered CUDA C compile as host C++.
+static const char *kPrelude = R"(
+#include <cmath>
+#include <cstring>
+struct fg_dim3 { unsigned x, y, z; };
+static fg_dim3 blockIdx, threadIdx;
+#define __global__
+#define __launch_bounds__(x)
+#define __restrict__ __restrict
+static inline float __fadd_rn(float a, float b) { return a + b; }
+static inline float __fmul_rn(float a, float b) { return a * b; }
+static inline float __frcp_rn(float a) { return 1.0f / a; }
+static inline float __fsqrt_rn(float a) { return std::sqrt(a); }
+static inline float __int_as_float(int i) { float f; std::memcpy(&f, &i, 4); return f; }
+using std::exp2;
+using std::log2;
+)";
+
+extern "C" {
+
+const char *fg_last_error(void) { return fg::g_err.c_str(); }
+
+int fg_device_open(int ordinal, fg_device **out) {
+  *out = new fg_device{ordinal};
+  return FG_OK;
+}
+int fg_device_close(fg_device *dev) {
+  delete dev;
+  return FG_OK;
+}
+int fg_device_stream(fg_device *, void **stream) {
+  *stream = nullptr;
+  return FG_OK;
+}
+int fg_device_sync(fg_device *) { return FG_OK; }
+
+int fg_alloc(fg_device *, int dtype, size_t numel, fg_buffer **out) {
+  void *p = numel ? calloc(numel, esize(dtype)) : nullptr;
+  *out = new fg_buffer{p, dtype, numel};
+  return FG_OK;
+}
+int fg_free(fg_buffer *b) {
+  if (b) free(b->p);
+  delete b;
+  return FG_OK;
+}
+int fg_buffer_info(const fg_buffer *b, void **p, int *dtype, size_t *numel) {
+  if (p) *p = b->p;
+  if (dtype) *dtype = b->dtype;
+  if (numel) *numel = b->numel;
+  return FG_OK;
+}
+int fg_copy_h2d(fg_buffer *b, const void *src, size_t n) {
+  if (n != b->numel * esize(b->dtype))
+    return fg::set_error(FG_ERR_INVALID, "copy_from_host: expected %zu bytes, got %zu",
+                         b->numel * esize(b->dtype), n);
+  if (n) memcpy(b->p, src, n);
+  return FG_OK;
+}
+int fg_copy_d2h(const fg_buffer *b, void *dst, size_t n) {
+  if (n != b->numel * esize(b->dtype))
+    return fg::set_error(FG_ERR_INVALID, "copy_to_host: expected %zu bytes, got %zu",
+                         b->numel * esize(b->dtype), n);
+  if (n) memcpy(dst, b->p, n);
+  return FG_OK;
+}
+
+int fg_compile(fg_device *, const char *source, const char *func_name, int num_args,
+               const uint32_t grid[3], const uint32_t block[3], fg_program **out) {
+  // The launcher needs the parameter types: read them off the signature.
+  std::string src(source);
+  std::smatch m;
+  std::regex sig(std::string(func_name) + R"(\(([^)]*)\))");
+  if (!std::regex_search(src, m, sig)) return fg::set_error(FG_ERR_COMPILE, "no signature");
+  std::vector<std::string> types;
+  std::string params = m[1].str();
+  size_t pos = 0;
+  while (pos <= params.size()) {
+    size_t c = params.find(',', pos);
+    std::string p = params.substr(pos, c == std::string::npos ? std::string::npos : c - pos);
+    size_t last = p.find_last_of(" *");
+    std::string t = p.substr(0, last + 1);
+    size_t r = t.find("__restrict__");
+    if (r != std::string::npos) t.erase(r, 12);
+    types.push_back(t);
+    if (c == std::string::npos) break;
+    pos = c + 1;
+  }
+  std::string launcher = "\nextern \"C\" void fg_host_launch(void **a, unsigned grid, unsigned block) {\n"
+                         "  for (unsigned b = 0; b < grid; b++) for (unsigned t = 0; t < block; t++) {\n"
+                         "    blockIdx.x = b; threadIdx.x = t;\n    " + std::string(func_name) + "(";
+  for (size_t i = 0; i < types.size(); i++)
+    launcher += (i ? ", " : "") + std::string("*(") + types[i] + "*)a[" + std::to_string(i) + "]";
+  launcher += ");\n  }\n}\n";
+  // Compiled kernels are cached on disk (FG_HOSTDEV_CACHE) by a hash of the
+  // full source; the stored source is compared before reuse.
+  const std::string full = std::string(kPrelude) + src + launcher;
+  const char *cache_dir = getenv("FG_HOSTDEV_CACHE");
+  std::string cached_so, cached_src;
+  if (cache_dir && *cache_dir) {
+    char name[64];
+    snprintf(name, sizeof(name), "/k%016zx", std::hash<std::string>()(full));
+    cached_so = std::string(cache_dir) + name + ".so";
+    cached_src = std::string(cache_dir) + name + ".cpp";
+    std::ifstream cf(cached_src);
+    std::string prev((std::istreambuf_iterator<char>(cf)), std::istreambuf_iterator<char>());
+    if (prev == full && access(cached_so.c_str(), R_OK) == 0) {
+      void *h = dlopen(cached_so.c_str(), RTLD_NOW | RTLD_LOCAL);
+      auto fn = h ? (void (*)(void **, unsigned, unsigned))dlsym(h, "fg_host_launch") : nullptr;
+      if (fn) {
+        *out = new fg_program{h, fn, num_args, grid[0] ? grid[0] : 1, block[0] ? block[0] : 1};
+        return FG_OK;
+      }
+    }
+  }
+  char dir[] = "/tmp/fg_hostdev_XXXXXX";
+  if (!mkdtemp(dir)) return fg::set_error(FG_ERR_COMPILE, "mkdtemp failed");
+  std::string cpp = std::string(dir) + "/k.cpp", so = std::string(dir) + "/k.so";
+  {
+    std::ofstream f(cpp);
+    f << full;
+  }
+  std::string cmd = "g++ -O1 -std=c++17 -shared -fPIC -ffp-contract=off -fno-fast-math -w -o " +
+                    so + " " + cpp + " 2>" + std::string(dir) + "/log.txt";
+  if (system(cmd.c_str()) != 0) {
+    std::ifstream lf(std::string(dir) + "/log.txt");
+    std::string log((std::istreambuf_iterator<char>(lf)), std::istreambuf_iterator<char>());
+    return fg::set_error(FG_ERR_COMPILE, "g++ failed:\n%s", log.c_str());
+  }
+  if (!cached_so.empty()) {
+    std::string cp = "cp " + so + " " + cached_so + " && cp " + cpp + " " + cached_src;
+    if (system(cp.c_str()) != 0) unlink(cached_so.c_str());
+  }
+  void *h = dlopen(so.c_str(), RTLD_NOW | RTLD_LOCAL);
+  unlink(cpp.c_str());
+  unlink(so.c_str());
+  unlink((std::string(dir) + "/log.txt").c_str());
+  rmdir(dir);
+  if (!h) return fg::set_error(FG_ERR_COMPILE, "dlopen: %s", dlerror());
+  auto fn = (void (*)(void **, unsigned, unsigned))dlsym(h, "fg_host_launch");
+  if (!fn) return fg::set_error(FG_ERR_COMPILE, "launcher missing");
+  *out = new fg_program{h, fn, num_args, grid[0] ? grid[0] : 1, block[0] ? block[0] : 1};
+  return FG_OK;
+}
+
+int fg_program_free(fg_program *p) {
+  if (p) dlclose(p->so);
+  delete p;
+  return FG_OK;
+}
+
+int fg_execute(fg_program *prog, const fg_kernel_arg *args, int nargs) {
+  if (nargs != prog->num_args)
+    return fg::set_error(FG_ERR_INVALID, "expected %d kernel args, got %d", prog->num_args, nargs);
+  std::vector<void *> ptrs(nargs), slots(nargs);
+  std::vector<int32_t> ints(nargs);
+  std::vector<float> floats(nargs);
+  for (int i = 0; i < nargs; i++) {
+    switch (args[i].kind) {
+      case FG_ARG_BUFFER:
+        ptrs[i] = args[i].v.buffer->p;
+        slots[i] = &ptrs[i];
+        break;
+      case FG_ARG_I32:
+        ints[i] = args[i].v.i32;
+        slots[i] = &ints[i];
+        break;
+      case FG_ARG_F32:
+        floats[i] = args[i].v.f32;
+        slots[i] = &floats[i];
+        break;
+      default:
+        ints[i] = args[i].v.b;
+        slots[i] = &ints[i];
+        break;
+    }
+  }
+  prog->launch(slots.data(), prog->grid, prog->block);
+  return FG_OK;
+}
+
+// Building blocks that only the GPU runs (tensor cores, HBM kernels).
+int fg_gemm_3xtf32(int, int, int, const float *, const float *, int, const float *, const float *,
+                   int, float *, float *, int, int, int, const float *, const float *, int, void *) {
+  return fg::set_error(FG_ERR_UNSUPPORTED, "host test device: exact mode only (no GEMM)");
+}
+int fg_split_lo(const float *, float *, size_t, void *) {
+  return fg::set_error(FG_ERR_UNSUPPORTED, "host test device: exact mode only (no TF32 split)");
+}
+int fg_reduce_rows(int, int, const void *, void *, size_t, size_t, void *) {
+  return fg::set_error(FG_ERR_UNSUPPORTED, "host test device: exact mode only (no HBM reduce)");
+}
+int fg_reduce_cols(int, int, const void *, void *, size_t, size_t, void *) {
+  return fg::set_error(FG_ERR_UNSUPPORTED, "host test device: exact mode only (no HBM reduce)");
+}
+
+int fg_u8_to_f32_div(const uint8_t *src, float *dst, size_t n, float divisor, void *) {
+  for (size_t i = 0; i < n; i++) dst[i] = (float)src[i] / divisor;
+  return FG_OK;
+}
+int fg_one_hot_u8(const uint8_t *labels, float *out, size_t n, int classes, void *) {
+  for (size_t i = 0; i < n; i++)
+    for (int c = 0; c < classes; c++) out[i * classes + c] = (int)labels[i] == c ? 1.0f : 0.0f;
+  return FG_OK;
+}
+
+}  // extern "C"

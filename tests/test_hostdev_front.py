@@ -1,0 +1,58 @@
+"""The front end's schedule and rendered kernels executed on the CPU (a
+host implementation of the device ABI, tests/hostdev/) -- an independent
+second oracle for exact mode: whole training steps of Linear/relu/
+cross_entropy/backward/Sgd must equal the C oracle bit for bit.  Runs
+without a GPU; the kernels are the same CUDA C the GPU build compiles."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from ferrograd_b200 import data
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.fixture(scope="module")
+def hostdev():
+    sys.path.insert(0, os.path.join(HERE, "hostdev"))
+    try:
+        import build as hb
+        hb.build()
+    finally:
+        sys.path.pop(0)
+    return os.path.join(HERE, "hostdev", "run_step.py")
+
+
+def run(runner, tmp_path, dims, batch, steps, lr=0.01, seeds=(1, 2)):
+    x, t = data.mlp_batch(batch, dims[0], dims[-1], *seeds)
+    src, dst = tmp_path / "in.npz", tmp_path / "out.npz"
+    np.savez(src, x=x, t=t, dims=np.array(dims), lr=np.array(lr), steps=np.array(steps))
+    subprocess.run([sys.executable, runner, str(src), str(dst)], check=True, timeout=600)
+    return x, t, dict(np.load(dst))
+
+
+@pytest.mark.parametrize("dims,batch", [((64, 32, 10), 32), ((48, 40, 24, 10), 16)])
+def test_host_executed_step_matches_oracle_bitwise(oracle, hostdev, tmp_path, dims, batch):
+    x, t, r = run(hostdev, tmp_path, dims, batch, steps=1)
+    nl = len(dims) - 1
+    ws = [r[f"w0_{i}"] for i in range(nl)]
+    bs = [r[f"b0_{i}"] for i in range(nl)]
+    oloss, ow, ob, odw, odb, _ = oracle.mlp_step(ws, bs, x, t, 0.01)
+    assert np.float32(r["loss"][0]) == np.float32(oloss)
+    for i in range(nl):
+        assert np.array_equal(r[f"dw_{i}"], odw[i])
+        assert np.array_equal(r[f"db_{i}"], odb[i])
+        assert np.array_equal(r[f"w_{i}"], ow[i]) and np.array_equal(r[f"b_{i}"], ob[i])
+
+
+def test_host_executed_steps_track_oracle_and_reuse_programs(oracle, hostdev, tmp_path):
+    dims = (32, 16, 10)
+    x, t, r = run(hostdev, tmp_path, dims, 16, steps=3)
+    ws, bs = [r["w0_0"], r["w0_1"]], [r["b0_0"], r["b0_1"]]
+    for s in range(3):
+        oloss, ws, bs, _, _, _ = oracle.mlp_step(ws, bs, x, t, 0.01)
+        assert np.float32(r["loss"][s]) == np.float32(oloss)
+    assert np.array_equal(r["w_0"], ws[0]) and np.array_equal(r["w_1"], ws[1])
