@@ -183,8 +183,7 @@ UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, std::vector<int64_t> arg = 
   u->dtype = dt;
   u->src = std::move(srcs);
   u->arg = std::move(arg);
-  u->reduce_op = k.rop ? rop : Op::Add;
-  if (op == Op::ReduceAxis) u->reduce_op = rop;
+  u->reduce_op = op == Op::ReduceAxis ? rop : Op::Add;
   u->value = value;
   u->buf = buf;
   u->uid = g_uid++;
