@@ -353,16 +353,18 @@ std::vector<bool> deps(const UOp *n) {
 
 // ---- program cache and generic launches -----------------------------------
 void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelInput> &params,
-                 const BufferP &out);
+                 const BufferP &out, const DeviceBuffer *written = nullptr);
 
-// A one-element buffer passed in the slot of a known-zero input.
+// A one-element buffer passed in the slot of a known-zero input (never in
+// the slot the kernel writes).
 fg_buffer *placeholder_buffer() {
   static fg_buffer *b = nullptr;
   if (!b) check(fg_alloc(device(), FG_F32, 1, &b), "allocate");
   return b;
 }
 
-void launch_rendered(const RenderedKernel &rk, const BufferP &out) {
+void launch_rendered(const RenderedKernel &rk, const BufferP &out,
+                     const DeviceBuffer *written = nullptr) {
   auto &cache = program_cache();
   fg_program *prog = nullptr;
   auto it = cache.find(rk.source);
@@ -384,11 +386,11 @@ void launch_rendered(const RenderedKernel &rk, const BufferP &out) {
                                     (unsigned long long)kid, (unsigned long long)kid, nargs);
   }
   g_last_source = rk.source;
-  launch_args(prog, rk.has_out_slot, rk.params, out);
+  launch_args(prog, rk.has_out_slot, rk.params, out, written);
 }
 
 void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelInput> &params,
-                 const BufferP &out) {
+                 const BufferP &out, const DeviceBuffer *written) {
   const int nargs = (int)params.size() + (has_out_slot ? 1 : 0);
   std::vector<fg_kernel_arg> args;
   args.reserve((size_t)nargs);
@@ -404,7 +406,7 @@ void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelIn
     switch (in.kind) {
       case KernelInput::Buffer:
         a.kind = FG_ARG_BUFFER;
-        if (in.buffer->known_zero() && !in.buffer->is_allocated()) {
+        if (in.buffer->known_zero() && !in.buffer->is_allocated() && in.buffer.get() != written) {
           a.v.buffer = placeholder_buffer();  // the kernel never reads it
         } else {
           in.buffer->ensure_allocated();
@@ -496,6 +498,12 @@ std::unordered_map<std::string, CachedKernel> &spec_cache() {
 // Render (on a miss) and launch one generic kernel.
 void launch_spec(const RenderSpec &spec, const BufferP &out) {
   const bool view = spec.store == RenderSpec::View;
+  const DeviceBuffer *written = nullptr;  // an in-place store's destination
+  if (view) {
+    const UOp *d = spec.dest.get();
+    while (d->op != Op::Buffer && !d->src.empty()) d = d->src[0].get();
+    if (d->op == Op::Buffer) written = d->buf.get();
+  }
   ParamSlots ps = view ? collect_params(make_store(spec.dest, spec.value), 0)
                        : collect_params(spec.value, 1);
   std::string key = spec_key(spec, ps);
@@ -503,7 +511,7 @@ void launch_spec(const RenderSpec &spec, const BufferP &out) {
   auto it = cache.find(key);
   if (it == cache.end()) {
     RenderedKernel rk = render_kernel(spec);
-    launch_rendered(rk, out);
+    launch_rendered(rk, out, written);
     auto pit = program_cache().find(rk.source);
     if (pit != program_cache().end()) cache.emplace(key, CachedKernel{pit->second, rk.has_out_slot});
     return;
@@ -513,7 +521,7 @@ void launch_spec(const RenderSpec &spec, const BufferP &out) {
     fprintf(stderr, "*** CUDA %4llu  (cached)         arg %2d\n",
             (unsigned long long)g_kernel_count++,
             (int)ps.inputs.size() + (it->second.has_out_slot ? 1 : 0));
-  launch_args(it->second.prog, it->second.has_out_slot, ps.inputs, out);
+  launch_args(it->second.prog, it->second.has_out_slot, ps.inputs, out, written);
 }
 
 BufferP temp_buffer(DType dt, int64_t n) {

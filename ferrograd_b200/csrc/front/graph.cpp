@@ -482,8 +482,32 @@ bool should_materialize(const UOp *node, const std::unordered_set<const UOp *> &
 
 }  // namespace
 
+// Post-order walk that does not descend below nodes for which stop() holds
+// (other than the root): a rewrite never needs what lies under a node it
+// replaces or has already rewritten.
+template <typename Stop>
+static std::vector<UOpP> toposort_until(const UOpP &root, Stop stop) {
+  std::vector<UOpP> out;
+  std::unordered_set<const UOp *> visited;
+  std::vector<std::pair<UOpP, bool>> stack{{root, false}};
+  while (!stack.empty()) {
+    auto [node, processed] = stack.back();
+    stack.pop_back();
+    if (visited.count(node.get())) continue;
+    if (processed || (node != root && stop(node.get()))) {
+      visited.insert(node.get());
+      out.push_back(node);
+      continue;
+    }
+    stack.push_back({node, true});
+    for (auto it = node->src.rbegin(); it != node->src.rend(); ++it)
+      if (!visited.count(it->get())) stack.push_back({*it, false});
+  }
+  return out;
+}
+
 UOpP substitute_materialized(const UOpP &root, const ReplMap &repl) {
-  auto order = toposort(root);
+  auto order = toposort_until(root, [&](const UOp *n) { return repl.count(n) > 0; });
   std::unordered_map<const UOp *, UOpP> sub;
   for (auto &node : order) {
     if (node != root) {
@@ -512,7 +536,8 @@ UOpP substitute_materialized(const UOpP &root, const ReplMap &repl) {
 
 UOpP substitute_with_map(const UOpP &root, const std::unordered_map<const UOp *, UOpP> &repl,
                          std::unordered_map<const UOp *, UOpP> &memo) {
-  auto order = toposort(root);
+  auto order = toposort_until(
+      root, [&](const UOp *n) { return repl.count(n) > 0 || memo.count(n) > 0; });
   for (auto &node : order) {
     if (memo.count(node.get())) continue;
     auto r = repl.find(node.get());

@@ -102,15 +102,10 @@ void Tensor::apply_map_to_tensors(const std::map<const UOp *, UOpP> &replacement
   if (replacements.empty()) return;
   std::unordered_map<const UOp *, UOpP> repl(replacements.begin(), replacements.end());
   std::unordered_map<const UOp *, UOpP> memo;
+  // One memoised rewrite over all live tensors: shared subgraphs are walked
+  // once, and a graph that reaches no replaced node comes back unchanged.
   for (Tensor &t : live_tensors()) {
     UOpP cur = t.uop();
-    bool uses = false;
-    for (auto &n : toposort(cur))
-      if (repl.count(n.get())) {
-        uses = true;
-        break;
-      }
-    if (!uses) continue;
     UOpP rewritten = substitute_with_map(cur, repl, memo);
     if (rewritten != cur) t.set_uop(rewritten);
   }

@@ -51,6 +51,7 @@ struct fg_buffer {
   size_t numel;
 };
 struct fg_program {
+  std::string source;
   void *so;
   void (*launch)(void **args, unsigned grid, unsigned block);
   int num_args;
@@ -95,8 +96,18 @@ int fg_device_stream(fg_device *, void **stream) {
 }
 int fg_device_sync(fg_device *) { return FG_OK; }
 
+// Every allocation carries a guard band after its data; fg_execute checks
+// the bands of its buffer arguments after each kernel, so an out-of-bounds
+// write by a rendered kernel is reported with the kernel that made it.
+constexpr size_t kGuard = 256;
+constexpr unsigned char kGuardByte = 0xA7;
+
 int fg_alloc(fg_device *, int dtype, size_t numel, fg_buffer **out) {
-  void *p = numel ? calloc(numel, esize(dtype)) : nullptr;
+  void *p = nullptr;
+  if (numel) {
+    p = calloc(numel * esize(dtype) + kGuard, 1);
+    memset(static_cast<char *>(p) + numel * esize(dtype), kGuardByte, kGuard);
+  }
   *out = new fg_buffer{p, dtype, numel};
   return FG_OK;
 }
@@ -104,6 +115,13 @@ int fg_free(fg_buffer *b) {
   if (b) free(b->p);
   delete b;
   return FG_OK;
+}
+static bool guard_ok(const fg_buffer *b) {
+  if (!b->p) return true;
+  const unsigned char *g = static_cast<const unsigned char *>(b->p) + b->numel * esize(b->dtype);
+  for (size_t i = 0; i < kGuard; i++)
+    if (g[i] != kGuardByte) return false;
+  return true;
 }
 int fg_buffer_info(const fg_buffer *b, void **p, int *dtype, size_t *numel) {
   if (p) *p = b->p;
@@ -169,7 +187,7 @@ int fg_compile(fg_device *, const char *source, const char *func_name, int num_a
       void *h = dlopen(cached_so.c_str(), RTLD_NOW | RTLD_LOCAL);
       auto fn = h ? (void (*)(void **, unsigned, unsigned))dlsym(h, "fg_host_launch") : nullptr;
       if (fn) {
-        *out = new fg_program{h, fn, num_args, grid[0] ? grid[0] : 1, block[0] ? block[0] : 1};
+        *out = new fg_program{src, h, fn, num_args, grid[0] ? grid[0] : 1, block[0] ? block[0] : 1};
         return FG_OK;
       }
     }
@@ -200,7 +218,7 @@ int fg_compile(fg_device *, const char *source, const char *func_name, int num_a
   if (!h) return fg::set_error(FG_ERR_COMPILE, "dlopen: %s", dlerror());
   auto fn = (void (*)(void **, unsigned, unsigned))dlsym(h, "fg_host_launch");
   if (!fn) return fg::set_error(FG_ERR_COMPILE, "launcher missing");
-  *out = new fg_program{h, fn, num_args, grid[0] ? grid[0] : 1, block[0] ? block[0] : 1};
+  *out = new fg_program{src, h, fn, num_args, grid[0] ? grid[0] : 1, block[0] ? block[0] : 1};
   return FG_OK;
 }
 
@@ -237,6 +255,11 @@ int fg_execute(fg_program *prog, const fg_kernel_arg *args, int nargs) {
     }
   }
   prog->launch(slots.data(), prog->grid, prog->block);
+  for (int i = 0; i < nargs; i++)
+    if (args[i].kind == FG_ARG_BUFFER && !guard_ok(args[i].v.buffer))
+      return fg::set_error(FG_ERR_DEVICE,
+                           "kernel wrote past the end of argument %d (%zu elements):\n%s", i,
+                           args[i].v.buffer->numel, prog->source.c_str());
   return FG_OK;
 }
 

@@ -21,10 +21,15 @@ def main(src, dst):
     d = np.load(src)
     dims = [int(v) for v in d["dims"]]
     lr = float(d["lr"])
+    # Initial values from a twin built from the same seed, so the trained
+    # model's parameters are not read (and so not allocated) before the first
+    # step: their first write is the in-place SGD store.
+    F.reset_init_seed(42)
+    twin = [F.Linear(dims[i], dims[i + 1]) for i in range(len(dims) - 1)]
+    ws = [l.weight.numpy() for l in twin]
+    bs = [l.bias.numpy() for l in twin]
     F.reset_init_seed(42)
     layers = [F.Linear(dims[i], dims[i + 1]) for i in range(len(dims) - 1)]
-    ws = [l.weight.numpy() for l in layers]
-    bs = [l.bias.numpy() for l in layers]
     params = [p for l in layers for p in l.parameters()]
     opt = F.Sgd(params, lr)
     x, t = F.Tensor.new(d["x"]), F.Tensor.new(d["t"])

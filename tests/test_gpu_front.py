@@ -245,3 +245,23 @@ def test_front_training_reduces_loss():
     xt, tt = F.tensor(x), F.tensor(t)
     losses = [F.train_step(model, opt, xt, tt) for _ in range(10)]
     assert losses[-1] < losses[0]
+
+
+def test_parameters_never_read_before_training_are_updated(oracle):
+    """The first write of a zero-initialised bias is the in-place SGD store;
+    it must land in the bias itself."""
+    dims, batch = (64, 32, 10), 32
+    x, t = data.mlp_batch(batch, dims[0], dims[-1], 1, 2)
+    ws, bs = mlp_init(dims)
+    F.reset_init_seed(42)
+    model = F.Mlp(dims)
+    opt = F.Sgd(model.parameters(), 0.01)
+    xt, tt = F.tensor(x), F.tensor(t)
+    for _ in range(2):
+        F.train_step(model, opt, xt, tt)
+    for _ in range(2):
+        _, ws, bs, _, _, _ = oracle.mlp_step(ws, bs, x, t, 0.01)
+    for layer, w, b in zip(model.layers, ws, bs):
+        assert np.abs(b).max() > 0
+        assert normrel(layer.bias.numpy(), b) <= TOL
+        assert normrel(layer.weight.numpy(), w) <= TOL
