@@ -210,11 +210,14 @@ def our_arm(args):
     ws, bs = mlp_init(DIMS)  # seeded: identical on every rank
 
     comm = None
-    if world > 1:
+    if world > 1 and args.dp == "nccl":
         uid = dp.exchange_unique_id(dist, rank, Communicator.unique_id)
         comm = Communicator(rank, world, uid, timeout_ms=120000)
     dev = CudaDevice(local)
     tr = MlpTrainer(dev, DIMS, B, LR, ws, bs, comm=comm, use_graph=True)
+    if world > 1 and args.dp == "peer":
+        tr.shard_over_peers(rank, world, lambda h: dp.all_gather_bytes(dist, h, world),
+                            dist.barrier, chunks=args.dp_chunks)
     tr.enable_gemm_timing(True)
 
     xp = torch.from_numpy(x).pin_memory()
@@ -308,6 +311,11 @@ def our_arm(args):
                     "reference Linear::new init (seed-42 LCG Kaiming normal, zero bias)",
             "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "dims": list(DIMS),
                        "per_gpu_batch": B, "parallelism": f"dp{world}",
+                       "gradient_exchange": (None if world == 1 else
+                                             "NCCL all-reduce per layer bucket" if args.dp == "nccl"
+                                             else f"peer-sharded: copy-engine reduce-scatter, owner "
+                                                  f"reduce+SGD, copy-engine all-gather "
+                                                  f"({args.dp_chunks} row chunks of layer 0)"),
                        "l2": "inputs larger than L2 (x shard + 2x64 MiB weights + residuals)",
                        "gemm": "3xTF32 tcgen05 (fp32-accurate)", "graph": "CUDA graph replay"},
             "roofline": roofline,
@@ -638,6 +646,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dp", choices=["nccl", "peer"], default="nccl",
+                    help="gradient exchange of the data-parallel step (N > 1)")
+    ap.add_argument("--dp-chunks", type=int, default=4,
+                    help="row chunks of layer 0's gradient in the peer-sharded exchange")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c5gemm", "c1front",
                                          "c5front"], default="c5",

@@ -4,7 +4,7 @@ C ABI, ``include/ferro_cuda.h``); this package is the host-side binding.
 """
 from ._lib import FerroError, lib  # noqa: F401
 from .device import Buffer, CudaDevice, KernelArg, Program  # noqa: F401
-from .mlp import Communicator, InitRng, MlpTrainer, linear_init, mlp_init  # noqa: F401
+from .mlp import Communicator, InitRng, MlpTrainer, linear_init, mlp_init, peer_layout  # noqa: F401
 
 __all__ = ["FerroError", "lib", "Buffer", "CudaDevice", "KernelArg", "Program", "Communicator",
-           "InitRng", "MlpTrainer", "linear_init", "mlp_init"]
+           "InitRng", "MlpTrainer", "linear_init", "mlp_init", "peer_layout"]

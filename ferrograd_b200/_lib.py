@@ -21,6 +21,7 @@ EPI_NONE, EPI_BIAS, EPI_BIAS_RELU, EPI_RELU_MASK = 0, 1, 2, 3
 GEMM_A_MN_MAJOR, GEMM_B_MN_MAJOR, GEMM_1XTF32 = 1, 2, 4
 ARG_BUFFER, ARG_I32, ARG_F32, ARG_BOOL = 0, 1, 2, 3
 UNIQUE_ID_BYTES = 128
+PEER_HANDLE_BYTES = 96
 
 
 class FerroError(RuntimeError):
@@ -89,6 +90,11 @@ SIGNATURES = [
                                _i, ctypes.POINTER(_i)]),
     ("fg_mlp_comm_times", _i, [_vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double),
                                _i, ctypes.POINTER(_i)]),
+    ("fg_mlp_peer_prepare", _i, [_vp, _i, _i, _i, ctypes.c_char_p]),
+    ("fg_mlp_peer_connect", _i, [_vp, ctypes.c_char_p]),
+    ("fg_mlp_peer_disconnect", _i, [_vp]),
+    ("fg_peer_layout", _i, [_i, ctypes.POINTER(_i), _i, _i, ctypes.POINTER(_sz), ctypes.POINTER(_sz),
+                            ctypes.POINTER(_sz), _i, ctypes.POINTER(_i)]),
     ("fg_comm_unique_id", _i, [ctypes.c_char_p]),
     ("fg_comm_init", _i, [_i, _i, ctypes.c_char_p, _i, _pp]),
     ("fg_comm_destroy", _i, [_vp]),

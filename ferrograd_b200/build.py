@@ -16,7 +16,8 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libferro_cuda.so")
 OBJDIR = os.path.join(HERE, "_build")
 
-SOURCES = ["fg_runtime.cu", "fg_kernels.cu", "fg_gemm.cu", "fg_mlp.cu", "fg_comm.cu", "fg_init.cpp"]
+SOURCES = ["fg_runtime.cu", "fg_kernels.cu", "fg_gemm.cu", "fg_mlp.cu", "fg_comm.cu", "fg_peer.cu",
+           "fg_init.cpp"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -17,6 +17,7 @@
 // backward finishes, overlapping the remaining backward GEMMs.
 #include <cuda_runtime.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <vector>
 
@@ -24,6 +25,7 @@
 #include "fg_gemm.cuh"
 #include "fg_internal.h"
 #include "fg_kernels.cuh"
+#include "fg_peer.cuh"
 
 namespace fg {
 
@@ -281,6 +283,12 @@ struct Layer {
   // (used for layer 0, whose bucket is the last one of the backward pass)
   bool can_split_w = false;
   fg::gemm::GemmPlan bwd_w_half[2];
+  // Peer-sharded mode: this layer's parameters of even / odd steps inside
+  // the exchange region, the GEMM plans that read each of them, and (layer
+  // 0) dW as row blocks, one per gradient chunk.
+  float *Wp[2] = {nullptr, nullptr}, *bp[2] = {nullptr, nullptr}, *W_lo_p[2] = {nullptr, nullptr};
+  fg::gemm::GemmPlan fwd_p[2], bwd_x_p[2];
+  fg::gemm::GemmPlan bwd_w_part[fg::kMaxPeerParts];
 };
 
 size_t pad64(size_t n) { return (n + 63) / 64 * 64; }
@@ -318,6 +326,25 @@ struct fg_mlp {
   int comm_launches = 0;
   int launches_per_step = 0;
   int sms = 148;
+  float *sk_ws = nullptr;  // stream-K workspace shared by every GEMM plan
+  // Peer-sharded data parallelism (fg_mlp_peer_prepare / fg_mlp_peer_connect).
+  bool peer = false;  // connected: fg_mlp_step runs enqueue_step_peer
+  int peer_rank = 0, peer_n = 0;
+  fg::PeerLayout pl;
+  float *region = nullptr;  // this rank's exchange region (fg_peer.cuh)
+  float *pg = nullptr, *pstage = nullptr, *pP[2] = {nullptr, nullptr}, *pLO[2] = {nullptr, nullptr};
+  unsigned int *pflags = nullptr;
+  char *peer_base[fg::kMaxPeers] = {};  // other ranks' regions, mapped (null for self)
+  int par = 0;                          // parameter buffer the next step reads
+  int reduce_blocks = 64;
+  // all-gather the TF32 residual with the parameters (else each rank
+  // recomputes it for the chunks that arrive)
+  bool push_lo = true;
+  cudaStream_t rs_st[fg::kMaxPeers] = {}, ag_st[fg::kMaxPeers] = {};
+  cudaStream_t red_st = nullptr, sig_rs_st = nullptr, sig_ag_st = nullptr, arr_st = nullptr;
+  cudaEvent_t ev_ready = nullptr, ev_red = nullptr, ev_join = nullptr;
+  cudaEvent_t ev_rs[fg::kMaxPeers] = {}, ev_ag[fg::kMaxPeers] = {};
+  cudaGraphExec_t pgraph[2] = {nullptr, nullptr};
 };
 
 namespace {
@@ -549,6 +576,180 @@ int enqueue_step(fg_mlp *m) {
   return FG_OK;
 }
 
+// ---- peer-sharded data parallelism ----------------------------------------
+// Byte address of float `idx` of area `area` (0 grad, 1 stage, 2/3 P0/P1,
+// 4/5 LO0/LO1) in rank j's region (this rank's own or a peer's mapping).
+float *region_f(fg_mlp *m, int j, int area, size_t idx) {
+  char *base = (j == m->peer_rank) ? reinterpret_cast<char *>(m->region) : m->peer_base[j];
+  return reinterpret_cast<float *>(base) + (size_t)area * m->pl.grad + idx;
+}
+
+// Flag word of chunk ci set by sender `from` in rank j's region
+// (phase 0: reduce-scatter, 1: all-gather).
+unsigned int *region_flag(fg_mlp *m, int j, int phase, int ci, int from) {
+  char *base = (j == m->peer_rank) ? reinterpret_cast<char *>(m->region) : m->peer_base[j];
+  unsigned int *f = reinterpret_cast<unsigned int *>(reinterpret_cast<float *>(base) + 6 * m->pl.grad);
+  return f + ((size_t)phase * m->pl.chunks.size() + ci) * fg::kMaxPeers + from;
+}
+
+// Current-parameter pointers of every layer (what get/set_params and the
+// host see) follow the parity of the next step.
+void peer_point(fg_mlp *m) {
+  for (auto &ly : m->L) {
+    ly.W = ly.Wp[m->par];
+    ly.b = ly.bp[m->par];
+    ly.W_lo = ly.W_lo_p[m->par];
+  }
+}
+
+// Exchange of gradient chunk ci of a step that reads parameter buffer par:
+//   1. reduce-scatter: once the chunk is complete on the compute stream,
+//      this rank's part of every other rank's shard is copied (copy engine,
+//      one stream per peer) into that rank's staging slot for this rank,
+//      then the peers' flags are raised;
+//   2. the owner's kernel waits for every peer's flag, sums the
+//      contributions in rank order and writes the SGD update of its shard
+//      into buffer par ^ 1 (and its TF32 residual);
+//   3. all-gather: the updated shard is copied into every peer's buffer
+//      par ^ 1 and the peers' all-gather flags are raised.
+// Flags carry par + 1, so a waiter can never mistake the previous step's
+// value for the current one (ranks are at most one step apart).
+int peer_chunk(fg_mlp *m, int ci, int par) {
+  const fg::PeerChunk &c = m->pl.chunks[ci];
+  const int n = m->peer_n, r = m->peer_rank, nx = par ^ 1;
+  const size_t S = c.len / n;
+  const unsigned int val = (unsigned int)par + 1;
+  int rc;
+  FG_CUDA_TRY(cudaEventRecord(m->ev_ready, m->st));
+  for (int p = 0; p < n; p++) {
+    if (p == r) continue;
+    FG_CUDA_TRY(cudaStreamWaitEvent(m->rs_st[p], m->ev_ready, 0));
+    FG_CUDA_TRY(cudaMemcpyAsync(region_f(m, p, 1, c.off + (size_t)r * S), m->pg + c.off + (size_t)p * S,
+                                S * sizeof(float), cudaMemcpyDefault, m->rs_st[p]));
+    FG_CUDA_TRY(cudaEventRecord(m->ev_rs[p], m->rs_st[p]));
+    FG_CUDA_TRY(cudaStreamWaitEvent(m->sig_rs_st, m->ev_rs[p], 0));
+  }
+  fg::PeerFlagPtrs f{};
+  for (int p = 0; p < n; p++) f.p[p] = (p == r) ? nullptr : region_flag(m, p, 0, ci, r);
+  if ((rc = fg::launch_peer_signal(f, val, m->sig_rs_st))) return rc;
+
+  FG_CUDA_TRY(cudaStreamWaitEvent(m->red_st, m->ev_ready, 0));
+  const size_t loss = m->pl.loss_off;
+  const long long loss_idx = (loss >= c.off && loss < c.off + c.len) ? (long long)(loss - c.off) : -1;
+  fg::DevCtx *ctx = fg::ctx_current();
+  if ((rc = fg::launch_peer_reduce_sgd(m->pg + c.off, m->pstage + c.off, m->pP[par] + c.off,
+                                       m->pP[nx] + c.off, m->pLO[nx] + c.off, S, r, n, m->lr,
+                                       loss_idx, region_flag(m, r, 0, ci, 0), val,
+                                       ctx ? ctx->d_err : nullptr, m->reduce_blocks, m->red_st)))
+    return rc;
+  FG_CUDA_TRY(cudaEventRecord(m->ev_red, m->red_st));
+  for (int p = 0; p < n; p++) {
+    if (p == r) continue;
+    const size_t at = c.off + (size_t)r * S;
+    FG_CUDA_TRY(cudaStreamWaitEvent(m->ag_st[p], m->ev_red, 0));
+    FG_CUDA_TRY(cudaMemcpyAsync(region_f(m, p, 2 + nx, at), m->pP[nx] + at, S * sizeof(float),
+                                cudaMemcpyDefault, m->ag_st[p]));
+    if (m->push_lo)
+      FG_CUDA_TRY(cudaMemcpyAsync(region_f(m, p, 4 + nx, at), m->pLO[nx] + at, S * sizeof(float),
+                                  cudaMemcpyDefault, m->ag_st[p]));
+    FG_CUDA_TRY(cudaEventRecord(m->ev_ag[p], m->ag_st[p]));
+    FG_CUDA_TRY(cudaStreamWaitEvent(m->sig_ag_st, m->ev_ag[p], 0));
+  }
+  for (int p = 0; p < n; p++) f.p[p] = (p == r) ? nullptr : region_flag(m, p, 1, ci, r);
+  if ((rc = fg::launch_peer_signal(f, val, m->sig_ag_st))) return rc;
+  if (m->push_lo) return FG_OK;
+  // 4. without residuals on the wire: once every peer's shard of this chunk
+  //    has landed (and this rank's own reduce is done), recompute the
+  //    chunk's TF32 residual here
+  FG_CUDA_TRY(cudaStreamWaitEvent(m->arr_st, m->ev_red, 0));
+  if ((rc = fg::launch_peer_wait(region_flag(m, r, 1, ci, 0), 1, n, r, val,
+                                 ctx ? ctx->d_err : nullptr, m->arr_st)))
+    return rc;
+  return fg::launch_peer_lo(m->pP[nx] + c.off, m->pLO[nx] + c.off, c.len, m->reduce_blocks,
+                            m->arr_st);
+}
+
+int join_into(fg_mlp *m, cudaStream_t from) {
+  FG_CUDA_TRY(cudaEventRecord(m->ev_join, from));
+  FG_CUDA_TRY(cudaStreamWaitEvent(m->st, m->ev_join, 0));
+  return FG_OK;
+}
+
+// One training step in peer-sharded mode, reading parameter buffer par and
+// leaving the updated parameters (and the global loss) in buffer par ^ 1 on
+// every rank.  Same kernels as enqueue_step; the gradient exchange of each
+// chunk starts as soon as the chunk is complete and overlaps the remaining
+// backward GEMMs; the step ends when every peer's all-gather has landed.
+int enqueue_step_peer(fg_mlp *m, int par) {
+  cudaStream_t st = m->st;
+  const int B = m->B;
+  int rc;
+  m->gemm_launches = 0;
+  m->comm_launches = 0;
+  if (m->L[0].tc && (rc = fg::launch_split_lo(m->x, m->x_lo, (size_t)B * m->dims[0], st))) return rc;
+  for (int l = 0; l < m->nl; l++) {
+    Layer &ly = m->L[l];
+    const float *in = (l == 0) ? m->x : m->act[l - 1];
+    if (ly.tc) {
+      if ((rc = run_gemm(m, ly.fwd_p[par], st))) return rc;
+    } else if ((rc = fg::launch_skinny_fwd(ly.out, in, ly.Wp[par], ly.bp[par], m->act[l], B, ly.in,
+                                           st, m->sms))) {
+      return rc;
+    }
+  }
+  const int C = m->dims[m->nl];
+  const float rank_scale = 1.0f / (float)m->peer_n;
+  if ((rc = fg::launch_xent(m->act[m->nl - 1], m->t, (size_t)B, (size_t)C, m->loss, m->G[m->nl - 1],
+                            rank_scale, st, m->scratch, rank_scale)))
+    return rc;
+  if (m->L[m->nl - 1].tc &&
+      (rc = fg::launch_split_lo(m->G[m->nl - 1], m->G_lo[m->nl - 1], (size_t)B * C, st)))
+    return rc;
+  for (int l = m->nl - 1; l >= 0; l--) {
+    Layer &ly = m->L[l];
+    const float *in = (l == 0) ? m->x : m->act[l - 1];
+    const int c0 = m->pl.first_chunk[l], nc = m->pl.n_chunks[l];
+    if (!ly.tc) {
+      if ((rc = fg::launch_skinny_bwd(ly.out, m->G[l], in, ly.Wp[par], m->scratch, ly.dW,
+                                      l > 0 ? m->G[l - 1] : nullptr,
+                                      (l > 0 && m->L[l - 1].tc) ? m->G_lo[l - 1] : nullptr, B,
+                                      ly.in, st, m->sms)))
+        return rc;
+    } else if (nc > 1) {  // layer 0: dW row block q is chunk q
+      for (int q = 0; q < nc; q++) {
+        if ((rc = run_gemm(m, ly.bwd_w_part[q], st))) return rc;
+        if (q == nc - 1 &&
+            (rc = fg::launch_reduce_cols(FG_F32, FG_REDUCE_SUM, m->G[l], ly.db, (size_t)B,
+                                         (size_t)ly.out, st, m->scratch, m->scratch_bytes)))
+          return rc;
+        if ((rc = peer_chunk(m, c0 + q, par))) return rc;
+      }
+      continue;
+    } else if ((rc = run_gemm(m, ly.bwd_w, st))) {
+      return rc;
+    }
+    if ((rc = fg::launch_reduce_cols(FG_F32, FG_REDUCE_SUM, m->G[l], ly.db, (size_t)B, (size_t)ly.out,
+                                     st, m->scratch, m->scratch_bytes)))
+      return rc;
+    for (int q = 0; q < nc; q++)
+      if ((rc = peer_chunk(m, c0 + q, par))) return rc;
+    if (ly.tc && l > 0 && (rc = run_gemm(m, ly.bwd_x_p[par], st))) return rc;
+  }
+  for (int p = 0; p < m->peer_n; p++) {
+    if (p == m->peer_rank) continue;
+    if ((rc = join_into(m, m->rs_st[p])) || (rc = join_into(m, m->ag_st[p]))) return rc;
+  }
+  // join every side stream this step used (a stream with no work in a
+  // captured step must not be joined: it is not part of the capture)
+  for (cudaStream_t s2 : {m->red_st, m->sig_rs_st, m->sig_ag_st})
+    if ((rc = join_into(m, s2))) return rc;
+  if (!m->push_lo && (rc = join_into(m, m->arr_st))) return rc;
+  fg::DevCtx *ctx = fg::ctx_current();
+  return fg::launch_peer_wait(region_flag(m, m->peer_rank, 1, 0, 0), (int)m->pl.chunks.size(),
+                              m->peer_n, m->peer_rank, (unsigned int)par + 1,
+                              ctx ? ctx->d_err : nullptr, st);
+}
+
 }  // namespace
 
 extern "C" {
@@ -647,6 +848,7 @@ int fg_mlp_create(fg_device *dev, int n_layers, const int *dims, int batch, floa
   {
     float *ws = nullptr;
     if ((rc = mlp_alloc(m, &ws, fg::gemm::stream_k_ws_bytes(m->sms) / 4 + 1))) return fail(rc);
+    m->sk_ws = ws;
     for (int l = 0; l < m->nl; l++) {
       Layer &ly = m->L[l];
       if (!ly.tc) continue;
@@ -674,6 +876,19 @@ int fg_mlp_destroy(fg_mlp *m) {
   if (m->ev_comm_done) cudaEventDestroy(m->ev_comm_done);
   if (m->ev_half) cudaEventDestroy(m->ev_half);
   if (m->comm_st) cudaStreamDestroy(m->comm_st);
+  for (auto g : m->pgraph)
+    if (g) cudaGraphExecDestroy(g);
+  for (int j = 0; j < fg::kMaxPeers; j++) {
+    if (m->peer_base[j]) cudaIpcCloseMemHandle(m->peer_base[j]);
+    if (m->rs_st[j]) cudaStreamDestroy(m->rs_st[j]);
+    if (m->ag_st[j]) cudaStreamDestroy(m->ag_st[j]);
+    if (m->ev_rs[j]) cudaEventDestroy(m->ev_rs[j]);
+    if (m->ev_ag[j]) cudaEventDestroy(m->ev_ag[j]);
+  }
+  for (cudaStream_t s2 : {m->red_st, m->sig_rs_st, m->sig_ag_st, m->arr_st})
+    if (s2) cudaStreamDestroy(s2);
+  for (cudaEvent_t e : {m->ev_ready, m->ev_red, m->ev_join})
+    if (e) cudaEventDestroy(e);
   for (void *p : m->allocations) cudaFree(p);
   delete m;
   return FG_OK;
@@ -714,6 +929,26 @@ int fg_mlp_get_grads(fg_mlp *m, int layer, float *h_dweight, float *h_dbias) {
   FG_REQUIRE(m && layer >= 0 && layer < m->nl, "fg_mlp_get_grads: bad layer");
   Layer &ly = m->L[layer];
   FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  if (m->peer) {
+    // Each shard's reduced gradient lives in its owner's gradient area.
+    FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+    const int c0 = m->pl.first_chunk[layer], nc = m->pl.n_chunks[layer];
+    const size_t base = m->pl.chunks[c0].off;
+    const fg::PeerChunk &last = m->pl.chunks[c0 + nc - 1];
+    std::vector<float> bucket(last.off + last.len - base);
+    for (int ci = c0; ci < c0 + nc; ci++) {
+      const fg::PeerChunk &c = m->pl.chunks[ci];
+      const size_t S = c.len / m->peer_n;
+      for (int j = 0; j < m->peer_n; j++)
+        FG_CUDA_TRY(cudaMemcpy(bucket.data() + (c.off - base) + (size_t)j * S,
+                               region_f(m, j, 0, c.off + (size_t)j * S), S * sizeof(float),
+                               cudaMemcpyDefault));
+    }
+    if (h_dweight)
+      memcpy(h_dweight, bucket.data() + (m->pl.w_off[layer] - base), sizeof(float) * ly.out * ly.in);
+    if (h_dbias) memcpy(h_dbias, bucket.data() + (m->pl.b_off[layer] - base), sizeof(float) * ly.out);
+    return fg_check_device_error();
+  }
   if (h_dweight)
     FG_CUDA_TRY(cudaMemcpyAsync(h_dweight, ly.dW, sizeof(float) * ly.out * ly.in,
                                 cudaMemcpyDeviceToHost, m->st));
@@ -725,6 +960,7 @@ int fg_mlp_get_grads(fg_mlp *m, int layer, float *h_dweight, float *h_dbias) {
 
 int fg_mlp_attach_comm(fg_mlp *m, fg_comm *comm) {
   FG_REQUIRE(m, "fg_mlp_attach_comm: null mlp");
+  FG_REQUIRE(!m->region, "fg_mlp_attach_comm: this step uses the peer-sharded exchange");
   FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
   if (m->graph) {
     cudaGraphExecDestroy(m->graph);
@@ -769,6 +1005,11 @@ int fg_mlp_use_graph(fg_mlp *m, int enable) {
     cudaGraphExecDestroy(m->graph);
     m->graph = nullptr;
   }
+  for (auto &g : m->pgraph)
+    if (!m->use_graph && g) {
+      cudaGraphExecDestroy(g);
+      g = nullptr;
+    }
   return FG_OK;
 }
 
@@ -776,6 +1017,40 @@ int fg_mlp_step(fg_mlp *m, float *d_loss_out) {
   FG_REQUIRE(m, "fg_mlp_step: null mlp");
   FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
   int rc;
+  if (m->region) {
+    FG_REQUIRE(m->peer, "fg_mlp_step: fg_mlp_peer_connect has not been called");
+    const int par = m->par;
+    if (m->use_graph && m->pgraph[par]) {
+      FG_CUDA_TRY(cudaGraphLaunch(m->pgraph[par], m->st));
+    } else {
+      // the first step of each parity runs eagerly (every rank takes part),
+      // then its graph is captured for the later steps of that parity
+      uint64_t before = fg_kernel_launches();
+      if ((rc = enqueue_step_peer(m, par))) return rc;
+      m->launches_per_step = (int)(fg_kernel_launches() - before);
+      if (m->use_graph) {
+        FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+        cudaGraph_t g;
+        FG_CUDA_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+        rc = enqueue_step_peer(m, par);
+        cudaError_t ce = cudaStreamEndCapture(m->st, &g);
+        if (rc) {
+          if (ce == cudaSuccess) cudaGraphDestroy(g);
+          return rc;
+        }
+        FG_CUDA_TRY(ce);
+        cudaError_t ie = cudaGraphInstantiate(&m->pgraph[par], g, 0);
+        cudaGraphDestroy(g);
+        FG_CUDA_TRY(ie);
+      }
+    }
+    m->par ^= 1;
+    peer_point(m);
+    if (d_loss_out)
+      FG_CUDA_TRY(cudaMemcpyAsync(d_loss_out, m->pP[m->par] + m->pl.loss_off, sizeof(float),
+                                  cudaMemcpyDeviceToDevice, m->st));
+    return FG_OK;
+  }
   if (m->use_graph) {
     if (!m->graph) {
       // First call: run eagerly once (counts launches, settles lazy init),
@@ -819,7 +1094,9 @@ int fg_mlp_step_host(fg_mlp *m, const float *h_x, const float *h_targets, float 
   int rc = fg_mlp_step(m, nullptr);
   if (rc) return rc;
   if (h_loss) {
-    FG_CUDA_TRY(cudaMemcpyAsync(h_loss, m->loss, sizeof(float), cudaMemcpyDeviceToHost, m->st));
+    // peer-sharded: the global loss travels with the parameters it produced
+    const float *src = m->region ? m->pP[m->par] + m->pl.loss_off : m->loss;
+    FG_CUDA_TRY(cudaMemcpyAsync(h_loss, src, sizeof(float), cudaMemcpyDeviceToHost, m->st));
     FG_CUDA_TRY(cudaStreamSynchronize(m->st));
     return fg_check_device_error();
   }
@@ -852,9 +1129,14 @@ int fg_mlp_enable_gemm_timing(fg_mlp *m, int enable) {
     cudaGraphExecDestroy(m->graph);
     m->graph = nullptr;
   }
+  for (auto &g : m->pgraph)
+    if (g) {
+      cudaGraphExecDestroy(g);
+      g = nullptr;
+    }
   m->timing = enable != 0;
   if (m->timing && m->ev_t0.empty()) {
-    const int n = 3 * m->nl;
+    const int n = 3 * m->nl + fg::kMaxPeerParts;
     m->ev_t0.resize(n);
     m->ev_t1.resize(n);
     m->gemm_flops.assign(n, 0.0);
@@ -908,6 +1190,195 @@ int fg_mlp_launch_count(fg_mlp *m, int *count) {
   FG_REQUIRE(m && count, "fg_mlp_launch_count: null argument");
   *count = m->launches_per_step;
   return FG_OK;
+}
+
+// ---- peer-sharded data parallelism ----------------------------------------
+// Handle bytes: [0, 64) cudaIpcMemHandle_t of the region, then region bytes
+// (u64), rank, nranks, parts (i32 each), layout digest (u32), magic.
+static const char kPeerMagic[8] = {'F', 'G', 'P', 'E', 'E', 'R', '0', '1'};
+struct PeerHandle {
+  cudaIpcMemHandle_t ipc;
+  unsigned long long bytes;
+  int rank, nranks, parts;
+  unsigned int digest;
+  char magic[8];
+};
+static_assert(sizeof(PeerHandle) <= FG_PEER_HANDLE_BYTES, "peer handle size");
+
+static int env_int(const char *name, int dflt, int lo, int hi) {
+  const char *e = getenv(name);
+  int v = (e && *e) ? atoi(e) : dflt;
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+
+int fg_mlp_peer_prepare(fg_mlp *m, int rank, int nranks, int chunks,
+                        char handle_out[FG_PEER_HANDLE_BYTES]) {
+  FG_REQUIRE(m && handle_out, "fg_mlp_peer_prepare: null argument");
+  FG_REQUIRE(!m->comm, "fg_mlp_peer_prepare: an NCCL communicator is attached");
+  FG_REQUIRE(!m->region, "fg_mlp_peer_prepare: already prepared");
+  FG_REQUIRE(nranks >= 2 && nranks <= fg::kMaxPeers && rank >= 0 && rank < nranks,
+             "fg_mlp_peer_prepare: rank %d of %d (2 to %d ranks)", rank, nranks, fg::kMaxPeers);
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  fg::PeerLayout L;
+  int rc = fg::peer_layout(m->nl, m->dims.data(), nranks, chunks, &L);
+  if (rc) return rc;
+  FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+  float *region = nullptr;
+  if ((rc = mlp_alloc(m, &region, L.region))) return rc;
+  m->region = region;
+  m->pl = L;
+  m->peer_rank = rank;
+  m->peer_n = nranks;
+  m->pg = region;
+  m->pstage = region + L.grad;
+  for (int q = 0; q < 2; q++) {
+    m->pP[q] = region + (size_t)(2 + q) * L.grad;
+    m->pLO[q] = region + (size_t)(4 + q) * L.grad;
+  }
+  m->pflags = reinterpret_cast<unsigned int *>(region + 6 * L.grad);
+  // the current parameters (and residuals) become buffer 0
+  for (int l = 0; l < m->nl; l++) {
+    Layer &ly = m->L[l];
+    const size_t nw = (size_t)ly.out * ly.in;
+    for (int q = 0; q < 2; q++) {
+      ly.Wp[q] = m->pP[q] + L.w_off[l];
+      ly.bp[q] = m->pP[q] + L.b_off[l];
+      ly.W_lo_p[q] = m->pLO[q] + L.w_off[l];
+    }
+    FG_CUDA_TRY(cudaMemcpyAsync(ly.Wp[0], ly.W, nw * sizeof(float), cudaMemcpyDeviceToDevice, m->st));
+    FG_CUDA_TRY(cudaMemcpyAsync(ly.bp[0], ly.b, ly.out * sizeof(float), cudaMemcpyDeviceToDevice, m->st));
+    if ((rc = fg::launch_split_lo(ly.Wp[0], ly.W_lo_p[0], nw, m->st))) return rc;
+    ly.dW = m->pg + L.w_off[l];
+    ly.db = m->pg + L.b_off[l];
+  }
+  m->loss = m->pg + L.loss_off;
+  // GEMM plans for both parameter buffers, and layer 0's dW row blocks
+  for (int q = 1; q >= 0; q--) {
+    m->par = q;
+    peer_point(m);
+    if ((rc = build_plans(m))) return rc;
+    for (auto &ly : m->L) {
+      ly.fwd_p[q] = ly.fwd;
+      ly.bwd_x_p[q] = ly.bwd_x;
+    }
+  }
+  Layer &l0 = m->L[0];
+  const int parts = L.n_chunks[0];
+  if (l0.tc && parts > 1) {
+    const int rows = l0.out / parts;
+    for (int q = 0; q < parts; q++)
+      if ((rc = fg::gemm::make_plan(rows, l0.in, m->B, m->G[0] + q * rows, m->G_lo[0] + q * rows,
+                                    l0.out, m->x, m->x_lo, l0.in, l0.dW + (size_t)q * rows * l0.in,
+                                    nullptr, l0.in, FG_GEMM_A_MN_MAJOR | FG_GEMM_B_MN_MAJOR,
+                                    FG_EPI_NONE, nullptr, nullptr, 0, &l0.bwd_w_part[q])))
+        return rc;
+  }
+  // SMs left free beside the backward GEMMs (FG_PEER_SM_RESERVE, default 0:
+  // the exchange moves bytes with the copy engines; the owner's reduce
+  // kernel shares SMs with the GEMM's CTAs)
+  const int reserve = env_int("FG_PEER_SM_RESERVE", 0, 0, 64);
+  const int cap = reserve ? m->sms - reserve : 0;
+  for (auto &ly : m->L) {
+    if (!ly.tc) continue;
+    for (fg::gemm::GemmPlan *p2 : {&ly.fwd_p[0], &ly.fwd_p[1], &ly.bwd_w, &ly.bwd_x_p[0], &ly.bwd_x_p[1],
+                                   &ly.fwd, &ly.bwd_x})
+      fg::gemm::stream_k_attach(p2, m->sk_ws, m->sms);
+    ly.bwd_w.max_ctas = cap;
+    ly.bwd_x_p[0].max_ctas = ly.bwd_x_p[1].max_ctas = cap;
+    for (int q = 0; q < parts && &ly == &l0; q++) {
+      fg::gemm::stream_k_attach(&ly.bwd_w_part[q], m->sk_ws, m->sms);
+      ly.bwd_w_part[q].max_ctas = cap;
+    }
+  }
+  m->reduce_blocks = env_int("FG_PEER_REDUCE_BLOCKS", 64, 1, 1024);
+  m->push_lo = env_int("FG_PEER_PUSH_LO", 1, 0, 1) != 0;
+  m->par = 0;
+  peer_point(m);
+  // streams: copies to each peer (reduce-scatter and all-gather apart, so
+  // one chunk's all-gather never holds up the next chunk's reduce-scatter);
+  // the owner's reduce and the two signal streams at the highest priority
+  int lo_prio = 0, hi_prio = 0;
+  FG_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio));
+  for (int p = 0; p < nranks; p++) {
+    if (p == rank) continue;
+    FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->rs_st[p], cudaStreamNonBlocking));
+    FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->ag_st[p], cudaStreamNonBlocking));
+    FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_rs[p], cudaEventDisableTiming));
+    FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_ag[p], cudaEventDisableTiming));
+  }
+  for (cudaStream_t *s2 : {&m->red_st, &m->sig_rs_st, &m->sig_ag_st, &m->arr_st})
+    FG_CUDA_TRY(cudaStreamCreateWithPriority(s2, cudaStreamNonBlocking, hi_prio));
+  for (cudaEvent_t *e : {&m->ev_ready, &m->ev_red, &m->ev_join})
+    FG_CUDA_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+  if (m->graph) {
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  PeerHandle h;
+  memset(&h, 0, sizeof(h));
+  FG_CUDA_TRY(cudaIpcGetMemHandle(&h.ipc, region));
+  h.bytes = (unsigned long long)L.region * sizeof(float);
+  h.rank = rank;
+  h.nranks = nranks;
+  h.parts = L.parts;
+  h.digest = L.digest;
+  memcpy(h.magic, kPeerMagic, sizeof(kPeerMagic));
+  memset(handle_out, 0, FG_PEER_HANDLE_BYTES);
+  memcpy(handle_out, &h, sizeof(h));
+  FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+  return FG_OK;
+}
+
+int fg_mlp_peer_connect(fg_mlp *m, const char *handles) {
+  FG_REQUIRE(m && handles, "fg_mlp_peer_connect: null argument");
+  FG_REQUIRE(m->region, "fg_mlp_peer_connect: fg_mlp_peer_prepare has not been called");
+  FG_REQUIRE(!m->peer, "fg_mlp_peer_connect: already connected");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  // every handle must describe the same layout, in rank order
+  for (int j = 0; j < m->peer_n; j++) {
+    PeerHandle h;
+    memcpy(&h, handles + (size_t)j * FG_PEER_HANDLE_BYTES, sizeof(h));
+    FG_REQUIRE(memcmp(h.magic, kPeerMagic, sizeof(kPeerMagic)) == 0,
+               "fg_mlp_peer_connect: handle %d is not a peer handle", j);
+    FG_REQUIRE(h.rank == j && h.nranks == m->peer_n,
+               "fg_mlp_peer_connect: handle %d is rank %d of %d (expected %d of %d)", j, h.rank,
+               h.nranks, j, m->peer_n);
+    FG_REQUIRE(h.digest == m->pl.digest && h.bytes == (unsigned long long)m->pl.region * sizeof(float),
+               "fg_mlp_peer_connect: rank %d has a different exchange layout (dims, ranks or chunks differ)",
+               j);
+  }
+  for (int j = 0; j < m->peer_n; j++) {
+    if (j == m->peer_rank) continue;
+    PeerHandle h;
+    memcpy(&h, handles + (size_t)j * FG_PEER_HANDLE_BYTES, sizeof(h));
+    void *p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h.ipc, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int k = 0; k < j; k++)
+        if (m->peer_base[k]) {
+          cudaIpcCloseMemHandle(m->peer_base[k]);
+          m->peer_base[k] = nullptr;
+        }
+      return fg::set_error(FG_ERR_CUDA, "fg_mlp_peer_connect: mapping rank %d's region failed: %s", j,
+                           cudaGetErrorString(e));
+    }
+    m->peer_base[j] = static_cast<char *>(p);
+  }
+  m->peer = true;
+  return FG_OK;
+}
+
+int fg_mlp_peer_disconnect(fg_mlp *m) {
+  FG_REQUIRE(m, "fg_mlp_peer_disconnect: null mlp");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  FG_CUDA_TRY(cudaDeviceSynchronize());
+  for (int j = 0; j < fg::kMaxPeers; j++)
+    if (m->peer_base[j]) {
+      FG_CUDA_TRY(cudaIpcCloseMemHandle(m->peer_base[j]));
+      m->peer_base[j] = nullptr;
+    }
+  m->peer = false;
+  return fg_check_device_error();
 }
 
 }  // extern "C"

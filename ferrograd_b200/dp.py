@@ -5,7 +5,8 @@ shards; every rank starts from the same seeded parameters (the reference's
 init is deterministic, src/nn.rs:12-26), computes the mean loss / gradients
 of its shard, and the gradients are averaged across ranks (NCCL, on the GPU)
 before the SGD update, so the update equals the full-batch one.  The NCCL
-unique id travels over the torch.distributed store/process group.
+unique id, or the peer-sharded exchange's handles, travel over the
+torch.distributed process group.
 """
 from __future__ import annotations
 
@@ -30,6 +31,13 @@ def exchange_unique_id(dist, rank: int, make_id) -> bytes:
     box = [make_id() if rank == 0 else None]
     dist.broadcast_object_list(box, src=0)
     return box[0]
+
+
+def all_gather_bytes(dist, data: bytes, world: int):
+    """Every rank's ``data`` in rank order (peer-sharded exchange handles)."""
+    out = [None] * world
+    dist.all_gather_object(out, bytes(data))
+    return out
 
 
 def params_digest(arrays: Sequence[np.ndarray]) -> str:

@@ -6,12 +6,13 @@
 * :class:`MlpTrainer` -- one ``forward -> cross_entropy -> zero_grad ->
   backward -> Sgd::step -> loss.to_vec()`` step per call, planned once and
   replayed (optionally as a CUDA graph), data parallel when given a
-  :class:`Communicator`.
+  :class:`Communicator` or after :meth:`MlpTrainer.shard_over_peers`.
+* :func:`peer_layout` -- the chunks of the peer-sharded gradient exchange.
 """
 from __future__ import annotations
 
 import ctypes
-from typing import List, Optional, Sequence, Tuple
+from typing import Callable, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -99,8 +100,30 @@ class MlpTrainer:
             call("fg_mlp_attach_comm", self._h, comm._h)
         call("fg_mlp_use_graph", self._h, 1 if use_graph else 0)
 
+    def shard_over_peers(self, rank: int, world: int, all_gather: Callable[[bytes], List[bytes]],
+                         barrier: Callable[[], None], chunks: int = 4) -> None:
+        """Peer-sharded data parallelism instead of an NCCL communicator: the
+        gradients move between the ranks' GPUs with the copy engines, each rank
+        reduces and updates its shard of the parameters, and the updated shards
+        are copied back to every rank (``fg_mlp_peer_prepare`` / ``_connect``).
+        ``all_gather(handle)`` returns every rank's handle in rank order;
+        ``barrier()`` is a host barrier over the same ranks (used at close)."""
+        buf = ctypes.create_string_buffer(_lib.PEER_HANDLE_BYTES)
+        call("fg_mlp_peer_prepare", self._h, int(rank), int(world), int(chunks), buf)
+        handles = [bytes(h) for h in all_gather(buf.raw)]
+        if len(handles) != world or any(len(h) != _lib.PEER_HANDLE_BYTES for h in handles):
+            raise ValueError("shard_over_peers: expected one handle per rank")
+        call("fg_mlp_peer_connect", self._h, b"".join(handles))
+        self._peer_barrier = barrier
+
     def close(self) -> None:
         if getattr(self, "_h", None):
+            barrier = getattr(self, "_peer_barrier", None)
+            if barrier is not None:
+                # unmap the peers' regions everywhere before any region is freed
+                call("fg_mlp_peer_disconnect", self._h)
+                barrier()
+                self._peer_barrier = None
             call("fg_mlp_destroy", self._h)
             self._h = None
 
@@ -190,3 +213,17 @@ class MlpTrainer:
         n = ctypes.c_int()
         call("fg_mlp_launch_count", self._h, ctypes.byref(n))
         return n.value
+
+
+def peer_layout(dims: Sequence[int], nranks: int, chunks: int = 4):
+    """(region floats, [(offset, length)] of the gradient chunks in exchange
+    order) of the peer-sharded data-parallel step (host-only, no GPU)."""
+    d = (ctypes.c_int * len(dims))(*[int(x) for x in dims])
+    region = ctypes.c_size_t()
+    cap = 64
+    off = (ctypes.c_size_t * cap)()
+    ln = (ctypes.c_size_t * cap)()
+    n = ctypes.c_int()
+    call("fg_peer_layout", len(dims) - 1, d, int(nranks), int(chunks), ctypes.byref(region), off, ln,
+         cap, ctypes.byref(n))
+    return region.value, [(off[i], ln[i]) for i in range(min(n.value, cap))]

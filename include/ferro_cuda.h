@@ -227,6 +227,45 @@ int fg_mlp_gemm_times(fg_mlp *mlp, float *ms, double *flops, int capacity, int *
  * all-reduce of the most recent step. */
 int fg_mlp_comm_times(fg_mlp *mlp, float *ms, double *bytes, int capacity, int *count);
 
+/* ---- Peer-sharded data parallelism (no reference counterpart: the
+ * reference is single-device, src/device.rs:37-41) -------------------------
+ * The alternative to fg_mlp_attach_comm for ranks on GPUs of one NVLink
+ * domain.  Gradients are cut into chunks (layer 0's dW into `chunks` row
+ * blocks, every other layer one chunk); each chunk is split into nranks
+ * shards and shard r belongs to rank r.  As soon as a chunk is complete a
+ * rank copies every other rank's shard into that rank's staging area with
+ * the copy engines (no SMs), the owner sums the nranks contributions in rank
+ * order and applies the SGD update to its shard of the parameters in one
+ * kernel, and copies the updated shard (and its TF32 residual) to every
+ * peer.  Parameters are double-buffered (even steps read buffer 0 and write
+ * buffer 1), so no rank overwrites weights a peer is still reading; ranks
+ * order the phases through flag words in each other's memory, and every
+ * wait is bounded (FG_ERR_DEVICE from fg_check_device_error on expiry).
+ *
+ * fg_mlp_peer_prepare: allocates this rank's exchange region (gradients,
+ * staging, both parameter buffers, flags), moves the current parameters
+ * into it and writes this rank's handle (FG_PEER_HANDLE_BYTES) to
+ * handle_out.  fg_mlp_peer_connect: takes the nranks handles in rank order
+ * and maps the peers' regions; from then on fg_mlp_step runs the sharded
+ * schedule.  Every rank must call both (same dims, batch, nranks, chunks)
+ * and run the same number of steps.  fg_mlp_get_grads then reads each rank's
+ * reduced shard and must not overlap another rank's next step.  To shut
+ * down, every rank calls fg_mlp_peer_disconnect (unmaps the peers' regions),
+ * then all pass a host barrier, then each calls fg_mlp_destroy: a region
+ * must not be freed while another rank still maps it.  Not combinable with
+ * fg_mlp_attach_comm. */
+#define FG_PEER_HANDLE_BYTES 96
+int fg_mlp_peer_prepare(fg_mlp *mlp, int rank, int nranks, int chunks,
+                        char handle_out[FG_PEER_HANDLE_BYTES]);
+int fg_mlp_peer_connect(fg_mlp *mlp, const char *handles);
+int fg_mlp_peer_disconnect(fg_mlp *mlp);
+/* Host-only layout query for the sharded exchange (no GPU needed): floats in
+ * a rank's exchange region, and the chunks' offsets and lengths (floats from
+ * the start of the gradient area; at most `capacity` written, *n_chunks set
+ * to the total). */
+int fg_peer_layout(int n_layers, const int *dims, int nranks, int chunks, size_t *region_floats,
+                   size_t *chunk_off, size_t *chunk_len, int capacity, int *n_chunks);
+
 /* ---- Data-parallel communicator (no reference counterpart: the reference
  * is single-device, src/device.rs:37-41) ----------------------------------- */
 #define FG_UNIQUE_ID_BYTES 128
