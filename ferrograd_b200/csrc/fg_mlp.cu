@@ -12,9 +12,12 @@
 //   cross_entropy fwd+bwd      -> one fused pass
 //   Sgd::step                  -> one multi-tensor pass (+ TF32 residual of W)
 //
-// Data parallel: each rank holds batch rows, gradients of every layer are
-// averaged over ranks by NCCL on a second stream as soon as the layer's
-// backward finishes, overlapping the remaining backward GEMMs.
+// Data parallel: each rank holds batch rows, and the gradients are combined
+// across ranks while the remaining backward GEMMs run, either by NCCL
+// all-reduces on a second stream (one bucket per layer, enqueue_step), or by
+// the peer-sharded exchange (enqueue_step_peer, fg_peer.cu): copy-engine
+// reduce-scatter of each gradient chunk to its owning rank, the owner's fused
+// reduce + SGD, copy-engine all-gather of the updated parameters.
 #include <cuda_runtime.h>
 #include <stdlib.h>
 #include <string.h>
@@ -284,8 +287,8 @@ struct Layer {
   bool can_split_w = false;
   fg::gemm::GemmPlan bwd_w_half[2];
   // Peer-sharded mode: this layer's parameters of even / odd steps inside
-  // the exchange region, the GEMM plans that read each of them, and (layer
-  // 0) dW as row blocks, one per gradient chunk.
+  // the exchange region, the GEMM plans that read each of them, and dW as
+  // row blocks, one per gradient chunk.
   float *Wp[2] = {nullptr, nullptr}, *bp[2] = {nullptr, nullptr}, *W_lo_p[2] = {nullptr, nullptr};
   fg::gemm::GemmPlan fwd_p[2], bwd_x_p[2];
   fg::gemm::GemmPlan bwd_w_part[fg::kMaxPeerParts];
@@ -715,7 +718,7 @@ int enqueue_step_peer(fg_mlp *m, int par) {
                                       (l > 0 && m->L[l - 1].tc) ? m->G_lo[l - 1] : nullptr, B,
                                       ly.in, st, m->sms)))
         return rc;
-    } else if (nc > 1) {  // layer 0: dW row block q is chunk q
+    } else if (nc > 1) {  // dW row block q is chunk q (the last also holds db)
       for (int q = 0; q < nc; q++) {
         if ((rc = run_gemm(m, ly.bwd_w_part[q], st))) return rc;
         if (q == nc - 1 &&
@@ -724,6 +727,7 @@ int enqueue_step_peer(fg_mlp *m, int par) {
           return rc;
         if ((rc = peer_chunk(m, c0 + q, par))) return rc;
       }
+      if (l > 0 && (rc = run_gemm(m, ly.bwd_x_p[par], st))) return rc;
       continue;
     } else if ((rc = run_gemm(m, ly.bwd_w, st))) {
       return rc;
@@ -1262,15 +1266,18 @@ int fg_mlp_peer_prepare(fg_mlp *m, int rank, int nranks, int chunks,
       ly.bwd_x_p[q] = ly.bwd_x;
     }
   }
-  Layer &l0 = m->L[0];
-  const int parts = L.n_chunks[0];
-  if (l0.tc && parts > 1) {
-    const int rows = l0.out / parts;
+  for (int l = 0; l < m->nl; l++) {
+    Layer &ly = m->L[l];
+    const int parts = L.n_chunks[l];
+    if (!ly.tc || parts < 2) continue;
+    const int rows = ly.out / parts;
+    const float *in = (l == 0) ? m->x : m->act[l - 1];
+    const float *in_lo = (l == 0) ? m->x_lo : m->act_lo[l - 1];
     for (int q = 0; q < parts; q++)
-      if ((rc = fg::gemm::make_plan(rows, l0.in, m->B, m->G[0] + q * rows, m->G_lo[0] + q * rows,
-                                    l0.out, m->x, m->x_lo, l0.in, l0.dW + (size_t)q * rows * l0.in,
-                                    nullptr, l0.in, FG_GEMM_A_MN_MAJOR | FG_GEMM_B_MN_MAJOR,
-                                    FG_EPI_NONE, nullptr, nullptr, 0, &l0.bwd_w_part[q])))
+      if ((rc = fg::gemm::make_plan(rows, ly.in, m->B, m->G[l] + q * rows, m->G_lo[l] + q * rows,
+                                    ly.out, in, in_lo, ly.in, ly.dW + (size_t)q * rows * ly.in,
+                                    nullptr, ly.in, FG_GEMM_A_MN_MAJOR | FG_GEMM_B_MN_MAJOR,
+                                    FG_EPI_NONE, nullptr, nullptr, 0, &ly.bwd_w_part[q])))
         return rc;
   }
   // SMs left free beside the backward GEMMs (FG_PEER_SM_RESERVE, default 0:
@@ -1285,7 +1292,8 @@ int fg_mlp_peer_prepare(fg_mlp *m, int rank, int nranks, int chunks,
       fg::gemm::stream_k_attach(p2, m->sk_ws, m->sms);
     ly.bwd_w.max_ctas = cap;
     ly.bwd_x_p[0].max_ctas = ly.bwd_x_p[1].max_ctas = cap;
-    for (int q = 0; q < parts && &ly == &l0; q++) {
+    const int l = (int)(&ly - m->L.data());
+    for (int q = 0; q < L.n_chunks[l] && L.n_chunks[l] > 1; q++) {
       fg::gemm::stream_k_attach(&ly.bwd_w_part[q], m->sk_ws, m->sms);
       ly.bwd_w_part[q].max_ctas = cap;
     }

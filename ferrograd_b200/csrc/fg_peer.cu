@@ -175,6 +175,7 @@ int peer_layout(int n_layers, const int *dims, int nranks, int parts, PeerLayout
                      kMaxPeerParts);
   PeerLayout L;
   L.nranks = nranks;
+  L.parts = parts;
   const size_t unit = 64 * (size_t)nranks;  // every shard 256-byte aligned
   L.w_off.resize(n_layers);
   L.b_off.resize(n_layers);
@@ -193,8 +194,9 @@ int peer_layout(int n_layers, const int *dims, int nranks, int parts, PeerLayout
       raw += 64;
     }
     const size_t end = off + pad_to(raw, unit);
-    const int p = (l == 0 && o > 16 && peer_parts_ok((int)o, (int)in, nranks, parts)) ? parts : 1;
-    if (l == 0) L.parts = p;
+    // every tensor-core layer's dW in row blocks, so each block's exchange
+    // starts while the next block is computed
+    const int p = (o > 16 && peer_parts_ok((int)o, (int)in, nranks, parts)) ? parts : 1;
     size_t c0 = off;
     for (int q = 0; q < p; q++) {
       PeerChunk c;

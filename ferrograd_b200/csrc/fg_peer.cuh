@@ -10,7 +10,7 @@
 namespace fg {
 
 constexpr int kMaxPeers = 8;       // ranks of one NVLink domain (one box)
-constexpr int kMaxPeerParts = 8;   // row blocks of layer 0's dW
+constexpr int kMaxPeerParts = 8;   // row blocks of a layer's dW
 
 // One gradient chunk: [off, off + len) floats of the gradient area, split
 // into nranks shards of len / nranks floats (shard r is owned by rank r).
@@ -41,7 +41,7 @@ struct PeerLayout {
 
 // Host-only.  Returns 0 or an FG_ERR_* code (error message set).
 int peer_layout(int n_layers, const int *dims, int nranks, int parts, PeerLayout *out);
-// Whether layer 0 of these dims can take `parts` dW row blocks.
+// Whether a layer [out, in] can take `parts` dW row blocks.
 bool peer_parts_ok(int out, int in, int nranks, int parts);
 
 struct PeerFlagPtrs {

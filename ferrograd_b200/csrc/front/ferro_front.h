@@ -296,6 +296,9 @@ struct Stats {
   uint64_t rendered = 0;     // launches of NVRTC-rendered kernels
   uint64_t compiled = 0;     // NVRTC compilations (program cache misses)
   uint64_t cache_hits = 0;
+  // host time inside realize_many, seconds: scheduling, enqueueing the
+  // items (routing, program lookup, launches) and the live-tensor rewrite
+  double schedule_s = 0, run_s = 0, rewrite_s = 0;
 };
 Stats &stats();
 void reset_stats();

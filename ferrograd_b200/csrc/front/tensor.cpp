@@ -1,6 +1,7 @@
 // tensor.cpp -- Tensor (src/tensor.rs), nn::Linear (src/nn.rs) and
 // optim::Sgd (src/optim.rs) over the interned UOp graph.
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <unordered_set>
@@ -364,10 +365,21 @@ void Tensor::realize_many(const std::vector<Tensor> &ts) {
     if (seen.insert(r.get()).second) roots.push_back(r);
   }
   if (roots.empty()) return;
+  using clk = std::chrono::steady_clock;
+  auto secs = [](clk::time_point a, clk::time_point b) {
+    return std::chrono::duration<double>(b - a).count();
+  };
+  const auto t0 = clk::now();
   SchedulePlan plan = schedule_many(roots);
+  const auto t1 = clk::now();
   for (const ScheduleItem &item : plan.items) run_item(item);
   end_realize();
+  const auto t2 = clk::now();
   apply_map_to_tensors(plan.replacements);
+  Stats &st = stats();
+  st.schedule_s += secs(t0, t1);
+  st.run_s += secs(t1, t2);
+  st.rewrite_s += secs(t2, clk::now());
 }
 
 Tensor Tensor::realize() const {

@@ -1,7 +1,7 @@
 """Host-side checks of the peer-sharded gradient exchange's layout (no GPU):
 the chunks tile each rank's gradient area exactly, in exchange (backward)
-order, every shard is 256-byte aligned, layer 0's dW is cut into the
-requested row blocks where its shape allows, and the region holds the six
+order, every shard is 256-byte aligned, each tensor-core layer's dW is cut
+into the requested row blocks where its shape allows, and the region holds the six
 areas plus the flag words.  The copies of the exchange index only through
 these offsets, so an overlap or gap here would be a wrong copy on the GPU."""
 import pytest
@@ -32,25 +32,25 @@ def test_chunks_tile_the_gradient_area(dims, nranks, chunks):
     for off_c, len_c in ch:
         assert len_c > 0 and len_c % unit == 0 and off_c % unit == 0
         assert off_c + len_c <= grad
-    # chunks of each layer are contiguous and cover its bucket; layers in backward order
+    # chunks of each layer are contiguous and cover its bucket; layers in
+    # backward order; a layer's dW row blocks are equal where it is split
     pos = 0
     for l in reversed(range(nl)):
         b0, blen = buckets[l]
-        cur = b0
+        o, i = dims[l + 1], dims[l]
+        splittable = (chunks > 1 and o > 16 and o % chunks == 0 and (o // chunks) % 32 == 0
+                      and ((o // chunks) * i) % unit == 0)
+        first, cur = pos, b0
         while pos < len(ch) and cur < b0 + blen:
             assert ch[pos][0] == cur
             cur += ch[pos][1]
             pos += 1
         assert cur == b0 + blen, (l, cur, b0 + blen)
+        assert pos - first == (chunks if splittable else 1), (l, pos - first)
+        if splittable:
+            for k in range(chunks - 1):
+                assert ch[first + k][1] == (o // chunks) * i
     assert pos == len(ch)
-    n0 = len(ch) - sum(1 for _ in range(nl - 1))  # layer 0's chunks
-    o0, i0 = dims[1], dims[0]
-    splittable = (chunks > 1 and o0 > 16 and o0 % chunks == 0 and (o0 // chunks) % 32 == 0
-                  and ((o0 // chunks) * i0) % unit == 0)
-    assert n0 == (chunks if splittable else 1)
-    if splittable:
-        for k in range(chunks - 1):
-            assert ch[nl - 1 + k][1] == (o0 // chunks) * i0
     flags = _pad(2 * len(ch) * 8, 64)
     assert region == 6 * grad + flags
 
