@@ -701,7 +701,9 @@ void attach_stream_ws(GemmPlan *pl, cudaStream_t st) {
   }
   void *ws = nullptr;
   const size_t bytes = stream_k_ws_bytes(sms);
-  if (cudaMalloc(&ws, bytes) != cudaSuccess || cudaMemset(ws, 0, bytes) != cudaSuccess) {
+  // zero-filled on the GEMM's own stream, so the fill is ordered before the
+  // first launch that reads the stream-K flags
+  if (cudaMalloc(&ws, bytes) != cudaSuccess || cudaMemsetAsync(ws, 0, bytes, st) != cudaSuccess) {
     cudaGetLastError();
     if (ws) cudaFree(ws);
     return;

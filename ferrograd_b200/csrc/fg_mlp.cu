@@ -1229,6 +1229,9 @@ int fg_mlp_peer_prepare(fg_mlp *m, int rank, int nranks, int chunks,
   FG_CUDA_TRY(cudaStreamSynchronize(m->st));
   float *region = nullptr;
   if ((rc = mlp_alloc(m, &region, L.region))) return rc;
+  // the zero fill runs on the legacy default stream, which does not order
+  // with the step's non-blocking stream: finish it before the copies below
+  FG_CUDA_TRY(cudaDeviceSynchronize());
   m->region = region;
   m->pl = L;
   m->peer_rank = rank;
