@@ -610,9 +610,9 @@ void peer_point(fg_mlp *m) {
 //      this rank's part of every other rank's shard is copied (copy engine,
 //      one stream per peer) into that rank's staging slot for this rank,
 //      then the peers' flags are raised;
-//   2. the owner's kernel waits for every peer's flag, sums the
-//      contributions in rank order and writes the SGD update of its shard
-//      into buffer par ^ 1 (and its TF32 residual);
+//   2. on the owner, a one-block kernel waits for every peer's flag, then
+//      one pass sums the contributions in rank order and writes the SGD
+//      update of its shard into buffer par ^ 1 (and its TF32 residual);
 //   3. all-gather: the updated shard is copied into every peer's buffer
 //      par ^ 1 and the peers' all-gather flags are raised.
 // Flags carry par + 1, so a waiter can never mistake the previous step's
