@@ -64,6 +64,40 @@ int debug_level() {
   return e ? std::atoi(e) : 0;
 }
 
+OptimizeConfig parse_optimize_config(const char *raw) {
+  // parse_optimize_config (src/optimize/mod.rs:80-108)
+  OptimizeConfig all;
+  if (!raw) return all;
+  std::string s(raw);
+  auto trim = [](std::string t) {
+    const char *ws = " \t\n\r\f\v";
+    const size_t b = t.find_first_not_of(ws);
+    if (b == std::string::npos) return std::string();
+    return t.substr(b, t.find_last_not_of(ws) - b + 1);
+  };
+  s = trim(s);
+  if (s.empty() || s == "1" || s == "on" || s == "all") return all;
+  OptimizeConfig c;
+  c.symbolic = c.upcast = c.unroll = false;
+  if (s == "0" || s == "off" || s == "none") return c;
+  size_t pos = 0;
+  while (pos <= s.size()) {
+    size_t comma = s.find(',', pos);
+    if (comma == std::string::npos) comma = s.size();
+    const std::string pass = trim(s.substr(pos, comma - pos));
+    if (pass == "symbolic") c.symbolic = true;
+    if (pass == "upcast") c.upcast = true;
+    if (pass == "unroll") c.unroll = true;
+    pos = comma + 1;
+  }
+  return c;
+}
+
+const OptimizeConfig &optimize_config() {
+  static const OptimizeConfig c = parse_optimize_config(std::getenv("OPT"));
+  return c;
+}
+
 Stats &stats() { return g_stats; }
 void reset_stats() { g_stats = Stats{}; }
 const std::string &last_source() { return g_last_source; }

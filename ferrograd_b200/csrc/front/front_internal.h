@@ -62,6 +62,17 @@ std::string float_literal(double v);
 // hand-written reductions), reproducing the reference's arithmetic order.
 bool exact_mode();
 int debug_level();
+// The reference's OPT environment variable (src/optimize/mod.rs:80-112),
+// read once per process: "0"/"off"/"none" disables every pass, "1"/"on"/
+// "all" or unset enables every pass, otherwise a comma list of "symbolic",
+// "upcast", "unroll".  unroll decides the reduction order (4-lane blocks)
+// and symbolic the constant folds of rendered kernels; upcast only changes
+// the reference's loop structure, never a value.
+struct OptimizeConfig {
+  bool symbolic = true, upcast = true, unroll = true;
+};
+OptimizeConfig parse_optimize_config(const char *raw);
+const OptimizeConfig &optimize_config();
 
 // Device-side conversions behind Tensor::from_u8_div / one_hot_u8.
 BufferP device_u8_to_f32(const uint8_t *data, size_t n, float divisor);

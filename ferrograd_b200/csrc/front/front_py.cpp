@@ -229,6 +229,28 @@ PYBIND11_MODULE(_front, m) {
       },
       "CUDA stream (as an integer handle) the front end launches on.");
   m.def("exact_mode", &exact_mode);
+  m.def(
+      "parse_optimize_config",
+      [](const std::string &raw) {
+        OptimizeConfig c = parse_optimize_config(raw.c_str());
+        py::dict d;
+        d["symbolic"] = c.symbolic;
+        d["upcast"] = c.upcast;
+        d["unroll"] = c.unroll;
+        return d;
+      },
+      "The reference's OPT parsing (src/optimize/mod.rs:80-108) of the given string.");
+  m.def(
+      "optimize_config",
+      []() {
+        const OptimizeConfig &c = optimize_config();
+        py::dict d;
+        d["symbolic"] = c.symbolic;
+        d["upcast"] = c.upcast;
+        d["unroll"] = c.unroll;
+        return d;
+      },
+      "This process's OPT setting (read once, at first use).");
   m.def("last_source", []() { return last_source(); });
   m.def("reset_stats", &reset_stats);
   m.def("stats", []() {

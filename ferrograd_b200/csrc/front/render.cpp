@@ -19,6 +19,9 @@
 //   * symbolic_simple (src/optimize/symbolic.rs:42-56) folds ALU ops on
 //     literal constants: const op const in f64, x+0, 0+x, x*1, 1*x -> x,
 //     x*0, 0*x -> 0.
+// Both the 4-lane reduction blocks and the folds follow the reference's OPT
+// setting (optimize_config(): without "unroll" every reduction is
+// sequential, without "symbolic" nothing is folded).
 // The thread mapping is the B200's: one thread per output element (or
 // `unroll` elements, loads of all of them issued before the stores), 256
 // threads per block, a grid covering the domain.
@@ -263,7 +266,7 @@ std::string Emitter::view_index(const UOp *n, const std::vector<std::string> &ct
 
 Val Emitter::emit_alu(Op op, DType dt, const std::vector<Val> &a) {
   // symbolic_simple folds (src/optimize/symbolic.rs:42-56).
-  if ((op == Op::Add || op == Op::Mul) && a.size() == 2) {
+  if ((op == Op::Add || op == Op::Mul) && a.size() == 2 && optimize_config().symbolic) {
     const Val &x = a[0], &y = a[1];
     if (x.is_const && y.is_const) {
       double r = op == Op::Add ? x.c + y.c : x.c * y.c;
@@ -353,7 +356,7 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
   };
   size_t last = axes.empty() ? 0 : (size_t)axes.back();
   int64_t R = axes.empty() ? 1 : ss[last];
-  if (!axes.empty() && R > 4 && R % 4 == 0) {
+  if (!axes.empty() && R > 4 && R % 4 == 0 && optimize_config().unroll) {
     std::string r = fresh("r");
     if (R / 4 > 8) line("#pragma unroll 4");
     open("for (long long " + r + " = 0; " + r + " < " + std::to_string(R / 4) + "LL; ++" + r + ")");

@@ -46,7 +46,12 @@
 static const float LOG2E_F = 1.44269504088896340736f;
 static const float LN2_F = 0.693147180559945309417f;
 
-static int orc_blocked(long n) { return n > ORC_UNROLL && n % ORC_UNROLL == 0; }
+/* The reference's OPT "unroll" pass (src/optimize/mod.rs:80-112): with it
+ * off (OPT=0, or a pass list without "unroll") every reduction is
+ * sequential. */
+static int orc_unroll_on = 1;
+void orc_set_unroll(int on) { orc_unroll_on = on != 0; }
+static int orc_blocked(long n) { return orc_unroll_on && n > ORC_UNROLL && n % ORC_UNROLL == 0; }
 static inline float orc_maxf(float a, float b) { return (a > b) ? a : b; }
 static inline int32_t orc_maxi(int32_t a, int32_t b) { return (a > b) ? a : b; }
 static inline int32_t orc_addi(int32_t a, int32_t b) {

@@ -41,6 +41,7 @@ def lib():
         build()
     L = ctypes.CDLL(LIB_PATH)
     L.orc_set_threads.argtypes = [ctypes.c_int]
+    L.orc_set_unroll.argtypes = [ctypes.c_int]
     L.orc_max_threads.restype = ctypes.c_int
     L.orc_kaiming_normal.argtypes = [_f32p, _c_long, _c_long, ctypes.POINTER(ctypes.c_uint64)]
     for name, p in (("orc_reduce_last_f32", _f32p), ("orc_reduce_axis0_f32", _f32p),
@@ -68,6 +69,12 @@ def lib():
 
 def set_threads(n: int) -> None:
     lib().orc_set_threads(int(n))
+
+
+def set_unroll(on: bool) -> None:
+    """The reference's OPT "unroll" pass (src/optimize/mod.rs:80-112): off
+    makes every reduction sequential (process-wide; restore it after use)."""
+    lib().orc_set_unroll(1 if on else 0)
 
 
 def max_threads() -> int:

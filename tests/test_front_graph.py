@@ -303,3 +303,23 @@ def test_only_zeros_tensors_render_as_known_zero():
     src = F.schedule([z.add(d)], with_source=True)[0]["source"]
     body = src.split("{", 1)[1]
     assert body.count("p1[") == 0 and body.count("p2[") > 0  # only the data tensor is loaded
+
+
+def test_opt_parsing_matches_the_reference():
+    """parse_optimize_config (src/optimize/mod.rs:80-108) and its tests
+    (src/optimize/mod.rs, mod tests): unset/empty/all enable every pass,
+    0/off/none disable every pass, otherwise a comma list of pass names
+    (unknown names ignored, whitespace trimmed)."""
+    from ferrograd_b200 import front as F
+    allp = {"symbolic": True, "upcast": True, "unroll": True}
+    nonep = {"symbolic": False, "upcast": False, "unroll": False}
+    for raw in ("", "all", "1", "on", "  all  "):
+        assert F._front.parse_optimize_config(raw) == allp, raw
+    for raw in ("0", "off", "none", " none "):
+        assert F._front.parse_optimize_config(raw) == nonep, raw
+    assert F._front.parse_optimize_config("symbolic") == {"symbolic": True, "upcast": False,
+                                                          "unroll": False}
+    assert F._front.parse_optimize_config("symbolic,upcast,unroll,unknown") == allp
+    assert F._front.parse_optimize_config(" unroll , symbolic") == {"symbolic": True,
+                                                                   "upcast": False,
+                                                                   "unroll": True}

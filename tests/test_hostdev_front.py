@@ -26,11 +26,15 @@ def hostdev():
     return os.path.join(HERE, "hostdev", "run_step.py")
 
 
-def run(runner, tmp_path, dims, batch, steps, lr=0.01, seeds=(1, 2)):
+def run(runner, tmp_path, dims, batch, steps, lr=0.01, seeds=(1, 2), opt=None):
     x, t = data.mlp_batch(batch, dims[0], dims[-1], *seeds)
     src, dst = tmp_path / "in.npz", tmp_path / "out.npz"
     np.savez(src, x=x, t=t, dims=np.array(dims), lr=np.array(lr), steps=np.array(steps))
-    subprocess.run([sys.executable, runner, str(src), str(dst)], check=True, timeout=600)
+    env = dict(os.environ)
+    env.pop("OPT", None)
+    if opt is not None:
+        env["OPT"] = opt
+    subprocess.run([sys.executable, runner, str(src), str(dst)], check=True, timeout=600, env=env)
     return x, t, dict(np.load(dst))
 
 
@@ -56,3 +60,32 @@ def test_host_executed_steps_track_oracle_and_reuse_programs(oracle, hostdev, tm
         oloss, ws, bs, _, _, _ = oracle.mlp_step(ws, bs, x, t, 0.01)
         assert np.float32(r["loss"][s]) == np.float32(oloss)
     assert np.array_equal(r["w_0"], ws[0]) and np.array_equal(r["w_1"], ws[1])
+
+
+@pytest.mark.parametrize("opt,unroll", [("0", False), ("symbolic,upcast", False),
+                                        ("unroll", True), ("symbolic, unroll ,upcast", True)])
+def test_host_executed_step_follows_the_reference_opt_setting(oracle, hostdev, tmp_path, opt,
+                                                              unroll):
+    """OPT (src/optimize/mod.rs:80-112) changes the arithmetic: without the
+    unroll pass every reduction (the contractions over K and the batch, the
+    row sums of log_softmax) is one sequential chain instead of 4-lane
+    blocks.  The step must equal the oracle run with the same reduction
+    order, bit for bit; with symbolic off nothing is folded, which leaves
+    this step's values unchanged."""
+    dims, batch = (64, 32, 10), 32
+    x, t, r = run(hostdev, tmp_path, dims, batch, steps=1, opt=opt)
+    ws, bs = [r["w0_0"], r["w0_1"]], [r["b0_0"], r["b0_1"]]
+    oracle.set_unroll(unroll)
+    try:
+        oloss, ow, ob, odw, odb, _ = oracle.mlp_step(ws, bs, x, t, 0.01)
+    finally:
+        oracle.set_unroll(True)
+    assert np.float32(r["loss"][0]) == np.float32(oloss)
+    for i in range(2):
+        assert np.array_equal(r[f"dw_{i}"], odw[i]), i
+        assert np.array_equal(r[f"w_{i}"], ow[i]) and np.array_equal(r[f"b_{i}"], ob[i]), i
+    if not unroll:
+        # the sequential order is a different computation: it must not
+        # coincide with the default (4-lane) one
+        _, _, _, ddw, _, _ = oracle.mlp_step(ws, bs, x, t, 0.01)
+        assert not np.array_equal(odw[0], ddw[0])
