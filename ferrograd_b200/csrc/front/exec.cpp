@@ -17,6 +17,7 @@
 // FG_FRONT_EXACT=1 every kernel is rendered and the arithmetic is the
 // reference's.
 #include <algorithm>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -63,6 +64,28 @@ int debug_level() {
   const char *e = std::getenv("DEBUG");
   return e ? std::atoi(e) : 0;
 }
+
+// DEBUG >= 2 prints each launch's execution time (src/tensor.rs:1017-1028,
+// which times the reference's synchronous Device::execute): the device is
+// synchronised before the launch and after it, and the wall time between is
+// printed.  At lower levels this costs nothing.
+struct ExecTimer {
+  bool on;
+  std::chrono::steady_clock::time_point t0;
+  ExecTimer() : on(debug_level() >= 2) {
+    if (on) {
+      synchronize();
+      t0 = std::chrono::steady_clock::now();
+    }
+  }
+  ~ExecTimer() {
+    if (!on) return;
+    synchronize();
+    const double ms =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    fprintf(stderr, "              exec time=%.3fms\n", ms);
+  }
+};
 
 OptimizeConfig parse_optimize_config(const char *raw) {
   // parse_optimize_config (src/optimize/mod.rs:80-108)
@@ -416,8 +439,10 @@ void launch_rendered(const RenderedKernel &rk, const BufferP &out,
     cache.emplace(rk.source, prog);
     g_stats.compiled++;
     if (debug_level() >= 4) fprintf(stderr, "%s\n", rk.source.c_str());
-    if (debug_level() >= 1) fprintf(stderr, "*** CUDA %4llu  kernel_%-9llu arg %2d  (compiled)\n",
-                                    (unsigned long long)kid, (unsigned long long)kid, nargs);
+    // src/tensor.rs:870-874: "(compiled)" from DEBUG=2 on
+    if (debug_level() >= 1)
+      fprintf(stderr, "*** CUDA %4llu  kernel_%-9llu arg %2d%s\n", (unsigned long long)kid,
+              (unsigned long long)kid, nargs, debug_level() >= 2 ? "  (compiled)" : "");
   }
   g_last_source = rk.source;
   launch_args(prog, rk.has_out_slot, rk.params, out, written);
@@ -462,7 +487,10 @@ void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelIn
     }
     args.push_back(a);
   }
-  check(fg_execute(prog, args.data(), nargs), "execute");
+  {
+    ExecTimer timer;
+    check(fg_execute(prog, args.data(), nargs), "execute");
+  }
   g_stats.rendered++;
 }
 
@@ -731,15 +759,16 @@ void run_contraction(const Contraction &c, const UOpP &a, const UOpP &b, const B
   Operand A = prepare_operand(a, c.ai, c.r, bc_a, c.M, c.K);
   Operand B = prepare_operand(b, c.bj, c.r, bc_b, c.N, c.K);
   int flags = (A.mn_major ? FG_GEMM_A_MN_MAJOR : 0) | (B.mn_major ? FG_GEMM_B_MN_MAJOR : 0);
+  if (debug_level() >= 1)
+    fprintf(stderr, "*** CUDA %4llu  gemm3xtf32 %lldx%lldx%lld%s%s\n",
+            (unsigned long long)g_kernel_count++, (long long)c.M, (long long)c.N,
+            (long long)c.K, A.mn_major ? " A:mn" : "", B.mn_major ? " B:mn" : "");
+  ExecTimer timer;
   check(fg_gemm_3xtf32((int)c.M, (int)c.N, (int)c.K, A.ptr, A.lo_ptr, A.ld, B.ptr, B.lo_ptr, B.ld,
                        fptr(out), nullptr, (int)c.N, flags, FG_EPI_NONE, nullptr, nullptr, 0,
                        stream()),
         "gemm");
   g_stats.gemm++;
-  if (debug_level() >= 1)
-    fprintf(stderr, "*** CUDA %4llu  gemm3xtf32 %lldx%lldx%lld%s%s\n",
-            (unsigned long long)g_kernel_count++, (long long)c.M, (long long)c.N,
-            (long long)c.K, A.mn_major ? " A:mn" : "", B.mn_major ? " B:mn" : "");
 }
 
 // ---- hand-written reductions ------------------------------------------------
@@ -796,17 +825,19 @@ std::optional<HandReduce> match_hand_reduce(const UOp *n) {
 void run_hand_reduce(const HandReduce &h, const BufferP &out) {
   int op = h.reduce->reduce_op == Op::Add ? FG_REDUCE_SUM : FG_REDUCE_MAX;
   const float *x = fptr(h.v.buf, h.v.offset);
-  if (h.rows)
-    check(fg_reduce_rows(FG_F32, op, x, fptr(out), (size_t)h.outer, (size_t)h.extent, stream()),
-          "reduce_rows");
-  else
-    check(fg_reduce_cols(FG_F32, op, x, fptr(out), (size_t)h.extent, (size_t)h.inner, stream()),
-          "reduce_cols");
-  g_stats.hand_reduce++;
+  float *y = fptr(out);
   if (debug_level() >= 1)
     fprintf(stderr, "*** CUDA %4llu  reduce_%s %lldx%lld\n", (unsigned long long)g_kernel_count++,
             h.rows ? "rows" : "cols", (long long)(h.rows ? h.outer : h.extent),
             (long long)(h.rows ? h.extent : h.inner));
+  ExecTimer timer;
+  if (h.rows)
+    check(fg_reduce_rows(FG_F32, op, x, y, (size_t)h.outer, (size_t)h.extent, stream()),
+          "reduce_rows");
+  else
+    check(fg_reduce_cols(FG_F32, op, x, y, (size_t)h.extent, (size_t)h.inner, stream()),
+          "reduce_cols");
+  g_stats.hand_reduce++;
 }
 
 // Root of an allocating item, looking through a same-size Reshape.
@@ -860,6 +891,12 @@ void end_realize() { staged_cache().clear(); }
 
 void run_item(const ScheduleItem &item) {
   g_stats.kernels++;
+  // DEBUG >= 3 dumps each kernel's graph (src/tensor.rs:855-869,900-904);
+  // the proto-kernel as scheduled is the one stage this front end has
+  if (debug_level() >= 3)
+    fprintf(stderr, "\u2501\u2501\u2501 kernel_%llu [schedule] \u2501\u2501\u2501\n%s\n",
+            (unsigned long long)g_kernel_count,
+            dump(item.store_dest ? make_store(item.store_dest, item.value) : item.value).c_str());
   UOpP value = item.value;
   if (!exact_mode()) {
     // Extract routed reductions bottom-up, substituting each result.

@@ -89,3 +89,28 @@ def test_host_executed_step_follows_the_reference_opt_setting(oracle, hostdev, t
         # coincide with the default (4-lane) one
         _, _, _, ddw, _, _ = oracle.mlp_step(ws, bs, x, t, 0.01)
         assert not np.array_equal(odw[0], ddw[0])
+
+
+@pytest.mark.parametrize("level", [1, 2, 3, 4])
+def test_debug_levels_follow_the_reference(hostdev, tmp_path, level):
+    """DEBUG (src/tensor.rs:62-67): >= 1 one line per launch, "(compiled)"
+    on a program-cache miss from 2 on (:870-874), >= 2 each launch's exec
+    time (:1017-1028), >= 3 each kernel's graph (:855-869), >= 4 the
+    rendered source (:852-854)."""
+    x, t = data.mlp_batch(8, 16, 10, 1, 2)
+    src, dst = tmp_path / "in.npz", tmp_path / "out.npz"
+    np.savez(src, x=x, t=t, dims=np.array((16, 16, 10)), lr=np.array(0.01), steps=np.array(1))
+    env = dict(os.environ, DEBUG=str(level))
+    env.pop("OPT", None)
+    r = subprocess.run([sys.executable, hostdev, str(src), str(dst)], env=env, timeout=600,
+                       capture_output=True, text=True, check=True)
+    lines = r.stderr.splitlines()
+    launches = [l for l in lines if l.startswith("*** CUDA ")]
+    assert launches
+    compiled = [l for l in launches if "kernel_" in l]
+    assert compiled and all(l.endswith("(compiled)") == (level >= 2) for l in compiled)
+    times = [l for l in lines if l.strip().startswith("exec time=")]
+    assert len(times) == (len(launches) if level >= 2 else 0)
+    dumps = [l for l in lines if "[schedule]" in l]
+    assert (len(dumps) > 0) == (level >= 3)
+    assert any("extern \"C\" __global__" in l for l in lines) == (level >= 4)
