@@ -51,6 +51,10 @@ SIGNATURES = [
     ("fg_device_close", _i, [_vp]),
     ("fg_device_stream", _i, [_vp, _pp]),
     ("fg_device_sync", _i, [_vp]),
+    ("fg_event_create", _i, [_vp, _pp]),
+    ("fg_event_record", _i, [_vp, _vp]),
+    ("fg_event_elapsed_ms", _i, [_vp, _vp, ctypes.POINTER(ctypes.c_float)]),
+    ("fg_event_destroy", _i, [_vp]),
     ("fg_alloc", _i, [_vp, _i, _sz, _pp]),
     ("fg_free", _i, [_vp]),
     ("fg_buffer_info", _i, [_vp, _pp, ctypes.POINTER(_i), ctypes.POINTER(_sz)]),

@@ -202,6 +202,47 @@ int fg_device_sync(fg_device *dev) {
   return fg_check_device_error();
 }
 
+// ---- device-side timing ----------------------------------------------------
+struct fg_event {
+  int ordinal;
+  cudaEvent_t ev;
+  cudaStream_t stream;  // the device's stream (used when record gets NULL)
+};
+
+int fg_event_create(fg_device *dev, fg_event **out) {
+  FG_REQUIRE(dev && out, "fg_event_create: null argument");
+  FG_CUDA_TRY(cudaSetDevice(dev->ordinal));
+  cudaEvent_t e = nullptr;
+  FG_CUDA_TRY(cudaEventCreate(&e));
+  *out = new fg_event{dev->ordinal, e, dev->stream};
+  return FG_OK;
+}
+
+int fg_event_record(fg_event *ev, void *stream) {
+  FG_REQUIRE(ev, "fg_event_record: null event");
+  FG_CUDA_TRY(cudaSetDevice(ev->ordinal));
+  FG_CUDA_TRY(cudaEventRecord(ev->ev, stream ? (cudaStream_t)stream : ev->stream));
+  return FG_OK;
+}
+
+int fg_event_elapsed_ms(fg_event *start, fg_event *end, float *ms) {
+  FG_REQUIRE(start && end && ms, "fg_event_elapsed_ms: null argument");
+  FG_REQUIRE(start->ordinal == end->ordinal, "fg_event_elapsed_ms: events of devices %d and %d",
+             start->ordinal, end->ordinal);
+  FG_CUDA_TRY(cudaSetDevice(start->ordinal));
+  FG_CUDA_TRY(cudaEventSynchronize(end->ev));
+  FG_CUDA_TRY(cudaEventElapsedTime(ms, start->ev, end->ev));
+  return FG_OK;
+}
+
+int fg_event_destroy(fg_event *ev) {
+  if (!ev) return FG_OK;
+  cudaSetDevice(ev->ordinal);
+  cudaEventDestroy(ev->ev);
+  delete ev;
+  return FG_OK;
+}
+
 int fg_alloc(fg_device *dev, int dtype, size_t numel, fg_buffer **out) {
   FG_REQUIRE(dev && out, "fg_alloc: null argument");
   size_t es = dtype_size(dtype);

@@ -93,6 +93,34 @@ class Program:
             self._h = None
 
 
+class Event:
+    """A point on a device stream (``fg_event_*``); ``elapsed_ms(start, end)``
+    waits for ``end`` and returns the device time between the two points."""
+
+    def __init__(self, device: "CudaDevice"):
+        h = ctypes.c_void_p()
+        call("fg_event_create", device.handle, ctypes.byref(h))
+        self._h = h.value
+
+    def record(self, stream: Optional[int] = None) -> "Event":
+        call("fg_event_record", self._h, stream)
+        return self
+
+    @staticmethod
+    def elapsed_ms(start: "Event", end: "Event") -> float:
+        ms = ctypes.c_float()
+        call("fg_event_elapsed_ms", start._h, end._h, ctypes.byref(ms))
+        return float(ms.value)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            try:
+                _lib.lib().fg_event_destroy(self._h)
+            except Exception:
+                pass
+            self._h = None
+
+
 class CudaDevice:
     """``device::get(DeviceId::Cuda(ordinal))``: one per ordinal per process."""
 

@@ -67,6 +67,15 @@ int fg_device_close(fg_device *dev);
 /* Stream that buffer copies and fg_execute launches are ordered on. */
 int fg_device_stream(fg_device *dev, void **stream);
 int fg_device_sync(fg_device *dev);
+/* Device-side timing (the CUDA counterpart of the per-kernel wall-clock
+ * timing of DEBUG >= 2, src/tensor.rs:1017-1028): an event records a point
+ * on a stream (NULL = the device's stream); fg_event_elapsed_ms waits for
+ * `end` and returns the milliseconds between the two points. */
+typedef struct fg_event fg_event;
+int fg_event_create(fg_device *dev, fg_event **out);
+int fg_event_record(fg_event *ev, void *stream);
+int fg_event_elapsed_ms(fg_event *start, fg_event *end, float *ms);
+int fg_event_destroy(fg_event *ev);
 
 /* Device::allocate (src/device.rs:282-283): zero-initialised buffer of
  * numel elements of dtype.  numel == 0 is allowed (no storage). */

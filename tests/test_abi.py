@@ -77,3 +77,14 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert b"positive" in L.fg_last_error()
     assert L.fg_reduce_rows(7, 0, None, None, 1, 1, None) == 1
     assert L.fg_kaiming_normal(None, 4, 1, None) == 1
+
+
+def test_event_entry_points_reject_null_arguments_without_a_gpu():
+    from ferrograd_b200 import _lib
+    L = _lib.lib()
+    out = ctypes.c_void_p()
+    ms = ctypes.c_float()
+    assert L.fg_event_create(None, ctypes.byref(out)) == 1  # FG_ERR_INVALID
+    assert L.fg_event_record(None, None) == 1
+    assert L.fg_event_elapsed_ms(None, None, ctypes.byref(ms)) == 1
+    assert L.fg_event_destroy(None) == 0
