@@ -30,20 +30,6 @@ def read_f32(dev, buf):
     return np.frombuffer(dev.copy_to_host(buf), dtype=np.float32).tolist()
 
 
-def test_events_time_work_on_the_device_stream(dev):
-    """fg_event_*: two points on the device's stream around a 16 MiB upload."""
-    from ferrograd_b200.device import Event
-    n = 1 << 22
-    buf = dev.allocate(F32, n)
-    start, end = Event(dev), Event(dev)
-    start.record()
-    dev.copy_from_host(buf, np.ones(n, np.float32).tobytes())
-    end.record()
-    ms = Event.elapsed_ms(start, end)
-    assert 0.0 <= ms < 10_000.0
-    assert read_f32(dev, buf)[-1] == 1.0
-
-
 def test_allocate_zeroed(dev):
     buf = dev.allocate(F32, 4)
     assert buf.numel == 4 and buf.nbytes == 16
