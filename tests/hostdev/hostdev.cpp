@@ -9,9 +9,11 @@
 // exp2((double)x) is libm's), and fg_execute runs the kernel over its grid.
 // That makes an independent CPU execution of the front end's schedule and
 // rendered arithmetic -- a second oracle for exact mode (FG_FRONT_EXACT=1).
-// The tensor-core GEMM, the HBM reductions and the TF32 split are not
-// emulated: they report FG_ERR_UNSUPPORTED, so only exact mode runs here.
-// Nothing in the product loads this library.
+// The building blocks the default mode routes to (3xTF32 GEMM, HBM
+// reductions, TF32 split) are restated on the CPU from their C-ABI
+// contracts, so the front end's routing (contraction matching, operand
+// layouts, staged operands, residual caching) runs here as well, held to
+// tolerance.  Nothing in the product loads this library.
 #include <dlfcn.h>
 #include <stdarg.h>
 #include <unistd.h>
@@ -263,19 +265,98 @@ int fg_execute(fg_program *prog, const fg_kernel_arg *args, int nargs) {
   return FG_OK;
 }
 
-// Building blocks that only the GPU runs (tensor cores, HBM kernels).
-int fg_gemm_3xtf32(int, int, int, const float *, const float *, int, const float *, const float *,
-                   int, float *, float *, int, int, int, const float *, const float *, int, void *) {
-  return fg::set_error(FG_ERR_UNSUPPORTED, "host test device: exact mode only (no GEMM)");
+// The building blocks the front end routes to (tensor-core GEMM, HBM
+// reductions, TF32 residual split), on the CPU with the GPU kernels'
+// contracts (include/ferro_cuda.h), so the routed (default) mode of the
+// front end runs here too.  Sums are taken in double and rounded once: the
+// routed mode is held to tolerance against the oracle, not to bits.  The
+// GEMM forms the three products of the 3xTF32 split from the truncated
+// operands and the residuals the caller passes (as the tensor cores do), so
+// a residual that does not belong to its operand shows up here as well.
+static float tf32_hi(float v) {
+  uint32_t u;
+  std::memcpy(&u, &v, 4);
+  u &= 0xffffe000u;
+  float h;
+  std::memcpy(&h, &u, 4);
+  return h;
 }
-int fg_split_lo(const float *, float *, size_t, void *) {
-  return fg::set_error(FG_ERR_UNSUPPORTED, "host test device: exact mode only (no TF32 split)");
+
+int fg_gemm_3xtf32(int M, int N, int K, const float *a, const float *a_lo, int lda, const float *b,
+                   const float *b_lo, int ldb, float *c, float *c_lo, int ldc, int flags,
+                   int epilogue, const float *bias, const float *mask, int ldmask, void *) {
+  if (M <= 0 || N <= 0 || K <= 0)
+    return fg::set_error(FG_ERR_INVALID, "gemm: M, N, K must be positive (got %d, %d, %d)", M, N, K);
+  if (!a || !b || !c) return fg::set_error(FG_ERR_INVALID, "gemm: null operand");
+  const bool a_mn = flags & FG_GEMM_A_MN_MAJOR, b_mn = flags & FG_GEMM_B_MN_MAJOR;
+  const bool one = flags & FG_GEMM_1XTF32;
+  if (!one && (!a_lo || !b_lo)) return fg::set_error(FG_ERR_INVALID, "gemm: residuals required");
+  auto at = [&](const float *p, int ld, bool mn, int i, int k) {
+    return mn ? p[(size_t)k * ld + i] : p[(size_t)i * ld + k];
+  };
+  for (int m = 0; m < M; m++)
+    for (int n = 0; n < N; n++) {
+      double acc = 0.0;
+      for (int k = 0; k < K; k++) {
+        const double ah = tf32_hi(at(a, lda, a_mn, m, k)), bh = tf32_hi(at(b, ldb, b_mn, n, k));
+        acc += ah * bh;
+        if (!one) acc += ah * (double)at(b_lo, ldb, b_mn, n, k) + (double)at(a_lo, lda, a_mn, m, k) * bh;
+      }
+      float v = (float)acc;
+      switch (epilogue) {
+        case FG_EPI_BIAS: v = v + bias[n]; break;
+        case FG_EPI_BIAS_RELU: v = v + bias[n]; v = v > 0.f ? v : 0.f; break;
+        case FG_EPI_RELU_MASK: v = mask[(size_t)m * ldmask + n] > 0.f ? v : 0.f; break;
+        default: break;
+      }
+      c[(size_t)m * ldc + n] = v;
+      if (c_lo) c_lo[(size_t)m * ldc + n] = v - tf32_hi(v);
+    }
+  return FG_OK;
 }
-int fg_reduce_rows(int, int, const void *, void *, size_t, size_t, void *) {
-  return fg::set_error(FG_ERR_UNSUPPORTED, "host test device: exact mode only (no HBM reduce)");
+
+int fg_split_lo(const float *x, float *lo, size_t n, void *) {
+  for (size_t i = 0; i < n; i++) lo[i] = x[i] - tf32_hi(x[i]);
+  return FG_OK;
 }
-int fg_reduce_cols(int, int, const void *, void *, size_t, size_t, void *) {
-  return fg::set_error(FG_ERR_UNSUPPORTED, "host test device: exact mode only (no HBM reduce)");
+
+}  // extern "C"
+
+template <typename T>
+static int host_reduce(int op, const T *x, T *out, size_t outer, size_t extent, size_t inner) {
+  // out[o, i] = op over e of x[o, e, i]
+  for (size_t o = 0; o < outer; o++)
+    for (size_t i = 0; i < inner; i++) {
+      const T *p = x + o * extent * inner + i;
+      if (op == FG_REDUCE_MAX) {
+        T m = p[0];
+        for (size_t e = 1; e < extent; e++) m = p[e * inner] > m ? p[e * inner] : m;
+        out[o * inner + i] = extent ? m : T(0);
+      } else {
+        double acc = 0.0;
+        for (size_t e = 0; e < extent; e++) acc += (double)p[e * inner];
+        out[o * inner + i] = (T)acc;
+      }
+    }
+  return FG_OK;
+}
+
+extern "C" {
+
+int fg_reduce_rows(int dtype, int op, const void *x, void *out, size_t rows, size_t cols, void *) {
+  if (dtype == FG_F32)
+    return host_reduce(op, (const float *)x, (float *)out, rows, cols, 1);
+  if (dtype == FG_I32)
+    return host_reduce(op, (const int32_t *)x, (int32_t *)out, rows, cols, 1);
+  return fg::set_error(FG_ERR_INVALID, "fg_reduce_rows: dtype must be F32 or I32");
+}
+
+int fg_reduce_cols(int dtype, int op, const void *x, void *out, size_t rows, size_t cols, void *) {
+  if (dtype == FG_F32)
+    return host_reduce(op, (const float *)x, (float *)out, 1, rows, cols);
+  if (dtype == FG_I32)
+    return host_reduce(op, (const int32_t *)x, (int32_t *)out, 1, rows, cols);
+  return fg::set_error(FG_ERR_INVALID, "fg_reduce_cols: dtype must be F32 or I32");
 }
 
 int fg_u8_to_f32_div(const uint8_t *src, float *dst, size_t n, float divisor, void *) {

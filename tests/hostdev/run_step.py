@@ -2,14 +2,15 @@
 INFRASTRUCTURE; executed in a subprocess by tests/test_hostdev_front.py so
 that this _front module never shares a process with the GPU build's).
 
-argv: input .npz (x, t, dims, lr, steps), output .npz.
+argv: input .npz (x, t, dims, lr, steps), output .npz.  Exact mode unless
+the caller's environment sets FG_FRONT_EXACT=0 (the routed default mode).
 """
 import os
 import sys
 
 import numpy as np
 
-os.environ["FG_FRONT_EXACT"] = "1"
+os.environ.setdefault("FG_FRONT_EXACT", "1")
 _BUILD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build")
 os.environ.setdefault("FG_HOSTDEV_CACHE", os.path.join(_BUILD, "kcache"))
 os.makedirs(os.environ["FG_HOSTDEV_CACHE"], exist_ok=True)
@@ -33,13 +34,14 @@ def main(src, dst):
     params = [p for l in layers for p in l.parameters()]
     opt = F.Sgd(params, lr)
     x, t = F.Tensor.new(d["x"]), F.Tensor.new(d["t"])
-    losses, grads = [], None
-    for _ in range(int(d["steps"])):
-        h = x
+    losses, grads, acts = [], None, None
+    for step in range(int(d["steps"])):
+        h, hs = x, []
         for i, l in enumerate(layers):
             h = l.forward(h)
             if i + 1 < len(layers):
                 h = h.relu()
+                hs.append(h)
         loss = h.cross_entropy(t)
         opt.zero_grad()
         loss.backward()
@@ -47,12 +49,19 @@ def main(src, dst):
         opt.step()
         losses.append(loss.to_vec()[0])
         grads = [gg.numpy() for gg in g]
+        if step == 0:
+            acts = [a.numpy() for a in hs]
     out = {"loss": np.array(losses, np.float32)}
     for i, l in enumerate(layers):
         out[f"w0_{i}"], out[f"b0_{i}"] = ws[i], bs[i]
         out[f"w_{i}"], out[f"b_{i}"] = l.weight.numpy(), l.bias.numpy()
         out[f"dw_{i}"], out[f"db_{i}"] = grads[i], grads[len(layers) + i].ravel()
-    out["compiled"] = np.array(F.stats()["compiled"])
+    for i, a in enumerate(acts):
+        out[f"act_{i}"] = a
+    st = F.stats()
+    out["compiled"] = np.array(st["compiled"])
+    out["gemm"] = np.array(st["gemm"])
+    out["hand_reduce"] = np.array(st["hand_reduce"])
     np.savez(dst, **out)
 
 

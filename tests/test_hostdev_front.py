@@ -2,7 +2,10 @@
 host implementation of the device ABI, tests/hostdev/) -- an independent
 second oracle for exact mode: whole training steps of Linear/relu/
 cross_entropy/backward/Sgd must equal the C oracle bit for bit.  Runs
-without a GPU; the kernels are the same CUDA C the GPU build compiles."""
+without a GPU; the kernels are the same CUDA C the GPU build compiles.
+The default (routed) mode runs here too, its GEMM / reduction / residual
+building blocks restated on the CPU from their C-ABI contracts, held to the
+GPU tests' tolerance."""
 import os
 import subprocess
 import sys
@@ -26,12 +29,13 @@ def hostdev():
     return os.path.join(HERE, "hostdev", "run_step.py")
 
 
-def run(runner, tmp_path, dims, batch, steps, lr=0.01, seeds=(1, 2), opt=None):
+def run(runner, tmp_path, dims, batch, steps, lr=0.01, seeds=(1, 2), opt=None, routed=False):
     x, t = data.mlp_batch(batch, dims[0], dims[-1], *seeds)
     src, dst = tmp_path / "in.npz", tmp_path / "out.npz"
     np.savez(src, x=x, t=t, dims=np.array(dims), lr=np.array(lr), steps=np.array(steps))
     env = dict(os.environ)
     env.pop("OPT", None)
+    env["FG_FRONT_EXACT"] = "0" if routed else "1"
     if opt is not None:
         env["OPT"] = opt
     subprocess.run([sys.executable, runner, str(src), str(dst)], check=True, timeout=600, env=env)
@@ -114,3 +118,57 @@ def test_debug_levels_follow_the_reference(hostdev, tmp_path, level):
     dumps = [l for l in lines if "[schedule]" in l]
     assert (len(dumps) > 0) == (level >= 3)
     assert any("extern \"C\" __global__" in l for l in lines) == (level >= 4)
+
+
+def test_host_routed_step_matches_oracle_within_tolerance(oracle, hostdev, tmp_path):
+    """The default (routed) mode on the host test device: contractions go to
+    the GEMM contract (operands in place or staged, TF32 residuals made or
+    reused), the rest is rendered.  Held to the GPU tests' 1e-4 and
+    ReLU-tie-aware check (tests/mlp_check.py)."""
+    from mlp_check import check_step
+    dims, batch = (512, 256, 256, 10), 64
+    x, t, r = run(hostdev, tmp_path, dims, batch, steps=1, routed=True)
+    assert int(r["gemm"]) >= 4  # both forward contractions, both dW, the dX of layer 1
+    nl = len(dims) - 1
+    ws = [r[f"w0_{i}"] for i in range(nl)]
+    bs = [r[f"b0_{i}"] for i in range(nl)]
+    oacts = []
+    out = oracle.mlp_step(ws, bs, x, t, 0.01, acts=oacts)
+    assert abs(float(r["loss"][0]) - out[0]) <= 1e-4 * abs(out[0])
+    gacts = [r[f"act_{i}"] for i in range(nl - 1)]
+    grads = ([r[f"dw_{i}"] for i in range(nl)], [r[f"db_{i}"] for i in range(nl)])
+    params = ([r[f"w_{i}"] for i in range(nl)], [r[f"b_{i}"] for i in range(nl)])
+    check_step(ws, bs, x, t, 0.01, gacts, grads, params, out, oacts, tol=1e-4)
+
+
+def test_host_routed_steps_track_oracle(oracle, hostdev, tmp_path):
+    """Three routed steps: the TF32 residual of each parameter is cached per
+    version of its contents, so after every SGD store it must be remade; a
+    stale residual would drift from the oracle here."""
+    dims, batch = (512, 256, 256, 10), 64
+    x, t, r = run(hostdev, tmp_path, dims, batch, steps=3, routed=True, seeds=(7, 8))
+    ws = [r[f"w0_{i}"] for i in range(3)]
+    bs = [r[f"b0_{i}"] for i in range(3)]
+    w0 = [w.copy() for w in ws]
+    for s in range(3):
+        oloss, ws, bs, _, _, _ = oracle.mlp_step(ws, bs, x, t, 0.01, want_grads=False)
+        assert abs(float(r["loss"][s]) - oloss) <= 1e-4 * abs(oloss), s
+    for i in range(3):
+        d_got, d_ref = r[f"w_{i}"] - w0[i], ws[i] - w0[i]
+        assert np.max(np.abs(d_got - d_ref)) <= 3e-4 * np.max(np.abs(d_ref)), i
+
+
+def test_host_routed_matmul_and_big_reductions(oracle, hostdev, tmp_path):
+    runner = os.path.join(os.path.dirname(hostdev), "run_ops.py")
+    dst = tmp_path / "ops.npz"
+    subprocess.run([sys.executable, runner, str(dst)], check=True, timeout=600)
+    r = dict(np.load(dst))
+    assert int(r["gemm"]) == 1 and int(r["hand_reduce"]) == 3
+    ref = r["a"].astype(np.float64) @ r["b"].astype(np.float64)
+    assert np.max(np.abs(r["c"] - ref)) <= 1e-5 * np.max(np.abs(ref))
+    x = r["x"]
+    s_ref = oracle.reduce_last(x, oracle.SUM)
+    assert np.max(np.abs(r["s_rows"] - s_ref)) <= 1e-4 * np.max(np.abs(s_ref))
+    assert np.array_equal(r["m_rows"], oracle.reduce_last(x, oracle.MAX))
+    c_ref = oracle.reduce_axis0(x, oracle.SUM)
+    assert np.max(np.abs(r["s_cols"] - c_ref)) <= 1e-4 * np.max(np.abs(c_ref))
