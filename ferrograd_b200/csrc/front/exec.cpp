@@ -509,7 +509,8 @@ struct KeyBuf {
   }
 };
 
-std::string spec_key(const RenderSpec &spec, const ParamSlots &ps) {
+std::string spec_key(const RenderSpec &spec, const ParamSlots &ps,
+                     const std::vector<UOpP> &order) {
   KeyBuf k;
   k.put((int64_t)spec.store);
   k.put(spec.pitch);
@@ -519,9 +520,9 @@ std::string spec_key(const RenderSpec &spec, const ParamSlots &ps) {
   for (int64_t d : spec.domain) k.put(d);
   k.put((int64_t)spec.value_ctx.size());
   for (auto &c : spec.value_ctx) k.put_str(c);
-  UOpP root = spec.store == RenderSpec::View ? make_store(spec.dest, spec.value) : spec.value;
   std::unordered_map<const UOp *, int64_t> pos;
-  for (auto &n : toposort(root)) {
+  pos.reserve(order.size());
+  for (auto &n : order) {
     pos[n.get()] = (int64_t)pos.size();
     k.put((int64_t)n->op);
     k.put((int64_t)n->dtype);
@@ -566,9 +567,11 @@ void launch_spec(const RenderSpec &spec, const BufferP &out) {
     while (d->op != Op::Buffer && !d->src.empty()) d = d->src[0].get();
     if (d->op == Op::Buffer) written = d->buf.get();
   }
-  ParamSlots ps = view ? collect_params(make_store(spec.dest, spec.value), 0)
-                       : collect_params(spec.value, 1);
-  std::string key = spec_key(spec, ps);
+  // one walk of the kernel's graph gives both its parameter slots and its
+  // structural key
+  const std::vector<UOpP> order = toposort(view ? make_store(spec.dest, spec.value) : spec.value);
+  ParamSlots ps = collect_params_from(order, view ? 0 : 1);
+  std::string key = spec_key(spec, ps, order);
   auto &cache = spec_cache();
   auto it = cache.find(key);
   if (it == cache.end()) {

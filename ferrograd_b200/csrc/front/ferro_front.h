@@ -111,6 +111,9 @@ struct UOp {
   bool has_shape = false;
   Shape shape;               // inferred as src/uop.rs:806-866
   uint64_t uid = 0;          // creation order (debug output only)
+  // Graph walks mark a node visited by stamping their own walk number here
+  // (toposort); the front end is single-threaded, so no two walks overlap.
+  mutable uint64_t walk_mark = 0;
 };
 
 // Interned constructors (src/uop.rs:536-760, 926-1040): structurally equal

@@ -24,6 +24,8 @@ struct ParamSlots {
   std::unordered_map<const UOp *, std::vector<int>> shrink_slots;
 };
 ParamSlots collect_params(const UOpP &root, int slot_offset);
+// The same over an existing toposort of the kernel's root.
+ParamSlots collect_params_from(const std::vector<UOpP> &order, int slot_offset);
 
 UOpP substitute_materialized(const UOpP &root, const std::map<const UOp *, UOpP> &repl);
 UOpP substitute_with_map(const UOpP &root, const std::unordered_map<const UOp *, UOpP> &repl,

@@ -62,42 +62,43 @@ bool is_movement(Op op) {
 
 // ---------------------------------------------------------------------------
 // Interning (src/uop.rs:536-570): a node is looked up by (op, dtype, source
-// identities, arg, literal, buffer identity).  Entries hold weak references;
-// an expired entry is overwritten, and sources of a live entry are alive
-// (the node owns them), so a live key never carries a dangling pointer.
+// identities, arg, literal, buffer identity).  The table maps the hash of
+// those fields to weak references of the nodes that have it; a lookup
+// compares the candidates' own fields, so it allocates nothing.  Sources of
+// a live node are alive (the node owns them), so comparing source pointers
+// of a live candidate is sound; expired entries are swept when the table
+// has doubled.
 namespace {
 
-struct Key {
-  int op;
-  int dtype;
-  int rop;
-  uint64_t vbits;
-  const void *buf;
-  std::vector<const UOp *> src;
-  std::vector<int64_t> arg;
-  bool operator==(const Key &o) const {
-    return op == o.op && dtype == o.dtype && rop == o.rop && vbits == o.vbits && buf == o.buf &&
-           src == o.src && arg == o.arg;
-  }
-};
+uint64_t node_hash(Op op, DType dt, Op rop, uint64_t vbits, const DeviceBuffer *buf,
+                   const std::vector<UOpP> &srcs, const std::vector<int64_t> &arg) {
+  uint64_t h = 1469598103934665603ULL;
+  auto mix = [&h](uint64_t v) { h = (h ^ v) * 1099511628211ULL; };
+  mix((uint64_t)op);
+  mix((uint64_t)dt);
+  mix((uint64_t)(op == Op::ReduceAxis ? (int)rop : 0));
+  mix(vbits);
+  mix((uint64_t)(uintptr_t)buf);
+  for (auto &p : srcs) mix((uint64_t)(uintptr_t)p.get());
+  for (auto a : arg) mix((uint64_t)a);
+  return h;
+}
 
-struct KeyHash {
-  size_t operator()(const Key &k) const {
-    uint64_t h = 1469598103934665603ULL;
-    auto mix = [&h](uint64_t v) { h = (h ^ v) * 1099511628211ULL; };
-    mix((uint64_t)k.op);
-    mix((uint64_t)k.dtype);
-    mix((uint64_t)k.rop);
-    mix(k.vbits);
-    mix((uint64_t)(uintptr_t)k.buf);
-    for (auto *p : k.src) mix((uint64_t)(uintptr_t)p);
-    for (auto a : k.arg) mix((uint64_t)a);
-    return (size_t)h;
-  }
-};
+bool same_node(const UOp &u, Op op, DType dt, Op rop, uint64_t vbits, const DeviceBuffer *buf,
+               const std::vector<UOpP> &srcs, const std::vector<int64_t> &arg) {
+  if (u.op != op || u.dtype != dt || u.buf.get() != buf || u.src.size() != srcs.size())
+    return false;
+  if (op == Op::ReduceAxis && u.reduce_op != rop) return false;
+  uint64_t ub;
+  std::memcpy(&ub, &u.value, sizeof(ub));
+  if (ub != vbits) return false;
+  for (size_t i = 0; i < srcs.size(); i++)
+    if (u.src[i].get() != srcs[i].get()) return false;
+  return u.arg == arg;
+}
 
-std::unordered_map<Key, std::weak_ptr<const UOp>, KeyHash> &interner() {
-  static std::unordered_map<Key, std::weak_ptr<const UOp>, KeyHash> m;
+std::unordered_multimap<uint64_t, std::weak_ptr<const UOp>> &interner() {
+  static std::unordered_multimap<uint64_t, std::weak_ptr<const UOp>> m;
   return m;
 }
 size_t g_sweep_at = 4096;
@@ -164,20 +165,14 @@ void infer_shape(UOp &u) {
 
 UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, std::vector<int64_t> arg = {},
             Op rop = Op::Add, double value = 0.0, const BufferP &buf = nullptr) {
-  Key k;
-  k.op = (int)op;
-  k.dtype = (int)dt;
-  k.rop = op == Op::ReduceAxis ? (int)rop : 0;
-  std::memcpy(&k.vbits, &value, sizeof(double));
-  k.buf = buf.get();
-  k.src.reserve(srcs.size());
-  for (auto &s : srcs) k.src.push_back(s.get());
-  k.arg = arg;
+  uint64_t vbits;
+  std::memcpy(&vbits, &value, sizeof(double));
+  const uint64_t h = node_hash(op, dt, rop, vbits, buf.get(), srcs, arg);
   auto &m = interner();
-  auto it = m.find(k);
-  if (it != m.end()) {
-    if (auto live = it->second.lock()) return live;
-  }
+  auto range = m.equal_range(h);
+  for (auto it = range.first; it != range.second; ++it)
+    if (auto live = it->second.lock())
+      if (same_node(*live, op, dt, rop, vbits, buf.get(), srcs, arg)) return live;
   auto u = std::make_shared<UOp>();
   u->op = op;
   u->dtype = dt;
@@ -189,7 +184,7 @@ UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, std::vector<int64_t> arg = 
   u->uid = g_uid++;
   infer_shape(*u);
   UOpP out = u;
-  m[k] = out;
+  m.emplace(h, out);
   if (m.size() > g_sweep_at) sweep_interner();
   return out;
 }
@@ -251,29 +246,39 @@ bool has_buffer_identity(const UOp *u) {
   return false;
 }
 
+// A fresh walk number for the visited stamps (UOp::walk_mark), shared by
+// every walker so two walks never use the same number.
+static uint64_t new_walk() {
+  static uint64_t walks = 0;
+  return ++walks;
+}
+
 std::vector<UOpP> toposort(const UOpP &root) {
   // Iterative post-order DFS.  Sources are pushed in reverse so the first
   // source is finished first; After walks its effect last-pushed-first
-  // (src/uop.rs:1044-1074).
+  // (src/uop.rs:1044-1074).  The stack holds pointers to the handles inside
+  // the (immutable) parents, so a node's handle is copied once, into `out`.
+  const uint64_t mark = new_walk();
+  auto visited = [mark](const UOp *n) { return n->walk_mark == mark; };
   std::vector<UOpP> out;
-  std::unordered_set<const UOp *> visited;
-  std::vector<std::pair<UOpP, bool>> stack{{root, false}};
+  std::vector<std::pair<const UOpP *, bool>> stack{{&root, false}};
   while (!stack.empty()) {
-    auto [node, processed] = stack.back();
+    auto [hp, processed] = stack.back();
     stack.pop_back();
-    if (visited.count(node.get())) continue;
+    const UOp *node = hp->get();
+    if (visited(node)) continue;
     if (processed) {
-      visited.insert(node.get());
-      out.push_back(node);
+      node->walk_mark = mark;
+      out.push_back(*hp);
       continue;
     }
-    stack.push_back({node, true});
+    stack.push_back({hp, true});
     if (node->op == Op::After) {
       for (auto &s : node->src)
-        if (!visited.count(s.get())) stack.push_back({s, false});
+        if (!visited(s.get())) stack.push_back({&s, false});
     } else {
       for (auto it = node->src.rbegin(); it != node->src.rend(); ++it)
-        if (!visited.count(it->get())) stack.push_back({*it, false});
+        if (!visited(it->get())) stack.push_back({&*it, false});
     }
   }
   return out;
@@ -308,10 +313,12 @@ std::string dump(const UOpP &root) {
 // Gradient rules (src/gradient.rs:97-205).
 namespace {
 
-std::unordered_map<const UOp *, std::vector<UOpP>> consumer_map(const std::vector<UOpP> &order) {
-  std::unordered_map<const UOp *, std::vector<UOpP>> m;
+std::unordered_map<const UOp *, std::vector<const UOp *>> consumer_map(
+    const std::vector<UOpP> &order) {
+  std::unordered_map<const UOp *, std::vector<const UOp *>> m;
+  m.reserve(order.size());
   for (auto &n : order)
-    for (auto &s : n->src) m[s.get()].push_back(n);
+    for (auto &s : n->src) m[s.get()].push_back(n.get());
   return m;
 }
 
@@ -409,7 +416,7 @@ std::map<const UOp *, UOpP> compute_gradient(const UOpP &root, const UOpP &root_
     if (!needed.insert(n).second) continue;
     auto it = consumers.find(n);
     if (it != consumers.end())
-      for (auto &c : it->second) stack.push_back(c.get());
+      for (const UOp *c : it->second) stack.push_back(c);
   }
   needed.insert(root.get());
 
@@ -459,7 +466,7 @@ std::unordered_set<const UOp *> nested_reduce_inputs(const std::vector<UOpP> &or
 }
 
 bool should_materialize(const UOp *node, const std::unordered_set<const UOp *> &roots,
-                        const std::unordered_map<const UOp *, std::vector<UOpP>> &consumers,
+                        const std::unordered_map<const UOp *, std::vector<const UOp *>> &consumers,
                         const std::unordered_set<const UOp *> &nested) {
   if (roots.count(node) || !node->has_shape) return false;
   switch (node->op) {
@@ -475,7 +482,7 @@ bool should_materialize(const UOp *node, const std::unordered_set<const UOp *> &
   if (it != consumers.end() && it->second.size() > 1) return true;
   if (node->op == Op::ReduceAxis && it != consumers.end() &&
       std::any_of(it->second.begin(), it->second.end(),
-                  [](const UOpP &c) { return is_alu(c->op); }))
+                  [](const UOp *c) { return is_alu(c->op); }))
     return true;
   return node->op == Op::ReduceAxis && nested.count(node);
 }
@@ -487,21 +494,23 @@ bool should_materialize(const UOp *node, const std::unordered_set<const UOp *> &
 // replaces or has already rewritten.
 template <typename Stop>
 static std::vector<UOpP> toposort_until(const UOpP &root, Stop stop) {
+  const uint64_t mark = new_walk();
+  auto visited = [mark](const UOp *n) { return n->walk_mark == mark; };
   std::vector<UOpP> out;
-  std::unordered_set<const UOp *> visited;
-  std::vector<std::pair<UOpP, bool>> stack{{root, false}};
+  std::vector<std::pair<const UOpP *, bool>> stack{{&root, false}};
   while (!stack.empty()) {
-    auto [node, processed] = stack.back();
+    auto [hp, processed] = stack.back();
     stack.pop_back();
-    if (visited.count(node.get())) continue;
-    if (processed || (node != root && stop(node.get()))) {
-      visited.insert(node.get());
-      out.push_back(node);
+    const UOp *node = hp->get();
+    if (visited(node)) continue;
+    if (processed || (node != root.get() && stop(node))) {
+      node->walk_mark = mark;
+      out.push_back(*hp);
       continue;
     }
-    stack.push_back({node, true});
+    stack.push_back({hp, true});
     for (auto it = node->src.rbegin(); it != node->src.rend(); ++it)
-      if (!visited.count(it->get())) stack.push_back({*it, false});
+      if (!visited(it->get())) stack.push_back({&*it, false});
   }
   return out;
 }
@@ -562,10 +571,14 @@ UOpP substitute_with_map(const UOpP &root, const std::unordered_map<const UOp *,
 }
 
 ParamSlots collect_params(const UOpP &root, int slot_offset) {
+  return collect_params_from(toposort(root), slot_offset);
+}
+
+ParamSlots collect_params_from(const std::vector<UOpP> &order, int slot_offset) {
   // parameterize_inputs (src/schedule.rs:176-245): buffers by first
   // appearance, one scalar per parameterised Shrink start.
   ParamSlots ps;
-  for (auto &node : toposort(root)) {
+  for (auto &node : order) {
     if (node->op == Op::Buffer) {
       if (!ps.buffer_slot.count(node->buf.get())) {
         ps.buffer_slot[node->buf.get()] = (int)ps.inputs.size() + slot_offset;

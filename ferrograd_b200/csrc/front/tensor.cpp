@@ -26,9 +26,12 @@ std::vector<std::weak_ptr<TensorInner>> &live_list() {
   return v;
 }
 
-void require(bool ok, const std::string &msg) {
-  if (!ok) throw Panic(msg);
-}
+// Checks a precondition; the message (often built from shapes) is only
+// formatted when the check fails.
+#define require(ok, msg)         \
+  do {                           \
+    if (!(ok)) throw Panic(msg); \
+  } while (0)
 
 // Numpy-style broadcast target (src/shape.rs:66-89).
 bool broadcast_shape(const Shape &a, const Shape &b, Shape *out) {
