@@ -2,9 +2,10 @@
 
 The device math runs in the oracle here (CPU); what is tested is the
 sharding, the mean of per-shard gradients equalling the full-batch gradient,
-the communicator-id exchange, the cross-rank parameter digest, and that a rank
-which never joins a collective turns into an error on the others (not a
-hang)."""
+the communicator-id exchange, the cross-rank parameter digest, the
+peer-sharded exchange's arithmetic over the product's chunk layout, and that
+a rank which never joins a collective turns into an error on the others (not
+a hang)."""
 import datetime
 import os
 import socket
@@ -117,6 +118,99 @@ def test_rank_that_never_joins_is_an_error():
             p.kill()
     assert res[1] == "left"
     assert res[0].startswith("error"), res[0]
+
+
+def _peer_worker(rank, world, port, q):
+    """The peer-sharded exchange's arithmetic on the host: every rank lays its
+    gradients out with fg_peer_layout (the product's layout), each chunk's
+    shard r is summed by rank r over all ranks in rank order and updated with
+    SGD (the loss slot carries the summed loss), and the updated shards are
+    gathered back; the exchange itself goes over gloo instead of copy
+    engines."""
+    sys.path.insert(0, ROOT)
+    try:
+        import torch
+        from ferrograd_b200 import data, dp, peer_layout
+        from oracle import oracle as orc
+        dist = _init(rank, world, port)
+        dims, B, lr, chunks = (48, 64, 32, 10), 16, 0.05, 2
+        x, t = data.mlp_batch(B, dims[0], dims[-1], 3, 4)
+        rng = orc.InitRng()
+        ws, bs = map(list, zip(*[rng.linear(dims[i], dims[i + 1]) for i in range(len(dims) - 1)]))
+        _, ch = peer_layout(dims, world, chunks)
+        unit = 64 * world
+        pad = lambda n, u: (n + u - 1) // u * u  # noqa: E731
+        w_off, b_off, off = [], [], 0
+        for l in range(len(dims) - 1):
+            o, i = dims[l + 1], dims[l]
+            w_off.append(off)
+            b_off.append(off + pad(o * i, 64))
+            raw = pad(o * i, 64) + pad(o, 64) + (64 if l == 0 else 0)
+            off += pad(raw, unit)
+        loss_off = b_off[0] + pad(dims[1], 64)
+        G = off
+        # this rank's local gradients, pre-scaled by 1/world like the step's
+        lo, hi = dp.shard_rows(B, rank, world)
+        loss, _, _, dW, db, _ = orc.mlp_step(ws, bs, x[lo:hi], t[lo:hi], lr)
+        grad = np.zeros(G, np.float32)
+        par = np.zeros(G, np.float32)
+        for l in range(len(dims) - 1):
+            grad[w_off[l]:w_off[l] + dW[l].size] = dW[l].ravel() / world
+            grad[b_off[l]:b_off[l] + db[l].size] = db[l] / world
+            par[w_off[l]:w_off[l] + ws[l].size] = ws[l].ravel()
+            par[b_off[l]:b_off[l] + bs[l].size] = bs[l]
+        grad[loss_off] = np.float32(loss) / world
+        everyone = [torch.zeros(G) for _ in range(world)]
+        dist.all_gather(everyone, torch.from_numpy(grad))
+        parts = [e.numpy() for e in everyone]
+        new = np.zeros(G, np.float32)
+        for c_off, c_len in ch:
+            S = c_len // world
+            sl = slice(c_off + rank * S, c_off + (rank + 1) * S)
+            g = parts[0][sl].copy()
+            for j in range(1, world):
+                g = (g + parts[j][sl]).astype(np.float32)
+            upd = (par[sl] + (-(g * np.float32(lr)))).astype(np.float32)
+            if c_off + rank * S <= loss_off < c_off + (rank + 1) * S:
+                upd[loss_off - (c_off + rank * S)] = g[loss_off - (c_off + rank * S)]
+            new[sl] = upd
+        shards = [torch.zeros(G) for _ in range(world)]
+        dist.all_gather(shards, torch.from_numpy(new))
+        full = np.zeros(G, np.float32)
+        for c_off, c_len in ch:
+            S = c_len // world
+            for j in range(world):
+                sl = slice(c_off + j * S, c_off + (j + 1) * S)
+                full[sl] = shards[j].numpy()[sl]
+        pw = [full[w_off[l]:w_off[l] + ws[l].size].reshape(ws[l].shape) for l in range(len(ws))]
+        pb = [full[b_off[l]:b_off[l] + bs[l].size] for l in range(len(bs))]
+        agree = dp.digests_agree(dist, dp.params_digest(pw + pb), world)
+        floss, fw, fb, _, _, _ = orc.mlp_step(ws, bs, x, t, lr)
+        err = max(np.max(np.abs((pw[l] - ws[l]) - (fw[l] - ws[l]))) / np.max(np.abs(fw[l] - ws[l]))
+                  for l in range(len(ws)))
+        dist.destroy_process_group()
+        q.put((rank, float(err), abs(float(full[loss_off]) - floss) / floss, agree, len(ch)))
+    except Exception as e:  # report, never hang the parent
+        q.put((rank, repr(e), None, False, 0))
+
+
+def test_peer_sharded_exchange_arithmetic_on_gloo_ranks():
+    world, port = 2, free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, err, loss_err, agree, nchunks in res:
+        assert isinstance(err, float), err
+        # layer 0 (64 outputs) in 2 row blocks of 32; layer 1 (32 outputs)
+        # whole, as blocks of 16 rows fall under the 32-row rule; layer 2 whole
+        assert nchunks == 4
+        assert err <= 1e-5 and loss_err <= 1e-6, (rank, err, loss_err)
+        assert agree
 
 
 def test_shard_rows_partition():
