@@ -172,3 +172,40 @@ def test_host_routed_matmul_and_big_reductions(oracle, hostdev, tmp_path):
     assert np.array_equal(r["m_rows"], oracle.reduce_last(x, oracle.MAX))
     c_ref = oracle.reduce_axis0(x, oracle.SUM)
     assert np.max(np.abs(r["s_cols"] - c_ref)) <= 1e-4 * np.max(np.abs(c_ref))
+
+
+@pytest.mark.parametrize("routed", [False, True])
+def test_host_narrow_batch_loop_tracks_oracle(oracle, hostdev, tmp_path, routed):
+    """examples/mnist.rs's loop over narrow() batches of one resident tensor:
+    each batch start is a kernel argument, so later batches reuse the
+    programs.  Exact mode equals the oracle run on the same slices bit
+    for bit; the routed mode (narrowed inputs reach the GEMM as strided
+    views) stays within the per-step 1e-4."""
+    dims, batch, nb = (512, 256, 10), 32, 4
+    x, t = data.mlp_batch(batch * nb, dims[0], dims[-1], 5, 6)
+    src, dst = tmp_path / "in.npz", tmp_path / "out.npz"
+    np.savez(src, x=x, t=t, dims=np.array(dims), lr=np.array(0.01), batch=np.array(batch))
+    env = dict(os.environ, FG_FRONT_EXACT="0" if routed else "1")
+    env.pop("OPT", None)
+    runner = os.path.join(os.path.dirname(hostdev), "run_narrow.py")
+    subprocess.run([sys.executable, runner, str(src), str(dst)], check=True, timeout=600, env=env)
+    r = dict(np.load(dst))
+    assert (int(r["gemm"]) > 0) == routed
+    # the first step reads the zero biases as literal zeros (never-written
+    # buffers); from the second batch on every program is reused
+    assert r["compiled"][-1] == r["compiled"][1]
+    ws, bs = [r["w0_0"], r["w0_1"]], [r["b0_0"], r["b0_1"]]
+    w0 = [w.copy() for w in ws]
+    for b in range(nb):
+        sl = slice(b * batch, (b + 1) * batch)
+        oloss, ws, bs, _, _, _ = oracle.mlp_step(ws, bs, x[sl], t[sl], 0.01, want_grads=False)
+        if routed:
+            assert abs(float(r["loss"][b]) - oloss) <= 1e-4 * abs(oloss), b
+        else:
+            assert np.float32(r["loss"][b]) == np.float32(oloss), b
+    for i in range(2):
+        if routed:
+            d_got, d_ref = r[f"w_{i}"] - w0[i], ws[i] - w0[i]
+            assert np.max(np.abs(d_got - d_ref)) <= nb * 1e-4 * np.max(np.abs(d_ref)), i
+        else:
+            assert np.array_equal(r[f"w_{i}"], ws[i]) and np.array_equal(r[f"b_{i}"], bs[i]), i
