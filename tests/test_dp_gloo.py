@@ -133,7 +133,7 @@ def _peer_worker(rank, world, port, q):
         from ferrograd_b200 import data, dp, peer_layout
         from oracle import oracle as orc
         dist = _init(rank, world, port)
-        dims, B, lr, chunks = (48, 64, 32, 10), 16, 0.05, 2
+        dims, B, lr, chunks = (48, 64, 32, 10), 24, 0.05, 2
         x, t = data.mlp_batch(B, dims[0], dims[-1], 3, 4)
         rng = orc.InitRng()
         ws, bs = map(list, zip(*[rng.linear(dims[i], dims[i + 1]) for i in range(len(dims) - 1)]))
@@ -159,7 +159,7 @@ def _peer_worker(rank, world, port, q):
             grad[b_off[l]:b_off[l] + db[l].size] = db[l] / world
             par[w_off[l]:w_off[l] + ws[l].size] = ws[l].ravel()
             par[b_off[l]:b_off[l] + bs[l].size] = bs[l]
-        grad[loss_off] = np.float32(loss) / world
+        grad[loss_off] = np.float32(np.float32(loss) / world)
         everyone = [torch.zeros(G) for _ in range(world)]
         dist.all_gather(everyone, torch.from_numpy(grad))
         parts = [e.numpy() for e in everyone]
@@ -194,8 +194,9 @@ def _peer_worker(rank, world, port, q):
         q.put((rank, repr(e), None, False, 0))
 
 
-def test_peer_sharded_exchange_arithmetic_on_gloo_ranks():
-    world, port = 2, free_port()
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_sharded_exchange_arithmetic_on_gloo_ranks(world):
+    port = free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
@@ -206,8 +207,10 @@ def test_peer_sharded_exchange_arithmetic_on_gloo_ranks():
         p.join(timeout=60)
     for rank, err, loss_err, agree, nchunks in res:
         assert isinstance(err, float), err
-        # layer 0 (64 outputs) in 2 row blocks of 32; layer 1 (32 outputs)
-        # whole, as blocks of 16 rows fall under the 32-row rule; layer 2 whole
+        # layer 0 (64 outputs) in 2 row blocks of 32 (a block's 32 x 48
+        # floats split into 64-float shards for 2 and 3 ranks alike); layer 1
+        # (32 outputs) whole, as blocks of 16 rows fall under the 32-row
+        # rule; layer 2 whole
         assert nchunks == 4
         assert err <= 1e-5 and loss_err <= 1e-6, (rank, err, loss_err)
         assert agree
