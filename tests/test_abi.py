@@ -88,3 +88,12 @@ def test_event_entry_points_reject_null_arguments_without_a_gpu():
     assert L.fg_event_record(None, None) == 1
     assert L.fg_event_elapsed_ms(None, None, ctypes.byref(ms)) == 1
     assert L.fg_event_destroy(None) == 0
+
+
+def test_python_constants_match_the_header():
+    """Sizes the binding allocates for handles must be the header's."""
+    from ferrograd_b200 import _lib
+    text = open(HEADER).read()
+    defs = dict(re.findall(r"#define\s+(FG_[A-Z0-9_]+)\s+(\d+)", text))
+    assert int(defs["FG_UNIQUE_ID_BYTES"]) == _lib.UNIQUE_ID_BYTES
+    assert int(defs["FG_PEER_HANDLE_BYTES"]) == _lib.PEER_HANDLE_BYTES
