@@ -12,16 +12,18 @@ Prints ONE JSON line on rank 0.  `value` is global training steps per second
 measured on the device with inputs resident in HBM (CUDA events on the step's
 stream, max over ranks); `e2e` is the same metric through the C-ABI host entry
 point (fg_mlp_step_host) with the batch copied from pinned host memory and the
-loss copied back every step.  `--impl reference` times the reference CPU
-arithmetic (the oracle port: the Rust reference cannot be built here) with all
-host threads.
+loss copied back every step.  At one GPU the line also carries `per_config`
+(configs 1-4 and the lazy-Tensor front end at configs 1 and 5, each with its
+roofline) and `cpu_baseline` (the oracle on one pinned host core, as the
+single-threaded reference runs; an all-cores figure is attached as secondary).
+`--impl reference` times the reference CPU arithmetic (the oracle port: the
+Rust reference cannot be built here) on one pinned host core.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -57,75 +59,122 @@ def load_peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def gemm_traffic_per_flop():
-    """DRAM bytes per algorithmic flop of the GEMM, from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "gemm3x_c5_shapes_ncu.md")
-    try:
-        text = open(path).read()
-    except OSError:
-        return None
-    m = re.search(r"traffic_bytes_per_flop:\s*([0-9.eE+-]+)", text)
-    return float(m.group(1)) if m else None
+# DRAM bytes per algorithmic flop of the config-5 forward GEMM launch, from one
+# ncu capture of `python bench.py --config c5gemm --steps 1 --warmup 3`
+# (dram__bytes_read.sum + dram__bytes_write.sum = 1.252e9 + 0.238e9 B over
+# 2.749e11 flop); `roofline.traffic` is this times the flops of one launch.
+GEMM_TRAFFIC_BYTES_PER_FLOP = 5.42e-3
+# A timed region shorter than this runs at the burst clock; longer ones settle
+# at the sustained (power-capped) clock.
+SUSTAINED_AFTER_S = 2.0
 
 
 # ---------------------------------------------------------------------------
 # CPU side: the oracle (reference arithmetic) on a bounded sample
 # ---------------------------------------------------------------------------
-def cpu_step_sample(rows: int, threads: int):
-    """Time one C5 step restricted to `rows` batch rows on the oracle; returns seconds."""
+def _c5_params():
     from oracle import oracle as orc
-    from ferrograd_b200 import data
-    orc.set_threads(threads)
-    x, t = data.mlp_batch(rows, DIMS[0], DIMS[-1], X_SEED, LABEL_SEED)
     rng = orc.InitRng()
     ws, bs = [], []
     for i in range(len(DIMS) - 1):
         w, b = rng.linear(DIMS[i], DIMS[i + 1])
         ws.append(w)
         bs.append(b)
+    return ws, bs
+
+
+def cpu_step_sample(rows: int, threads: int, params=None):
+    """Seconds of one C5 step restricted to `rows` batch rows on the oracle."""
+    from oracle import oracle as orc
+    from ferrograd_b200 import data
+    orc.set_threads(threads)
+    x, t = data.mlp_batch(rows, DIMS[0], DIMS[-1], X_SEED, LABEL_SEED)
+    ws, bs = params if params is not None else _c5_params()
     t0 = time.perf_counter()
     orc.mlp_step(ws, bs, x, t, LR, want_grads=False)
     return time.perf_counter() - t0
 
 
+class _Pinned:
+    """Run the enclosed code on one host core (the reference is
+    single-threaded: its generated loops run one at a time on the calling
+    thread, src/device/cpu.rs:328-380)."""
+
+    def __enter__(self):
+        self.saved = os.sched_getaffinity(0)
+        self.core = min(self.saved)
+        os.sched_setaffinity(0, {self.core})
+        return self
+
+    def __exit__(self, *exc):
+        os.sched_setaffinity(0, self.saved)
+
+
+def _extrapolate(t_small: float, t_big: float, r_small: int, r_big: int) -> float:
+    """Full-batch step seconds from two row samples: a step costs a fixed part
+    (the SGD update and weight-only work) plus a part linear in the rows (every
+    GEMM and the cross-entropy)."""
+    per_row = max(t_big - t_small, 0.0) / (r_big - r_small)
+    fixed = max(t_big - per_row * r_big, 0.0)
+    return fixed + per_row * GLOBAL_BATCH
+
+
 def cpu_baseline(target_s: float = 15.0):
+    """The oracle on one pinned core (primary, as the reference runs), plus all
+    host cores through OpenMP (secondary, labelled: not how the reference runs)."""
+    params = _c5_params()
+    with _Pinned() as pin:
+        cpu_step_sample(8, 1, params)  # first touch of the weights
+        t16 = cpu_step_sample(16, 1, params)
+        t48 = cpu_step_sample(48, 1, params)
+        per_row = max(t48 - t16, 1e-4) / 32
+        rows = int(min(GLOBAL_BATCH, max(64, (target_s - t16) / per_row)))
+        rows = max(64, rows // 16 * 16)
+        tr = cpu_step_sample(rows, 1, params)
+        core = pin.core
+    step_s = _extrapolate(t16, tr, 16, rows)
     threads = os.cpu_count() or 1
-    probe_rows = 128
-    tp = cpu_step_sample(probe_rows, threads)
-    rows = int(min(GLOBAL_BATCH, max(probe_rows, probe_rows * target_s / max(tp, 1e-3))))
-    rows = max(probe_rows, (rows // 128) * 128)
-    ts = cpu_step_sample(rows, threads) if rows != probe_rows else tp
-    step_s = ts * GLOBAL_BATCH / rows
-    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": threads, "kind": "port",
-            "sample": (f"one config-5 training step of the oracle (C restatement of the reference "
-                       f"CPU arithmetic, OpenMP over output rows) on {rows} of {GLOBAL_BATCH} batch "
-                       f"rows ({ts:.2f} s), scaled x{GLOBAL_BATCH / rows:.0f} to the full batch")}
+    tp = cpu_step_sample(256, threads, params)
+    tq = cpu_step_sample(1024, threads, params)
+    mt_step_s = _extrapolate(tp, tq, 256, 1024)
+    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": 1, "kind": "port",
+            "sample": (f"oracle (C restatement of the reference CPU arithmetic) pinned to host core "
+                       f"{core}: one config-5 step on {rows} of {GLOBAL_BATCH} batch rows "
+                       f"({tr:.2f} s) and on 16 rows ({t16:.2f} s), extrapolated linearly in the "
+                       f"rows to the full batch (x{GLOBAL_BATCH / rows:.2f} on the per-row part)"),
+            "secondary_all_cores": {
+                "value": 1.0 / mt_step_s, "unit": "steps/s", "cores": threads,
+                "note": "not how the reference runs: the oracle's output loops split over all "
+                        "host cores by OpenMP; 256- and 1024-row samples "
+                        f"({tp:.2f} s, {tq:.2f} s) extrapolated linearly"}}
 
 
 def reference_arm(args):
     rank, world, _ = env_dist()
     if rank != 0:
         return 0
-    from oracle import oracle as orc
-    threads = os.cpu_count() or 1
-    # size one sample at ~3 s so K+W samples fit in a few minutes
-    tp = cpu_step_sample(128, threads)
-    rows = int(min(GLOBAL_BATCH, max(128, 128 * 3.0 / max(tp, 1e-3))))
-    rows = max(128, (rows // 128) * 128)
-    for _ in range(args.warmup):
-        cpu_step_sample(rows, threads)
-    times = [cpu_step_sample(rows, threads) for _ in range(args.steps)]
-    step_s = statistics.mean(times) * GLOBAL_BATCH / rows
+    params = _c5_params()
+    rows_small, rows = 16, 64
+    with _Pinned() as pin:
+        cpu_step_sample(8, 1, params)
+        t_small = statistics.median(cpu_step_sample(rows_small, 1, params) for _ in range(3))
+        for _ in range(args.warmup):
+            cpu_step_sample(rows, 1, params)
+        times = [cpu_step_sample(rows, 1, params) for _ in range(args.steps)]
+        core = pin.core
+    step_s = _extrapolate(t_small, statistics.mean(times), rows_small, rows)
     value = 1.0 / step_s
-    sample = (f"oracle port of the reference CPU arithmetic, {threads} threads; each step is "
-              f"{rows} of {GLOBAL_BATCH} batch rows of a config-5 step scaled x{GLOBAL_BATCH / rows:.0f}")
+    sample = (f"oracle port of the reference CPU arithmetic on 1 pinned host core ({core}; the "
+              f"reference is single-threaded); each timed step is {rows} of {GLOBAL_BATCH} batch "
+              f"rows of a config-5 step, extrapolated linearly in the rows to the full batch "
+              f"(fixed part from {rows_small}-row samples, per-row part x{GLOBAL_BATCH / rows:.2f})")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded uniform inputs, one-hot labels)",
             "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "dims": list(DIMS),
-                       "parallelism": "none (CPU)"},
-            "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "port",
+                       "parallelism": "none (CPU, 1 core)"},
+            "cpu_baseline": {"value": value, "unit": "steps/s", "cores": 1, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
@@ -133,6 +182,35 @@ def reference_arm(args):
                               "restates its arithmetic in C"}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def measure_tf32_tflops():
+    """Dense TF32 tensor throughput of this GPU: torch fp32 matmul 8192^3 with
+    TF32 allowed (cuBLAS), best of 10, CUDA events."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        n = 8192
+        g = torch.Generator(device="cuda").manual_seed(0)
+        a = torch.randn((n, n), device="cuda", generator=g)
+        b = torch.randn((n, n), device="cuda", generator=g)
+        c = torch.empty((n, n), device="cuda")
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b, c
+        torch.cuda.empty_cache()
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 # ---------------------------------------------------------------------------
@@ -276,24 +354,34 @@ def our_arm(args):
     last_loss = float(lossp.item())
 
     peaks, peak_src = load_peaks()
+    region_s = ms * args.steps * 1e-3
+    tf32_measured = measure_tf32_tflops() if rank == 0 else None
     gemm_ms = sum(g[0] for g in gemms)
     gemm_flops = sum(g[1] for g in gemms)
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
-    tf32_peak = peaks["bf16_tflops_sustained"] / 2.0
+    peak_key = "bf16_tflops" if region_s < SUSTAINED_AFTER_S else "bf16_tflops_sustained"
+    tf32_peak = peaks[peak_key] / 2.0
     peak_3x = tf32_peak / 3.0
-    tpf = gemm_traffic_per_flop()
     per_launch_flops = gemm_flops / len(gemms) if gemms else 0
     roofline = {
         "bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s",
         "frac": (achieved / peak_3x) if achieved else None,
-        "traffic": (tpf * per_launch_flops) if tpf else None,
+        "traffic": GEMM_TRAFFIC_BYTES_PER_FLOP * per_launch_flops if per_launch_flops else None,
         "kernel": "k_gemm3x (3xTF32 tcgen05, persistent, 128x256 tiles)",
         "achieved_basis": (f"2*M*N*K algorithmic flops / CUDA-event duration, averaged over the "
                            f"{len(gemms)} GEMM launches of the last timed step ({per_launch_flops:.3e} "
                            f"flop each)"),
-        "peak_basis": (f"{peak_src} bf16_tflops_sustained {peaks['bf16_tflops_sustained']} / 2 "
-                       f"(dense TF32 = half the bf16 rate) / 3 (3xTF32 issues three MMAs per product)"),
+        "peak_basis": (f"{peak_src} {peak_key} {peaks[peak_key]} / 2 (dense TF32 = half the bf16 "
+                       f"rate) / 3 (3xTF32 issues three MMAs per product); {peak_key} because the "
+                       f"timed region lasts {region_s:.3f} s (burst below {SUSTAINED_AFTER_S} s)"),
+        "traffic_basis": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the config-5 forward "
+                          "GEMM launch per algorithmic flop (5.42e-3 B/flop) x the flops of one launch"),
         "frac_of_tf32_issue": ((3 * achieved) / tf32_peak) if achieved else None,
+        "tf32_tflops_measured": tf32_measured,
+        "frac_vs_measured_tf32": ((3 * achieved) / tf32_measured) if achieved and tf32_measured
+        else None,
+        "tf32_basis": "torch fp32 matmul 8192^3 with allow_tf32 (cuBLAS), best of 10, measured in "
+                      "this run; frac_vs_measured_tf32 = 3 x achieved / it (three MMAs per product)",
     }
     # Parameters must stay identical across ranks (config 5): every rank hashes
     # its weights and biases after the last step; the digests are compared.
@@ -339,10 +427,34 @@ def our_arm(args):
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
+        if world == 1 and not args.no_per_config:
+            line["per_config"] = per_config(peaks, peak_src)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         print(json.dumps(line), flush=True)
     return 0
+
+
+PER_CONFIG = (("c1", 200, 5), ("c2", 20, 3), ("c3", 10, 3), ("c4", 20, 3), ("c1front", 100, 5),
+              ("c5front", 10, 3))
+
+
+def per_config(peaks, src):
+    """Configs 1-4 and the lazy-Tensor front end (configs 1 and 5 through
+    Linear / cross_entropy / backward / Sgd::step) at one GPU, each with its
+    own roofline (and e2e for the training steps): one object per config.
+    A config that fails reports its error instead of a value."""
+    out = {}
+    for name, iters, warm in PER_CONFIG:
+        t0 = time.perf_counter()
+        try:
+            r = run_config(name, iters, warm, peaks, src)
+            r.update({"steps": iters, "warmup": warm})
+        except Exception as e:  # one failing leg must not lose the headline line
+            r = {"error": repr(e)[:500]}
+        r["wall_s"] = round(time.perf_counter() - t0, 2)
+        out[name] = r
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -406,6 +518,15 @@ def _graph_time(fn, iters):
     return ms
 
 
+def _step_roofline(flops, ms, peaks, src, bound):
+    """Whole-step algorithmic flop rate against the 3xTF32 tensor peak (burst)."""
+    tf = flops / (ms * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"] / 2 / 3
+    return {"bound": bound, "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+            "traffic": None, "kernel": "whole step (all launches)",
+            "peak_basis": f"{src} bf16_tflops (burst) / 2 (TF32) / 3 (3 MMAs per product)"}
+
+
 def _hbm_roofline(nbytes, ms, peaks, src, kernel):
     gbs = nbytes / (ms * 1e-3) / 1e9
     return {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -414,19 +535,28 @@ def _hbm_roofline(nbytes, ms, peaks, src, kernel):
 
 
 def config_bench(args):
+    peaks, src = load_peaks()
+    iters, warm = args.steps, max(args.warmup, 3)
+    line = run_config(args.config, iters, warm, peaks, src)
+    line.update({"n_gpus": 1, "steps": iters, "warmup": warm, "dtype": "f32", "data": "synthetic"})
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_config(config, iters, warm, peaks, src):
+    """One JSON object for configuration `config` (c1-c4, c5gemm, c1front,
+    c5front) on cuda:0."""
     import torch
 
     from ferrograd_b200 import CudaDevice, MlpTrainer, data, kernels, mlp_init
     from ferrograd_b200._lib import REDUCE_MAX, REDUCE_SUM
 
-    peaks, src = load_peaks()
-    iters, warm = args.steps, max(args.warmup, 3)
     flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MiB > L2
 
     def flush():
         flush_buf.zero_()
 
-    if args.config == "c1":
+    if config == "c1":
         dims, B = (784, 128, 10), 256
         x, t = data.mlp_batch(B, dims[0], dims[-1], 1, 2)
         tr = MlpTrainer(CudaDevice(0), dims, B, 0.01, *mlp_init(dims), use_graph=True)
@@ -452,8 +582,9 @@ def config_bench(args):
                 "unit": "steps/s", "ms_per_step": ms, "launches_per_step": tr.launches_per_step,
                 "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s",
                         "h2d_bytes_per_step": int(x.nbytes + t.nbytes), "d2h_bytes_per_step": 4},
-                "flop_per_step": flops, "bound": "latency (launch-bound; CUDA graph replay)"}
-    elif args.config == "c2":
+                "flop_per_step": flops, "bound": "latency (launch-bound; CUDA graph replay)",
+                "roofline": _step_roofline(flops, ms, peaks, src, "latency")}
+    elif config == "c2":
         n = data.C2_N
         g = torch.Generator(device="cuda").manual_seed(3)
         a, b, c = (torch.randn(n, device="cuda", generator=g) for _ in range(3))
@@ -492,7 +623,7 @@ def config_bench(args):
                            "timing": "elementwise: back-to-back launches between CUDA events; "
                                      "reductions (~12 us each): a CUDA graph of back-to-back "
                                      "launches, so the host call rate does not bound them"}}
-    elif args.config == "c3":
+    elif config == "c3":
         nn_ = data.C3_N
         g = torch.Generator(device="cuda").manual_seed(8)
         A = (torch.rand((nn_, nn_), device="cuda", generator=g) * 2 - 1) / 64
@@ -527,7 +658,7 @@ def config_bench(args):
                 "contractions": res,
                 "config": {"workload": "config3", "M": nn_, "N": nn_, "K": nn_,
                            "l2": "operands + residuals 256 MiB > L2"}}
-    elif args.config == "c5gemm":
+    elif config == "c5gemm":
         # the three GEMM shapes of the config-5 step at one GPU, with the step's epilogues
         M, N = GLOBAL_BATCH, 4096
         g = torch.Generator(device="cuda").manual_seed(13)
@@ -564,7 +695,7 @@ def config_bench(args):
                              "frac": avg / peak, "traffic": None, "kernel": "k_gemm3x",
                              "peak_basis": f"{src} bf16_tflops (burst) / 2 (TF32) / 3 (3 MMAs)"},
                 "contractions": res, "config": {"workload": "config5 GEMM shapes"}}
-    elif args.config == "c4":
+    elif config == "c4":
         Bx, C = data.C4
         g = torch.Generator(device="cuda").manual_seed(11)
         x = torch.randn((Bx, C), device="cuda", generator=g) * 2
@@ -580,16 +711,15 @@ def config_bench(args):
                 "value": r["achieved"], "unit": "GB/s", "roofline": r,
                 "config": {"workload": "config4", "shape": [Bx, C],
                            "l2": "logits + targets + dlogits 786 MB > L2"}}
-    elif args.config in ("c1front", "c5front"):
-        line = front_bench(args, iters, warm, peaks, src)
+    elif config in ("c1front", "c5front"):
+        line = front_bench(config, iters, warm, peaks, src)
     else:
-        raise SystemExit(f"unknown config {args.config}")
-    line.update({"n_gpus": 1, "steps": iters, "warmup": warm, "dtype": "f32", "data": "synthetic"})
-    print(json.dumps(line), flush=True)
-    return 0
+        raise SystemExit(f"unknown config {config}")
+    del flush_buf
+    return line
 
 
-def front_bench(args, iters, warm, peaks, src):
+def front_bench(config, iters, warm, peaks, src):
     """The training step through the lazy-Tensor front end (the reference's
     public API: Linear / relu / cross_entropy / backward / Sgd::step /
     loss.to_vec(), examples/mnist.rs:90-97), every kernel scheduled, routed
@@ -599,7 +729,7 @@ def front_bench(args, iters, warm, peaks, src):
     from ferrograd_b200 import data
     from ferrograd_b200 import front as F
 
-    if args.config == "c1front":
+    if config == "c1front":
         dims, B = (784, 128, 10), 256
     else:
         dims, B = (4096, 4096, 4096, 10), 8192
@@ -628,13 +758,18 @@ def front_bench(args, iters, warm, peaks, src):
     for _ in range(iters):
         F.train_step(model, opt, F.tensor(x), F.tensor(t))
     e2e_ms = (time.perf_counter() - t0) / iters * 1e3
+    nl = len(dims) - 1
+    flops = sum(2 * B * dims[l] * dims[l + 1] * (3 if l > 0 else 2) for l in range(nl))
     return {"metric": f"config{'1' if dims[0] == 784 else '5'} MLP train steps/s through the "
                       "lazy-Tensor front end", "value": 1e3 / wall_ms, "unit": "steps/s",
+            "roofline": _step_roofline(flops, dev_ms, peaks, src,
+                                       "latency" if config == "c1front" else "tensor"),
+            "flop_per_step": flops,
             "ms_per_step": wall_ms, "device_ms_per_step": dev_ms, "loss": loss,
             "per_step": st,
             "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s",
                     "h2d_bytes_per_step": int(x.nbytes + t.nbytes), "d2h_bytes_per_step": 4},
-            "config": {"workload": args.config, "dims": list(dims), "batch": B,
+            "config": {"workload": config, "dims": list(dims), "batch": B,
                        "timing": "wall clock per step (loss.to_vec() synchronises each step); "
                                  "device time from CUDA events on the front end's stream"}}
 
@@ -646,6 +781,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip the configs 1-4 / front-end objects of the N=1 headline line")
     ap.add_argument("--dp", choices=["nccl", "peer"], default="nccl",
                     help="gradient exchange of the data-parallel step (N > 1)")
     ap.add_argument("--dp-chunks", type=int, default=4,

@@ -99,6 +99,10 @@ SIGNATURES = [
     ("fg_mlp_peer_disconnect", _i, [_vp]),
     ("fg_peer_layout", _i, [_i, ctypes.POINTER(_i), _i, _i, ctypes.POINTER(_sz), ctypes.POINTER(_sz),
                             ctypes.POINTER(_sz), _i, ctypes.POINTER(_i)]),
+    ("fg_peer_layout_offsets", _i, [_i, ctypes.POINTER(_i), _i, _i, ctypes.POINTER(_sz),
+                                    ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
+    ("fg_peer_reduce_sgd_local", _i, [_vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _f, ctypes.c_longlong,
+                                      _vp, ctypes.c_uint, _i, _vp]),
     ("fg_comm_unique_id", _i, [ctypes.c_char_p]),
     ("fg_comm_init", _i, [_i, _i, ctypes.c_char_p, _i, _pp]),
     ("fg_comm_destroy", _i, [_vp]),
@@ -106,6 +110,7 @@ SIGNATURES = [
     ("fg_allreduce_mean_f32", _i, [_vp, _vp, _sz, _vp]),
     ("fg_check_device_error", _i, []),
     ("fg_kernel_launches", ctypes.c_uint64, []),
+    ("fg_kernel_arch", _i, [ctypes.POINTER(_i), ctypes.POINTER(_i)]),
 ]
 
 _lib = None

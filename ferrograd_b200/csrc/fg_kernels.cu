@@ -931,7 +931,11 @@ std::mutex g_noalloc_mu;
 NoallocDevice g_noalloc[64];
 
 // Once per device, with that device current: resolve the array's device
-// address and the SM count.  Neither call allocates.
+// address and the SM count.  Neither call allocates by itself, but under
+// lazy module loading the symbol lookup (like the first launch of any kernel
+// of this library) loads the library's device code on this device, and that
+// allocates the array and the code; callers warm up once per device before
+// they reserve their memory budget.
 int noalloc_setup(NoallocDevice **out) {
   int dev = 0;
   FG_CUDA_TRY(cudaGetDevice(&dev));
@@ -1029,6 +1033,15 @@ int fg_sgd(float *d_p, const float *d_g, size_t n, float lr, float *d_p_lo, void
 int fg_split_lo(const float *d_x, float *d_lo, size_t n, void *stream) {
   FG_REQUIRE(n == 0 || (d_x && d_lo), "fg_split_lo: null pointer");
   return fg::launch_split_lo(d_x, d_lo, n, (cudaStream_t)stream);
+}
+
+int fg_kernel_arch(int *binary_version, int *ptx_version) {
+  FG_REQUIRE(binary_version, "fg_kernel_arch: null pointer");
+  cudaFuncAttributes a;
+  FG_CUDA_TRY(cudaFuncGetAttributes(&a, fg::k_split_lo));
+  *binary_version = a.binaryVersion;
+  if (ptx_version) *ptx_version = a.ptxVersion;
+  return FG_OK;
 }
 
 }  // extern "C"

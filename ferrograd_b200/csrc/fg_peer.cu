@@ -17,9 +17,6 @@
 namespace fg {
 
 constexpr unsigned kErrPeer = 4u << 16;
-// Waits give up after this many nanoseconds of the global timer: long enough
-// for ranks whose hosts enqueue the same step some time apart.
-constexpr unsigned long long kPeerWaitNs = 10ull * 1000 * 1000 * 1000;
 
 namespace {
 
@@ -52,12 +49,12 @@ __device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v) 
 
 // Bounded wait until flags[j] == val for all j < n, j != skip.
 __device__ bool wait_flags(const unsigned int *flags, int n, int skip, unsigned int val,
-                           unsigned int *err, unsigned int code) {
+                           unsigned int *err, unsigned int code, unsigned long long wait_ns) {
   const unsigned long long t0 = global_ns();
   for (int j = 0; j < n; j++) {
     if (j == skip) continue;
     while (ld_acquire_sys(flags + j) != val) {
-      if (global_ns() - t0 > kPeerWaitNs) {
+      if (global_ns() - t0 > wait_ns) {
         if (err) atomicOr(err, kErrPeer | code);
         return false;
       }
@@ -87,12 +84,16 @@ __global__ void k_peer_signal(PeerFlagPtrs ptrs, unsigned int val) {
 }
 
 // Runs after a one-block k_peer_wait on its stream has seen every sender's
-// flag, so its blocks never sit on SMs waiting.
+// flag, so its blocks never sit on SMs waiting.  If a wait of the exchange
+// gave up (the error word carries kErrPeer), the staged contributions may be
+// stale: nothing is written, so no update built from them reaches the next
+// step's parameters before the host reads the error.
 __global__ void __launch_bounds__(256)
     k_peer_reduce_sgd(float *__restrict__ grad, const float *__restrict__ stage,
                       const float *__restrict__ p_cur, float *__restrict__ p_next,
                       float *__restrict__ lo_next, size_t shard, int rank, int nranks, float lr,
-                      long long loss_idx) {
+                      long long loss_idx, const unsigned int *err) {
+  if (err && (*reinterpret_cast<const volatile unsigned int *>(err) & kErrPeer)) return;
   const size_t base = (size_t)rank * shard;
   const size_t n4 = shard / 4;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -135,10 +136,10 @@ __global__ void __launch_bounds__(256) k_peer_lo(const float *__restrict__ p, fl
 }
 
 __global__ void k_peer_wait(const unsigned int *flags, int n_chunks, int nranks, int rank,
-                            unsigned int val, unsigned int *err) {
+                            unsigned int val, unsigned int *err, unsigned long long wait_ns) {
   if (threadIdx.x != 0) return;
   for (int c = 0; c < n_chunks; c++)
-    if (!wait_flags(flags + (size_t)c * kMaxPeers, nranks, rank, val, err, 2)) return;
+    if (!wait_flags(flags + (size_t)c * kMaxPeers, nranks, rank, val, err, 2, wait_ns)) return;
 }
 
 // The exchange's kernels run beside the persistent GEMM, whose CTAs need
@@ -243,16 +244,17 @@ int launch_peer_signal(const PeerFlagPtrs &ptrs, unsigned int val, cudaStream_t 
 int launch_peer_reduce_sgd(float *grad, const float *stage, const float *p_cur, float *p_next,
                            float *lo_next, size_t shard, int rank, int nranks, float lr,
                            long long loss_idx, const unsigned int *flags, unsigned int val,
-                           unsigned int *err, int blocks, cudaStream_t st) {
+                           unsigned int *err, int blocks, cudaStream_t st,
+                           unsigned long long wait_ns) {
   if (shard % 4) return set_error(FG_ERR_INVALID, "peer reduce: shard of %zu floats", shard);
-  int rc = launch_peer_wait(flags, 1, nranks, rank, val, err, st);
+  int rc = launch_peer_wait(flags, 1, nranks, rank, val, err, st, wait_ns);
   if (rc || (rc = prefer_max_shared(k_peer_reduce_sgd, 1))) return rc;
   const size_t n4 = shard / 4;
   size_t need = (n4 + 255) / 256;
   int grid = blocks > 0 ? blocks : 64;
   if ((size_t)grid > need) grid = (int)(need ? need : 1);
   k_peer_reduce_sgd<<<grid, 256, 0, st>>>(grad, stage, p_cur, p_next, lo_next, shard, rank, nranks,
-                                          lr, loss_idx);
+                                          lr, loss_idx, err);
   FG_LAUNCH_TRY();
   return FG_OK;
 }
@@ -270,10 +272,11 @@ int launch_peer_lo(const float *p, float *lo, size_t n, int blocks, cudaStream_t
 }
 
 int launch_peer_wait(const unsigned int *flags, int n_chunks, int nranks, int rank,
-                     unsigned int val, unsigned int *err, cudaStream_t st) {
+                     unsigned int val, unsigned int *err, cudaStream_t st,
+                     unsigned long long wait_ns) {
   int rc = prefer_max_shared(k_peer_wait, 2);
   if (rc) return rc;
-  k_peer_wait<<<1, 32, 0, st>>>(flags, n_chunks, nranks, rank, val, err);
+  k_peer_wait<<<1, 32, 0, st>>>(flags, n_chunks, nranks, rank, val, err, wait_ns);
   FG_LAUNCH_TRY();
   return FG_OK;
 }
@@ -294,4 +297,40 @@ extern "C" int fg_peer_layout(int n_layers, const int *dims, int nranks, int chu
   }
   if (n_chunks) *n_chunks = n;
   return FG_OK;
+}
+
+extern "C" int fg_peer_layout_offsets(int n_layers, const int *dims, int nranks, int chunks,
+                                      size_t *w_off, size_t *b_off, size_t *loss_off) {
+  fg::PeerLayout L;
+  int rc = fg::peer_layout(n_layers, dims, nranks, chunks, &L);
+  if (rc) return rc;
+  for (int l = 0; l < n_layers; l++) {
+    if (w_off) w_off[l] = L.w_off[l];
+    if (b_off) b_off[l] = L.b_off[l];
+  }
+  if (loss_off) *loss_off = L.loss_off;
+  return FG_OK;
+}
+
+extern "C" int fg_peer_reduce_sgd_local(float *d_grad, const float *d_stage, const float *d_p_cur,
+                                        float *d_p_next, float *d_lo_next, size_t shard, int rank,
+                                        int nranks, float lr, long long loss_idx,
+                                        const unsigned int *d_flags, unsigned int val, int wait_ms,
+                                        void *stream) {
+  FG_REQUIRE(d_grad && d_stage && d_p_cur && d_p_next && d_lo_next && d_flags,
+             "fg_peer_reduce_sgd_local: null pointer");
+  FG_REQUIRE(nranks >= 2 && nranks <= fg::kMaxPeers && rank >= 0 && rank < nranks,
+             "fg_peer_reduce_sgd_local: rank %d of %d", rank, nranks);
+  FG_REQUIRE(wait_ms > 0 && wait_ms <= 60000, "fg_peer_reduce_sgd_local: wait of %d ms", wait_ms);
+  FG_REQUIRE(loss_idx < (long long)(shard * (size_t)nranks),
+             "fg_peer_reduce_sgd_local: loss index outside the chunk");
+  fg::DevCtx *ctx = fg::ctx_current();
+  if (!ctx) return fg::set_error(FG_ERR_CUDA, "fg_peer_reduce_sgd_local: no CUDA device context");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = fg::launch_peer_reduce_sgd(d_grad, d_stage, d_p_cur, d_p_next, d_lo_next, shard, rank,
+                                      nranks, lr, loss_idx, d_flags, val, ctx->d_err, 64, st,
+                                      (unsigned long long)wait_ms * 1000000ull);
+  if (rc) return rc;
+  FG_CUDA_TRY(cudaStreamSynchronize(st));
+  return fg_check_device_error();
 }

@@ -11,6 +11,10 @@ namespace fg {
 
 constexpr int kMaxPeers = 8;       // ranks of one NVLink domain (one box)
 constexpr int kMaxPeerParts = 8;   // row blocks of a layer's dW
+// The exchange's waits give up after this many nanoseconds of the global
+// timer: long enough for ranks whose hosts enqueue the same step some time
+// apart.
+constexpr unsigned long long kPeerWaitNs = 10ull * 1000 * 1000 * 1000;
 
 // One gradient chunk: [off, off + len) floats of the gradient area, split
 // into nranks shards of len / nranks floats (shard r is owned by rank r).
@@ -58,15 +62,19 @@ int launch_peer_signal(const PeerFlagPtrs &ptrs, unsigned int val, cudaStream_t 
 // (-(g*lr)) and its TF32 residual over the owned shard; the element at
 // loss_idx (chunk-relative, or -1) takes the summed value instead.  All
 // pointers are the chunk's base in their area.
+// If the wait gives up (after wait_ns of the global timer) it sets the error
+// word and the second kernel writes nothing.
 int launch_peer_reduce_sgd(float *grad, const float *stage, const float *p_cur, float *p_next,
                            float *lo_next, size_t shard, int rank, int nranks, float lr,
                            long long loss_idx, const unsigned int *flags, unsigned int val,
-                           unsigned int *err, int blocks, cudaStream_t st);
+                           unsigned int *err, int blocks, cudaStream_t st,
+                           unsigned long long wait_ns = kPeerWaitNs);
 // lo[i] = TF32 residual of p[i] (n a multiple of 4), on at most `blocks` blocks.
 int launch_peer_lo(const float *p, float *lo, size_t n, int blocks, cudaStream_t st);
 // Waits (bounded) until flags[c * kMaxPeers + j] == val for every chunk c <
 // n_chunks and every j < nranks, j != rank.
 int launch_peer_wait(const unsigned int *flags, int n_chunks, int nranks, int rank,
-                     unsigned int val, unsigned int *err, cudaStream_t st);
+                     unsigned int val, unsigned int *err, cudaStream_t st,
+                     unsigned long long wait_ns = kPeerWaitNs);
 
 }  // namespace fg

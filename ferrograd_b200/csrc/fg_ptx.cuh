@@ -72,18 +72,6 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
       : "memory");
 }
 
-// 1-D bulk copy (TMA engine) of `bytes` from global memory into this CTA's
-// shared memory, completing on `bar`.  Both addresses 16-byte aligned, bytes a
-// multiple of 16.
-__device__ __forceinline__ void bulk_load(void *smem_dst, const void *gsrc, uint32_t bytes,
-                                          uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"((uint64_t)gsrc), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Orders this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (TMA) writes to the same shared memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

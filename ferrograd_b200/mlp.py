@@ -227,3 +227,15 @@ def peer_layout(dims: Sequence[int], nranks: int, chunks: int = 4):
     call("fg_peer_layout", len(dims) - 1, d, int(nranks), int(chunks), ctypes.byref(region), off, ln,
          cap, ctypes.byref(n))
     return region.value, [(off[i], ln[i]) for i in range(min(n.value, cap))]
+
+
+def peer_offsets(dims: Sequence[int], nranks: int, chunks: int = 4):
+    """([dW offset], [db offset], loss-slot offset) per layer in the gradient
+    area of the peer-sharded step, in floats (host-only, no GPU)."""
+    nl = len(dims) - 1
+    d = (ctypes.c_int * len(dims))(*[int(x) for x in dims])
+    w = (ctypes.c_size_t * nl)()
+    b = (ctypes.c_size_t * nl)()
+    loss = ctypes.c_size_t()
+    call("fg_peer_layout_offsets", nl, d, int(nranks), int(chunks), w, b, ctypes.byref(loss))
+    return list(w), list(b), loss.value

@@ -140,7 +140,13 @@ int fg_xent_fwd_bwd(const float *d_logits, const float *d_targets, size_t rows, 
  * loads it, so rows is limited to FG_XENT_NOALLOC_MAX_ROWS; larger inputs
  * return FG_ERR_INVALID.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress) and should come before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race. */
+ * capture.  Under lazy module loading (the CUDA default since 12.2) that
+ * first call, or the first launch of any kernel of this library on the
+ * device, also loads the library's device code, which allocates the array
+ * and the code itself: make one warm-up call per device at start-up, before
+ * reserving the memory budget (or run with CUDA_MODULE_LOADING=EAGER).
+ * Later calls allocate nothing.  All calls share the array: calls that
+ * overlap on the GPU race. */
 #define FG_XENT_NOALLOC_MAX_ROWS 262144
 int fg_xent_fwd_bwd_noalloc(const float *d_logits, const float *d_targets, size_t rows,
                             size_t cols, float *d_loss, float *d_dx, float grad_scale,
@@ -274,6 +280,28 @@ int fg_mlp_peer_disconnect(fg_mlp *mlp);
  * to the total). */
 int fg_peer_layout(int n_layers, const int *dims, int nranks, int chunks, size_t *region_floats,
                    size_t *chunk_off, size_t *chunk_len, int capacity, int *n_chunks);
+/* Host-only, same layout: where each layer's dW (w_off[l]) and db (b_off[l])
+ * start in the gradient area (floats; n_layers entries each), and the loss
+ * slot (*loss_off, inside layer 0's bucket, averaged with it). */
+int fg_peer_layout_offsets(int n_layers, const int *dims, int nranks, int chunks, size_t *w_off,
+                           size_t *b_off, size_t *loss_off);
+/* The owner's pass of the sharded exchange for one chunk, run on this GPU
+ * alone with every rank's contribution already in place (a test of the
+ * exchange's kernels without a second GPU).  d_grad, d_stage, d_p_cur,
+ * d_p_next and d_lo_next point at the chunk's start (nranks * shard floats
+ * each): this rank's contribution is d_grad[rank*shard ..), sender j's is
+ * d_stage[j*shard ..).  A one-block kernel waits until d_flags[j] == val for
+ * every j != rank (d_flags: kMaxPeers = 8 words), at most wait_ms
+ * milliseconds; then the owned shard of d_grad receives the sum of the
+ * nranks contributions in rank order, d_p_next = d_p_cur + (-(g*lr))
+ * (src/optim.rs:60-71) and d_lo_next its TF32 residual, except that the
+ * element at loss_idx (chunk-relative, or -1) takes the summed value.  If
+ * the wait gives up, nothing is written and the call returns FG_ERR_DEVICE
+ * (the device error word).  Synchronous. */
+int fg_peer_reduce_sgd_local(float *d_grad, const float *d_stage, const float *d_p_cur,
+                             float *d_p_next, float *d_lo_next, size_t shard, int rank, int nranks,
+                             float lr, long long loss_idx, const unsigned int *d_flags,
+                             unsigned int val, int wait_ms, void *stream);
 
 /* ---- Data-parallel communicator (no reference counterpart: the reference
  * is single-device, src/device.rs:37-41) ----------------------------------- */
@@ -294,6 +322,10 @@ int fg_allreduce_mean_f32(fg_comm *comm, float *d_buf, size_t count, void *strea
 int fg_check_device_error(void);
 /* Total launches of this library's kernels in this process. */
 uint64_t fg_kernel_launches(void);
+/* Architecture the current device runs this library's kernels as:
+ * cudaFuncGetAttributes' binaryVersion (100 for sm_100a) and ptxVersion (0
+ * when no PTX is embedded).  Needs a GPU. */
+int fg_kernel_arch(int *binary_version, int *ptx_version);
 
 #ifdef __cplusplus
 }

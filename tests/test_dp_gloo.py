@@ -131,6 +131,7 @@ def _peer_worker(rank, world, port, q):
     try:
         import torch
         from ferrograd_b200 import data, dp, peer_layout
+        from ferrograd_b200.mlp import peer_offsets
         from oracle import oracle as orc
         dist = _init(rank, world, port)
         dims, B, lr, chunks = (48, 64, 32, 10), 24, 0.05, 2
@@ -138,17 +139,9 @@ def _peer_worker(rank, world, port, q):
         rng = orc.InitRng()
         ws, bs = map(list, zip(*[rng.linear(dims[i], dims[i + 1]) for i in range(len(dims) - 1)]))
         _, ch = peer_layout(dims, world, chunks)
-        unit = 64 * world
-        pad = lambda n, u: (n + u - 1) // u * u  # noqa: E731
-        w_off, b_off, off = [], [], 0
-        for l in range(len(dims) - 1):
-            o, i = dims[l + 1], dims[l]
-            w_off.append(off)
-            b_off.append(off + pad(o * i, 64))
-            raw = pad(o * i, 64) + pad(o, 64) + (64 if l == 0 else 0)
-            off += pad(raw, unit)
-        loss_off = b_off[0] + pad(dims[1], 64)
-        G = off
+        # where each layer's dW / db and the loss slot sit, from the product
+        w_off, b_off, loss_off = peer_offsets(dims, world, chunks)
+        G = max(o + n for o, n in ch)
         # this rank's local gradients, pre-scaled by 1/world like the step's
         lo, hi = dp.shard_rows(B, rank, world)
         loss, _, _, dW, db, _ = orc.mlp_step(ws, bs, x[lo:hi], t[lo:hi], lr)

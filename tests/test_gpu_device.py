@@ -136,3 +136,45 @@ def test_program_cache(dev):
     assert read_f32(dev, out) == [7.0] * 4
     dev.clear_for_tests()
     assert dev.cached_program("fill-key") is None
+
+
+def test_event_elapsed_times_of_a_known_kernel_are_positive_and_ordered(dev):
+    """fg_event_*: the device timing DEBUG >= 2 reports per kernel
+    (src/tensor.rs:1017-1028).  Three events bracket two launches of a kernel
+    that spins for a fixed number of global-timer nanoseconds, so the elapsed
+    times must be positive, ordered (start->mid <= start->end) and at least
+    the spin."""
+    from ferrograd_b200.device import Event
+    src = r'''extern "C" __global__ void spin(float* out, int ns) {
+        unsigned long long t0, t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        do { asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); } while (t - t0 < (unsigned long long)ns);
+        out[0] = (float)(t - t0); }'''
+    prog = _compile(dev, src, "spin", 2, n=1)
+    out = dev.allocate(F32, 1)
+    args = [KernelArg.buffer(out), KernelArg.i32(2_000_000)]  # 2 ms
+    dev.execute(prog, args)  # first launch loads the module
+    dev.synchronize()
+    e0, e1, e2 = Event(dev), Event(dev), Event(dev)
+    e0.record()
+    dev.execute(prog, args)
+    e1.record()
+    dev.execute(prog, args)
+    e2.record()
+    t01 = Event.elapsed_ms(e0, e1)
+    t02 = Event.elapsed_ms(e0, e2)
+    t12 = Event.elapsed_ms(e1, e2)
+    assert 2.0 <= t01 < 1000.0 and 2.0 <= t12 < 1000.0
+    assert t01 <= t02 and t12 <= t02
+    assert abs(t02 - (t01 + t12)) <= 0.05 * t02
+
+
+def test_library_kernels_run_as_sm100a():
+    """The kernels of libferro_cuda.so run from an sm_100a binary on this
+    device (cudaFuncGetAttributes: binaryVersion 100), not from PTX JIT."""
+    import ctypes
+
+    from ferrograd_b200 import _lib
+    bv, pv = ctypes.c_int(), ctypes.c_int()
+    _lib.call("fg_kernel_arch", ctypes.byref(bv), ctypes.byref(pv))
+    assert bv.value == 100, bv.value

@@ -7,6 +7,10 @@ escape the caller's accounting.  This entry point keeps its per-row scratch in
 a static array inside the library (1 MiB per GPU, FG_XENT_NOALLOC_MAX_ROWS
 rows) and must give the same result as the allocating entry point.
 
+Its results are also held to the oracle (the C restatement of the
+reference's cross_entropy arithmetic), and the test checks that the second of
+two calls leaves the device's free memory exactly as the first left it.
+
 The file is named so pytest collects it last; it passes on its own in a
 fresh process as well as after the other tests.
 """
@@ -47,6 +51,39 @@ def test_noalloc_matches_allocating_entry_point_twice(shape):
         # gradient 1e-4 norm-relative (the two paths run the same kernels)
         assert abs(loss.item() - ref_loss.item()) <= 1e-5 * abs(ref_loss.item())
         assert (torch.max(torch.abs(dx - ref_dx)) / torch.max(torch.abs(ref_dx))).item() <= 1e-4
+
+
+@pytest.mark.parametrize("shape", [(777, 10), (2048, 1000)])
+def test_noalloc_matches_oracle_and_allocates_nothing(oracle, shape):
+    """Two calls in a row against the oracle: loss within 1e-5 relative, dx
+    within 1e-4 norm-relative; (777, 10) runs the generic kernel (10 classes
+    are not a multiple of 4), (2048, 1000) the vectorised one.  Every buffer
+    is made before the first call, so cudaMemGetInfo's free bytes after the
+    second call must equal those after the first."""
+    import numpy as np
+    rows, cols = shape
+    rng = np.random.default_rng(12)
+    xs = [(rng.standard_normal((rows, cols), dtype=np.float32) * 2) for _ in range(2)]
+    ts = [np.eye(cols, dtype=np.float32)[rng.integers(0, cols, rows)] for _ in range(2)]
+    dev = [(torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda()) for x, t in zip(xs, ts)]
+    loss = torch.zeros(1, device="cuda")
+    dx = torch.empty((rows, cols), device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    free = []
+    for call, (x, t) in enumerate(dev):
+        dx.fill_(float("nan"))
+        torch.cuda.synchronize()
+        rc = _lib.lib().fg_xent_fwd_bwd_noalloc(x.data_ptr(), t.data_ptr(), rows, cols,
+                                                loss.data_ptr(), dx.data_ptr(), ctypes.c_float(1.0),
+                                                stream)
+        _lib.check(rc)
+        torch.cuda.synchronize()
+        free.append(torch.cuda.mem_get_info()[0])
+        oloss, odx = oracle.xent_fwd_bwd(xs[call], ts[call])
+        assert abs(loss.item() - oloss) <= 1e-5 * abs(oloss), (call, loss.item(), oloss)
+        got = dx.cpu().numpy().astype(np.float64)
+        assert np.max(np.abs(got - odx)) / np.max(np.abs(odx)) <= 1e-4, call
+    assert free[1] == free[0]
 
 
 def test_noalloc_rejects_rows_beyond_the_static_limit():
