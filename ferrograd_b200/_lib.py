@@ -85,6 +85,7 @@ SIGNATURES = [
     ("fg_mlp_input_slots", _i, [_vp, _pp, _pp]),
     ("fg_mlp_step", _i, [_vp, _vp]),
     ("fg_mlp_step_host", _i, [_vp, _vp, _vp, _vp]),
+    ("fg_mlp_step_host_next", _i, [_vp, _vp, _vp, _vp, _vp, _vp]),
     ("fg_mlp_use_graph", _i, [_vp, _i]),
     ("fg_mlp_get_logits", _i, [_vp, _vp]),
     ("fg_mlp_get_activations", _i, [_vp, _i, _vp]),

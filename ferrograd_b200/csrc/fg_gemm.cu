@@ -167,6 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_n = (p.N + BN - 1) / BN;
   const int nk = (p.K + BK - 1) / BK;
   const bool three = !p.one_pass;
+  // k-blocks per accumulation chain (segmented accumulation, GemmParams)
+  const int seglen = (p.seg_kb > 0 && p.seg_ws) ? p.seg_kb : nk;
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < C::STAGES; s++) {
@@ -273,7 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0, local = 0;
       SegIter segs(p, nk);
       Seg sg;
-      for (; ok && segs.next(sg); local++) {
+      // one accumulation chain per sub-segment of at most seglen k-blocks
+      for (; ok && segs.next(sg);)
+        for (int s0 = sg.k0; ok && s0 < sg.k1; s0 += seglen, local++) {
+        const int s1 = min(s0 + seglen, sg.k1);
         const int acc_buf = local & 1;
         if (local >= 2) {
           ok = mbar_wait(&tmem_empty[acc_buf], ((local >> 1) - 1) & 1, p.err, kErrMma | 2);
@@ -281,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc_buf * BN);
-        for (int kb = sg.k0; kb < sg.k1; kb++, it++) {
+        for (int kb = s0; kb < s1; kb++, it++) {
           const int s = it % C::STAGES;
           ok = mbar_wait(&full[s], (it / C::STAGES) & 1, p.err, kErrMma | 1);
           if (!ok) break;
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < BK / UMMA_K; kk++) {
             const uint64_t da = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_lay);
             const uint64_t db = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_lay);
-            const uint32_t acc = (kb > sg.k0 || kk > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > s0 || kk > 0) ? 1u : 0u;
             if (three) {
               const uint64_t dalo = smem_desc(salo + kk * a_kstep, a_lbo, a_sbo, a_lay);
               const uint64_t dblo = smem_desc(sblo + kk * b_kstep, b_lbo, b_sbo, b_lay);
@@ -325,12 +330,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool dead = false;
     SegIter segs(p, nk);
     Seg sg;
-    for (; segs.next(sg); local++) {
+    // this CTA's running partial of segmented accumulation: [BN][BM]
+    // floats, column-major so a warp's 32 rows of one column are one line
+    float *run = p.seg_ws ? p.seg_ws + (size_t)blockIdx.x * (BM * BN) + trow : nullptr;
+    while (segs.next(sg)) {
       int mb, nb;
       tile_coords(sg.tile, num_m, num_n, mb, nb);
       const int m0 = mb * BM, n0 = nb * BN;
-      const int acc_buf = local & 1;
       const int row = m0 + 32 * q + lane;
+      const int nsub = (sg.k1 - sg.k0 + seglen - 1) / seglen;
       // Stream-K roles: a segment without the tile's last k-block leaves a
       // partial (it is the first segment its CTA walks); one with the last
       // k-block but not the first finishes the tile, adding the partials of
@@ -339,7 +347,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool partial_out = sg.k1 < nk;
       const bool finisher = sg.k1 == nk && sg.k0 > 0;
       int c_lo = 0;  // contributors c_lo .. blockIdx.x-1, added from the top down
-      if (finisher) {
+      for (int sub = 0; sub < nsub; sub++, local++) {
+      const int acc_buf = local & 1;
+      const bool last = sub == nsub - 1;
+      if (last && finisher) {
         const long long tile_start = (long long)(sg.tile - p.dp_tiles) * nk;
         c_lo = blockIdx.x - 1;
         while (c_lo > 0 && sk_begin(p, c_lo) > tile_start) c_lo--;
@@ -361,19 +372,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc_buf * BN + c0),
                            r);
         tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+        // Fold this chain's sum into the running partial (round to
+        // nearest).  All 32 loads are issued before the first add: the
+        // cache-hinted loads and stores keep their program order, so a
+        // load-add-store per column would pay one L2 round trip per column.
+        if (sub > 0) {
+          float w[32];
+#pragma unroll
+          for (int j = 0; j < 32; j++) w[j] = __ldcg(run + (size_t)(c0 + j) * BM);
+#pragma unroll
+          for (int j = 0; j < 32; j++) v[j] = __fadd_rn(w[j], v[j]);
+        }
+        if (!last) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) __stcg(run + (size_t)(c0 + j) * BM, v[j]);
+          continue;
+        }
         if (partial_out) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4)
             __stcg(reinterpret_cast<float4 *>(my_ws + c0 + j),
-                   make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                               __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])));
+                   make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
           continue;
         }
         if (row >= p.M || n0 + c0 >= p.N) continue;
-        float v[32];
         const int col0 = n0 + c0;
-#pragma unroll
-        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
         if (finisher) {
           for (int c = (int)blockIdx.x - 1; c >= c_lo; c--) {
             const float *w = p.sk_ws + (size_t)c * (BM * BN) + (size_t)trow * BN + c0;
@@ -427,6 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // every TMEM load of this buffer has completed (tcgen05.wait::ld above)
       tc_fence_before();
       if (!dead) mbar_arrive(&tmem_empty[acc_buf]);
+      }
       if (partial_out) {
         // publish: every thread's stores, then one release of the flag
         __threadfence();
@@ -558,15 +585,29 @@ static int plan_stream_k(GemmParams &p, int ntiles, int nk, int cap, float *ws,
   return (int)g;
 }
 
+// Workspace layout: [ctas][BM * 256] stream-K partials, [ctas][BM * 256]
+// segment running partials, then [ctas] stream-K flags.
 size_t stream_k_ws_bytes(int ctas) {
-  return (size_t)ctas * BM * 256 * sizeof(float) + (size_t)ctas * sizeof(unsigned int) + 256;
+  return 2 * (size_t)ctas * BM * 256 * sizeof(float) + (size_t)ctas * sizeof(unsigned int) + 256;
 }
 
 void stream_k_attach(GemmPlan *pl, void *ws, int ctas) {
+  const size_t part = (size_t)ctas * BM * 256 * sizeof(float);
   pl->sk_ws = static_cast<float *>(ws);
-  pl->sk_flags = ws ? reinterpret_cast<unsigned int *>(static_cast<char *>(ws) +
-                                                        (size_t)ctas * BM * 256 * sizeof(float))
-                    : nullptr;
+  pl->seg_ws = ws ? reinterpret_cast<float *>(static_cast<char *>(ws) + part) : nullptr;
+  pl->sk_flags =
+      ws ? reinterpret_cast<unsigned int *>(static_cast<char *>(ws) + 2 * part) : nullptr;
+}
+
+// k-blocks per tensor-core accumulation chain (FG_GEMM_SEG_KB, default 32,
+// i.e. 1024 products of each output; 0 = one chain per tile).
+static int seg_kb_setting() {
+  static const int v = [] {
+    const char *e = getenv("FG_GEMM_SEG_KB");
+    const int x = e && *e ? atoi(e) : 32;
+    return x < 0 ? 0 : x;
+  }();
+  return v;
 }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -589,6 +630,8 @@ static int launch_t(const GemmPlan &pl, cudaStream_t st) {
   if (pl.max_ctas > 0 && pl.max_ctas < cap) cap = pl.max_ctas;
   GemmParams p = pl.p;
   const int grid = plan_stream_k(p, ntiles, nk, cap, pl.sk_ws, pl.sk_flags);
+  p.seg_ws = pl.seg_ws;
+  p.seg_kb = seg_kb_setting();
   kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(pl.a, pl.alo, pl.b, pl.blo, p);
   FG_LAUNCH_TRY();
   return FG_OK;
@@ -674,6 +717,9 @@ int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, c
   pl->max_ctas = 0;
   pl->sk_ws = nullptr;
   pl->sk_flags = nullptr;
+  pl->seg_ws = nullptr;
+  p.seg_ws = nullptr;
+  p.seg_kb = 0;
   return FG_OK;
 }
 

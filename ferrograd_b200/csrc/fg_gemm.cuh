@@ -28,6 +28,15 @@ struct GemmParams {
   long long sk_units;
   float *sk_ws;             // [grid][BM * BN] partial accumulators
   unsigned int *sk_flags;   // [grid], zero between launches
+  // Segmented accumulation: the tensor cores accumulate at most seg_kb
+  // k-blocks into a fresh TMEM accumulator; the epilogue warps add the
+  // segments' sums with round-to-nearest fp32 adds in a per-CTA running
+  // partial (seg_ws[blockIdx.x], [BN][BM] floats, L2-resident).  The
+  // tensor cores' own fp32 accumulation rounds its additions coarsely, so
+  // its error grows with the length of one accumulation chain; cutting the
+  // chain bounds it.  seg_kb == 0 or no seg_ws: one chain per output tile.
+  int seg_kb;
+  float *seg_ws;
 };
 
 // Everything a launch needs, built once per (shape, pointers) and replayed.
@@ -41,9 +50,11 @@ struct GemmPlan {
   // workspace must be ordered (same stream).
   float *sk_ws;
   unsigned int *sk_flags;
+  float *seg_ws;  // running partials of segmented accumulation (null: off)
 };
 
-// Bytes of stream-K workspace a plan needs for grids of up to `ctas` CTAs.
+// Bytes of stream-K + segment workspace a plan needs for grids of up to
+// `ctas` CTAs.
 size_t stream_k_ws_bytes(int ctas);
 // Lays out a zeroed workspace of stream_k_ws_bytes(ctas) bytes for plans.
 void stream_k_attach(GemmPlan *pl, void *ws, int ctas);

@@ -861,6 +861,35 @@ int launch_split_lo(const float *x, float *lo, size_t n, cudaStream_t st) {
   return FG_OK;
 }
 
+// dst_a <- src_a (na floats) and dst_b <- src_b (nb floats) in one launch on
+// the SMs; every pointer 16-byte aligned, na and nb multiples of 4.  A
+// device-to-device cudaMemcpyAsync may be given to a copy engine that is
+// busy with a long host upload, so the step's own staging copy is a kernel.
+__global__ void __launch_bounds__(256) k_copy2(const float4 *__restrict__ src_a,
+                                               float4 *__restrict__ dst_a, size_t na4,
+                                               const float4 *__restrict__ src_b,
+                                               float4 *__restrict__ dst_b, size_t nb4) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (size_t i = i0; i < na4; i += stride) __stcs(dst_a + i, __ldcs(src_a + i));
+  for (size_t i = i0; i < nb4; i += stride) __stcs(dst_b + i, __ldcs(src_b + i));
+}
+
+int launch_copy2(const float *src_a, float *dst_a, size_t na, const float *src_b, float *dst_b,
+                 size_t nb, cudaStream_t st) {
+  if (na % 4 || nb % 4 || !aligned16(src_a) || !aligned16(dst_a) || (nb && (!aligned16(src_b) ||
+      !aligned16(dst_b))))
+    return set_error(FG_ERR_INVALID, "copy2: sizes must be multiples of 4 floats, 16-byte aligned");
+  const size_t n4 = (na > nb ? na : nb) / 4;
+  if (!n4) return FG_OK;
+  k_copy2<<<grid_for(n4, 256, 16), 256, 0, st>>>(reinterpret_cast<const float4 *>(src_a),
+                                                 reinterpret_cast<float4 *>(dst_a), na / 4,
+                                                 reinterpret_cast<const float4 *>(src_b),
+                                                 reinterpret_cast<float4 *>(dst_b), nb / 4);
+  FG_LAUNCH_TRY();
+  return FG_OK;
+}
+
 }  // namespace fg
 
 extern "C" {

@@ -34,5 +34,7 @@ int launch_xent(const float *x, const float *t, size_t rows, size_t cols, float 
                 float gscale, cudaStream_t st, float *row_scratch, float loss_scale = 1.0f);
 int launch_sgd_multi(const SgdSegments &segs, float lr, cudaStream_t st);
 int launch_split_lo(const float *x, float *lo, size_t n, cudaStream_t st);
+int launch_copy2(const float *src_a, float *dst_a, size_t na, const float *src_b, float *dst_b,
+                 size_t nb, cudaStream_t st);
 
 }  // namespace fg

@@ -348,6 +348,14 @@ struct fg_mlp {
   cudaEvent_t ev_ready = nullptr, ev_red = nullptr, ev_join = nullptr;
   cudaEvent_t ev_rs[fg::kMaxPeers] = {}, ev_ag[fg::kMaxPeers] = {};
   cudaGraphExec_t pgraph[2] = {nullptr, nullptr};
+  // Overlapped uploads (fg_mlp_step_host_next): two device staging slots for
+  // a batch and its targets, filled from host memory on copy_st while a step
+  // runs; staged_x/staged_t are the host pointers slot next_slot holds.
+  float *stage_x[2] = {nullptr, nullptr}, *stage_t[2] = {nullptr, nullptr};
+  cudaStream_t copy_st = nullptr;
+  cudaEvent_t ev_staged[2] = {nullptr, nullptr}, ev_consumed[2] = {nullptr, nullptr};
+  int next_slot = 0;
+  const float *staged_x = nullptr, *staged_t = nullptr;
 };
 
 namespace {
@@ -891,8 +899,10 @@ int fg_mlp_destroy(fg_mlp *m) {
   }
   for (cudaStream_t s2 : {m->red_st, m->sig_rs_st, m->sig_ag_st, m->arr_st})
     if (s2) cudaStreamDestroy(s2);
-  for (cudaEvent_t e : {m->ev_ready, m->ev_red, m->ev_join})
+  for (cudaEvent_t e : {m->ev_ready, m->ev_red, m->ev_join, m->ev_staged[0], m->ev_staged[1],
+                        m->ev_consumed[0], m->ev_consumed[1]})
     if (e) cudaEventDestroy(e);
+  if (m->copy_st) cudaStreamDestroy(m->copy_st);
   for (void *p : m->allocations) cudaFree(p);
   delete m;
   return FG_OK;
@@ -1099,6 +1109,67 @@ int fg_mlp_step_host(fg_mlp *m, const float *h_x, const float *h_targets, float 
   if (rc) return rc;
   if (h_loss) {
     // peer-sharded: the global loss travels with the parameters it produced
+    const float *src = m->region ? m->pP[m->par] + m->pl.loss_off : m->loss;
+    FG_CUDA_TRY(cudaMemcpyAsync(h_loss, src, sizeof(float), cudaMemcpyDeviceToHost, m->st));
+    FG_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return fg_check_device_error();
+  }
+  return FG_OK;
+}
+
+int fg_mlp_step_host_next(fg_mlp *m, const float *h_x, const float *h_targets,
+                          const float *h_x_next, const float *h_targets_next, float *h_loss) {
+  FG_REQUIRE(m && h_x && h_targets, "fg_mlp_step_host_next: null argument");
+  FG_REQUIRE(!h_x_next == !h_targets_next,
+             "fg_mlp_step_host_next: give both next-batch pointers or neither");
+  FG_CUDA_TRY(cudaSetDevice(m->dev->ordinal));
+  const size_t xb = sizeof(float) * (size_t)m->B * m->dims[0];
+  const size_t tb = sizeof(float) * (size_t)m->B * m->dims[m->nl];
+  int rc;
+  if (!m->copy_st) {
+    for (int i = 0; i < 2; i++) {
+      if ((rc = mlp_alloc(m, &m->stage_x[i], (size_t)m->B * m->dims[0]))) return rc;
+      if ((rc = mlp_alloc(m, &m->stage_t[i], (size_t)m->B * m->dims[m->nl]))) return rc;
+      FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_staged[i], cudaEventDisableTiming));
+      FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_consumed[i], cudaEventDisableTiming));
+    }
+    FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->copy_st, cudaStreamNonBlocking));
+  }
+  // This step's batch: staged by the previous call when it named these
+  // buffers as its next batch, else uploaded now.
+  const int cur = m->next_slot;
+  if (m->staged_x != h_x || m->staged_t != h_targets) {
+    FG_CUDA_TRY(cudaStreamWaitEvent(m->copy_st, m->ev_consumed[cur], 0));
+    FG_CUDA_TRY(cudaMemcpyAsync(m->stage_x[cur], h_x, xb, cudaMemcpyHostToDevice, m->copy_st));
+    FG_CUDA_TRY(cudaMemcpyAsync(m->stage_t[cur], h_targets, tb, cudaMemcpyHostToDevice, m->copy_st));
+    FG_CUDA_TRY(cudaEventRecord(m->ev_staged[cur], m->copy_st));
+  }
+  m->staged_x = m->staged_t = nullptr;
+  FG_CUDA_TRY(cudaStreamWaitEvent(m->st, m->ev_staged[cur], 0));
+  if ((size_t)m->B * m->dims[0] % 4 == 0 && (size_t)m->B * m->dims[m->nl] % 4 == 0) {
+    if ((rc = fg::launch_copy2(m->stage_x[cur], m->x, (size_t)m->B * m->dims[0], m->stage_t[cur],
+                               m->t, (size_t)m->B * m->dims[m->nl], m->st)))
+      return rc;
+  } else {
+    FG_CUDA_TRY(cudaMemcpyAsync(m->x, m->stage_x[cur], xb, cudaMemcpyDeviceToDevice, m->st));
+    FG_CUDA_TRY(cudaMemcpyAsync(m->t, m->stage_t[cur], tb, cudaMemcpyDeviceToDevice, m->st));
+  }
+  FG_CUDA_TRY(cudaEventRecord(m->ev_consumed[cur], m->st));
+  // The next batch goes into the other slot on the copy stream while this
+  // step computes (once that slot's previous batch has been moved out).
+  if (h_x_next) {
+    const int nxt = cur ^ 1;
+    FG_CUDA_TRY(cudaStreamWaitEvent(m->copy_st, m->ev_consumed[nxt], 0));
+    FG_CUDA_TRY(cudaMemcpyAsync(m->stage_x[nxt], h_x_next, xb, cudaMemcpyHostToDevice, m->copy_st));
+    FG_CUDA_TRY(cudaMemcpyAsync(m->stage_t[nxt], h_targets_next, tb, cudaMemcpyHostToDevice,
+                                m->copy_st));
+    FG_CUDA_TRY(cudaEventRecord(m->ev_staged[nxt], m->copy_st));
+    m->next_slot = nxt;
+    m->staged_x = h_x_next;
+    m->staged_t = h_targets_next;
+  }
+  if ((rc = fg_mlp_step(m, nullptr))) return rc;
+  if (h_loss) {
     const float *src = m->region ? m->pP[m->par] + m->pl.loss_off : m->loss;
     FG_CUDA_TRY(cudaMemcpyAsync(h_loss, src, sizeof(float), cudaMemcpyDeviceToHost, m->st));
     FG_CUDA_TRY(cudaStreamSynchronize(m->st));

@@ -152,6 +152,27 @@ class MlpTrainer:
         """Step from raw (pinned) host pointers; the loss lands in loss_ptr."""
         call("fg_mlp_step_host", self._h, x_ptr, t_ptr, loss_ptr)
 
+    def step_host_next(self, x: np.ndarray, targets: np.ndarray, x_next: Optional[np.ndarray],
+                       targets_next: Optional[np.ndarray]) -> float:
+        """One step on (x, targets) while (x_next, targets_next) is uploaded
+        for the next call (``fg_mlp_step_host_next``); returns the loss.  The
+        next batch's arrays must stay alive and unchanged until that call."""
+        for a, cols in ((x, self.dims[0]), (targets, self.dims[-1]), (x_next, self.dims[0]),
+                        (targets_next, self.dims[-1])):
+            if a is not None:
+                assert a.shape == (self.batch, cols) and a.dtype == np.float32
+                assert a.flags["C_CONTIGUOUS"]
+        loss = ctypes.c_float()
+        call("fg_mlp_step_host_next", self._h, x.ctypes.data, targets.ctypes.data,
+             None if x_next is None else x_next.ctypes.data,
+             None if targets_next is None else targets_next.ctypes.data, ctypes.byref(loss))
+        return float(loss.value)
+
+    def step_host_next_ptr(self, x_ptr: int, t_ptr: int, xn_ptr: Optional[int],
+                           tn_ptr: Optional[int], loss_ptr: int) -> None:
+        """``step_host_next`` from raw (pinned) host pointers."""
+        call("fg_mlp_step_host_next", self._h, x_ptr, t_ptr, xn_ptr, tn_ptr, loss_ptr)
+
     def step(self, loss_out_ptr: Optional[int] = None) -> None:
         """Step on inputs already in the device input slots (asynchronous)."""
         call("fg_mlp_step", self._h, loss_out_ptr)

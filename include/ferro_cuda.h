@@ -219,6 +219,18 @@ int fg_mlp_step(fg_mlp *mlp, float *d_loss_out);
  * copies the loss out (blocking), the ferrograd call sequence
  * forward/backward/step/loss.to_vec(). */
 int fg_mlp_step_host(fg_mlp *mlp, const float *h_x, const float *h_targets, float *h_loss);
+/* fg_mlp_step_host with the next batch's upload overlapped: runs the step
+ * on (h_x, h_targets) and returns its loss like fg_mlp_step_host, and while
+ * the step computes, the copy engine uploads (h_x_next, h_targets_next) into
+ * a second device staging slot.  A call whose (h_x, h_targets) are the
+ * pointers the previous call named as its next batch uses that upload
+ * instead of copying again; any other pair is uploaded first.  The training
+ * loop of examples/mnist.rs:87-97 passes batch i+1 with batch i.  The next
+ * batch's host buffers must stay unchanged until the following call
+ * returns, and must be pinned (page-locked) for the copy to overlap.  Both
+ * next pointers NULL: no prefetch. */
+int fg_mlp_step_host_next(fg_mlp *mlp, const float *h_x, const float *h_targets,
+                          const float *h_x_next, const float *h_targets_next, float *h_loss);
 /* Capture the device part of fg_mlp_step in a CUDA graph and replay it. */
 int fg_mlp_use_graph(fg_mlp *mlp, int enable);
 /* Pre-update logits of the last step, [batch, dims[n_layers]] (loss.to_vec()

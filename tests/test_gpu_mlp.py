@@ -104,3 +104,25 @@ def test_unsupported_width_is_an_error():
     from ferrograd_b200 import FerroError
     with pytest.raises(FerroError):
         MlpTrainer(CudaDevice(0), (64, 40, 10), 32, 0.01, *mlp_init((64, 40, 10)))
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_overlapped_upload_step_matches_plain_host_step(graph):
+    """fg_mlp_step_host_next (batch i+1 uploaded while step i runs) gives
+    bit-identical losses and parameters to fg_mlp_step_host over four steps
+    that alternate two batches, including a call whose batch was not the
+    staged one and a final call without a next batch."""
+    dims, batch = (512, 256, 256, 10), 256
+    xa, ta = data.mlp_batch(batch, dims[0], dims[-1], 5, 6)
+    xb, tb = data.mlp_batch(batch, dims[0], dims[-1], 7, 8)
+    ws, bs = mlp_init(dims)
+    plain = MlpTrainer(CudaDevice(0), dims, batch, 0.01, ws, bs, use_graph=graph)
+    piped = MlpTrainer(CudaDevice(0), dims, batch, 0.01, ws, bs, use_graph=graph)
+    order = [(xa, ta), (xb, tb), (xa, ta), (xb, tb)]
+    nexts = [(xb, tb), (xb, tb), (xb, tb), (None, None)]  # call 2 finds xa, not the staged xb
+    for (x, t), (xn, tn) in zip(order, nexts):
+        lp = plain.step_host(x, t)
+        lq = piped.step_host_next(x, t, xn, tn)
+        assert lp == lq
+    for a, b in zip(plain.params()[0] + plain.params()[1], piped.params()[0] + piped.params()[1]):
+        assert np.array_equal(a, b)
