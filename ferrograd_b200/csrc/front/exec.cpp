@@ -254,14 +254,9 @@ float *fptr(const BufferP &b, int64_t offset = 0) {
   return static_cast<float *>(b->ptr()) + offset;
 }
 
-// ---- strided views --------------------------------------------------------
-struct View {
-  BufferP buf;
-  int64_t offset = 0;
-  Shape shape;
-  std::vector<int64_t> strides;
-};
+}  // namespace
 
+// ---- strided views --------------------------------------------------------
 // Strides of `nd` over the same memory as (od, os), or nothing when the
 // reshape is not expressible as a strided view.
 std::optional<std::vector<int64_t>> reshape_strides(const Shape &od, const std::vector<int64_t> &os,
@@ -351,6 +346,8 @@ std::optional<View> try_view(const UOp *n) {
       return std::nullopt;
   }
 }
+
+namespace {
 
 // Which axes of a node's value vary (used to classify contraction operands).
 std::vector<bool> deps(const UOp *n) {
@@ -516,6 +513,7 @@ std::string spec_key(const RenderSpec &spec, const ParamSlots &ps,
   k.put(spec.pitch);
   k.put((int64_t)spec.out_dtype);
   k.put(spec.unroll);
+  k.put((int64_t)spec.coop);
   k.put((int64_t)spec.domain.size());
   for (int64_t d : spec.domain) k.put(d);
   k.put((int64_t)spec.value_ctx.size());
@@ -783,7 +781,7 @@ struct HandReduce {
 };
 
 std::optional<HandReduce> match_hand_reduce(const UOp *n) {
-  if (n->op != Op::ReduceAxis || n->dtype != DType::F32) return {};
+  if (n->op != Op::ReduceAxis || (n->dtype != DType::F32 && n->dtype != DType::I32)) return {};
   auto v = try_view(n->src[0].get());
   if (!v || numel(v->shape) < kHandReduceMin) return {};
   // The view must be contiguous row-major.
@@ -827,6 +825,8 @@ std::optional<HandReduce> match_hand_reduce(const UOp *n) {
 
 void run_hand_reduce(const HandReduce &h, const BufferP &out) {
   int op = h.reduce->reduce_op == Op::Add ? FG_REDUCE_SUM : FG_REDUCE_MAX;
+  const int dt = h.reduce->dtype == DType::I32 ? FG_I32 : FG_F32;
+  // i32 and f32 elements are both 4 bytes
   const float *x = fptr(h.v.buf, h.v.offset);
   float *y = fptr(out);
   if (debug_level() >= 1)
@@ -835,10 +835,10 @@ void run_hand_reduce(const HandReduce &h, const BufferP &out) {
             (long long)(h.rows ? h.extent : h.inner));
   ExecTimer timer;
   if (h.rows)
-    check(fg_reduce_rows(FG_F32, op, x, y, (size_t)h.outer, (size_t)h.extent, stream()),
+    check(fg_reduce_rows(dt, op, x, y, (size_t)h.outer, (size_t)h.extent, stream()),
           "reduce_rows");
   else
-    check(fg_reduce_cols(FG_F32, op, x, y, (size_t)h.extent, (size_t)h.inner, stream()),
+    check(fg_reduce_cols(dt, op, x, y, (size_t)h.extent, (size_t)h.inner, stream()),
           "reduce_cols");
   g_stats.hand_reduce++;
 }
@@ -887,6 +887,7 @@ std::string render_item_source(const ScheduleItem &item) {
   } else {
     spec.out_dtype = item.value->dtype;
   }
+  choose_thread_mapping(spec);
   return render_kernel(spec).source;
 }
 
@@ -912,7 +913,7 @@ void run_item(const ScheduleItem &item) {
       if (!c) h = match_hand_reduce(n.get());
       if (!c && !h) continue;
       const bool is_root = !item.store_dest && root_reduce(item.value) == n.get();
-      BufferP out = is_root ? item.output : temp_buffer(DType::F32, numel(n->shape));
+      BufferP out = is_root ? item.output : temp_buffer(n->dtype, numel(n->shape));
       if (c) {
         std::unordered_map<const UOp *, UOpP> memo_a, memo_b;
         UOpP a = repl.empty() ? c->a : substitute_with_map(c->a, repl, memo_a);
@@ -941,6 +942,7 @@ void run_item(const ScheduleItem &item) {
   } else {
     spec.out_dtype = item.value->dtype;
   }
+  choose_thread_mapping(spec);
   launch_spec(spec, item.output);
   if (item.store_dest) {
     // the destination's contents changed: cached residuals and staged

@@ -1,6 +1,7 @@
 // front_internal.h -- declarations shared by the front end's translation units.
 #pragma once
 #include <map>
+#include <optional>
 #include <stdexcept>
 #include <string>
 #include <unordered_map>
@@ -27,6 +28,18 @@ ParamSlots collect_params(const UOpP &root, int slot_offset);
 // The same over an existing toposort of the kernel's root.
 ParamSlots collect_params_from(const std::vector<UOpP> &order, int slot_offset);
 
+// A node's value as a strided view of one buffer: element (c0..cn) of the
+// node is buf[offset + sum_a c_a * strides[a]].
+struct View {
+  BufferP buf;
+  int64_t offset = 0;
+  Shape shape;
+  std::vector<int64_t> strides;
+};
+// The view of a movement chain (Reshape/Permute/Expand/Shrink with literal
+// starts) over a Buffer, or nothing when some step is not a strided view.
+std::optional<View> try_view(const UOp *n);
+
 UOpP substitute_materialized(const UOpP &root, const std::map<const UOp *, UOpP> &repl);
 UOpP substitute_with_map(const UOpP &root, const std::unordered_map<const UOp *, UOpP> &repl,
                          std::unordered_map<const UOp *, UOpP> &memo);
@@ -45,7 +58,21 @@ struct RenderSpec {
   UOpP dest;          // View: movement chain over the destination buffer
   DType out_dtype = DType::F32;
   int unroll = 1;     // elements per thread
+  // Thread mapping of a kernel with reductions.  Thread: one thread per
+  // output element, each reduction walked sequentially in the reference's
+  // order.  Warp: one warp per output element; the lanes split the
+  // reduction's innermost reduced axis and fold their partials with a
+  // shuffle tree.  Block: 32 output elements per 256-thread block, one per
+  // lane; the 8 warps split the reduced axis and fold through shared memory.
+  // Warp and Block change the summation order, so only the default mode
+  // (not FG_FRONT_EXACT) picks them (choose_thread_mapping).
+  enum Coop { Thread, Warp, Block } coop = Thread;
 };
+
+// Picks spec.coop from the kernel's reductions: Warp when the longest
+// reduced axis (>= 32 elements) is its source's innermost axis, Block when it
+// is an outer axis and the kernel has few outputs, else Thread.
+void choose_thread_mapping(RenderSpec &spec);
 
 struct RenderedKernel {
   std::string source;

@@ -487,6 +487,54 @@ bool should_materialize(const UOp *node, const std::unordered_set<const UOp *> &
   return node->op == Op::ReduceAxis && nested.count(node);
 }
 
+// Default-mode fusion (not in the reference, which materialises every node
+// with two or more consumers, src/schedule.rs:303-335): an elementwise node
+// whose value involves no reduction, whose consumers are all elementwise ops
+// at its own coordinates, and whose consumers all end up in the same kernel
+// is recomputed inside that kernel instead of being written out and read
+// back.  Its value is the same either way (one correctly rounded op per
+// node), so only HBM traffic changes: relu(a*b+c) is one kernel, not two.
+// Kernel membership is found from the roots down: a node that is not
+// materialised belongs to the kernel of its consumers when they agree.
+std::unordered_set<const UOp *> fusible_shared_nodes(
+    const std::vector<UOpP> &order, const std::unordered_set<const UOp *> &roots,
+    const std::unordered_map<const UOp *, std::vector<const UOp *>> &consumers,
+    const std::unordered_set<const UOp *> &nested) {
+  std::unordered_set<const UOp *> fused;
+  if (exact_mode()) return fused;
+  std::unordered_map<const UOp *, bool> has_reduce;
+  for (auto &n : order) {
+    bool r = n->op == Op::ReduceAxis;
+    for (auto &s : n->src) r = r || has_reduce[s.get()];
+    has_reduce[n.get()] = r;
+  }
+  // kernel[n]: the node whose kernel computes n (itself when materialised);
+  // nullptr when its consumers lie in different kernels
+  std::unordered_map<const UOp *, const UOp *> kernel;
+  for (auto it = order.rbegin(); it != order.rend(); ++it) {
+    const UOp *n = it->get();
+    auto c = consumers.find(n);
+    const std::vector<const UOp *> none;
+    const std::vector<const UOp *> &cs = c != consumers.end() ? c->second : none;
+    const UOp *common = nullptr;
+    bool agree = !cs.empty();
+    for (size_t i = 0; i < cs.size(); i++) {
+      auto k = kernel.find(cs[i]);
+      const UOp *kc = k != kernel.end() ? k->second : nullptr;
+      if (!kc || (i > 0 && kc != common)) agree = false;
+      common = kc;
+    }
+    bool mat = roots.count(n) || should_materialize(n, roots, consumers, nested);
+    if (mat && cs.size() > 1 && agree && is_alu(n->op) && !has_reduce[n] && !roots.count(n) &&
+        std::all_of(cs.begin(), cs.end(), [](const UOp *u) { return is_alu(u->op); })) {
+      fused.insert(n);
+      mat = false;
+    }
+    kernel[n] = mat || cs.empty() ? n : (agree ? common : nullptr);
+  }
+  return fused;
+}
+
 }  // namespace
 
 // Post-order walk that does not descend below nodes for which stop() holds
@@ -638,9 +686,12 @@ SchedulePlan schedule_many(const std::vector<UOpP> &exprs) {
   std::unordered_set<const UOp *> roots;
   for (auto &e : exprs) roots.insert(e.get());
 
+  auto fused = fusible_shared_nodes(order, roots, consumers, nested);
+
   SchedulePlan plan;
   for (auto &node : order) {
-    if (!should_materialize(node.get(), roots, consumers, nested)) continue;
+    if (fused.count(node.get()) || !should_materialize(node.get(), roots, consumers, nested))
+      continue;
     UOpP k = substitute_materialized(node, plan.replacements);
     ScheduleItem item = parameterize(k);
     plan.replacements[node.get()] = buffer_replacement(item);

@@ -27,6 +27,8 @@
 // threads per block, a grid covering the domain.
 #include <algorithm>
 #include <charconv>
+#include <functional>
+#include <unordered_set>
 #include <cmath>
 #include <cstring>
 #include <sstream>
@@ -163,6 +165,21 @@ class Emitter {
   const ParamSlots &ps_;
   std::vector<Scope> scopes_;
   int tmp_ = 0;
+
+ public:
+  // Thread mapping of the kernel's reductions (RenderSpec::coop).
+  RenderSpec::Coop coop = RenderSpec::Thread;
+  // Block mapping: which shared-memory fold arrays the kernel declares.
+  bool smem_f = false, smem_i = false;
+  // 128-bit path: the value of a vector-loaded leaf at lane `lane` is a
+  // component of the loaded vector; keyed by the leaf node and the lane's
+  // coordinate key.
+  std::unordered_map<std::string, std::string> vec_vals;
+  static std::string vec_key(const UOp *n, const std::vector<std::string> &ctx) {
+    std::string k = std::to_string((uintptr_t)n);
+    for (auto &c : ctx) k += "," + c;
+    return k;
+  }
 };
 
 std::string mul_idx(const std::string &a, int64_t k) {
@@ -339,6 +356,75 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
   std::vector<std::string> sc = ctx;
   sc.resize(ss.size(), "0");
   size_t opened = 0;
+  auto combine = [&](const Val &x, const Val &y) {
+    // Reduce combination is built after symbolic folding in the reference,
+    // so it is never folded.
+    Val nx = x, ny = y;
+    nx.is_const = ny.is_const = false;
+    return emit_alu(rop, dt, {nx, ny});
+  };
+  // Warp / Block mapping: the last reduced axis longer than 1 is split over
+  // the lanes (Warp) or the warps (Block) of the threads sharing an output
+  // element; the other reduced axes are walked in order by every thread.
+  int64_t split = -1;
+  for (int64_t a : axes)
+    if (ss[(size_t)a] > 1) split = a;
+  if (coop != RenderSpec::Thread && split >= 0) {
+    const bool warp = coop == RenderSpec::Warp;
+    for (int64_t a : axes) {
+      if (a == split) continue;
+      if (ss[(size_t)a] == 1) {
+        sc[(size_t)a] = "0";
+        continue;
+      }
+      std::string r = fresh("r");
+      open("for (long long " + r + " = 0; " + r + " < " + std::to_string(ss[(size_t)a]) +
+           "LL; ++" + r + ")");
+      opened++;
+      sc[(size_t)a] = r;
+    }
+    std::string r = fresh("r");
+    line("#pragma unroll 4");
+    open(std::string("for (long long ") + r + " = " + (warp ? "fg_lane" : "fg_warp") + "; " + r +
+         " < " + std::to_string(ss[(size_t)split]) + "LL; " + r + " += " + (warp ? "32" : "8") +
+         "LL)");
+    opened++;
+    sc[(size_t)split] = r;
+    Val v = value(s, sc);
+    Val upd = combine(Val{acc, dt}, v);
+    line(acc + " = " + upd.expr + ";");
+    while (opened--) close();
+    if (warp) {
+      // xor-shuffle tree: every lane ends with the fold of all 32 partials
+      for (int off = 16; off >= 1; off >>= 1) {
+        open_block();
+        std::string t = fresh("t");
+        line(std::string("const ") + ctype(dt) + " " + t + " = __shfl_xor_sync(0xffffffffu, " +
+             acc + ", " + std::to_string(off) + ");");
+        Val u = combine(Val{acc, dt}, Val{t, dt});
+        line(acc + " = " + u.expr + ";");
+        close();
+      }
+    } else {
+      // warp w's partial goes to sm[w*32 + lane]; warp 0 folds the 8 partials
+      // in warp order and every warp reads the result back
+      const std::string sm = dt == DType::I32 ? "fg_sm_i" : "fg_sm_f";
+      (dt == DType::I32 ? smem_i : smem_f) = true;
+      line(sm + "[threadIdx.x] = " + acc + ";");
+      line("__syncthreads();");
+      open("if (fg_warp == 0)");
+      for (int w = 1; w < 8; w++) {
+        Val u = combine(Val{acc, dt}, Val{sm + "[" + std::to_string(32 * w) + " + fg_lane]", dt});
+        line(acc + " = " + u.expr + ";");
+      }
+      line(sm + "[fg_lane] = " + acc + ";");
+      close();
+      line("__syncthreads();");
+      line(acc + " = " + sm + "[fg_lane];");
+      line("__syncthreads();");
+    }
+    return Val{acc, dt};
+  }
   for (size_t i = 0; i + 1 < axes.size(); i++) {
     size_t a = (size_t)axes[i];
     std::string r = fresh("r");
@@ -347,13 +433,6 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
     opened++;
     sc[a] = r;
   }
-  auto combine = [&](const Val &x, const Val &y) {
-    // Reduce combination is built after symbolic folding in the reference,
-    // so it is never folded.
-    Val nx = x, ny = y;
-    nx.is_const = ny.is_const = false;
-    return emit_alu(rop, dt, {nx, ny});
-  };
   size_t last = axes.empty() ? 0 : (size_t)axes.back();
   int64_t R = axes.empty() ? 1 : ss[last];
   if (!axes.empty() && R > 4 && R % 4 == 0 && optimize_config().unroll) {
@@ -393,8 +472,11 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
 
 Val Emitter::value(const UOp *n, const std::vector<std::string> &ctx) {
   if (n->op == Op::Const) return Val{literal_of(n->value, n->dtype), n->dtype, true, n->value};
-  std::string key = std::to_string((uintptr_t)n);
-  for (auto &c : ctx) key += "," + c;
+  std::string key = vec_key(n, ctx);
+  if (!vec_vals.empty()) {
+    auto f = vec_vals.find(key);
+    if (f != vec_vals.end()) return Val{f->second, n->dtype};
+  }
   Val m = lookup(key);
   if (!m.expr.empty()) return m;
   Val out;
@@ -444,7 +526,110 @@ bool contains_reduce(const UOpP &root) {
   return false;
 }
 
+const char *vec_type(DType d) {
+  switch (d) {
+    case DType::F32: return "float4";
+    case DType::I32: return "int4";
+    case DType::Bool: return "uchar4";
+  }
+  return "float4";
+}
+
+// A view whose 4 consecutive elements along the innermost axis are 4
+// consecutive, 16-byte aligned (4-byte for bool) elements of its buffer,
+// given that the innermost coordinate is a multiple of 4.
+bool vec_view(const View &v) {
+  const size_t r = v.strides.size();
+  if (r == 0 || v.strides[r - 1] != 1 || v.offset % 4 != 0) return false;
+  for (size_t a = 0; a + 1 < r; a++)
+    if (v.shape[a] != 1 && v.strides[a] % 4 != 0) return false;
+  return true;
+}
+
+// 128-bit path of an elementwise kernel: the leaves (maximal movement chains
+// over a buffer, at the domain's shape) whose 4 consecutive elements can be
+// one vector load.  Empty when the kernel does not qualify.
+struct VecPlan {
+  bool ok = false;
+  std::vector<const UOp *> leaves;  // vector-loaded chain tops
+  bool vec_store = false;
+};
+
+VecPlan plan_vec4(const RenderSpec &spec) {
+  VecPlan vp;
+  const Shape &D = spec.domain;
+  if (spec.store == RenderSpec::Pitched || !spec.value_ctx.empty() || D.empty()) return vp;
+  if (D.back() % 4 != 0 || numel(D) == 0 || spec.value->shape != D) return vp;
+  bool ok = true;
+  std::unordered_set<const UOp *> seen;
+  std::function<void(const UOp *)> visit = [&](const UOp *n) {
+    if (!ok || !seen.insert(n).second) return;
+    if (n->op == Op::Const) return;
+    if (n->op == Op::Contiguous || n->op == Op::After) return visit(n->src[0].get());
+    if (is_alu(n->op)) {
+      for (auto &c : n->src) visit(c.get());
+      return;
+    }
+    if (n->op == Op::Buffer || is_movement(n->op)) {
+      if (n->shape != D) return;  // read element by element
+      auto v = try_view(n);
+      if (v && !v->buf->known_zero() && vec_view(*v)) vp.leaves.push_back(n);
+      return;
+    }
+    ok = false;  // a reduction or an op the 128-bit path does not cover
+  };
+  visit(spec.value.get());
+  if (!ok) return vp;
+  if (spec.store == RenderSpec::View) {
+    auto v = try_view(spec.dest.get());
+    vp.vec_store = v && spec.dest->shape == D && vec_view(*v);
+  } else {
+    vp.vec_store = true;
+  }
+  vp.ok = vp.vec_store || !vp.leaves.empty();
+  return vp;
+}
+
 }  // namespace
+
+void choose_thread_mapping(RenderSpec &spec) {
+  spec.coop = RenderSpec::Thread;
+  if (exact_mode() || spec.store == RenderSpec::Pitched) return;
+  const int64_t outputs = numel(spec.domain);
+  if (outputs <= 0) return;
+  int64_t best = 0;
+  bool inner = false;
+  int reduces = 0;
+  auto order = toposort(spec.value);
+  for (auto &n : order) {
+    if (n->op != Op::ReduceAxis) continue;
+    reduces++;
+    if (n->dtype == DType::Bool) return;
+    const Shape &ss = n->src[0]->shape;
+    int64_t split = -1;
+    for (int64_t a : n->arg)
+      if (ss[(size_t)a] > 1 && a > split) split = a;
+    if (split < 0) continue;
+    if (ss[(size_t)split] > best) {
+      best = ss[(size_t)split];
+      inner = true;
+      for (size_t b = (size_t)split + 1; b < ss.size(); b++)
+        if (ss[b] != 1) inner = false;
+    }
+  }
+  // A reduction inside another's source (the scheduler materialises those;
+  // kept as a guard) stays on the sequential mapping.
+  if (reduces > 1)
+    for (auto &n : order)
+      if (n->op == Op::ReduceAxis)
+        for (auto &m : toposort(n->src[0]))
+          if (m->op == Op::ReduceAxis) return;
+  if (best < 32) return;
+  if (inner)
+    spec.coop = RenderSpec::Warp;
+  else if (outputs < (int64_t(1) << 17))
+    spec.coop = RenderSpec::Block;
+}
 
 RenderedKernel render_kernel(const RenderSpec &spec) {
   const bool store_view = spec.store == RenderSpec::View;
@@ -456,7 +641,13 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
   const Shape &D = spec.domain;
   const int64_t N = numel(D);
   const bool has_reduce = contains_reduce(spec.value);
-  const int U = has_reduce ? 1 : std::max(1, spec.unroll);
+  const RenderSpec::Coop coop = has_reduce && N > 0 ? spec.coop : RenderSpec::Thread;
+  em.coop = coop;
+  const VecPlan vp = has_reduce ? VecPlan{} : plan_vec4(spec);
+  // elements per thread: `U` groups (of 4 consecutive elements on the
+  // 128-bit path, of one element otherwise) 256 * group apart
+  const int V = vp.ok ? 4 : 1;
+  const int U = coop != RenderSpec::Thread ? 1 : vp.ok ? 2 : has_reduce ? 1 : std::max(1, spec.unroll);
   int dest_slot = -1;
   if (store_view) {
     const DeviceBuffer *db = nullptr;
@@ -473,19 +664,52 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
     st *= D[a];
   }
   const DType odt = store_view ? spec.dest->dtype : spec.out_dtype;
-  em.line("const long long e0 = (long long)blockIdx.x * " + std::to_string(256 * U) +
-          "LL + threadIdx.x;");
-  std::vector<std::string> res(U), sidx(U);
+  const DType vdt = spec.value->dtype;
+  const std::string Ns = std::to_string(N) + "LL";
+  int64_t per_block = 256LL * U * V;
+  if (coop == RenderSpec::Warp) {
+    em.line("const int fg_lane = threadIdx.x & 31;");
+    em.line("const long long e0 = (long long)blockIdx.x * 8LL + (threadIdx.x >> 5);");
+    per_block = 8;
+  } else if (coop == RenderSpec::Block) {
+    // every thread takes part in the block's folds, so an out-of-range lane
+    // evaluates the last element and does not store
+    em.line("const int fg_lane = threadIdx.x & 31, fg_warp = threadIdx.x >> 5;");
+    em.line("const bool fg_in = (long long)blockIdx.x * 32LL + fg_lane < " + Ns + ";");
+    em.line("const long long e0 = fg_in ? (long long)blockIdx.x * 32LL + fg_lane : " + Ns +
+            " - 1LL;");
+    per_block = 32;
+  } else if (vp.ok) {
+    em.line("const long long e0 = ((long long)blockIdx.x * " + std::to_string(256 * U) +
+            "LL + threadIdx.x) * 4LL;");
+  } else {
+    em.line("const long long e0 = (long long)blockIdx.x * " + std::to_string(256 * U) +
+            "LL + threadIdx.x;");
+  }
+  // res[u][j]: value of lane j of group u; sidx[u]: its store index (lane 0
+  // of the group on the 128-bit path), -1 when out of range
+  std::vector<std::vector<std::string>> res(U, std::vector<std::string>(V));
+  std::vector<std::string> sidx(U);
+  std::vector<std::vector<std::string>> lane_sidx(U, std::vector<std::string>(V));
+  const bool scalar_stores = vp.ok && !vp.vec_store;
   for (int u = 0; u < U; u++) {
-    res[u] = "res" + std::to_string(u);
+    for (int j = 0; j < V; j++) {
+      res[u][j] = "res" + std::to_string(u) + (V > 1 ? "_" + std::to_string(j) : "");
+      em.line(std::string(ctype(vdt)) + " " + res[u][j] + " = " + literal_of(0.0, vdt) + ";");
+      if (scalar_stores) {
+        lane_sidx[u][j] = "st" + std::to_string(u) + "_" + std::to_string(j);
+        em.line("long long " + lane_sidx[u][j] + " = -1;");
+      }
+    }
     sidx[u] = "st" + std::to_string(u);
-    em.line(std::string(ctype(store_view ? spec.value->dtype : spec.value->dtype)) + " " + res[u] +
-            " = " + literal_of(0.0, spec.value->dtype) + ";");
     em.line("long long " + sidx[u] + " = -1;");
   }
   for (int u = 0; u < U; u++) {
-    std::string e = u == 0 ? "e0" : "(e0 + " + std::to_string(256 * u) + "LL)";
-    em.open("if (" + e + " < " + std::to_string(N) + "LL)");
+    std::string e = u == 0 ? "e0" : "(e0 + " + std::to_string(256 * V * u) + "LL)";
+    if (coop == RenderSpec::Block)
+      em.open_block();
+    else
+      em.open("if (" + e + " < " + Ns + ")");
     std::string ev = em.idx(e);
     std::vector<std::string> c(D.size(), "0");
     bool first = true;
@@ -509,11 +733,44 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
         vctx.push_back(em.idx(x));
       }
     }
-    Val v = em.value(spec.value.get(), vctx);
-    em.line(res[u] + " = " + v.expr + ";");
+    // lane j's coordinates: the innermost one + j
+    std::vector<std::vector<std::string>> lctx(V, vctx);
+    for (int j = 1; j < V; j++)
+      lctx[j].back() = em.idx(vctx.back() + " + " + std::to_string(j) + "LL");
+    if (vp.ok) {
+      // one 128-bit load per vector leaf; its lanes stand for the leaf's
+      // value at the group's 4 elements
+      em.vec_vals.clear();
+      for (const UOp *leaf : vp.leaves) {
+        const DeviceBuffer *db = nullptr;
+        std::string at = em.view_index(leaf, vctx, &db);
+        std::string q = em.fresh("q");
+        const int slot = ps.buffer_slot.at(db);
+        em.line(std::string("const ") + vec_type(leaf->dtype) + " " + q + " = *reinterpret_cast<const " +
+                vec_type(leaf->dtype) + " *>(p" + std::to_string(slot) + " + " + at + ");");
+        static const char *comp[4] = {".x", ".y", ".z", ".w"};
+        for (int j = 0; j < V; j++) {
+          std::string x = q + comp[j];
+          if (leaf->dtype == DType::Bool) x = "(" + x + " != 0)";
+          em.vec_vals[Emitter::vec_key(leaf, lctx[j])] = x;
+        }
+      }
+    }
+    for (int j = 0; j < V; j++) {
+      Val v = em.value(spec.value.get(), lctx[j]);
+      em.line(res[u][j] + " = " + v.expr + ";");
+    }
+    em.vec_vals.clear();
     std::string s;
     if (store_view) {
       const DeviceBuffer *db = nullptr;
+      if (scalar_stores) {
+        for (int j = 0; j < V; j++) {
+          std::vector<std::string> cj = c;
+          cj.back() = lctx[j].back();
+          em.line(lane_sidx[u][j] + " = " + em.view_index(spec.dest.get(), cj, &db) + ";");
+        }
+      }
       s = em.view_index(spec.dest.get(), c, &db);
     } else if (spec.store == RenderSpec::Pitched) {
       s = c.size() == 2 ? em.idx(mul_idx(c[0], spec.pitch) + " + " + c[1]) : ev;
@@ -524,10 +781,28 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
     em.close();
   }
   const int out_slot = store_view ? dest_slot : 0;
+  const std::string out = "p" + std::to_string(out_slot);
+  std::string guard = coop == RenderSpec::Warp    ? "fg_lane == 0 && "
+                      : coop == RenderSpec::Block ? "fg_warp == 0 && fg_in && "
+                                                  : "";
+  auto cast = [&](const std::string &r) {
+    return odt == DType::Bool ? "(unsigned char)(" + r + ")" : r;
+  };
   for (int u = 0; u < U; u++) {
-    std::string val = odt == DType::Bool ? "(unsigned char)(" + res[u] + ")" : res[u];
-    em.line("if (" + sidx[u] + " >= 0) p" + std::to_string(out_slot) + "[" + sidx[u] + "] = " +
-            val + ";");
+    if (vp.ok && vp.vec_store) {
+      const char *mk = odt == DType::F32 ? "make_float4" : odt == DType::I32 ? "make_int4"
+                                                                            : "make_uchar4";
+      em.line("if (" + sidx[u] + " >= 0) *reinterpret_cast<" + vec_type(odt) + " *>(" + out +
+              " + " + sidx[u] + ") = " + mk + "(" + cast(res[u][0]) + ", " + cast(res[u][1]) +
+              ", " + cast(res[u][2]) + ", " + cast(res[u][3]) + ");");
+    } else if (scalar_stores) {
+      for (int j = 0; j < V; j++)
+        em.line("if (" + sidx[u] + " >= 0) " + out + "[" + lane_sidx[u][j] + "] = " +
+                cast(res[u][j]) + ";");
+    } else {
+      em.line("if (" + guard + sidx[u] + " >= 0) " + out + "[" + sidx[u] + "] = " +
+              cast(res[u][0]) + ";");
+    }
   }
 
   std::ostringstream src;
@@ -550,12 +825,15 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
     }
   }
   for (size_t i = 0; i < params.size(); i++) src << (i ? ", " : "") << params[i];
-  src << ") {\n" << em.body.str() << "}\n";
+  src << ") {\n";
+  if (em.smem_f) src << "  __shared__ float fg_sm_f[256];\n";
+  if (em.smem_i) src << "  __shared__ int fg_sm_i[256];\n";
+  src << em.body.str() << "}\n";
 
   RenderedKernel rk;
   rk.source = src.str();
   rk.block = 256;
-  int64_t blocks = (N + 256LL * U - 1) / (256LL * U);
+  int64_t blocks = (N + per_block - 1) / per_block;
   rk.grid = (uint32_t)std::max<int64_t>(1, blocks);
   rk.has_out_slot = !store_view;
   rk.params = ps.inputs;

@@ -64,13 +64,42 @@ static size_t esize(int dt) { return dt == FG_BOOL ? 1 : 4; }
 
 // Prelude that lets the rendered CUDA C compile as host C++.
 static const char *kPrelude = R"(
+#include <barrier>
 #include <cmath>
 #include <cstring>
+#include <memory>
+#include <thread>
+#include <vector>
 struct fg_dim3 { unsigned x, y, z; };
-static fg_dim3 blockIdx, threadIdx;
+static thread_local fg_dim3 blockIdx, threadIdx;
 #define __global__
 #define __launch_bounds__(x)
 #define __restrict__ __restrict
+#define __shared__ static
+struct float4 { float x, y, z, w; };
+struct int4 { int x, y, z, w; };
+struct uchar4 { unsigned char x, y, z, w; };
+static inline float4 make_float4(float a, float b, float c, float d) { return {a, b, c, d}; }
+static inline int4 make_int4(int a, int b, int c, int d) { return {a, b, c, d}; }
+static inline uchar4 make_uchar4(unsigned char a, unsigned char b, unsigned char c,
+                                 unsigned char d) { return {a, b, c, d}; }
+// Cooperative kernels (warp shuffles, __syncthreads) run with one host
+// thread per CUDA thread of a block: a barrier per warp and one per block.
+static std::unique_ptr<std::barrier<>> fg_block_bar;
+static std::vector<std::unique_ptr<std::barrier<>>> fg_warp_bar;
+static double fg_xch[1024];
+static inline void __syncthreads() { fg_block_bar->arrive_and_wait(); }
+template <class T>
+static inline T __shfl_xor_sync(unsigned, T v, int off) {
+  const unsigned t = threadIdx.x;
+  std::barrier<> &b = *fg_warp_bar[t >> 5];
+  std::memcpy(&fg_xch[t], &v, sizeof(T));
+  b.arrive_and_wait();
+  T r;
+  std::memcpy(&r, &fg_xch[t ^ (unsigned)off], sizeof(T));
+  b.arrive_and_wait();
+  return r;
+}
 static inline float __fadd_rn(float a, float b) { return a + b; }
 static inline float __fmul_rn(float a, float b) { return a * b; }
 static inline float __frcp_rn(float a) { return 1.0f / a; }
@@ -167,12 +196,36 @@ int fg_compile(fg_device *, const char *source, const char *func_name, int num_a
     if (c == std::string::npos) break;
     pos = c + 1;
   }
-  std::string launcher = "\nextern \"C\" void fg_host_launch(void **a, unsigned grid, unsigned block) {\n"
-                         "  for (unsigned b = 0; b < grid; b++) for (unsigned t = 0; t < block; t++) {\n"
-                         "    blockIdx.x = b; threadIdx.x = t;\n    " + std::string(func_name) + "(";
+  std::string call = std::string(func_name) + "(";
   for (size_t i = 0; i < types.size(); i++)
-    launcher += (i ? ", " : "") + std::string("*(") + types[i] + "*)a[" + std::to_string(i) + "]";
-  launcher += ");\n  }\n}\n";
+    call += (i ? ", " : "") + std::string("*(") + types[i] + "*)a[" + std::to_string(i) + "]";
+  call += ");";
+  const bool coop = src.find("__syncthreads") != std::string::npos ||
+                    src.find("__shfl_xor_sync") != std::string::npos;
+  std::string launcher;
+  if (!coop) {
+    launcher = "\nextern \"C\" void fg_host_launch(void **a, unsigned grid, unsigned block) {\n"
+               "  for (unsigned b = 0; b < grid; b++) for (unsigned t = 0; t < block; t++) {\n"
+               "    blockIdx.x = b; threadIdx.x = t;\n    " + call + "\n  }\n}\n";
+  } else {
+    // one host thread per CUDA thread; the block's threads finish block b
+    // together (block barrier) before any starts block b + 1
+    launcher = "\nextern \"C\" void fg_host_launch(void **a, unsigned grid, unsigned block) {\n"
+               "  fg_block_bar.reset(new std::barrier<>(block));\n"
+               "  fg_warp_bar.clear();\n"
+               "  for (unsigned w = 0; w < (block + 31) / 32; w++)\n"
+               "    fg_warp_bar.emplace_back(new std::barrier<>(block - 32 * w < 32 ? block - 32 * w : 32));\n"
+               "  std::vector<std::thread> team;\n"
+               "  for (unsigned t = 0; t < block; t++) team.emplace_back([=] {\n"
+               "    threadIdx.x = t;\n"
+               "    for (unsigned b = 0; b < grid; b++) {\n"
+               "      blockIdx.x = b;\n      " + call + "\n"
+               "      fg_block_bar->arrive_and_wait();\n"
+               "    }\n"
+               "  });\n"
+               "  for (auto &th : team) th.join();\n"
+               "}\n";
+  }
   // Compiled kernels are cached on disk (FG_HOSTDEV_CACHE) by a hash of the
   // full source; the stored source is compared before reuse.
   const std::string full = std::string(kPrelude) + src + launcher;
@@ -201,7 +254,7 @@ int fg_compile(fg_device *, const char *source, const char *func_name, int num_a
     std::ofstream f(cpp);
     f << full;
   }
-  std::string cmd = "g++ -O1 -std=c++17 -shared -fPIC -ffp-contract=off -fno-fast-math -w -o " +
+  std::string cmd = "g++ -O1 -std=c++20 -pthread -shared -fPIC -ffp-contract=off -fno-fast-math -w -o " +
                     so + " " + cpp + " 2>" + std::string(dir) + "/log.txt";
   if (system(cmd.c_str()) != 0) {
     std::ifstream lf(std::string(dir) + "/log.txt");

@@ -302,7 +302,9 @@ def test_only_zeros_tensors_render_as_known_zero():
     d = F.tensor([1.0, 2.0, 3.0, 4.0])
     src = F.schedule([z.add(d)], with_source=True)[0]["source"]
     body = src.split("{", 1)[1]
-    assert body.count("p1[") == 0 and body.count("p2[") > 0  # only the data tensor is loaded
+    # only the data tensor is loaded (a scalar or a 128-bit load)
+    assert "p1[" not in body and "p1 +" not in body
+    assert "p2[" in body or "p2 +" in body
 
 
 def test_opt_parsing_matches_the_reference():
@@ -323,3 +325,42 @@ def test_opt_parsing_matches_the_reference():
     assert F._front.parse_optimize_config(" unroll , symbolic") == {"symbolic": True,
                                                                    "upcast": False,
                                                                    "unroll": True}
+
+
+# -------------------------------------------------- thread mapping (default mode)
+def test_elementwise_kernels_use_128_bit_accesses():
+    """An elementwise chain over contiguous operands whose innermost extent is
+    a multiple of 4 loads and stores 4 elements at a time (float4); a
+    broadcast operand is read once per group, a strided one element-wise."""
+    def data(*shape):  # uploaded data: never treated as known zeros
+        return F.tensor(np.ones(shape, np.float32))
+    a, b, bias = data(8, 16), data(8, 16), data(16)
+    src = F.schedule([a.mul(b).add(bias.reshape([1, 16]).expand([8, 16]))],
+                     with_source=True)[0]["source"]
+    assert src.count("*reinterpret_cast<const float4 *>") == 2 * 3  # a, b, bias per group
+    assert "make_float4" in src
+    t = data(16, 8).permute([1, 0])  # innermost stride 16: gathered
+    src = F.schedule([a.add(t)], with_source=True)[0]["source"]
+    assert src.count("*reinterpret_cast<const float4 *>") == 2 and "p2[" in src
+    odd = data(5, 3)  # innermost extent not a multiple of 4
+    src = F.schedule([odd.add(odd)], with_source=True)[0]["source"]
+    assert "float4" not in src
+
+
+def test_long_reductions_use_warp_and_block_mappings(monkeypatch):
+    monkeypatch.delenv("FG_FRONT_EXACT", raising=False)
+    x = F.Tensor.empty([64, 100])
+    rows = F.schedule([x.sum([1])], with_source=True)[0]["source"]
+    assert "__shfl_xor_sync" in rows and "r < 100LL" not in rows
+    cols = F.schedule([x.max([0])], with_source=True)[0]["source"]
+    assert "__syncthreads" in cols and "fg_sm_f" in cols
+    short = F.schedule([F.Tensor.empty([64, 8]).sum([1])], with_source=True)[0]["source"]
+    assert "__shfl" not in short and "__syncthreads" not in short
+
+
+def test_exact_mode_keeps_the_sequential_reduction_order(monkeypatch):
+    monkeypatch.setenv("FG_FRONT_EXACT", "1")
+    x = F.Tensor.empty([64, 100])
+    for red in (x.sum([1]), x.max([0])):
+        src = F.schedule([red], with_source=True)[0]["source"]
+        assert "__shfl" not in src and "__syncthreads" not in src

@@ -209,3 +209,41 @@ def test_host_narrow_batch_loop_tracks_oracle(oracle, hostdev, tmp_path, routed)
             assert np.max(np.abs(d_got - d_ref)) <= nb * 1e-4 * np.max(np.abs(d_ref)), i
         else:
             assert np.array_equal(r[f"w_{i}"], ws[i]) and np.array_equal(r[f"b_{i}"], bs[i]), i
+
+
+def test_host_thread_mappings_and_128_bit_kernels(oracle, hostdev, tmp_path):
+    """Default mode's rendered kernels (tests/hostdev/run_mapping.py):
+    warp-per-output and block reductions within 1e-5 of sum|x| (f32 sums),
+    bit-exact for max and for i32; the 128-bit elementwise kernels bit-exact
+    (same single-rounded ops); relu(a*b+c)*0.5 in one kernel."""
+    runner = os.path.join(os.path.dirname(hostdev), "run_mapping.py")
+    dst = tmp_path / "map.npz"
+    subprocess.run([sys.executable, runner, str(dst)], check=True, timeout=600)
+    r = dict(np.load(dst))
+    assert int(r["hand_reduce"]) == 0  # every case below the hand-kernel size: rendered
+
+    def close(got, x, axis):
+        ref = x.astype(np.float64).sum(axis)
+        scale = np.abs(x.astype(np.float64)).sum(axis)
+        assert np.all(np.abs(got.ravel() - ref.ravel()) <= 1e-5 * scale.ravel() + 1e-30)
+
+    close(r["x_sum1"], r["x"], 1)
+    close(r["c_sum0"], r["c"], 0)
+    close(r["m3_sum01"], r["m3"], (0, 1))
+    assert np.array_equal(r["x_max1"].ravel(), r["x"].max(1))
+    assert np.array_equal(r["c_max0"].ravel(), r["c"].max(0))
+    xi, ci = r["xi"], r["ci"]
+    assert np.array_equal(r["xi_sum1"].ravel(), xi.sum(1, dtype=np.int32))
+    assert np.array_equal(r["xi_max1"].ravel(), xi.max(1))
+    assert np.array_equal(r["ci_sum0"].ravel(), ci.sum(0, dtype=np.int32))
+    ab = r["a"].astype(np.float64) @ r["b"].astype(np.float64)
+    sab = np.abs(r["a"].astype(np.float64)) @ np.abs(r["b"].astype(np.float64))
+    assert np.all(np.abs(r["ab"] - ab) <= 1e-5 * sab)
+    e1, e2, e3 = r["e1"], r["e2"], r["e3"]
+    chain = np.maximum(e1 * e2 + e3, np.float32(0)) * np.float32(0.5)
+    assert np.array_equal(r["chain"], chain)
+    assert int(r["chain_kernels"]) == 1  # t = a*b+c is recomputed, not materialised
+    assert np.array_equal(r["relu"], np.where(e1 > 0, e1, np.float32(0)))
+    assert np.array_equal(r["relu_grad"], np.where(e1 > 0, e2, np.float32(0)))
+    assert np.array_equal(r["narrow_rows"], e1[3:13] + e1[20:30])
+    assert np.array_equal(r["narrow_cols"], e1[:, 1:65] * e1[:, 8:72])
