@@ -297,6 +297,8 @@ std::optional<std::vector<int64_t>> reshape_strides(const Shape &od, const std::
 
 std::optional<View> try_view(const UOp *n) {
   switch (n->op) {
+    case Op::Contiguous:
+      return try_view(n->src[0].get());
     case Op::Buffer: {
       View v;
       v.buf = n->buf;
@@ -850,11 +852,162 @@ const UOp *root_reduce(const UOpP &value) {
   return v;
 }
 
+// ---- fused cross-entropy ------------------------------------------------------
+bool contiguous_view(const View &v) {
+  int64_t s = 1;
+  for (size_t a = v.shape.size(); a-- > 0;) {
+    if (v.shape[a] != 1 && v.strides[a] != s) return false;
+    s *= v.shape[a];
+  }
+  return true;
+}
+
+// x as contiguous f32 memory: in place when it is a contiguous view of a
+// buffer (*view set), else a rendered copy held in *hold.
+const float *contiguous_operand(const UOpP &x, BufferP *hold, std::optional<View> *view) {
+  auto v = try_view(x.get());
+  if (v && contiguous_view(*v)) {
+    *view = v;
+    return fptr(v->buf, v->offset);
+  }
+  *hold = temp_buffer(DType::F32, numel(x->shape));
+  RenderSpec spec;
+  spec.value = x;
+  spec.domain = x->shape;
+  spec.out_dtype = DType::F32;
+  spec.unroll = 4;
+  choose_thread_mapping(spec);
+  launch_spec(spec, *hold);
+  return fptr(*hold);
+}
+
+// Losses computed by an XentGrad pass, kept until the XentLoss of the same
+// logits and targets (same buffers, offsets and contents versions) is
+// realized -- in a training step backward's pass runs in Sgd::step's realize
+// and loss.to_vec() comes after it.
+struct XentDone {
+  BufferP logits, targets;
+  int64_t loff, toff;
+  uint64_t lver, tver;
+  BufferP loss;
+};
+std::vector<XentDone> &xent_done() {
+  static std::vector<XentDone> v;
+  return v;
+}
+
+void run_xent(const ScheduleItem &item, const UOp *node) {
+  const UOpP &lg = node->src[0], &tg = node->src[1];
+  const Shape &ls = lg->shape;
+  const size_t rows = ls.size() == 2 ? (size_t)ls[0] : 1, cols = (size_t)ls.back();
+  BufferP hl, ht;
+  std::optional<View> vl, vt;
+  const float *L = contiguous_operand(lg, &hl, &vl);
+  const float *T = contiguous_operand(tg, &ht, &vt);
+  auto &done = xent_done();
+  const bool keyed = vl && vt;
+  auto same = [&](const XentDone &d) {
+    return d.logits == vl->buf && d.targets == vt->buf && d.loff == vl->offset &&
+           d.toff == vt->offset && d.lver == vl->buf->version && d.tver == vt->buf->version;
+  };
+  if (node->op == Op::XentLoss && keyed) {
+    for (auto it = done.begin(); it != done.end(); ++it) {
+      if (!same(*it)) continue;
+      // the loss is already on the device: hand its storage to this item
+      std::swap(item.output->h, it->loss->h);
+      done.erase(it);
+      g_stats.xent_reused++;
+      if (debug_level() >= 1)
+        fprintf(stderr, "*** CUDA %4llu  xent loss (from the gradient pass)\n",
+                (unsigned long long)g_kernel_count++);
+      return;
+    }
+  }
+  if (debug_level() >= 1)
+    fprintf(stderr, "*** CUDA %4llu  xent_fwd_bwd %zux%zu%s\n", (unsigned long long)g_kernel_count++,
+            rows, cols, node->op == Op::XentGrad ? " +grad" : "");
+  ExecTimer timer;
+  if (node->op == Op::XentLoss) {
+    check(fg_xent_fwd_bwd(L, T, rows, cols, fptr(item.output), nullptr, 1.0f, stream()), "xent");
+  } else {
+    BufferP loss = temp_buffer(DType::F32, 1);
+    check(fg_xent_fwd_bwd(L, T, rows, cols, fptr(loss), fptr(item.output), 1.0f, stream()),
+          "xent");
+    if (keyed) {
+      done.push_back({vl->buf, vt->buf, vl->offset, vt->offset, vl->buf->version,
+                      vt->buf->version, loss});
+      if (done.size() > 8) done.erase(done.begin());
+    }
+  }
+  g_stats.xent++;
+}
+
+// ---- fused SGD store ------------------------------------------------------------
+// Sgd::step's store (src/optim.rs:60-71): P <- P + (-(G * lr)) with P the
+// destination view, G a contiguous view (a routed contraction's result or a
+// realized gradient) and lr a Tensor::scalar buffer, runs on fg_sgd -- the
+// same single-rounded ops -- which also rewrites the TF32 residual that the
+// parameter keeps as a GEMM operand.  Returns false when the store does not
+// have that form; *wrote_lo tells the caller the residual is current.
+bool try_sgd(const ScheduleItem &item, const UOpP &value, bool *wrote_lo) {
+  *wrote_lo = false;
+  const UOp *v = value.get();
+  if (v->op != Op::Add || v->dtype != DType::F32 || v->src[0] != item.store_dest) return false;
+  const UOp *ng = v->src[1].get();
+  if (ng->op != Op::Neg) return false;
+  const UOp *m = ng->src[0].get();
+  if (m->op != Op::Mul) return false;
+  auto scalar_of = [](const UOp *x) -> const DeviceBuffer * {
+    while (x->op == Op::Expand || x->op == Op::Reshape) x = x->src[0].get();
+    if (x->op != Op::Buffer) return nullptr;
+    const DeviceBuffer *b = x->buf.get();
+    return b->count == 1 && b->has_host_scalar && b->version == 0 ? b : nullptr;
+  };
+  const DeviceBuffer *lr = scalar_of(m->src[1].get());
+  const UOp *g = m->src[0].get();
+  if (!lr) {
+    lr = scalar_of(m->src[0].get());
+    g = m->src[1].get();
+  }
+  if (!lr) return false;
+  auto pv = try_view(item.store_dest.get());
+  auto gv = try_view(g);
+  if (!pv || !gv || !contiguous_view(*pv) || !contiguous_view(*gv)) return false;
+  if (pv->buf->dtype != DType::F32 || gv->buf->dtype != DType::F32) return false;
+  if (pv->buf.get() == gv->buf.get()) return false;
+  const int64_t n = numel(pv->shape);
+  if (n != numel(gv->shape)) return false;
+  DeviceBuffer &pb = *pv->buf;
+  float *lo = nullptr;
+  if (pv->offset == 0 && n == (int64_t)pb.count && pb.lo && pb.lo->count == pb.count)
+    lo = fptr(pb.lo);
+  if (debug_level() >= 1)
+    fprintf(stderr, "*** CUDA %4llu  sgd %lld%s\n", (unsigned long long)g_kernel_count++,
+            (long long)n, lo ? " +lo" : "");
+  ExecTimer timer;
+  check(fg_sgd(fptr(pv->buf, pv->offset), fptr(gv->buf, gv->offset), (size_t)n, lr->host_scalar, lo,
+               stream()),
+        "sgd");
+  g_stats.sgd++;
+  *wrote_lo = lo != nullptr;
+  return true;
+}
+
+const UOp *xent_root(const UOpP &value) {
+  const UOp *v = value.get();
+  while (v->op == Op::Reshape) v = v->src[0].get();
+  return v->op == Op::XentLoss || v->op == Op::XentGrad ? v : nullptr;
+}
+
 }  // namespace
 
 RoutePlan plan_route(const ScheduleItem &item) {
   RoutePlan p;
   p.route = "rendered";
+  if (!item.store_dest && xent_root(item.value)) {
+    p.route = "xent";
+    return p;
+  }
   if (exact_mode()) return p;
   bool root_handled = false;
   for (auto &n : toposort(item.value)) {
@@ -877,6 +1030,8 @@ RoutePlan plan_route(const ScheduleItem &item) {
 }
 
 std::string render_item_source(const ScheduleItem &item) {
+  if (!item.store_dest && xent_root(item.value))
+    return "// fused cross-entropy: fg_xent_fwd_bwd (no rendered source)\n";
   RenderSpec spec;
   spec.value = item.value;
   spec.domain = item.out_shape;
@@ -901,6 +1056,12 @@ void run_item(const ScheduleItem &item) {
     fprintf(stderr, "\u2501\u2501\u2501 kernel_%llu [schedule] \u2501\u2501\u2501\n%s\n",
             (unsigned long long)g_kernel_count,
             dump(item.store_dest ? make_store(item.store_dest, item.value) : item.value).c_str());
+  if (!item.store_dest) {
+    if (const UOp *x = xent_root(item.value)) {
+      run_xent(item, x);
+      return;
+    }
+  }
   UOpP value = item.value;
   if (!exact_mode()) {
     // Extract routed reductions bottom-up, substituting each result.
@@ -932,24 +1093,31 @@ void run_item(const ScheduleItem &item) {
       value = substitute_with_map(item.value, repl, memo);
     }
   }
-  RenderSpec spec;
-  spec.value = value;
-  spec.domain = item.out_shape;
-  spec.unroll = 4;
-  if (item.store_dest) {
-    spec.store = RenderSpec::View;
-    spec.dest = item.store_dest;
-  } else {
-    spec.out_dtype = item.value->dtype;
+  bool wrote_lo = false;
+  if (!(item.store_dest && !exact_mode() && try_sgd(item, value, &wrote_lo))) {
+    RenderSpec spec;
+    spec.value = value;
+    spec.domain = item.out_shape;
+    spec.unroll = 4;
+    if (item.store_dest) {
+      spec.store = RenderSpec::View;
+      spec.dest = item.store_dest;
+    } else {
+      spec.out_dtype = item.value->dtype;
+    }
+    choose_thread_mapping(spec);
+    launch_spec(spec, item.output);
   }
-  choose_thread_mapping(spec);
-  launch_spec(spec, item.output);
   if (item.store_dest) {
     // the destination's contents changed: cached residuals and staged
-    // operands that read it are stale
+    // operands that read it are stale (unless the SGD pass rewrote the
+    // residual with the new contents)
     const UOp *d = item.store_dest.get();
     while (d->op != Op::Buffer && !d->src.empty()) d = d->src[0].get();
-    if (d->op == Op::Buffer) d->buf->version++;
+    if (d->op == Op::Buffer) {
+      d->buf->version++;
+      if (wrote_lo) d->buf->lo_version = d->buf->version;
+    }
   }
 }
 

@@ -59,7 +59,15 @@ enum class Op : int {
   ReduceAxis,
   Store,
   After,
-  Sink
+  Sink,
+  // Fused cross-entropy (default mode only; no counterpart op in the
+  // reference, whose Tensor::cross_entropy builds the decomposed graph of
+  // src/tensor.rs:715-752): XentLoss(logits [B,C], targets [B,C]) is the
+  // loss (every axis 1, as the reference's); XentGrad(logits, targets)
+  // [B,C] is d loss / d logits as src/gradient.rs:97-205 builds it for that
+  // graph.  Either runs as one fg_xent_fwd_bwd pass, which yields both.
+  XentLoss,
+  XentGrad
 };
 const char *op_name(Op op);
 bool is_alu(Op op);       // src/uop.rs:315-330
@@ -80,6 +88,11 @@ struct DeviceBuffer {
   uint64_t version = 0;
   std::shared_ptr<DeviceBuffer> lo;
   uint64_t lo_version = ~0ull;
+  // Tensor::scalar buffers keep their value on the host as well, so a kernel
+  // that takes it as a by-value argument (the SGD step's lr) needs no read
+  // back; valid while version == 0.
+  bool has_host_scalar = false;
+  float host_scalar = 0.0f;
   DeviceBuffer(DType dt, size_t n);
   ~DeviceBuffer();
   DeviceBuffer(const DeviceBuffer &) = delete;
@@ -136,6 +149,8 @@ UOpP make_reduce(const UOpP &s, Op rop, const std::vector<int64_t> &axes);
 UOpP make_store(const UOpP &dest, const UOpP &value);
 UOpP make_after(const UOpP &value, const UOpP &effect);
 UOpP make_sink(const std::vector<UOpP> &srcs);
+UOpP make_xent_loss(const UOpP &logits, const UOpP &targets);
+UOpP make_xent_grad(const UOpP &logits, const UOpP &targets);
 // UOp::full (src/uop.rs:734-744): Expand(Reshape(Const, [1..1]), shape).
 UOpP make_full(const Shape &shape, DType dt, double value);
 
@@ -296,6 +311,9 @@ struct Stats {
   uint64_t kernels = 0;      // schedule items executed
   uint64_t gemm = 0;         // contractions run on the tensor-core GEMM
   uint64_t hand_reduce = 0;  // reductions run on the hand-written HBM kernels
+  uint64_t xent = 0;         // fused cross-entropy passes (fg_xent_fwd_bwd)
+  uint64_t xent_reused = 0;  // losses taken from an earlier XentGrad pass
+  uint64_t sgd = 0;          // parameter stores run on the fused SGD kernel
   uint64_t rendered = 0;     // launches of NVRTC-rendered kernels
   uint64_t compiled = 0;     // NVRTC compilations (program cache misses)
   uint64_t cache_hits = 0;

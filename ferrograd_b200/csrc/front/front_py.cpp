@@ -259,6 +259,9 @@ PYBIND11_MODULE(_front, m) {
     d["kernels"] = s.kernels;
     d["gemm"] = s.gemm;
     d["hand_reduce"] = s.hand_reduce;
+    d["xent"] = s.xent;
+    d["xent_reused"] = s.xent_reused;
+    d["sgd"] = s.sgd;
     d["rendered"] = s.rendered;
     d["compiled"] = s.compiled;
     d["cache_hits"] = s.cache_hits;

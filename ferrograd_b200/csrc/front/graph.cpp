@@ -42,7 +42,7 @@ const char *op_name(Op op) {
   static const char *names[] = {"Buffer", "Const", "Reshape", "Permute", "Expand", "Shrink",
                                 "Contiguous", "Add", "Mul", "Neg", "Reciprocal", "Exp2", "Log2",
                                 "Sqrt", "Max", "CmpLt", "Where", "ReduceAxis", "Store", "After",
-                                "Sink"};
+                                "Sink", "XentLoss", "XentGrad"};
   return names[(int)op];
 }
 
@@ -154,6 +154,15 @@ void infer_shape(UOp &u) {
     case Op::Store:
     case Op::Sink:
       return;
+    case Op::XentLoss:
+      // the reference's loss keeps every axis as 1 ([1, 1] for rank-2 logits)
+      u.has_shape = u.src[0]->has_shape;
+      u.shape = Shape(u.src[0]->shape.size(), 1);
+      return;
+    case Op::XentGrad:
+      u.has_shape = u.src[0]->has_shape;
+      u.shape = u.src[0]->shape;
+      return;
     default:
       if (is_alu(u.op)) {
         u.has_shape = u.src[0]->has_shape;
@@ -232,6 +241,12 @@ UOpP make_after(const UOpP &value, const UOpP &effect) {
   return intern(Op::After, value->dtype, {value, effect});
 }
 UOpP make_sink(const std::vector<UOpP> &srcs) { return intern(Op::Sink, DType::F32, srcs); }
+UOpP make_xent_loss(const UOpP &logits, const UOpP &targets) {
+  return intern(Op::XentLoss, DType::F32, {logits, targets});
+}
+UOpP make_xent_grad(const UOpP &logits, const UOpP &targets) {
+  return intern(Op::XentGrad, DType::F32, {logits, targets});
+}
 
 UOpP make_full(const Shape &shape, DType dt, double value) {
   Shape base(shape.size(), 1);
@@ -391,6 +406,18 @@ std::vector<UOpP> gradient_for_op(const UOpP &nodep, const UOpP &grad) {
       UOpP weighted = make_mul(mask, make_reciprocal(make_expand(count, ss)));
       return {make_mul(weighted, grad_e)};
     }
+    case Op::XentLoss: {
+      // d loss / d logits scaled by the incoming gradient (one value); the
+      // plain loss.backward() seed 1.0 needs no scaling.  The targets get no
+      // gradient: the front end fuses only when they do not require one.
+      UOpP d = make_xent_grad(node->src[0], node->src[1]);
+      const UOp *g = grad.get();
+      while (g->op == Op::Reshape || g->op == Op::Expand) g = g->src[0].get();
+      if (g->op == Op::Const && g->value == 1.0) return {d, nullptr};
+      const Shape &ls = node->src[0]->shape;
+      UOpP ge = make_expand(make_reshape(grad, Shape(ls.size(), 1)), ls);
+      return {make_mul(d, ge), nullptr};
+    }
     case Op::Buffer:
     case Op::Const:
       return {};
@@ -475,11 +502,38 @@ bool should_materialize(const UOp *node, const std::unordered_set<const UOp *> &
     default:
       break;
   }
-  if (node->op == Op::Contiguous) return true;
+  if (node->op == Op::Contiguous) {
+    // Default mode: a contiguous() of what is already a contiguous view of a
+    // buffer (Linear's W.permute().permute().contiguous() inside matmul,
+    // src/tensor.rs:770-774) is that view; the copy would be bit-identical.
+    if (!exact_mode()) {
+      auto v = try_view(node->src[0].get());
+      if (v) {
+        int64_t st = 1;
+        bool contig = true;
+        for (size_t a = v->shape.size(); a-- > 0;) {
+          if (v->shape[a] != 1 && v->strides[a] != st) contig = false;
+          st *= v->shape[a];
+        }
+        if (contig) return false;
+      }
+    }
+    return true;
+  }
+  // the fused cross-entropy ops are kernels of their own
+  if (node->op == Op::XentLoss || node->op == Op::XentGrad) return true;
   if (is_movement(node->op)) return false;
   if (has_buffer_identity(node)) return false;
   auto it = consumers.find(node);
   if (it != consumers.end() && it->second.size() > 1) return true;
+  // the fused cross-entropy reads its operands from memory: compute them in
+  // kernels of their own (routed like any other: the logits' contraction
+  // still reaches the GEMM)
+  if (it != consumers.end() &&
+      std::any_of(it->second.begin(), it->second.end(), [](const UOp *c) {
+        return c->op == Op::XentLoss || c->op == Op::XentGrad;
+      }))
+    return true;
   if (node->op == Op::ReduceAxis && it != consumers.end() &&
       std::any_of(it->second.begin(), it->second.end(),
                   [](const UOp *c) { return is_alu(c->op); }))

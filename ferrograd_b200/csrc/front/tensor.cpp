@@ -177,7 +177,13 @@ Tensor Tensor::ones(const Shape &shape, DType dt) {
   return from_bool(v.data(), shape);
 }
 
-Tensor Tensor::scalar(float value) { return from_f32(&value, {1}); }
+Tensor Tensor::scalar(float value) {
+  Tensor t = from_f32(&value, {1});
+  const BufferP &b = t.uop()->src[0]->buf;  // Reshape(Buffer)
+  b->has_host_scalar = true;
+  b->host_scalar = value;
+  return t;
+}
 
 Shape Tensor::shape() const {
   UOpP u = uop();
@@ -339,6 +345,12 @@ Tensor Tensor::cross_entropy(const Tensor &targets) const {
                                           shape_str(targets.shape()) +
                                           " must match logits shape " + shape_str(shape()));
   const int64_t classes_axis = ndim() != 1 ? 1 : 0;
+  // Default mode: one fused op, run as a single fg_xent_fwd_bwd pass that
+  // also yields d loss / d logits for backward().  Exact mode (and targets
+  // that need a gradient, or other ranks/dtypes) build the reference graph.
+  if (!exact_mode() && (ndim() == 1 || ndim() == 2) && dtype() == DType::F32 &&
+      targets.dtype() == DType::F32 && !targets.requires_grad())
+    return from_uop(make_xent_loss(uop(), targets.uop()), requires_grad());
   Tensor log_probs = log_softmax(classes_axis);
   Tensor per_sample = targets.mul(log_probs).sum({classes_axis}).neg();
   std::vector<int64_t> axes;

@@ -416,6 +416,45 @@ int fg_u8_to_f32_div(const uint8_t *src, float *dst, size_t n, float divisor, vo
   for (size_t i = 0; i < n; i++) dst[i] = (float)src[i] / divisor;
   return FG_OK;
 }
+// The fused cross-entropy and SGD building blocks, restated from their
+// C-ABI contracts (include/ferro_cuda.h): the loss is the mean over rows of
+// -sum_c t * log_softmax(x) and dx = (softmax(x) * sum_c t - t) / rows *
+// grad_scale, each evaluated in double and rounded once (held to the GPU
+// tests' tolerance, not bit-exactness); the SGD step is p + (-(g * lr)) with
+// one rounding per op, as the reference's store, plus the new residual.
+int fg_xent_fwd_bwd(const float *x, const float *t, size_t rows, size_t cols, float *loss,
+                    float *dx, float grad_scale, void *) {
+  if (!x || !t || !loss) return fg::set_error(FG_ERR_INVALID, "fg_xent_fwd_bwd: null pointer");
+  double total = 0.0;
+  for (size_t r = 0; r < rows; r++) {
+    const float *xr = x + r * cols, *tr = t + r * cols;
+    double m = -INFINITY, se = 0.0, ts = 0.0, row = 0.0;
+    for (size_t c = 0; c < cols; c++) m = xr[c] > m ? xr[c] : m;
+    for (size_t c = 0; c < cols; c++) se += std::exp((double)xr[c] - m);
+    const double lse = m + std::log(se);
+    for (size_t c = 0; c < cols; c++) {
+      ts += tr[c];
+      row += tr[c] * ((double)xr[c] - lse);
+    }
+    total -= row;
+    if (dx)
+      for (size_t c = 0; c < cols; c++)
+        dx[r * cols + c] =
+            (float)((std::exp((double)xr[c] - lse) * ts - tr[c]) / (double)rows * grad_scale);
+  }
+  loss[0] = (float)(total / (double)rows);
+  return FG_OK;
+}
+
+int fg_sgd(float *p, const float *g, size_t n, float lr, float *lo, void *) {
+  for (size_t i = 0; i < n; i++) {
+    const float d = g[i] * lr;
+    p[i] = p[i] + (-d);
+    if (lo) lo[i] = p[i] - tf32_hi(p[i]);
+  }
+  return FG_OK;
+}
+
 int fg_one_hot_u8(const uint8_t *labels, float *out, size_t n, int classes, void *) {
   for (size_t i = 0; i < n; i++)
     for (int c = 0; c < classes; c++) out[i * classes + c] = (int)labels[i] == c ? 1.0f : 0.0f;

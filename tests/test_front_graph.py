@@ -193,20 +193,40 @@ def build_step(dims, batch, lr=0.01, empty_inputs=False):
     return model, ps, loss
 
 
-def test_mlp_step_schedule_config1():
+def test_mlp_step_schedule_config1_exact_mode_is_the_references(monkeypatch):
+    """Exact mode schedules the reference's kernels: 23 for the config-1
+    step, cross_entropy decomposed as src/tensor.rs:715-752 builds it."""
+    monkeypatch.setenv("FG_FRONT_EXACT", "1")
     _, ps, _ = build_step((784, 128, 10), 256)
     items = F.schedule(ps)
     stores = [it for it in items if it["kind"] == "store"]
     assert len(stores) == 4  # one in-place update per parameter
     assert len(items) == 23
+    assert all(it["route"] == "rendered" for it in items)
+
+
+def test_mlp_step_schedule_config1(monkeypatch):
+    """Default mode: cross_entropy is one fused op whose gradient pass is a
+    kernel of its own (the decomposed graph's 9 kernels become 1), the
+    logits it reads are materialised, and matmul's contiguous() copies of
+    the (already contiguous) weights are read in place (2 kernels fewer)."""
+    monkeypatch.delenv("FG_FRONT_EXACT", raising=False)
+    _, ps, loss = build_step((784, 128, 10), 256)
+    items = F.schedule(ps)
+    stores = [it for it in items if it["kind"] == "store"]
+    assert len(stores) == 4  # one in-place update per parameter
+    assert len(items) == 12
     routes = [it["route"] for it in items]
+    assert routes.count("xent") == 1
+    assert F.schedule([loss])[-1]["route"] == "xent"
     # The layer-1 forward contraction and the fused dW1 -> SGD store go to
     # the tensor cores; the 10-wide layer is too small and is rendered.
     assert routes.count("gemm") == 1
     assert any(it["steps"] == ["gemm 128x784x256"] for it in stores)
 
 
-def test_mlp_step_schedule_config5_routes_contractions_to_gemm():
+def test_mlp_step_schedule_config5_routes_contractions_to_gemm(monkeypatch):
+    monkeypatch.delenv("FG_FRONT_EXACT", raising=False)
     _, ps, _ = build_step((4096, 4096, 4096, 10), 8192, empty_inputs=True)
     items = F.schedule(ps)
     steps = [s for it in items for s in it["steps"]]

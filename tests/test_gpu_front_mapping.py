@@ -108,3 +108,28 @@ def test_128_bit_paths_with_views_and_bool_masks():
     F.Tensor.realize_many([y, g])
     assert np.array_equal(y.numpy(), np.where(e1 > 0, e1, np.float32(0)))
     assert np.array_equal(g.numpy(), np.where(e1 > 0, e2, np.float32(0)))
+
+
+def test_training_step_reaches_the_fused_kernels(oracle):
+    """loss.backward(); optim.step() through the Tensor API: cross_entropy
+    runs as one fg_xent_fwd_bwd pass (its loss reused by loss.to_vec()), the
+    routed weight stores run on fg_sgd with the weights' TF32 residuals, and
+    the step stays within 1e-4 of the oracle."""
+    from ferrograd_b200 import data
+    dims, batch, lr = (512, 256, 10), 256, 0.01
+    x, t = data.mlp_batch(batch, dims[0], dims[-1], 3, 4)
+    F.reset_init_seed(42)
+    model = F.Mlp(dims)
+    ws = [layer.weight.numpy() for layer in model.layers]
+    bs = [layer.bias.numpy() for layer in model.layers]
+    opt = F.Sgd(model.parameters(), lr)
+    F.reset_stats()
+    loss = F.train_step(model, opt, F.tensor(x), F.tensor(t))
+    st = F.stats()
+    assert st["xent"] == 1 and st["xent_reused"] == 1
+    assert st["sgd"] >= 1 and st["gemm"] >= 2
+    oloss, ow, ob, _, _, _ = oracle.mlp_step(ws, bs, x, t, lr)
+    assert abs(loss - oloss) <= 1e-4 * abs(oloss)
+    for layer, w0, w1 in zip(model.layers, ws, ow):
+        d_got, d_ref = layer.weight.numpy() - w0, w1 - w0
+        assert np.max(np.abs(d_got - d_ref)) <= 1e-4 * np.max(np.abs(d_ref))
