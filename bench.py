@@ -444,7 +444,7 @@ def our_arm(args):
 
 
 PER_CONFIG = (("c1", 200, 5), ("c2", 20, 3), ("c3", 10, 3), ("c4", 20, 3), ("c1front", 100, 5),
-              ("c5front", 10, 3))
+              ("c5front", 10, 3), ("c2front", 20, 3), ("c4front", 20, 3))
 
 
 def per_config(peaks, src):
@@ -721,6 +721,10 @@ def run_config(config, iters, warm, peaks, src):
                            "l2": "logits + targets + dlogits 786 MB > L2"}}
     elif config in ("c1front", "c5front"):
         line = front_bench(config, iters, warm, peaks, src)
+    elif config == "c2front":
+        line = front_c2_bench(iters, warm, peaks, src)
+    elif config == "c4front":
+        line = front_c4_bench(iters, warm, peaks, src)
     else:
         raise SystemExit(f"unknown config {config}")
     del flush_buf
@@ -782,6 +786,127 @@ def front_bench(config, iters, warm, peaks, src):
                                  "device time from CUDA events on the front end's stream"}}
 
 
+def _front_time(fn, iters, stream):
+    """Average device ms per fn() (which builds, schedules and realizes a
+    Tensor graph) between CUDA events on the front end's stream."""
+    import torch
+    from ferrograd_b200 import front as F
+    F.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def front_c2_bench(iters, warm, peaks, src):
+    """Config 2 through the Tensor API (graph built, scheduled and launched
+    per call): relu(a*b+c)*0.5 (one rendered 128-bit kernel), the row /
+    column reductions of X (routed to the HBM reduction kernels), and two
+    reductions of a lazy expression that the renderer maps to a warp per
+    row and to a block per 32 columns."""
+    import numpy as np
+    import torch
+
+    from ferrograd_b200 import data
+    from ferrograd_b200 import front as F
+
+    rng = np.random.default_rng(3)
+    n = data.C2_N
+    a, b, c = (F.tensor(rng.standard_normal(n, dtype=np.float32)) for _ in range(3))
+    half = F.Tensor.scalar(0.5)
+    for t in (a, b, c, half):
+        t.realize()
+    stream = torch.cuda.ExternalStream(F.stream())
+    ew = lambda: a.mul(b).add(c).relu().mul(half).realize()  # noqa: E731
+    for _ in range(warm):
+        ew()
+    F.reset_stats()
+    ms = _front_time(ew, iters, stream)
+    kernels_per_call = F.stats()["kernels"] / iters
+    ew_r = _hbm_roofline(16 * n, ms, peaks, src, "rendered relu(a*b+c)*0.5 (float4)")
+    ew_r.update(ms=ms, kernels_per_call=kernels_per_call)
+    ncopy = 5  # 5 x 64 MiB > L2: each call reads a copy the previous four did not
+    Xs = [F.tensor(rng.standard_normal(data.C2_X, dtype=np.float32)) for _ in range(ncopy)]
+    Xis = [F.tensor(rng.integers(-1000, 1001, data.C2_X).astype(np.int32)) for _ in range(ncopy)]
+    for t in Xs + Xis:
+        t.realize()
+    nbytes = int(np.prod(data.C2_X)) * 4
+    reds = {}
+    cases = (("f32 sum last axis (routed)", Xs, lambda x: x.sum([1]), 1),
+             ("f32 max last axis (routed)", Xs, lambda x: x.max([1]), 1),
+             ("f32 sum axis 0 (routed)", Xs, lambda x: x.sum([0]), 1),
+             ("i32 sum last axis (routed)", Xis, lambda x: x.sum([1]), 1),
+             ("i32 max last axis (routed)", Xis, lambda x: x.max([1]), 1),
+             ("f32 sum last axis of x*x (rendered, warp per row)", Xs,
+              lambda x: x.mul(x).sum([1]), 1),
+             ("f32 sum axis 0 of x*x (rendered, block per 32 columns)", Xs,
+              lambda x: x.mul(x).sum([0]), 1))
+    for name, arrs, f, _ in cases:
+        it = iter(range(10 ** 9))
+        call = lambda f=f, arrs=arrs: f(arrs[next(it) % ncopy]).realize()  # noqa: E731
+        for _ in range(warm):
+            call()
+        F.reset_stats()
+        rms = _front_time(call, iters, stream)
+        st = F.stats()
+        r = _hbm_roofline(nbytes, rms, peaks, src, name)
+        r.update(ms=rms, hand_reduce_per_call=st["hand_reduce"] / iters,
+                 rendered_per_call=st["rendered"] / iters)
+        reds[name] = r
+    return {"metric": "config2 relu(a*b+c)*0.5 over 64M f32 through the Tensor API (GB/s)",
+            "value": ew_r["achieved"], "unit": "GB/s", "roofline": ew_r, "reductions": reds,
+            "config": {"workload": "c2front", "n": n, "X": list(data.C2_X),
+                       "l2": "elementwise inputs 768 MiB > L2; reductions rotate over 5 copies "
+                             "of X (320 MiB > L2)",
+                       "timing": "CUDA events on the front end's stream around `steps` calls, "
+                                 "each building, scheduling and launching its graph (host work "
+                                 "included when it exceeds the kernel time)"}}
+
+
+def front_c4_bench(iters, warm, peaks, src):
+    """Config 4 through the Tensor API: logits.cross_entropy(targets), its
+    gradient with respect to the logits, then the loss -- one fused
+    fg_xent_fwd_bwd pass per call (the loss is taken from the gradient pass)."""
+    import numpy as np
+    import torch
+
+    from ferrograd_b200 import data
+    from ferrograd_b200 import front as F
+
+    Bx, C = data.C4
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((Bx, C), dtype=np.float32) * 2).astype(np.float32)
+    lab = rng.integers(0, C, Bx)
+    t = np.zeros((Bx, C), np.float32)
+    t[np.arange(Bx), lab] = 1.0
+    lg = F.tensor(x).with_requires_grad(True)
+    tt = F.tensor(t)
+    lg.realize()
+    tt.realize()
+
+    def call():
+        loss = lg.cross_entropy(tt)
+        (g,) = loss.gradient([lg])
+        g.realize()
+        loss.realize()
+
+    stream = torch.cuda.ExternalStream(F.stream())
+    for _ in range(warm):
+        call()
+    F.reset_stats()
+    ms = _front_time(call, iters, stream)
+    st = {k: v / iters for k, v in F.stats().items() if k in ("kernels", "xent", "xent_reused")}
+    r = _hbm_roofline(3 * Bx * C * 4, ms, peaks, src, "fg_xent_fwd_bwd via Tensor::cross_entropy")
+    r.update(ms=ms)
+    return {"metric": "config4 cross-entropy fwd+bwd [65536,1000] through the Tensor API (GB/s)",
+            "value": r["achieved"], "unit": "GB/s", "roofline": r, "per_call": st,
+            "config": {"workload": "c4front", "shape": [Bx, C],
+                       "l2": "logits + targets + dlogits 786 MB > L2"}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -797,7 +922,7 @@ def main():
                     help="row chunks of layer 0's gradient in the peer-sharded exchange")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c5gemm", "c1front",
-                                         "c5front"], default="c5",
+                                         "c5front", "c2front", "c4front"], default="c5",
                     help="c5 (default) is the headline training step; c1-c4 time one config")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -283,7 +283,8 @@ struct Layer {
   fg::gemm::GemmPlan fwd, bwd_w, bwd_x;
   // dW as two launches over the halves of its output rows, so that with a
   // communicator the first half's all-reduce overlaps the second half's GEMM
-  // (used for layer 0, whose bucket is the last one of the backward pass)
+  // (layer 0, whose bucket is the last one of the backward pass, and with
+  // FG_COMM_SPLIT_ALL=1 every tensor-core layer)
   bool can_split_w = false;
   fg::gemm::GemmPlan bwd_w_half[2];
   // Peer-sharded mode: this layer's parameters of even / odd steps inside
@@ -295,6 +296,17 @@ struct Layer {
 };
 
 size_t pad64(size_t n) { return (n + 63) / 64 * 64; }
+
+// FG_COMM_SPLIT_ALL=1: split every tensor-core layer's dW in two row halves
+// (the upper layers' SGD still waits for their dX GEMM), so each bucket's
+// first half is averaged while its second half is computed.
+bool split_all_layers() {
+  static const bool v = [] {
+    const char *e = getenv("FG_COMM_SPLIT_ALL");
+    return e && *e && atoi(e) != 0;
+  }();
+  return v;
+}
 
 }  // namespace
 
@@ -316,7 +328,7 @@ struct fg_mlp {
   std::vector<void *> allocations;
   fg_comm *comm = nullptr;
   std::vector<cudaEvent_t> ev_bucket, ev_wread;
-  cudaEvent_t ev_half = nullptr;
+  std::vector<cudaEvent_t> ev_half;  // per layer: first half of dW complete
   cudaEvent_t ev_comm_done = nullptr;
   bool use_graph = false;
   cudaGraphExec_t graph = nullptr;
@@ -387,7 +399,7 @@ int build_plans(fg_mlp *m) {
                              nullptr, ly.in, FG_GEMM_A_MN_MAJOR | FG_GEMM_B_MN_MAJOR, FG_EPI_NONE,
                              nullptr, nullptr, 0, &ly.bwd_w);
     if (rc) return rc;
-    if (l == 0 && ly.out % 64 == 0) {
+    if ((l == 0 || split_all_layers()) && ly.out % 64 == 0) {
       const int half = ly.out / 2;
       for (int h = 0; h < 2; h++) {
         rc = fg::gemm::make_plan(half, ly.in, B, m->G[l] + h * half, m->G_lo[l] + h * half, ly.out,
@@ -511,14 +523,16 @@ int enqueue_step(fg_mlp *m) {
       // first half of dW's rows: average and apply it while the second half
       // is computed (layer 0 has no dX GEMM, nothing reads W afterwards)
       if ((rc = run_gemm(m, ly.bwd_w_half[0], st))) return rc;
-      if ((rc = bucket_allreduce(m, m->ev_half, ly.bucket_off, half_elems))) return rc;
-      fg::SgdSegments segs{};
-      segs.count = 1;
-      segs.p[0] = ly.W;
-      segs.g[0] = ly.dW;
-      segs.lo[0] = ly.W_lo;
-      segs.n[0] = half_elems;
-      if ((rc = fg::launch_sgd_multi(segs, m->lr, m->comm_st))) return rc;
+      if ((rc = bucket_allreduce(m, m->ev_half[l], ly.bucket_off, half_elems))) return rc;
+      if (l == 0) {
+        fg::SgdSegments segs{};
+        segs.count = 1;
+        segs.p[0] = ly.W;
+        segs.g[0] = ly.dW;
+        segs.lo[0] = ly.W_lo;
+        segs.n[0] = half_elems;
+        if ((rc = fg::launch_sgd_multi(segs, m->lr, m->comm_st))) return rc;
+      }
       if ((rc = run_gemm(m, ly.bwd_w_half[1], st))) return rc;
     } else if (ly.tc) {
       if ((rc = run_gemm(m, ly.bwd_w, st))) return rc;
@@ -542,7 +556,7 @@ int enqueue_step(fg_mlp *m) {
         FG_CUDA_TRY(cudaEventRecord(m->ev_wread[l], st));
         FG_CUDA_TRY(cudaStreamWaitEvent(m->comm_st, m->ev_wread[l], 0));
       }
-      if (split) {
+      if (split && l == 0) {
         fg::SgdSegments segs{};
         segs.count = 2;
         segs.p[0] = ly.W + half_elems;
@@ -886,7 +900,7 @@ int fg_mlp_destroy(fg_mlp *m) {
   for (auto e : m->ev_bucket) cudaEventDestroy(e);
   for (auto e : m->ev_wread) cudaEventDestroy(e);
   if (m->ev_comm_done) cudaEventDestroy(m->ev_comm_done);
-  if (m->ev_half) cudaEventDestroy(m->ev_half);
+  for (auto e : m->ev_half) cudaEventDestroy(e);
   if (m->comm_st) cudaStreamDestroy(m->comm_st);
   for (auto g : m->pgraph)
     if (g) cudaGraphExecDestroy(g);
@@ -1000,7 +1014,8 @@ int fg_mlp_attach_comm(fg_mlp *m, fg_comm *comm) {
     m->ev_wread.resize(m->nl);
     for (auto &e : m->ev_wread) FG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_comm_done, cudaEventDisableTiming));
-    FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_half, cudaEventDisableTiming));
+    m->ev_half.resize(m->nl);
+    for (auto &e : m->ev_half) FG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   }
   return FG_OK;
 }

@@ -371,6 +371,16 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
     if (ss[(size_t)a] > 1) split = a;
   if (coop != RenderSpec::Thread && split >= 0) {
     const bool warp = coop == RenderSpec::Warp;
+    // kPar independent partial accumulators per thread, so kPar loads are in
+    // flight at once; folded pairwise after the loops (a fixed order)
+    constexpr int kPar = 8;
+    const int64_t R = ss[(size_t)split];
+    const int64_t step = warp ? 32 : 8;
+    std::vector<std::string> part(kPar);
+    for (int u = 0; u < kPar; u++) {
+      part[u] = fresh("acc");
+      line(std::string(ctype(dt)) + " " + part[u] + " = " + init + ";");
+    }
     for (int64_t a : axes) {
       if (a == split) continue;
       if (ss[(size_t)a] == 1) {
@@ -384,16 +394,25 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
       sc[(size_t)a] = r;
     }
     std::string r = fresh("r");
-    line("#pragma unroll 4");
     open(std::string("for (long long ") + r + " = " + (warp ? "fg_lane" : "fg_warp") + "; " + r +
-         " < " + std::to_string(ss[(size_t)split]) + "LL; " + r + " += " + (warp ? "32" : "8") +
-         "LL)");
+         " < " + std::to_string(R) + "LL; " + r + " += " + std::to_string(step * kPar) + "LL)");
     opened++;
-    sc[(size_t)split] = r;
-    Val v = value(s, sc);
-    Val upd = combine(Val{acc, dt}, v);
-    line(acc + " = " + upd.expr + ";");
+    for (int u = 0; u < kPar; u++) {
+      std::string ru = u == 0 ? r : idx(r + " + " + std::to_string(step * u) + "LL");
+      if (u > 0) open("if (" + ru + " < " + std::to_string(R) + "LL)");
+      sc[(size_t)split] = ru;
+      Val v = value(s, sc);
+      Val upd = combine(Val{part[u], dt}, v);
+      line(part[u] + " = " + upd.expr + ";");
+      if (u > 0) close();
+    }
     while (opened--) close();
+    for (int w = kPar / 2; w >= 1; w /= 2)
+      for (int u = 0; u < w; u++) {
+        Val f = combine(Val{part[u], dt}, Val{part[u + w], dt});
+        line(part[u] + " = " + f.expr + ";");
+      }
+    line(acc + " = " + part[0] + ";");
     if (warp) {
       // xor-shuffle tree: every lane ends with the fold of all 32 partials
       for (int off = 16; off >= 1; off >>= 1) {
