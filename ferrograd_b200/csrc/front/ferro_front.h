@@ -127,6 +127,9 @@ struct UOp {
   // Graph walks mark a node visited by stamping their own walk number here
   // (toposort); the front end is single-threaded, so no two walks overlap.
   mutable uint64_t walk_mark = 0;
+  // Scratch for the schedule cache: the node's position in the toposort of
+  // the graph being keyed (valid only inside that computation).
+  mutable int64_t topo_pos = -1;
 };
 
 // Interned constructors (src/uop.rs:536-760, 926-1040): structurally equal
@@ -184,7 +187,16 @@ struct SchedulePlan {
   std::map<const UOp *, UOpP> replacements;
   std::vector<UOpP> keep;  // keeps replaced keys alive while the plan lives
 };
-SchedulePlan schedule_many(const std::vector<UOpP> &roots);
+// with_inputs = false skips each item's slot list (ScheduleItem::inputs),
+// which only schedule summaries read; execution derives slots itself.
+SchedulePlan schedule_many(const std::vector<UOpP> &roots, bool with_inputs = true);
+// schedule_many through a cache keyed by the graph's structure (ops, dtypes,
+// shapes, args, edges, buffer sizes; not buffer identities or literal
+// values): a graph shaped like an earlier one -- the next step of a training
+// loop -- reuses that schedule with its buffers and literals renamed instead
+// of re-deriving kernel boundaries.  Items come without `inputs`.
+// FG_SCHEDULE_CACHE=0 turns it off.
+SchedulePlan schedule_cached(const std::vector<UOpP> &roots);
 
 // ---- Tensor (src/tensor.rs) ------------------------------------------------
 struct TensorInner;
@@ -317,6 +329,7 @@ struct Stats {
   uint64_t rendered = 0;     // launches of NVRTC-rendered kernels
   uint64_t compiled = 0;     // NVRTC compilations (program cache misses)
   uint64_t cache_hits = 0;
+  uint64_t schedule_hits = 0;  // realizes that reused a cached schedule
   // host time inside realize_many, seconds: scheduling, enqueueing the
   // items (routing, program lookup, launches) and the live-tensor rewrite
   double schedule_s = 0, run_s = 0, rewrite_s = 0;

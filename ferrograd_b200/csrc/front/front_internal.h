@@ -62,8 +62,8 @@ struct RenderSpec {
   // output element, each reduction walked sequentially in the reference's
   // order.  Warp: one warp per output element; the lanes split the
   // reduction's innermost reduced axis and fold their partials with a
-  // shuffle tree.  Block: 32 output elements per 256-thread block, one per
-  // lane; the 8 warps split the reduced axis and fold through shared memory.
+  // shuffle tree.  Block: 32 output elements per 1024-thread block, one per
+  // lane; the 32 warps split the reduced axis and fold through shared memory.
   // Warp and Block change the summation order, so only the default mode
   // (not FG_FRONT_EXACT) picks them (choose_thread_mapping).
   enum Coop { Thread, Warp, Block } coop = Thread;

@@ -265,6 +265,7 @@ PYBIND11_MODULE(_front, m) {
     d["rendered"] = s.rendered;
     d["compiled"] = s.compiled;
     d["cache_hits"] = s.cache_hits;
+    d["schedule_hits"] = s.schedule_hits;
     d["schedule_s"] = s.schedule_s;
     d["run_s"] = s.run_s;
     d["rewrite_s"] = s.rewrite_s;

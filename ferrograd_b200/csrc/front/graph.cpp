@@ -1,6 +1,7 @@
 // graph.cpp -- interned UOp graph nodes (src/uop.rs), reverse-mode gradient
 // rules (src/gradient.rs) and the kernel scheduler (src/schedule.rs).
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <sstream>
@@ -707,21 +708,21 @@ ParamSlots collect_params_from(const std::vector<UOpP> &order, int slot_offset) 
 
 namespace {
 
-ScheduleItem parameterize(const UOpP &expr) {
+ScheduleItem parameterize(const UOpP &expr, bool with_inputs) {
   ScheduleItem it;
   it.value = expr;
   it.out_shape = expr->has_shape ? expr->shape : Shape{1};
   it.output = std::make_shared<DeviceBuffer>(expr->dtype, (size_t)numel(it.out_shape));
-  it.inputs = collect_params(expr, 1).inputs;
+  if (with_inputs) it.inputs = collect_params(expr, 1).inputs;
   return it;
 }
 
-ScheduleItem parameterize_store(const UOpP &store) {
+ScheduleItem parameterize_store(const UOpP &store, bool with_inputs) {
   ScheduleItem it;
   it.store_dest = store->src[0];
   it.value = store->src[1];
   it.out_shape = it.value->has_shape ? it.value->shape : Shape{1};
-  it.inputs = collect_params(store, 0).inputs;
+  if (with_inputs) it.inputs = collect_params(store, 0).inputs;
   return it;
 }
 
@@ -731,7 +732,7 @@ UOpP buffer_replacement(const ScheduleItem &it) {
 
 }  // namespace
 
-SchedulePlan schedule_many(const std::vector<UOpP> &exprs) {
+SchedulePlan schedule_many(const std::vector<UOpP> &exprs, bool with_inputs) {
   if (exprs.empty()) throw Panic("schedule_many requires at least one root");
   UOpP uni = make_sink(exprs);
   auto order = toposort(uni);
@@ -747,7 +748,7 @@ SchedulePlan schedule_many(const std::vector<UOpP> &exprs) {
     if (fused.count(node.get()) || !should_materialize(node.get(), roots, consumers, nested))
       continue;
     UOpP k = substitute_materialized(node, plan.replacements);
-    ScheduleItem item = parameterize(k);
+    ScheduleItem item = parameterize(k, with_inputs);
     plan.replacements[node.get()] = buffer_replacement(item);
     plan.keep.push_back(node);
     plan.items.push_back(std::move(item));
@@ -755,15 +756,132 @@ SchedulePlan schedule_many(const std::vector<UOpP> &exprs) {
   for (auto &e : exprs) {
     UOpP fin = substitute_materialized(e, plan.replacements);
     if (fin->op == Op::After && fin->src.size() == 2 && fin->src[1]->op == Op::Store) {
-      plan.items.push_back(parameterize_store(fin->src[1]));
+      plan.items.push_back(parameterize_store(fin->src[1], with_inputs));
       plan.replacements[e.get()] = fin->src[0];
     } else {
-      ScheduleItem item = parameterize(fin);
+      ScheduleItem item = parameterize(fin, with_inputs);
       plan.replacements[e.get()] = buffer_replacement(item);
       plan.items.push_back(std::move(item));
     }
     plan.keep.push_back(e);
   }
+  return plan;
+}
+
+// ---- structural schedule cache ----------------------------------------------
+namespace {
+
+// A schedule whose leaves (buffers, literals) are placeholders: `leaves`
+// gives, per toposort position of the keyed graph, the template node that
+// stands for that position's leaf; item outputs are placeholder buffers too.
+struct CachedSchedule {
+  std::vector<std::pair<size_t, UOpP>> leaves;
+  std::vector<ScheduleItem> items;
+  std::vector<std::pair<size_t, UOpP>> repl;  // (position of the replaced node, template)
+};
+
+std::unordered_map<std::string, CachedSchedule> &schedule_cache() {
+  static std::unordered_map<std::string, CachedSchedule> c;
+  return c;
+}
+
+bool schedule_cache_on() {
+  static const bool on = [] {
+    const char *e = std::getenv("FG_SCHEDULE_CACHE");
+    return !(e && *e && std::strcmp(e, "0") == 0);
+  }();
+  return on;
+}
+
+// Everything schedule_many's decisions depend on: per node in toposort
+// order its op, dtype, reduce op, args and source positions, a buffer's
+// dtype and size; and the mode (exact mode schedules differently).
+std::string structure_key(const std::vector<UOpP> &order) {
+  std::string k;
+  k.reserve(order.size() * 48);
+  auto put = [&k](int64_t v) { k.append(reinterpret_cast<const char *>(&v), sizeof(v)); };
+  put(exact_mode() ? 1 : 0);
+  put((int64_t)order.size());
+  for (size_t i = 0; i < order.size(); i++) {
+    const UOp *n = order[i].get();
+    n->topo_pos = (int64_t)i;
+    put((int64_t)n->op | ((int64_t)n->dtype << 8) | ((int64_t)n->reduce_op << 16));
+    put((int64_t)n->arg.size());
+    for (int64_t a : n->arg) put(a);
+    put((int64_t)n->src.size());
+    for (auto &s : n->src) put(s->topo_pos);
+    if (n->op == Op::Buffer) put((int64_t)n->buf->count);
+  }
+  return k;
+}
+
+}  // namespace
+
+SchedulePlan schedule_cached(const std::vector<UOpP> &roots) {
+  if (!schedule_cache_on()) return schedule_many(roots, false);
+  if (roots.empty()) throw Panic("schedule_many requires at least one root");
+  std::vector<UOpP> order = toposort(make_sink(roots));
+  std::string key = structure_key(order);
+  auto &cache = schedule_cache();
+  auto hit = cache.find(key);
+  if (hit != cache.end()) {
+    const CachedSchedule &cs = hit->second;
+    std::unordered_map<const UOp *, UOpP> m, memo;
+    for (auto &[pos, tleaf] : cs.leaves)
+      if (order[pos] != tleaf) m[tleaf.get()] = order[pos];
+    SchedulePlan plan;
+    plan.items.reserve(cs.items.size());
+    for (const ScheduleItem &t : cs.items) {
+      ScheduleItem it;
+      it.out_shape = t.out_shape;
+      if (t.output) {
+        it.output = std::make_shared<DeviceBuffer>(t.output->dtype, t.output->count);
+        m[make_buffer(t.output).get()] = make_buffer(it.output);
+      }
+      plan.items.push_back(std::move(it));
+    }
+    for (size_t i = 0; i < cs.items.size(); i++) {
+      const ScheduleItem &t = cs.items[i];
+      plan.items[i].value = substitute_with_map(t.value, m, memo);
+      if (t.store_dest) plan.items[i].store_dest = substitute_with_map(t.store_dest, m, memo);
+    }
+    for (auto &[pos, trep] : cs.repl)
+      plan.replacements[order[pos].get()] = substitute_with_map(trep, m, memo);
+    plan.keep = std::move(order);
+    stats().schedule_hits++;
+    return plan;
+  }
+  SchedulePlan plan = schedule_many(roots, false);
+  // Template: every leaf and item output replaced by a placeholder that owns
+  // no device memory, so the cache keeps no tensor alive.
+  CachedSchedule cs;
+  std::unordered_map<const UOp *, UOpP> m, memo;
+  for (size_t i = 0; i < order.size(); i++) {
+    const UOpP &n = order[i];
+    if (n->op == Op::Buffer) {
+      UOpP ph = make_buffer(std::make_shared<DeviceBuffer>(n->buf->dtype, n->buf->count));
+      m[n.get()] = ph;
+      cs.leaves.emplace_back(i, ph);
+    } else if (n->op == Op::Const) {
+      cs.leaves.emplace_back(i, n);
+    }
+  }
+  for (const ScheduleItem &it : plan.items)
+    if (it.output)
+      m[make_buffer(it.output).get()] =
+          make_buffer(std::make_shared<DeviceBuffer>(it.output->dtype, it.output->count));
+  for (const ScheduleItem &it : plan.items) {
+    ScheduleItem t;
+    t.out_shape = it.out_shape;
+    t.value = substitute_with_map(it.value, m, memo);
+    if (it.store_dest) t.store_dest = substitute_with_map(it.store_dest, m, memo);
+    if (it.output) t.output = m.at(make_buffer(it.output).get())->buf;
+    cs.items.push_back(std::move(t));
+  }
+  for (auto &[node, rep] : plan.replacements)
+    cs.repl.emplace_back((size_t)node->topo_pos, substitute_with_map(rep, m, memo));
+  if (cache.size() >= 32) cache.clear();
+  cache.emplace(std::move(key), std::move(cs));
   return plan;
 }
 

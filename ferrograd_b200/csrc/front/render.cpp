@@ -22,9 +22,13 @@
 // Both the 4-lane reduction blocks and the folds follow the reference's OPT
 // setting (optimize_config(): without "unroll" every reduction is
 // sequential, without "symbolic" nothing is folded).
-// The thread mapping is the B200's: one thread per output element (or
-// `unroll` elements, loads of all of them issued before the stores), 256
-// threads per block, a grid covering the domain.
+// The thread mapping is the B200's: elementwise kernels give each thread
+// groups of 4 consecutive elements (one 128-bit access per operand where the
+// layout allows, several groups with all loads issued before the stores);
+// reductions run one thread per output in exact mode, and in the default
+// mode a warp per output (reduced axis innermost) or 32 outputs per
+// 1024-thread block (reduced axis outer), with 8 independent partials per
+// thread folded in a fixed order (choose_thread_mapping).
 #include <algorithm>
 #include <charconv>
 #include <functional>
@@ -181,6 +185,11 @@ class Emitter {
     return k;
   }
 };
+
+// Block mapping: 32 output elements per block (one per lane), the reduced
+// axis split over kBlockWarps warps (1024 threads, so enough loads are in
+// flight when the kernel has few outputs).
+constexpr int kBlockWarps = 32;
 
 std::string mul_idx(const std::string &a, int64_t k) {
   if (a == "0" || k == 0) return "0";
@@ -375,7 +384,7 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
     // flight at once; folded pairwise after the loops (a fixed order)
     constexpr int kPar = 8;
     const int64_t R = ss[(size_t)split];
-    const int64_t step = warp ? 32 : 8;
+    const int64_t step = warp ? 32 : kBlockWarps;
     std::vector<std::string> part(kPar);
     for (int u = 0; u < kPar; u++) {
       part[u] = fresh("acc");
@@ -425,14 +434,14 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
         close();
       }
     } else {
-      // warp w's partial goes to sm[w*32 + lane]; warp 0 folds the 8 partials
+      // warp w's partial goes to sm[w*32 + lane]; warp 0 folds the partials
       // in warp order and every warp reads the result back
       const std::string sm = dt == DType::I32 ? "fg_sm_i" : "fg_sm_f";
       (dt == DType::I32 ? smem_i : smem_f) = true;
       line(sm + "[threadIdx.x] = " + acc + ";");
       line("__syncthreads();");
       open("if (fg_warp == 0)");
-      for (int w = 1; w < 8; w++) {
+      for (int w = 1; w < kBlockWarps; w++) {
         Val u = combine(Val{acc, dt}, Val{sm + "[" + std::to_string(32 * w) + " + fg_lane]", dt});
         line(acc + " = " + u.expr + ";");
       }
@@ -828,7 +837,8 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
   src << "// rendered by the ferrograd_b200 front end\n";
   src << "#ifndef INFINITY\n#define INFINITY __int_as_float(0x7f800000)\n#endif\n"
          "#ifndef NAN\n#define NAN __int_as_float(0x7fffffff)\n#endif\n";
-  src << "extern \"C\" __global__ void __launch_bounds__(256) fg_kernel(";
+  const int threads = coop == RenderSpec::Block ? 32 * kBlockWarps : 256;
+  src << "extern \"C\" __global__ void __launch_bounds__(" << threads << ") fg_kernel(";
   std::vector<std::string> params;
   if (!store_view) params.push_back(std::string(storage_type(spec.out_dtype)) + "* __restrict__ p0");
   const int off = store_view ? 0 : 1;
@@ -845,13 +855,13 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
   }
   for (size_t i = 0; i < params.size(); i++) src << (i ? ", " : "") << params[i];
   src << ") {\n";
-  if (em.smem_f) src << "  __shared__ float fg_sm_f[256];\n";
-  if (em.smem_i) src << "  __shared__ int fg_sm_i[256];\n";
+  if (em.smem_f) src << "  __shared__ float fg_sm_f[" << threads << "];\n";
+  if (em.smem_i) src << "  __shared__ int fg_sm_i[" << threads << "];\n";
   src << em.body.str() << "}\n";
 
   RenderedKernel rk;
   rk.source = src.str();
-  rk.block = 256;
+  rk.block = (uint32_t)threads;
   int64_t blocks = (N + per_block - 1) / per_block;
   rk.grid = (uint32_t)std::max<int64_t>(1, blocks);
   rk.has_out_slot = !store_view;

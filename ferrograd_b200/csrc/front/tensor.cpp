@@ -385,7 +385,7 @@ void Tensor::realize_many(const std::vector<Tensor> &ts) {
     return std::chrono::duration<double>(b - a).count();
   };
   const auto t0 = clk::now();
-  SchedulePlan plan = schedule_many(roots);
+  SchedulePlan plan = schedule_cached(roots);
   const auto t1 = clk::now();
   for (const ScheduleItem &item : plan.items) run_item(item);
   end_realize();

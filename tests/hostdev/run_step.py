@@ -62,6 +62,7 @@ def main(src, dst):
     out["compiled"] = np.array(st["compiled"])
     out["gemm"] = np.array(st["gemm"])
     out["hand_reduce"] = np.array(st["hand_reduce"])
+    out["schedule_hits"] = np.array(st["schedule_hits"])
     np.savez(dst, **out)
 
 

@@ -247,3 +247,21 @@ def test_host_thread_mappings_and_128_bit_kernels(oracle, hostdev, tmp_path):
     assert np.array_equal(r["relu_grad"], np.where(e1 > 0, e2, np.float32(0)))
     assert np.array_equal(r["narrow_rows"], e1[3:13] + e1[20:30])
     assert np.array_equal(r["narrow_cols"], e1[:, 1:65] * e1[:, 8:72])
+
+
+@pytest.mark.parametrize("routed", [False, True])
+def test_schedule_cache_replays_the_same_kernels(hostdev, tmp_path, routed, monkeypatch):
+    """Steps 2.. of a training loop have the graph structure of step 1: their
+    realizes reuse its schedule (leaves renamed), and every output is bit for
+    bit the one the uncached scheduler gives."""
+    dims, batch, steps = (48, 40, 24, 10), 16, 3
+    monkeypatch.setenv("FG_SCHEDULE_CACHE", "0")
+    _, _, off = run(hostdev, tmp_path, dims, batch, steps, routed=routed)
+    monkeypatch.delenv("FG_SCHEDULE_CACHE")
+    _, _, on = run(hostdev, tmp_path, dims, batch, steps, routed=routed)
+    assert int(off["schedule_hits"]) == 0
+    # per step: Sgd::step's realize and loss.to_vec()'s, all but the first
+    assert int(on["schedule_hits"]) >= 2 * (steps - 1)
+    for k in off:
+        if k not in ("schedule_hits",):
+            assert np.array_equal(off[k], on[k]), k
