@@ -757,18 +757,20 @@ Operand prepare_operand(const UOpP &x, size_t row_axis, size_t red_axis, size_t 
   return op;
 }
 
-void run_contraction(const Contraction &c, const UOpP &a, const UOpP &b, const BufferP &out) {
+void run_contraction(const Contraction &c, const UOpP &a, const UOpP &b, const BufferP &out,
+                     int epilogue = FG_EPI_NONE, const float *bias = nullptr) {
   const size_t bc_a = c.bj, bc_b = c.ai;
   Operand A = prepare_operand(a, c.ai, c.r, bc_a, c.M, c.K);
   Operand B = prepare_operand(b, c.bj, c.r, bc_b, c.N, c.K);
   int flags = (A.mn_major ? FG_GEMM_A_MN_MAJOR : 0) | (B.mn_major ? FG_GEMM_B_MN_MAJOR : 0);
   if (debug_level() >= 1)
-    fprintf(stderr, "*** CUDA %4llu  gemm3xtf32 %lldx%lldx%lld%s%s\n",
+    fprintf(stderr, "*** CUDA %4llu  gemm3xtf32 %lldx%lldx%lld%s%s%s\n",
             (unsigned long long)g_kernel_count++, (long long)c.M, (long long)c.N,
-            (long long)c.K, A.mn_major ? " A:mn" : "", B.mn_major ? " B:mn" : "");
+            (long long)c.K, A.mn_major ? " A:mn" : "", B.mn_major ? " B:mn" : "",
+            epilogue == FG_EPI_BIAS ? " +bias" : "");
   ExecTimer timer;
   check(fg_gemm_3xtf32((int)c.M, (int)c.N, (int)c.K, A.ptr, A.lo_ptr, A.ld, B.ptr, B.lo_ptr, B.ld,
-                       fptr(out), nullptr, (int)c.N, flags, FG_EPI_NONE, nullptr, nullptr, 0,
+                       fptr(out), nullptr, (int)c.N, flags, epilogue, bias, nullptr, 0,
                        stream()),
         "gemm");
   g_stats.gemm++;
@@ -993,6 +995,34 @@ bool try_sgd(const ScheduleItem &item, const UOpP &value, bool *wrote_lo) {
   return true;
 }
 
+// Linear::forward's x.matmul(W^T).add(bias) (src/nn.rs:97-104): an item
+// whose value is a routed contraction [M,N] plus a row-broadcast bias vector
+// runs as one GEMM with the bias epilogue (acc + bias[n], one rounding, as
+// the rendered add), writing the item's output directly.
+bool try_gemm_bias(const ScheduleItem &item) {
+  const UOp *v = item.value.get();
+  if (v->op != Op::Add || v->dtype != DType::F32 || v->shape.size() != 2) return false;
+  for (int side = 0; side < 2; side++) {
+    const UOp *x = v->src[(size_t)side].get(), *bsrc = v->src[(size_t)(1 - side)].get();
+    if (x->op != Op::Reshape) continue;
+    auto c = match_contraction(x->src[0].get());
+    if (!c || c->r != 2 || c->ai != 0 || c->bj != 1) continue;
+    auto bv = try_view(bsrc);
+    if (!bv || bv->buf->dtype != DType::F32 || bv->strides.size() != 2 || bv->shape != v->shape)
+      continue;
+    if ((bv->shape[0] != 1 && bv->strides[0] != 0) || (bv->shape[1] != 1 && bv->strides[1] != 1))
+      continue;
+    if (bv->buf->known_zero() && !bv->buf->is_allocated()) {
+      // a never-written zero bias (Linear::new): the plain product
+      run_contraction(*c, c->a, c->b, item.output);
+    } else {
+      run_contraction(*c, c->a, c->b, item.output, FG_EPI_BIAS, fptr(bv->buf, bv->offset));
+    }
+    return true;
+  }
+  return false;
+}
+
 const UOp *xent_root(const UOpP &value) {
   const UOp *v = value.get();
   while (v->op == Op::Reshape) v = v->src[0].get();
@@ -1009,6 +1039,21 @@ RoutePlan plan_route(const ScheduleItem &item) {
     return p;
   }
   if (exact_mode()) return p;
+  {
+    const UOp *v = item.value.get();
+    if (!item.store_dest && v->op == Op::Add && v->shape.size() == 2)
+      for (auto &sv : v->src)
+        if (sv->op == Op::Reshape)
+          if (auto c = match_contraction(sv->src[0].get()))
+            if (c->r == 2 && c->ai == 0 && c->bj == 1 && try_view(v->src[&sv == &v->src[0] ? 1 : 0].get())) {
+              char buf[128];
+              snprintf(buf, sizeof(buf), "gemm %lldx%lldx%lld +bias", (long long)c->M,
+                       (long long)c->N, (long long)c->K);
+              p.route = "gemm";
+              p.steps.push_back(buf);
+              return p;
+            }
+  }
   bool root_handled = false;
   for (auto &n : toposort(item.value)) {
     if (auto c = match_contraction(n.get())) {
@@ -1062,6 +1107,7 @@ void run_item(const ScheduleItem &item) {
       return;
     }
   }
+  if (!item.store_dest && !exact_mode() && try_gemm_bias(item)) return;
   UOpP value = item.value;
   if (!exact_mode()) {
     // Extract routed reductions bottom-up, substituting each result.

@@ -590,6 +590,44 @@ std::unordered_set<const UOp *> fusible_shared_nodes(
   return fused;
 }
 
+// Default-mode fusion of Linear::forward (src/nn.rs:97-104): the
+// contraction of x.matmul(W^T) is materialised by the chained-reduction rule
+// (its value feeds the next layer's reductions), and the bias add that
+// consumes it becomes a second kernel.  When the contraction's only use is
+// that add (through matmul's reshape) and the add is a kernel boundary
+// itself, the contraction is computed inside the add's kernel instead (the
+// GEMM's bias epilogue), the same values in one pass.
+std::unordered_set<const UOp *> bias_fused_contractions(
+    const std::vector<UOpP> &order, const std::unordered_set<const UOp *> &roots,
+    const std::unordered_map<const UOp *, std::vector<const UOp *>> &consumers,
+    const std::unordered_set<const UOp *> &nested) {
+  std::unordered_set<const UOp *> fused;
+  if (exact_mode()) return fused;
+  auto only = [&](const UOp *n) -> const UOp * {
+    auto it = consumers.find(n);
+    return it != consumers.end() && it->second.size() == 1 ? it->second[0] : nullptr;
+  };
+  for (auto &np : order) {
+    const UOp *a = np.get();
+    if (a->op != Op::Add || a->dtype != DType::F32 || a->shape.size() != 2) continue;
+    if (!roots.count(a) && !should_materialize(a, roots, consumers, nested)) continue;
+    for (int side = 0; side < 2; side++) {
+      const UOp *x = a->src[(size_t)side].get(), *b = a->src[(size_t)(1 - side)].get();
+      if (x->op != Op::Reshape || only(x) != a) continue;
+      const UOp *r = x->src[0].get();
+      if (r->op != Op::ReduceAxis || r->reduce_op != Op::Add || r->arg != std::vector<int64_t>{2} ||
+          r->src[0]->op != Op::Mul || r->shape.size() != 3 || only(r) != x)
+        continue;
+      auto bv = try_view(b);
+      if (!bv || bv->strides.size() != 2 || (bv->shape[0] != 1 && bv->strides[0] != 0) ||
+          (bv->shape[1] != 1 && bv->strides[1] != 1))
+        continue;
+      fused.insert(r);
+    }
+  }
+  return fused;
+}
+
 }  // namespace
 
 // Post-order walk that does not descend below nodes for which stop() holds
@@ -742,6 +780,7 @@ SchedulePlan schedule_many(const std::vector<UOpP> &exprs, bool with_inputs) {
   for (auto &e : exprs) roots.insert(e.get());
 
   auto fused = fusible_shared_nodes(order, roots, consumers, nested);
+  for (const UOp *r : bias_fused_contractions(order, roots, consumers, nested)) fused.insert(r);
 
   SchedulePlan plan;
   for (auto &node : order) {

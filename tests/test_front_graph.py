@@ -208,16 +208,18 @@ def test_mlp_step_schedule_config1_exact_mode_is_the_references(monkeypatch):
 def test_mlp_step_schedule_config1(monkeypatch):
     """Default mode: cross_entropy is one fused op whose gradient pass is a
     kernel of its own (the decomposed graph's 9 kernels become 1), the
-    logits it reads are materialised, and matmul's contiguous() copies of
-    the (already contiguous) weights are read in place (2 kernels fewer)."""
+    logits it reads are materialised, matmul's contiguous() copies of the
+    (already contiguous) weights are read in place (2 kernels fewer), and
+    each Linear's contraction stays in its bias-add kernel (2 fewer)."""
     monkeypatch.delenv("FG_FRONT_EXACT", raising=False)
     _, ps, loss = build_step((784, 128, 10), 256)
     items = F.schedule(ps)
     stores = [it for it in items if it["kind"] == "store"]
     assert len(stores) == 4  # one in-place update per parameter
-    assert len(items) == 12
+    assert len(items) == 10
     routes = [it["route"] for it in items]
     assert routes.count("xent") == 1
+    assert any(st.endswith("+bias") for it in items for st in it["steps"])
     assert F.schedule([loss])[-1]["route"] == "xent"
     # The layer-1 forward contraction and the fused dW1 -> SGD store go to
     # the tensor cores; the 10-wide layer is too small and is rendered.
@@ -233,9 +235,11 @@ def test_mlp_step_schedule_config5_routes_contractions_to_gemm(monkeypatch):
     gemms = sorted(s for s in steps if s.startswith("gemm"))
     # 3 forward, 3 dW and 2 dX contractions; all at config-5 size.
     assert len(gemms) == 8, gemms
-    assert gemms.count("gemm 8192x4096x4096") == 3  # fwd 1, fwd 2, dX 2
+    # fwd 1 and fwd 2 with the bias epilogue, dX 2 plain
+    assert gemms.count("gemm 8192x4096x4096 +bias") == 2, gemms
+    assert gemms.count("gemm 8192x4096x4096") == 1
     assert gemms.count("gemm 4096x4096x8192") == 2  # dW 1, dW 2
-    assert {"gemm 8192x10x4096", "gemm 8192x4096x10", "gemm 10x4096x8192"} <= set(gemms)
+    assert {"gemm 8192x10x4096 +bias", "gemm 8192x4096x10", "gemm 10x4096x8192"} <= set(gemms)
     assert "reduce_cols" in steps  # bias gradients
 
 
