@@ -409,7 +409,8 @@ std::vector<bool> deps(const UOp *n) {
 
 // ---- program cache and generic launches -----------------------------------
 void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelInput> &params,
-                 const BufferP &out, const DeviceBuffer *written = nullptr);
+                 const BufferP &out, const DeviceBuffer *written = nullptr,
+                 const BufferP &lo_out = nullptr);
 
 // A one-element buffer passed in the slot of a known-zero input (never in
 // the slot the kernel writes).
@@ -420,11 +421,11 @@ fg_buffer *placeholder_buffer() {
 }
 
 void launch_rendered(const RenderedKernel &rk, const BufferP &out,
-                     const DeviceBuffer *written = nullptr) {
+                     const DeviceBuffer *written = nullptr, const BufferP &lo_out = nullptr) {
   auto &cache = program_cache();
   fg_program *prog = nullptr;
   auto it = cache.find(rk.source);
-  int nargs = (int)rk.params.size() + (rk.has_out_slot ? 1 : 0);
+  int nargs = (int)rk.params.size() + (rk.has_out_slot ? 1 : 0) + (lo_out ? 1 : 0);
   const uint64_t kid = g_kernel_count++;
   if (it != cache.end()) {
     prog = it->second;
@@ -444,12 +445,12 @@ void launch_rendered(const RenderedKernel &rk, const BufferP &out,
               (unsigned long long)kid, nargs, debug_level() >= 2 ? "  (compiled)" : "");
   }
   g_last_source = rk.source;
-  launch_args(prog, rk.has_out_slot, rk.params, out, written);
+  launch_args(prog, rk.has_out_slot, rk.params, out, written, lo_out);
 }
 
 void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelInput> &params,
-                 const BufferP &out, const DeviceBuffer *written) {
-  const int nargs = (int)params.size() + (has_out_slot ? 1 : 0);
+                 const BufferP &out, const DeviceBuffer *written, const BufferP &lo_out) {
+  const int nargs = (int)params.size() + (has_out_slot ? 1 : 0) + (lo_out ? 1 : 0);
   std::vector<fg_kernel_arg> args;
   args.reserve((size_t)nargs);
   if (has_out_slot) {
@@ -486,6 +487,13 @@ void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelIn
     }
     args.push_back(a);
   }
+  if (lo_out) {  // the residual output of a staging kernel (RenderSpec::with_lo)
+    lo_out->ensure_allocated();
+    fg_kernel_arg a{};
+    a.kind = FG_ARG_BUFFER;
+    a.v.buffer = lo_out->h;
+    args.push_back(a);
+  }
   {
     ExecTimer timer;
     check(fg_execute(prog, args.data(), nargs), "execute");
@@ -516,6 +524,7 @@ std::string spec_key(const RenderSpec &spec, const ParamSlots &ps,
   k.put((int64_t)spec.out_dtype);
   k.put(spec.unroll);
   k.put((int64_t)spec.coop);
+  k.put(spec.with_lo ? 1 : 0);
   k.put((int64_t)spec.domain.size());
   for (int64_t d : spec.domain) k.put(d);
   k.put((int64_t)spec.value_ctx.size());
@@ -559,7 +568,7 @@ std::unordered_map<std::string, CachedKernel> &spec_cache() {
 }
 
 // Render (on a miss) and launch one generic kernel.
-void launch_spec(const RenderSpec &spec, const BufferP &out) {
+void launch_spec(const RenderSpec &spec, const BufferP &out, const BufferP &lo_out = nullptr) {
   const bool view = spec.store == RenderSpec::View;
   const DeviceBuffer *written = nullptr;  // an in-place store's destination
   if (view) {
@@ -576,7 +585,7 @@ void launch_spec(const RenderSpec &spec, const BufferP &out) {
   auto it = cache.find(key);
   if (it == cache.end()) {
     RenderedKernel rk = render_kernel(spec);
-    launch_rendered(rk, out, written);
+    launch_rendered(rk, out, written, lo_out);
     auto pit = program_cache().find(rk.source);
     if (pit != program_cache().end()) cache.emplace(key, CachedKernel{pit->second, rk.has_out_slot});
     return;
@@ -586,7 +595,7 @@ void launch_spec(const RenderSpec &spec, const BufferP &out) {
     fprintf(stderr, "*** CUDA %4llu  (cached)         arg %2d\n",
             (unsigned long long)g_kernel_count++,
             (int)ps.inputs.size() + (it->second.has_out_slot ? 1 : 0));
-  launch_args(it->second.prog, it->second.has_out_slot, ps.inputs, out, written);
+  launch_args(it->second.prog, it->second.has_out_slot, ps.inputs, out, written, lo_out);
 }
 
 BufferP temp_buffer(DType dt, int64_t n) {
@@ -648,24 +657,27 @@ struct Operand {
   bool mn_major = false;
 };
 
+// A staged operand is keyed by the expression and the two domain axes that
+// index its rows and columns, so the forward GEMM (the ReLU output as A,
+// K-major) and the dW GEMM (the same matrix as B, MN-major) share one copy.
 struct StageKey {
   const UOp *x;
-  bool kmaj;
-  int64_t rows, K;
-  size_t row_axis, red_axis;
+  size_t outer_axis, inner_axis;
+  int64_t outer, inner;
   bool operator==(const StageKey &o) const {
-    return x == o.x && kmaj == o.kmaj && rows == o.rows && K == o.K && row_axis == o.row_axis &&
-           red_axis == o.red_axis;
+    return x == o.x && outer_axis == o.outer_axis && inner_axis == o.inner_axis &&
+           outer == o.outer && inner == o.inner;
   }
 };
 struct StageKeyHash {
   size_t operator()(const StageKey &k) const {
-    return std::hash<const void *>()(k.x) ^ (size_t)(k.rows * 1000003 + k.K * 31 + k.kmaj) ^
-           (k.row_axis << 7) ^ (k.red_axis << 11);
+    return std::hash<const void *>()(k.x) ^ (size_t)(k.outer * 1000003 + k.inner * 31) ^
+           (k.outer_axis << 7) ^ (k.inner_axis << 11);
   }
 };
 struct Staged {
-  Operand op;
+  BufferP hold, lo;
+  int64_t ld = 0;
   std::vector<std::pair<BufferP, uint64_t>> reads;  // buffers read, at their versions
   UOpP keep;
   bool valid() const {
@@ -712,48 +724,47 @@ Operand prepare_operand(const UOpP &x, size_t row_axis, size_t red_axis, size_t 
       return op;
     }
   }
-  // A lazy operand staged earlier in this realize (the ReLU output read by
-  // the forward GEMM and again by the dW GEMM) is reused while the buffers
-  // it reads are unchanged.
-  const bool kmaj0 = red_axis > row_axis;
-  StageKey sk0{x.get(), kmaj0, rows, K, row_axis, red_axis};
-  auto &stage = staged_cache();
-  auto sit = stage.find(sk0);
-  if (sit != stage.end() && sit->second.valid()) {
-    op = sit->second.op;
-    return op;
-  }
-  // Stage a copy whose contiguous axis is the operand's higher-numbered one
-  // (its natural row-major order, so the staging pass reads coalesced):
-  // K-major out[row][k] when the reduced axis is inner, else MN-major
-  // out[k][row].  The broadcast axis is read at 0.
+  // A lazy operand (the ReLU output) is staged once per realize, in a copy
+  // whose contiguous axis is the operand's higher-numbered domain axis (its
+  // natural row-major order, so the staging pass reads coalesced): K-major
+  // out[row][k] when the reduced axis is inner, else MN-major out[k][row].
+  // The broadcast axis is read at 0.  The staging kernel writes the TF32
+  // residual in the same pass.
   const bool kmaj = red_axis > row_axis;
+  const size_t outer_axis = kmaj ? row_axis : red_axis, inner_axis = kmaj ? red_axis : row_axis;
   const int64_t outer = kmaj ? rows : K, inner = kmaj ? K : rows;
-  const int64_t ld = (inner + 3) / 4 * 4;
-  op.hold = temp_buffer(DType::F32, outer * ld);
-  RenderSpec spec;
-  spec.value = x;
-  spec.domain = {outer, inner};
-  spec.value_ctx.assign(3, "0");
-  spec.value_ctx[row_axis] = kmaj ? "c0" : "c1";
-  spec.value_ctx[red_axis] = kmaj ? "c1" : "c0";
-  spec.store = RenderSpec::Pitched;
-  spec.pitch = ld;
-  spec.out_dtype = DType::F32;
-  spec.unroll = 4;
-  launch_spec(spec, op.hold);
-  op.ptr = fptr(op.hold);
-  op.ld = (int)ld;
+  StageKey key{x.get(), outer_axis, inner_axis, outer, inner};
+  auto &stage = staged_cache();
+  auto sit = stage.find(key);
+  if (sit == stage.end() || !sit->second.valid()) {
+    Staged st;
+    st.ld = (inner + 3) / 4 * 4;
+    st.hold = temp_buffer(DType::F32, outer * st.ld);
+    st.lo = temp_buffer(DType::F32, outer * st.ld);
+    RenderSpec spec;
+    spec.value = x;
+    spec.domain = {outer, inner};
+    spec.value_ctx.assign(3, "0");
+    spec.value_ctx[outer_axis] = "c0";
+    spec.value_ctx[inner_axis] = "c1";
+    spec.store = RenderSpec::Pitched;
+    spec.pitch = st.ld;
+    spec.out_dtype = DType::F32;
+    spec.unroll = 4;
+    spec.with_lo = true;
+    launch_spec(spec, st.hold, st.lo);
+    st.keep = x;
+    for (auto &n : toposort(x))
+      if (n->op == Op::Buffer) st.reads.emplace_back(n->buf, n->buf->version);
+    sit = stage.insert_or_assign(key, std::move(st)).first;
+  }
+  const Staged &st = sit->second;
+  op.hold = st.hold;
+  op.lo = st.lo;
+  op.ptr = fptr(st.hold);
+  op.lo_ptr = fptr(st.lo);
+  op.ld = (int)st.ld;
   op.mn_major = !kmaj;
-  op.lo = temp_buffer(DType::F32, outer * ld);
-  check(fg_split_lo(op.ptr, fptr(op.lo), (size_t)(outer * ld), stream()), "split_lo");
-  op.lo_ptr = fptr(op.lo);
-  Staged st;
-  st.op = op;
-  st.keep = x;
-  for (auto &n : toposort(x))
-    if (n->op == Op::Buffer) st.reads.emplace_back(n->buf, n->buf->version);
-  stage[sk0] = st;
   return op;
 }
 

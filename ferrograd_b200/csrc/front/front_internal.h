@@ -67,6 +67,10 @@ struct RenderSpec {
   // Warp and Block change the summation order, so only the default mode
   // (not FG_FRONT_EXACT) picks them (choose_thread_mapping).
   enum Coop { Thread, Warp, Block } coop = Thread;
+  // f32 stores only: the kernel takes one more argument after its inputs,
+  // plo, and stores there the TF32 residual of each value (v minus v with its
+  // low 13 mantissa bits cleared, as fg_split_lo), a GEMM operand's `lo`.
+  bool with_lo = false;
 };
 
 // Picks spec.coop from the kernel's reductions: Warp when the longest

@@ -816,6 +816,10 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
   auto cast = [&](const std::string &r) {
     return odt == DType::Bool ? "(unsigned char)(" + r + ")" : r;
   };
+  const bool with_lo = spec.with_lo && odt == DType::F32 && !vp.ok && coop == RenderSpec::Thread;
+  auto lo_of = [](const std::string &r) {
+    return "__fsub_rn(" + r + ", __uint_as_float(__float_as_uint(" + r + ") & 0xffffe000u))";
+  };
   for (int u = 0; u < U; u++) {
     if (vp.ok && vp.vec_store) {
       const char *mk = odt == DType::F32 ? "make_float4" : odt == DType::I32 ? "make_int4"
@@ -830,6 +834,8 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
     } else {
       em.line("if (" + guard + sidx[u] + " >= 0) " + out + "[" + sidx[u] + "] = " +
               cast(res[u][0]) + ";");
+      if (with_lo)
+        em.line("if (" + sidx[u] + " >= 0) plo[" + sidx[u] + "] = " + lo_of(res[u][0]) + ";");
     }
   }
 
@@ -853,6 +859,7 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
       params.push_back("int s" + std::to_string(slot));
     }
   }
+  if (with_lo) params.push_back("float* __restrict__ plo");
   for (size_t i = 0; i < params.size(); i++) src << (i ? ", " : "") << params[i];
   src << ") {\n";
   if (em.smem_f) src << "  __shared__ float fg_sm_f[" << threads << "];\n";

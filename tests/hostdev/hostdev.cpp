@@ -105,6 +105,9 @@ static inline float __fmul_rn(float a, float b) { return a * b; }
 static inline float __frcp_rn(float a) { return 1.0f / a; }
 static inline float __fsqrt_rn(float a) { return std::sqrt(a); }
 static inline float __int_as_float(int i) { float f; std::memcpy(&f, &i, 4); return f; }
+static inline float __uint_as_float(unsigned i) { float f; std::memcpy(&f, &i, 4); return f; }
+static inline unsigned __float_as_uint(float f) { unsigned i; std::memcpy(&i, &f, 4); return i; }
+static inline float __fsub_rn(float a, float b) { return a - b; }
 using std::exp2;
 using std::log2;
 )";
