@@ -102,6 +102,43 @@ bool bits_equal(double a, double b) {
   return x == y;
 }
 
+// A view whose 4 consecutive elements along `axis` are 4 consecutive
+// buffer elements on a 16-byte boundary (4-byte for bool) whenever that
+// axis's coordinate is a multiple of 4.
+bool vec_along(const View &v, size_t axis) {
+  if (axis >= v.strides.size() || v.strides[axis] != 1 || v.offset % 4 != 0) return false;
+  for (size_t a = 0; a < v.strides.size(); a++)
+    if (a != axis && v.shape[a] != 1 && v.strides[a] % 4 != 0) return false;
+  return true;
+}
+
+// The chain tops (Buffer or a movement chain over one) of an elementwise
+// expression; false when it holds anything else (a reduction).
+bool chain_tops(const UOp *n, std::vector<const UOp *> &tops,
+                std::unordered_set<const UOp *> &seen) {
+  if (!seen.insert(n).second || n->op == Op::Const) return true;
+  if (n->op == Op::Contiguous || n->op == Op::After) return chain_tops(n->src[0].get(), tops, seen);
+  if (is_alu(n->op)) {
+    for (auto &c : n->src)
+      if (!chain_tops(c.get(), tops, seen)) return false;
+    return true;
+  }
+  if (n->op == Op::Buffer || is_movement(n->op)) {
+    tops.push_back(n);
+    return true;
+  }
+  return false;
+}
+
+const char *vec4_type(DType d) {
+  switch (d) {
+    case DType::F32: return "float4";
+    case DType::I32: return "int4";
+    case DType::Bool: return "uchar4";
+  }
+  return "float4";
+}
+
 class Emitter {
  public:
   explicit Emitter(const ParamSlots &ps) : ps_(ps) { scopes_.emplace_back(); }
@@ -401,6 +438,72 @@ Val Emitter::emit_reduce(const UOp *n, const std::vector<std::string> &ctx) {
            "LL; ++" + r + ")");
       opened++;
       sc[(size_t)a] = r;
+    }
+    // Warp mapping over a split axis that every operand reads contiguously:
+    // each lane takes 4 consecutive elements per access (one 128-bit load
+    // per operand), 4 partials of 4 elements each per iteration.
+    std::vector<const UOp *> vleaves;
+    if (warp && R % 4 == 0 && R >= 128) {
+      std::vector<const UOp *> tops;
+      std::unordered_set<const UOp *> seen;
+      if (chain_tops(s, tops, seen))
+        for (const UOp *t : tops) {
+          if (t->shape != ss) continue;
+          auto v = try_view(t);
+          if (v && !v->buf->known_zero() && vec_along(*v, (size_t)split)) vleaves.push_back(t);
+        }
+    }
+    if (!vleaves.empty()) {
+      constexpr int kParV = 4;
+      std::string r = fresh("r");
+      open("for (long long " + r + " = fg_lane * 4LL; " + r + " < " + std::to_string(R) + "LL; " + r +
+           " += " + std::to_string(128 * kParV) + "LL)");
+      opened++;
+      static const char *comp[4] = {".x", ".y", ".z", ".w"};
+      for (int u = 0; u < kParV; u++) {
+        std::string ru = u == 0 ? r : idx(r + " + " + std::to_string(128 * u) + "LL");
+        if (u > 0) open("if (" + ru + " < " + std::to_string(R) + "LL)");
+        std::vector<std::vector<std::string>> lc(4, sc);
+        lc[0][(size_t)split] = ru;
+        for (int j = 1; j < 4; j++) lc[j][(size_t)split] = idx(ru + " + " + std::to_string(j) + "LL");
+        for (const UOp *leaf : vleaves) {
+          const DeviceBuffer *db = nullptr;
+          std::string at = view_index(leaf, lc[0], &db);
+          std::string q = fresh("q");
+          line(std::string("const ") + vec4_type(leaf->dtype) + " " + q +
+               " = *reinterpret_cast<const " + vec4_type(leaf->dtype) + " *>(p" +
+               std::to_string(ps_.buffer_slot.at(db)) + " + " + at + ");");
+          for (int j = 0; j < 4; j++) {
+            std::string xv = q + comp[j];
+            if (leaf->dtype == DType::Bool) xv = "(" + xv + " != 0)";
+            vec_vals[vec_key(leaf, lc[j])] = xv;
+          }
+        }
+        for (int j = 0; j < 4; j++) {
+          Val v = value(s, lc[j]);
+          Val upd = combine(Val{part[u], dt}, v);
+          line(part[u] + " = " + upd.expr + ";");
+        }
+        vec_vals.clear();
+        if (u > 0) close();
+      }
+      while (opened--) close();
+      for (int w = kParV / 2; w >= 1; w /= 2)
+        for (int u = 0; u < w; u++) {
+          Val f = combine(Val{part[u], dt}, Val{part[u + w], dt});
+          line(part[u] + " = " + f.expr + ";");
+        }
+      line(acc + " = " + part[0] + ";");
+      for (int off = 16; off >= 1; off >>= 1) {
+        open_block();
+        std::string t = fresh("t");
+        line(std::string("const ") + ctype(dt) + " " + t + " = __shfl_xor_sync(0xffffffffu, " +
+             acc + ", " + std::to_string(off) + ");");
+        Val u = combine(Val{acc, dt}, Val{t, dt});
+        line(acc + " = " + u.expr + ";");
+        close();
+      }
+      return Val{acc, dt};
     }
     std::string r = fresh("r");
     open(std::string("for (long long ") + r + " = " + (warp ? "fg_lane" : "fg_warp") + "; " + r +

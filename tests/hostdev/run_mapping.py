@@ -42,6 +42,11 @@ def main(dst):
     out["xi_max1"] = T(xi).max([1]).numpy()
     out["ci_sum0"] = T(ci).sum([0]).numpy()
     out["m3_sum01"] = T(m3).sum([0, 1]).numpy()
+    v = rng.standard_normal((33, 1024), dtype=np.float32)
+    out["v"] = v
+    tv = T(v)
+    out["v_sq_sum1"] = tv.mul(tv).sum([1]).numpy()  # 128-bit lane loads
+    out["v_sum1_narrow"] = tv.narrow(1, 4, 512).sum([1]).numpy()
     out["ab"] = T(a).matmul(T(b)).numpy()
     half = F.Tensor.scalar(0.5)
     hand = F.stats()["hand_reduce"]

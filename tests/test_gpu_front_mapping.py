@@ -45,6 +45,17 @@ def test_warp_reductions(shape):
     assert np.array_equal(ti.max([1]).numpy().ravel(), xi.max(1))
 
 
+@pytest.mark.parametrize("shape", [(33, 1024), (5, 4096), (3, 131072)])
+def test_warp_reductions_with_128_bit_lane_loads(shape):
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal(shape, dtype=np.float32)
+    t = F.tensor(x)
+    close_sums(t.mul(t).sum([1]).numpy(), x * x, 1)
+    close_sums(t.narrow(1, 4, shape[1] - 8).sum([1]).numpy(), x[:, 4:-4], 1)
+    assert np.array_equal(t.narrow(1, 8, shape[1] - 8).max([1]).numpy().ravel(),
+                          x[:, 8:].max(1))
+
+
 @pytest.mark.parametrize("shape", [(257, 40), (4000, 3), (64, 1000)])
 def test_block_reductions(shape):
     rng = np.random.default_rng(2)

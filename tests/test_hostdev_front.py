@@ -230,6 +230,8 @@ def test_host_thread_mappings_and_128_bit_kernels(oracle, hostdev, tmp_path):
     close(r["x_sum1"], r["x"], 1)
     close(r["c_sum0"], r["c"], 0)
     close(r["m3_sum01"], r["m3"], (0, 1))
+    close(r["v_sq_sum1"], r["v"] * r["v"], 1)
+    close(r["v_sum1_narrow"], r["v"][:, 4:516], 1)
     assert np.array_equal(r["x_max1"].ravel(), r["x"].max(1))
     assert np.array_equal(r["c_max0"].ravel(), r["c"].max(0))
     xi, ci = r["xi"], r["ci"]
