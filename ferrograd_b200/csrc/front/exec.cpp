@@ -769,7 +769,8 @@ Operand prepare_operand(const UOpP &x, size_t row_axis, size_t red_axis, size_t 
 }
 
 void run_contraction(const Contraction &c, const UOpP &a, const UOpP &b, const BufferP &out,
-                     int epilogue = FG_EPI_NONE, const float *bias = nullptr) {
+                     int epilogue = FG_EPI_NONE, const float *bias = nullptr,
+                     const float *mask = nullptr, int ldmask = 0) {
   const size_t bc_a = c.bj, bc_b = c.ai;
   Operand A = prepare_operand(a, c.ai, c.r, bc_a, c.M, c.K);
   Operand B = prepare_operand(b, c.bj, c.r, bc_b, c.N, c.K);
@@ -778,10 +779,10 @@ void run_contraction(const Contraction &c, const UOpP &a, const UOpP &b, const B
     fprintf(stderr, "*** CUDA %4llu  gemm3xtf32 %lldx%lldx%lld%s%s%s\n",
             (unsigned long long)g_kernel_count++, (long long)c.M, (long long)c.N,
             (long long)c.K, A.mn_major ? " A:mn" : "", B.mn_major ? " B:mn" : "",
-            epilogue == FG_EPI_BIAS ? " +bias" : "");
+            epilogue == FG_EPI_BIAS ? " +bias" : epilogue == FG_EPI_RELU_MASK ? " +relu-mask" : "");
   ExecTimer timer;
   check(fg_gemm_3xtf32((int)c.M, (int)c.N, (int)c.K, A.ptr, A.lo_ptr, A.ld, B.ptr, B.lo_ptr, B.ld,
-                       fptr(out), nullptr, (int)c.N, flags, epilogue, bias, nullptr, 0,
+                       fptr(out), nullptr, (int)c.N, flags, epilogue, bias, mask, ldmask,
                        stream()),
         "gemm");
   g_stats.gemm++;
@@ -1034,6 +1035,36 @@ bool try_gemm_bias(const ScheduleItem &item) {
   return false;
 }
 
+// ReLU's gradient where(0 < z, dX, 0) (src/gradient.rs:145-153 on
+// src/tensor.rs:519-531) over a routed contraction dX [M,N] and a
+// materialised z: one GEMM with the ReLU-mask epilogue
+// (C = z > 0 ? acc : 0, the same selection), writing the item's output.
+bool is_zero_value(const UOp *n) {
+  while (n->op == Op::Expand || n->op == Op::Reshape) n = n->src[0].get();
+  if (n->op == Op::Const) return n->value == 0.0;
+  return n->op == Op::Buffer && n->buf->known_zero();
+}
+
+bool try_gemm_relu_mask(const ScheduleItem &item) {
+  const UOp *v = item.value.get();
+  if (v->op != Op::Where || v->dtype != DType::F32 || v->shape.size() != 2) return false;
+  const UOp *cond = v->src[0].get(), *x = v->src[1].get();
+  if (cond->op != Op::CmpLt || !is_zero_value(cond->src[0].get()) ||
+      !is_zero_value(v->src[2].get()) || x->op != Op::Reshape)
+    return false;
+  auto zv = try_view(cond->src[1].get());
+  if (!zv || zv->buf->dtype != DType::F32 || !contiguous_view(*zv) || zv->shape != v->shape ||
+      (zv->offset * 4) % 16 != 0 || v->shape[1] % 4 != 0)
+    return false;
+  auto c = match_contraction(x->src[0].get());
+  if (!c || c->ai > c->bj) return false;
+  // output [M, N] row-major: rows along the contraction's A axis
+  if (c->M != v->shape[0] || c->N != v->shape[1]) return false;
+  run_contraction(*c, c->a, c->b, item.output, FG_EPI_RELU_MASK, nullptr,
+                  fptr(zv->buf, zv->offset), (int)v->shape[1]);
+  return true;
+}
+
 const UOp *xent_root(const UOpP &value) {
   const UOp *v = value.get();
   while (v->op == Op::Reshape) v = v->src[0].get();
@@ -1118,7 +1149,8 @@ void run_item(const ScheduleItem &item) {
       return;
     }
   }
-  if (!item.store_dest && !exact_mode() && try_gemm_bias(item)) return;
+  if (!item.store_dest && !exact_mode() && (try_gemm_bias(item) || try_gemm_relu_mask(item)))
+    return;
   UOpP value = item.value;
   if (!exact_mode()) {
     // Extract routed reductions bottom-up, substituting each result.

@@ -607,8 +607,22 @@ std::unordered_set<const UOp *> bias_fused_contractions(
     auto it = consumers.find(n);
     return it != consumers.end() && it->second.size() == 1 ? it->second[0] : nullptr;
   };
+  auto contraction_via = [&](const UOp *x, const UOp *a) -> const UOp * {
+    if (x->op != Op::Reshape || only(x) != a) return nullptr;
+    const UOp *r = x->src[0].get();
+    if (r->op != Op::ReduceAxis || r->reduce_op != Op::Add || r->arg.size() != 1 ||
+        r->src[0]->op != Op::Mul || r->shape.size() != 3 || only(r) != x)
+      return nullptr;
+    return r;
+  };
   for (auto &np : order) {
     const UOp *a = np.get();
+    // ReLU's gradient where(0 < z, dX, 0) keeps its dX contraction as well
+    // (the GEMM's mask epilogue; the executor checks the literal zeros)
+    if (a->op == Op::Where && a->dtype == DType::F32 && a->shape.size() == 2 &&
+        a->src[0]->op == Op::CmpLt &&
+        (roots.count(a) || should_materialize(a, roots, consumers, nested)))
+      if (const UOp *r = contraction_via(a->src[1].get(), a)) fused.insert(r);
     if (a->op != Op::Add || a->dtype != DType::F32 || a->shape.size() != 2) continue;
     if (!roots.count(a) && !should_materialize(a, roots, consumers, nested)) continue;
     for (int side = 0; side < 2; side++) {
@@ -782,9 +796,23 @@ SchedulePlan schedule_many(const std::vector<UOpP> &exprs, bool with_inputs) {
   auto fused = fusible_shared_nodes(order, roots, consumers, nested);
   for (const UOp *r : bias_fused_contractions(order, roots, consumers, nested)) fused.insert(r);
 
+  // Default mode: a comparison whose operands are all in memory (relu's
+  // 0 < z once z is materialised, with its zeros buffer) is recomputed by
+  // each consumer rather than written out as a bool tensor: the backward
+  // where(0 < z, dX, 0) then reads z itself, which lets the dX GEMM apply
+  // the mask in its epilogue.
+  const bool exact = exact_mode();
   SchedulePlan plan;
+  auto operand_ready = [&](const UOpP &x) {
+    const UOp *n = x.get();
+    while (is_movement(n->op)) n = n->src[0].get();
+    return n->op == Op::Const || n->op == Op::Buffer || plan.replacements.count(n) > 0;
+  };
   for (auto &node : order) {
     if (fused.count(node.get()) || !should_materialize(node.get(), roots, consumers, nested))
+      continue;
+    if (!exact && node->op == Op::CmpLt && !roots.count(node.get()) &&
+        std::all_of(node->src.begin(), node->src.end(), operand_ready))
       continue;
     UOpP k = substitute_materialized(node, plan.replacements);
     ScheduleItem item = parameterize(k, with_inputs);
