@@ -645,6 +645,10 @@ std::optional<Contraction> match_contraction(const UOp *n) {
   c.N = s[j];
   c.K = s[r];
   if (c.M * c.N * c.K < kGemmMinWork) return {};
+  // Shorter than one 32-deep k-block, a contraction is an HBM pass over its
+  // output (the 10-class layer's dX: K = 10); the tensor-core tile pipeline
+  // only adds overhead there, so it is rendered (~7x faster measured).
+  if (c.K < 32) return {};
   return c;
 }
 
@@ -747,6 +751,26 @@ Operand prepare_operand(const UOpP &x, size_t row_axis, size_t red_axis, size_t 
     spec.value_ctx.assign(3, "0");
     spec.value_ctx[outer_axis] = "c0";
     spec.value_ctx[inner_axis] = "c1";
+    // When x only broadcasts a 2-D expression y whose axes are the copy's
+    // rows and columns in order (matmul's reshape + expand of the ReLU
+    // output), the copy is y itself: render y over its own shape, so its
+    // loads see y's layout (128-bit accesses where it is contiguous).
+    {
+      const UOp *y = x.get();
+      while (y->op == Op::Expand || y->op == Op::Reshape) y = y->src[0].get();
+      const UOp *r = x->op == Op::Expand ? x->src[0].get() : nullptr;
+      if (r && r->op == Op::Reshape && r->src[0].get() == y && y->shape.size() == 2 &&
+          y->shape[0] == outer && y->shape[1] == inner) {
+        std::vector<size_t> live;  // axes of the reshape that carry y's axes
+        for (size_t a = 0; a < r->shape.size(); a++)
+          if (r->shape[a] != 1) live.push_back(a);
+        if (live.size() == 2 && live[0] == outer_axis && live[1] == inner_axis && outer > 1 &&
+            inner > 1) {
+          spec.value = r->src[0];
+          spec.value_ctx.clear();
+        }
+      }
+    }
     spec.store = RenderSpec::Pitched;
     spec.pitch = st.ld;
     spec.out_dtype = DType::F32;

@@ -684,13 +684,34 @@ struct VecPlan {
   bool ok = false;
   std::vector<const UOp *> leaves;  // vector-loaded chain tops
   bool vec_store = false;
+  size_t axis = 0;  // the value's axis that the domain's last coordinate walks
 };
 
 VecPlan plan_vec4(const RenderSpec &spec) {
   VecPlan vp;
   const Shape &D = spec.domain;
-  if (spec.store == RenderSpec::Pitched || !spec.value_ctx.empty() || D.empty()) return vp;
-  if (D.back() % 4 != 0 || numel(D) == 0 || spec.value->shape != D) return vp;
+  if (D.empty() || D.back() % 4 != 0 || numel(D) == 0) return vp;
+  const Shape &VS = spec.value->shape;
+  if (spec.value_ctx.empty()) {
+    if (VS != D) return vp;
+    vp.axis = VS.size() - 1;
+  } else {
+    // a staging copy: exactly one value axis is walked by the last domain
+    // coordinate, and no other axis depends on it
+    const std::string last = "c" + std::to_string(D.size() - 1);
+    int found = -1;
+    for (size_t a = 0; a < spec.value_ctx.size(); a++) {
+      if (spec.value_ctx[a] == last) {
+        if (found >= 0) return vp;
+        found = (int)a;
+      } else if (spec.value_ctx[a].find(last) != std::string::npos) {
+        return vp;
+      }
+    }
+    if (found < 0) return vp;
+    vp.axis = (size_t)found;
+  }
+  if (spec.store == RenderSpec::Pitched && (D.size() != 2 || spec.pitch % 4 != 0)) return vp;
   bool ok = true;
   std::unordered_set<const UOp *> seen;
   std::function<void(const UOp *)> visit = [&](const UOp *n) {
@@ -702,9 +723,9 @@ VecPlan plan_vec4(const RenderSpec &spec) {
       return;
     }
     if (n->op == Op::Buffer || is_movement(n->op)) {
-      if (n->shape != D) return;  // read element by element
+      if (n->shape != VS) return;  // read element by element
       auto v = try_view(n);
-      if (v && !v->buf->known_zero() && vec_view(*v)) vp.leaves.push_back(n);
+      if (v && !v->buf->known_zero() && vec_along(*v, vp.axis)) vp.leaves.push_back(n);
       return;
     }
     ok = false;  // a reduction or an op the 128-bit path does not cover
@@ -715,7 +736,7 @@ VecPlan plan_vec4(const RenderSpec &spec) {
     auto v = try_view(spec.dest.get());
     vp.vec_store = v && spec.dest->shape == D && vec_view(*v);
   } else {
-    vp.vec_store = true;
+    vp.vec_store = true;  // contiguous, or pitched rows with pitch % 4 == 0
   }
   vp.ok = vp.vec_store || !vp.leaves.empty();
   return vp;
@@ -864,10 +885,10 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
         vctx.push_back(em.idx(x));
       }
     }
-    // lane j's coordinates: the innermost one + j
+    // lane j's coordinates: the walked axis' one + j
     std::vector<std::vector<std::string>> lctx(V, vctx);
     for (int j = 1; j < V; j++)
-      lctx[j].back() = em.idx(vctx.back() + " + " + std::to_string(j) + "LL");
+      lctx[j][vp.axis] = em.idx(vctx[vp.axis] + " + " + std::to_string(j) + "LL");
     if (vp.ok) {
       // one 128-bit load per vector leaf; its lanes stand for the leaf's
       // value at the group's 4 elements
@@ -919,7 +940,7 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
   auto cast = [&](const std::string &r) {
     return odt == DType::Bool ? "(unsigned char)(" + r + ")" : r;
   };
-  const bool with_lo = spec.with_lo && odt == DType::F32 && !vp.ok && coop == RenderSpec::Thread;
+  const bool with_lo = spec.with_lo && odt == DType::F32 && coop == RenderSpec::Thread;
   auto lo_of = [](const std::string &r) {
     return "__fsub_rn(" + r + ", __uint_as_float(__float_as_uint(" + r + ") & 0xffffe000u))";
   };
@@ -930,10 +951,18 @@ RenderedKernel render_kernel(const RenderSpec &spec) {
       em.line("if (" + sidx[u] + " >= 0) *reinterpret_cast<" + vec_type(odt) + " *>(" + out +
               " + " + sidx[u] + ") = " + mk + "(" + cast(res[u][0]) + ", " + cast(res[u][1]) +
               ", " + cast(res[u][2]) + ", " + cast(res[u][3]) + ");");
+      if (with_lo)
+        em.line("if (" + sidx[u] + " >= 0) *reinterpret_cast<float4 *>(plo + " + sidx[u] +
+                ") = make_float4(" + lo_of(res[u][0]) + ", " + lo_of(res[u][1]) + ", " +
+                lo_of(res[u][2]) + ", " + lo_of(res[u][3]) + ");");
     } else if (scalar_stores) {
-      for (int j = 0; j < V; j++)
+      for (int j = 0; j < V; j++) {
         em.line("if (" + sidx[u] + " >= 0) " + out + "[" + lane_sidx[u][j] + "] = " +
                 cast(res[u][j]) + ";");
+        if (with_lo)
+          em.line("if (" + sidx[u] + " >= 0) plo[" + lane_sidx[u][j] + "] = " + lo_of(res[u][j]) +
+                  ";");
+      }
     } else {
       em.line("if (" + guard + sidx[u] + " >= 0) " + out + "[" + sidx[u] + "] = " +
               cast(res[u][0]) + ";");
