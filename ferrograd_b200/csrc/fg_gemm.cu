@@ -600,11 +600,20 @@ void stream_k_attach(GemmPlan *pl, void *ws, int ctas) {
 }
 
 // k-blocks per tensor-core accumulation chain (FG_GEMM_SEG_KB, default 32,
-// i.e. 1024 products of each output; 0 = one chain per tile).
+// i.e. 1024 products of each output; 0 = one chain per tile), applied to
+// GEMMs whose K is at least FG_GEMM_SEG_MIN_K (default 0: every GEMM).
 static int seg_kb_setting() {
   static const int v = [] {
     const char *e = getenv("FG_GEMM_SEG_KB");
     const int x = e && *e ? atoi(e) : 32;
+    return x < 0 ? 0 : x;
+  }();
+  return v;
+}
+static int seg_min_k_setting() {
+  static const int v = [] {
+    const char *e = getenv("FG_GEMM_SEG_MIN_K");
+    const int x = e && *e ? atoi(e) : 0;
     return x < 0 ? 0 : x;
   }();
   return v;
@@ -631,7 +640,7 @@ static int launch_t(const GemmPlan &pl, cudaStream_t st) {
   GemmParams p = pl.p;
   const int grid = plan_stream_k(p, ntiles, nk, cap, pl.sk_ws, pl.sk_flags);
   p.seg_ws = pl.seg_ws;
-  p.seg_kb = seg_kb_setting();
+  p.seg_kb = p.K >= seg_min_k_setting() ? seg_kb_setting() : 0;
   kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(pl.a, pl.alo, pl.b, pl.blo, p);
   FG_LAUNCH_TRY();
   return FG_OK;
