@@ -313,6 +313,12 @@ bool split_all_layers() {
 struct fg_mlp {
   fg_device *dev = nullptr;
   cudaStream_t st = nullptr, comm_st = nullptr;
+  // With a communicator, Sgd::step's updates run on their own stream after
+  // their bucket's all-reduce, so the comm stream goes straight on to the
+  // next bucket.
+  cudaStream_t sgd_st = nullptr;
+  std::vector<cudaEvent_t> ev_ar;  // [2 * layer + part]: a bucket's all-reduce done
+  cudaEvent_t ev_sgd_done = nullptr;
   int nl = 0, B = 0;
   float lr = 0.f;
   std::vector<int> dims;
@@ -479,7 +485,15 @@ int bucket_allreduce(fg_mlp *m, cudaEvent_t ev, size_t off, size_t len) {
   return FG_OK;
 }
 
-// Enqueue one training step on m->st (and m->comm_st).
+// Make m->sgd_st wait for everything enqueued on m->comm_st so far (the
+// all-reduce of the bucket it is about to apply).
+int sgd_after_comm(fg_mlp *m, int ev_index) {
+  FG_CUDA_TRY(cudaEventRecord(m->ev_ar[(size_t)ev_index], m->comm_st));
+  FG_CUDA_TRY(cudaStreamWaitEvent(m->sgd_st, m->ev_ar[(size_t)ev_index], 0));
+  return FG_OK;
+}
+
+// Enqueue one training step on m->st (and m->comm_st, m->sgd_st).
 int enqueue_step(fg_mlp *m) {
   cudaStream_t st = m->st;
   const int B = m->B;
@@ -531,7 +545,8 @@ int enqueue_step(fg_mlp *m) {
         segs.g[0] = ly.dW;
         segs.lo[0] = ly.W_lo;
         segs.n[0] = half_elems;
-        if ((rc = fg::launch_sgd_multi(segs, m->lr, m->comm_st))) return rc;
+        if ((rc = sgd_after_comm(m, 2 * l))) return rc;
+        if ((rc = fg::launch_sgd_multi(segs, m->lr, m->sgd_st))) return rc;
       }
       if ((rc = run_gemm(m, ly.bwd_w_half[1], st))) return rc;
     } else if (ly.tc) {
@@ -552,9 +567,10 @@ int enqueue_step(fg_mlp *m) {
       return rc;
     if (ly.tc && l > 0 && (rc = run_gemm(m, ly.bwd_x, st))) return rc;
     if (m->comm) {
+      if ((rc = sgd_after_comm(m, 2 * l + 1))) return rc;
       if (ly.tc && l > 0) {  // SGD must not overtake the dX GEMM reading W
         FG_CUDA_TRY(cudaEventRecord(m->ev_wread[l], st));
-        FG_CUDA_TRY(cudaStreamWaitEvent(m->comm_st, m->ev_wread[l], 0));
+        FG_CUDA_TRY(cudaStreamWaitEvent(m->sgd_st, m->ev_wread[l], 0));
       }
       if (split && l == 0) {
         fg::SgdSegments segs{};
@@ -567,8 +583,8 @@ int enqueue_step(fg_mlp *m) {
         segs.g[1] = ly.db;
         segs.lo[1] = nullptr;
         segs.n[1] = (size_t)ly.out;
-        if ((rc = fg::launch_sgd_multi(segs, m->lr, m->comm_st))) return rc;
-      } else if ((rc = sgd_layer(m, l, m->comm_st))) {
+        if ((rc = fg::launch_sgd_multi(segs, m->lr, m->sgd_st))) return rc;
+      } else if ((rc = sgd_layer(m, l, m->sgd_st))) {
         return rc;
       }
     }
@@ -576,6 +592,8 @@ int enqueue_step(fg_mlp *m) {
   if (m->comm) {
     FG_CUDA_TRY(cudaEventRecord(m->ev_comm_done, m->comm_st));
     FG_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_comm_done, 0));
+    FG_CUDA_TRY(cudaEventRecord(m->ev_sgd_done, m->sgd_st));
+    FG_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_sgd_done, 0));
     return FG_OK;
   }
   // Sgd::step over every parameter (weights of tensor-core layers also get
@@ -902,6 +920,9 @@ int fg_mlp_destroy(fg_mlp *m) {
   if (m->ev_comm_done) cudaEventDestroy(m->ev_comm_done);
   for (auto e : m->ev_half) cudaEventDestroy(e);
   if (m->comm_st) cudaStreamDestroy(m->comm_st);
+  for (auto e : m->ev_ar) cudaEventDestroy(e);
+  if (m->ev_sgd_done) cudaEventDestroy(m->ev_sgd_done);
+  if (m->sgd_st) cudaStreamDestroy(m->sgd_st);
   for (auto g : m->pgraph)
     if (g) cudaGraphExecDestroy(g);
   for (int j = 0; j < fg::kMaxPeers; j++) {
@@ -1016,6 +1037,10 @@ int fg_mlp_attach_comm(fg_mlp *m, fg_comm *comm) {
     FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_comm_done, cudaEventDisableTiming));
     m->ev_half.resize(m->nl);
     for (auto &e : m->ev_half) FG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->sgd_st, cudaStreamNonBlocking));
+    m->ev_ar.resize(2 * (size_t)m->nl);
+    for (auto &e : m->ev_ar) FG_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    FG_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_sgd_done, cudaEventDisableTiming));
   }
   return FG_OK;
 }
