@@ -37,16 +37,19 @@ namespace gemm {
 using namespace fg::ptx;
 
 constexpr int BM = 128;
-constexpr int BK = 32;      // fp32 elements per k-block: one 128-byte swizzle row
 constexpr int UMMA_K = 8;   // K of one kind::tf32 MMA
 constexpr int kThreads = 192;
 
-template <int BN>
+// BK: fp32 elements per k-block.  32 is one 128-byte swizzle row per K-major
+// operand row; 16 (64-byte swizzle) halves a stage, so the same shared
+// memory holds twice the stages and more operand bytes are in flight while
+// the tensor cores consume one stage (FG_GEMM_BK selects; 32 by default).
+template <int BN, int BK>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
-  static constexpr int STAGES = (BN <= 128) ? 3 : 2;
+  static constexpr int STAGES = (BN <= 128 ? 3 : 2) * (32 / BK);
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
@@ -145,12 +148,12 @@ __device__ __forceinline__ bool wait_flag(const unsigned int *flag, unsigned int
 // in one of two TMEM buffers (2 x BN columns): while the epilogue warps drain
 // tile i from one buffer, the MMA warp already accumulates tile i+1 in the
 // other.
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int BK>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm3x(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAlo,
              const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBlo,
              const GemmParams p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, BK>;
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzle atoms need 1024-byte aligned tiles.
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -227,8 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else if (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / 32; j++) {
-              tma_load_2d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, k0);
-              if (three) tma_load_2d(salo + j * 4096, &tmAlo, &full[s], m0 + 32 * j, k0);
+              tma_load_2d(sa + j * (BK * 128), &tmA, &full[s], m0 + 32 * j, k0);
+              if (three) tma_load_2d(salo + j * (BK * 128), &tmAlo, &full[s], m0 + 32 * j, k0);
             }
           } else {
             tma_load_2d(sa, &tmA, &full[s], k0, m0);
@@ -240,8 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 32; j++) {
-              tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
-              if (three) tma_load_2d(sblo + j * 4096, &tmBlo, &full[s], n0 + 32 * j, k0);
+              tma_load_2d(sb + j * (BK * 128), &tmB, &full[s], n0 + 32 * j, k0);
+              if (three) tma_load_2d(sblo + j * (BK * 128), &tmBlo, &full[s], n0 + 32 * j, k0);
             }
           } else {
             tma_load_2d(sb, &tmB, &full[s], k0, n0);
@@ -259,18 +262,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
-      // K-major (128B swizzle, 8-row atoms of 128-byte rows): the next
-      // 8-element K slice is +32 bytes inside the swizzle row; SBO = 8 rows.
-      // MN-major (128B swizzle with 32-byte atomicity, 4-row atoms): a K row
-      // is 128 bytes (32 elements of M or N), the next 8 K rows are +1024
-      // bytes, SBO = 4 rows = 512 bytes, LBO = 4096 bytes between the
+      // K-major (BK*4-byte rows, 128B or 64B swizzle, 8-row atoms): the
+      // next 8-element K slice is +32 bytes inside the swizzle row; SBO = 8
+      // rows.  MN-major (128B swizzle with 32-byte atomicity, 4-row atoms):
+      // a K row is 128 bytes (32 elements of M or N), the next 8 K rows are
+      // +1024 bytes, SBO = 4 rows = 512 bytes, LBO = BK*128 bytes between the
       // 32-element MN chunks that TMA wrote as separate boxes.
+      constexpr uint32_t kmaj_lay = BK == 32 ? kLayoutSw128 : kLayoutSw64;
       constexpr uint32_t a_kstep = A_MN ? 1024 : 32;
       constexpr uint32_t b_kstep = B_MN ? 1024 : 32;
-      constexpr uint32_t a_lbo = A_MN ? 4096 : 16, a_sbo = A_MN ? 512 : 1024;
-      constexpr uint32_t b_lbo = B_MN ? 4096 : 16, b_sbo = B_MN ? 512 : 1024;
-      constexpr uint32_t a_lay = A_MN ? kLayoutSw128Base32 : kLayoutSw128;
-      constexpr uint32_t b_lay = B_MN ? kLayoutSw128Base32 : kLayoutSw128;
+      constexpr uint32_t a_lbo = A_MN ? BK * 128 : 16, a_sbo = A_MN ? 512 : 8 * BK * 4;
+      constexpr uint32_t b_lbo = B_MN ? BK * 128 : 16, b_sbo = B_MN ? 512 : 8 * BK * 4;
+      constexpr uint32_t a_lay = A_MN ? kLayoutSw128Base32 : kmaj_lay;
+      constexpr uint32_t b_lay = B_MN ? kLayoutSw128Base32 : kmaj_lay;
       bool ok = true;
       int it = 0, local = 0;
       SegIter segs(p, nk);
@@ -502,16 +506,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // tiles use the 128-byte swizzle; MN-major tiles the 128-byte swizzle with
 // 32-byte atoms (the layout tcgen05 reads MN-major tf32 operands in).
 static int make_map(CUtensorMap *map, const float *ptr, int inner, int outer, int ld,
-                    int box_rows, bool mn_major) {
+                    int box_rows, bool mn_major, int bk) {
   auto fn = encode_fn();
   if (!fn) return set_error(FG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+  // K-major: bk columns of K per row; MN-major: 32 columns of M or N
+  cuuint32_t box[2] = {(cuuint32_t)(mn_major ? 32 : bk), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)ptr, dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  mn_major  ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                  : bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B
+                             : CU_TENSOR_MAP_SWIZZLE_64B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(FG_ERR_CUDA,
@@ -525,12 +532,13 @@ static int make_map(CUtensorMap *map, const float *ptr, int inner, int outer, in
 // shared memory as rows/32 chunks of 32 K-rows x 128 bytes -- the same layout
 // the per-chunk 2-D loads produce.  Only valid when mn % 32 == 0 (the last
 // chunk then ends exactly at the end of the row).
-static int make_map_mn3d(CUtensorMap *map, const float *ptr, int mn, int K, int ld, int box_rows) {
+static int make_map_mn3d(CUtensorMap *map, const float *ptr, int mn, int K, int ld, int box_rows,
+                         int bk) {
   auto fn = encode_fn();
   if (!fn) return set_error(FG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {32, (cuuint64_t)K, (cuuint64_t)(mn / 32)};
   cuuint64_t strides[2] = {(cuuint64_t)ld * 4, 128};
-  cuuint32_t box[3] = {32, 32, (cuuint32_t)(box_rows / 32)};
+  cuuint32_t box[3] = {32, (cuuint32_t)bk, (cuuint32_t)(box_rows / 32)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)ptr, dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
@@ -548,7 +556,7 @@ static int make_map_mn3d(CUtensorMap *map, const float *ptr, int mn, int K, int 
 // grid shrinks so that every CTA gets >= max(nk/8, 24) k-blocks, and below
 // one CTA per tail tile the split is not used.
 static int plan_stream_k(GemmParams &p, int ntiles, int nk, int cap, float *ws,
-                         unsigned int *flags) {
+                         unsigned int *flags, int min_kb) {
   p.dp_tiles = ntiles;
   p.sk_units = 0;
   p.sk_ws = ws;
@@ -575,7 +583,7 @@ static int plan_stream_k(GemmParams &p, int ntiles, int nk, int cap, float *ws,
   }
   // Each partial costs about one epilogue pass (~2-3 k-blocks of MMA time),
   // so a CTA's share must be long enough to amortise it.
-  const long long min_share = nk / 8 > 24 ? nk / 8 : 24;
+  const long long min_share = nk / 8 > min_kb ? nk / 8 : min_kb;
   long long g = units / min_share;
   if (g > cap) g = cap;
   if (full > 0 && g < cap) return grid;  // waves need the whole grid
@@ -619,10 +627,10 @@ static int seg_min_k_setting() {
   return v;
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int BK>
 static int launch_t(const GemmPlan &pl, cudaStream_t st) {
-  using C = Cfg<BN>;
-  auto kern = k_gemm3x<BN, A_MN, B_MN>;
+  using C = Cfg<BN, BK>;
+  auto kern = k_gemm3x<BN, A_MN, B_MN, BK>;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -638,9 +646,10 @@ static int launch_t(const GemmPlan &pl, cudaStream_t st) {
   int cap = sms;  // persistent: one CTA per SM
   if (pl.max_ctas > 0 && pl.max_ctas < cap) cap = pl.max_ctas;
   GemmParams p = pl.p;
-  const int grid = plan_stream_k(p, ntiles, nk, cap, pl.sk_ws, pl.sk_flags);
+  // stream-K shares and segment lengths are set in 32-deep k-block units
+  const int grid = plan_stream_k(p, ntiles, nk, cap, pl.sk_ws, pl.sk_flags, 24 * 32 / BK);
   p.seg_ws = pl.seg_ws;
-  p.seg_kb = p.K >= seg_min_k_setting() ? seg_kb_setting() : 0;
+  p.seg_kb = p.K >= seg_min_k_setting() ? seg_kb_setting() * 32 / BK : 0;
   kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(pl.a, pl.alo, pl.b, pl.blo, p);
   FG_LAUNCH_TRY();
   return FG_OK;
@@ -667,29 +676,34 @@ int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, c
   // than 128 x 128 (the tensor cores re-read A for every 8-deep K slice);
   // narrow outputs keep the 128-wide tile.
   const int bn = (N >= 256) ? 256 : 128;
+  static const int bk = [] {
+    const char *e = getenv("FG_GEMM_BK");
+    return e && *e && atoi(e) == 16 ? 16 : 32;
+  }();
   int rc;
   // A: [M,K] K-major (box 32 x BM rows) or [K,M] MN-major (box 32 x 32)
   if (a_mn) {
-    if ((rc = make_map(&pl->a, a, M, K, lda, 32, true))) return rc;
-    if ((rc = make_map(&pl->alo, one ? a : a_lo, M, K, lda, 32, true))) return rc;
+    if ((rc = make_map(&pl->a, a, M, K, lda, bk, true, bk))) return rc;
+    if ((rc = make_map(&pl->alo, one ? a : a_lo, M, K, lda, bk, true, bk))) return rc;
   } else {
-    if ((rc = make_map(&pl->a, a, K, M, lda, BM, false))) return rc;
-    if ((rc = make_map(&pl->alo, one ? a : a_lo, K, M, lda, BM, false))) return rc;
+    if ((rc = make_map(&pl->a, a, K, M, lda, BM, false, bk))) return rc;
+    if ((rc = make_map(&pl->alo, one ? a : a_lo, K, M, lda, BM, false, bk))) return rc;
   }
   if (b_mn) {
-    if ((rc = make_map(&pl->b, b, N, K, ldb, 32, true))) return rc;
-    if ((rc = make_map(&pl->blo, one ? b : b_lo, N, K, ldb, 32, true))) return rc;
+    if ((rc = make_map(&pl->b, b, N, K, ldb, bk, true, bk))) return rc;
+    if ((rc = make_map(&pl->blo, one ? b : b_lo, N, K, ldb, bk, true, bk))) return rc;
   } else {
-    if ((rc = make_map(&pl->b, b, K, N, ldb, bn, false))) return rc;
-    if ((rc = make_map(&pl->blo, one ? b : b_lo, K, N, ldb, bn, false))) return rc;
+    if ((rc = make_map(&pl->b, b, K, N, ldb, bn, false, bk))) return rc;
+    if ((rc = make_map(&pl->blo, one ? b : b_lo, K, N, ldb, bn, false, bk))) return rc;
   }
+  pl->bk = bk;
   // single 3-D boxes for MN-major operands whose extent is a multiple of 32
   pl->p.a3d = 0;
   pl->p.b3d = 0;
   if (a_mn && M % 32 == 0) {
     CUtensorMap t0, t1;
-    if (make_map_mn3d(&t0, a, M, K, lda, BM) == FG_OK &&
-        make_map_mn3d(&t1, one ? a : a_lo, M, K, lda, BM) == FG_OK) {
+    if (make_map_mn3d(&t0, a, M, K, lda, BM, bk) == FG_OK &&
+        make_map_mn3d(&t1, one ? a : a_lo, M, K, lda, BM, bk) == FG_OK) {
       pl->a = t0;
       pl->alo = t1;
       pl->p.a3d = 1;
@@ -697,8 +711,8 @@ int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, c
   }
   if (b_mn && N % 32 == 0) {
     CUtensorMap t0, t1;
-    if (make_map_mn3d(&t0, b, N, K, ldb, bn) == FG_OK &&
-        make_map_mn3d(&t1, one ? b : b_lo, N, K, ldb, bn) == FG_OK) {
+    if (make_map_mn3d(&t0, b, N, K, ldb, bn, bk) == FG_OK &&
+        make_map_mn3d(&t1, one ? b : b_lo, N, K, ldb, bn, bk) == FG_OK) {
       pl->b = t0;
       pl->blo = t1;
       pl->p.b3d = 1;
@@ -767,20 +781,25 @@ void attach_stream_ws(GemmPlan *pl, cudaStream_t st) {
   stream_k_attach(pl, ws, sms);
 }
 
-int run_plan(const GemmPlan &pl, cudaStream_t st) {
+template <int BK>
+static int run_plan_bk(const GemmPlan &pl, cudaStream_t st) {
   if (pl.bn == 128) {
-    if (!pl.a_mn && !pl.b_mn) return launch_t<128, false, false>(pl, st);
-    if (!pl.a_mn && pl.b_mn) return launch_t<128, false, true>(pl, st);
-    if (pl.a_mn && !pl.b_mn) return launch_t<128, true, false>(pl, st);
-    return launch_t<128, true, true>(pl, st);
+    if (!pl.a_mn && !pl.b_mn) return launch_t<128, false, false, BK>(pl, st);
+    if (!pl.a_mn && pl.b_mn) return launch_t<128, false, true, BK>(pl, st);
+    if (pl.a_mn && !pl.b_mn) return launch_t<128, true, false, BK>(pl, st);
+    return launch_t<128, true, true, BK>(pl, st);
   }
   if (pl.bn == 256) {
-    if (!pl.a_mn && !pl.b_mn) return launch_t<256, false, false>(pl, st);
-    if (!pl.a_mn && pl.b_mn) return launch_t<256, false, true>(pl, st);
-    if (pl.a_mn && !pl.b_mn) return launch_t<256, true, false>(pl, st);
-    return launch_t<256, true, true>(pl, st);
+    if (!pl.a_mn && !pl.b_mn) return launch_t<256, false, false, BK>(pl, st);
+    if (!pl.a_mn && pl.b_mn) return launch_t<256, false, true, BK>(pl, st);
+    if (pl.a_mn && !pl.b_mn) return launch_t<256, true, false, BK>(pl, st);
+    return launch_t<256, true, true, BK>(pl, st);
   }
   return set_error(FG_ERR_UNSUPPORTED, "gemm: tile width %d not built", pl.bn);
+}
+
+int run_plan(const GemmPlan &pl, cudaStream_t st) {
+  return pl.bk == 16 ? run_plan_bk<16>(pl, st) : run_plan_bk<32>(pl, st);
 }
 
 }  // namespace gemm

@@ -283,8 +283,8 @@ struct Layer {
   fg::gemm::GemmPlan fwd, bwd_w, bwd_x;
   // dW as two launches over the halves of its output rows, so that with a
   // communicator the first half's all-reduce overlaps the second half's GEMM
-  // (layer 0, whose bucket is the last one of the backward pass, and with
-  // FG_COMM_SPLIT_ALL=1 every tensor-core layer)
+  // (every tensor-core layer; FG_COMM_SPLIT_ALL=0: layer 0 only, whose
+  // bucket is the last one of the backward pass)
   bool can_split_w = false;
   fg::gemm::GemmPlan bwd_w_half[2];
   // Peer-sharded mode: this layer's parameters of even / odd steps inside
@@ -297,13 +297,15 @@ struct Layer {
 
 size_t pad64(size_t n) { return (n + 63) / 64 * 64; }
 
-// FG_COMM_SPLIT_ALL=1: split every tensor-core layer's dW in two row halves
-// (the upper layers' SGD still waits for their dX GEMM), so each bucket's
-// first half is averaged while its second half is computed.
+// With a communicator every tensor-core layer's dW is computed in two row
+// halves (the upper layers' SGD still waits for their dX GEMM), so each
+// bucket's first half is averaged while its second half is computed
+// (8 x B200: 647 steps/s against 627 with only layer 0 split).
+// FG_COMM_SPLIT_ALL=0 splits layer 0 only.
 bool split_all_layers() {
   static const bool v = [] {
     const char *e = getenv("FG_COMM_SPLIT_ALL");
-    return e && *e && atoi(e) != 0;
+    return !(e && *e && atoi(e) == 0);
   }();
   return v;
 }

@@ -157,6 +157,9 @@ __device__ __forceinline__ void tmem_ld_wait() {
 //                           32-bit (tf32) operands
 constexpr uint32_t kLayoutSw128 = 2;
 constexpr uint32_t kLayoutSw128Base32 = 1;
+//   kLayoutSw64        (4): 64-byte swizzle of 16-byte chunks, 8-row atoms of
+//                           64-byte rows (K-major operands with 16-deep k-blocks)
+constexpr uint32_t kLayoutSw64 = 4;
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
                                               uint32_t sbo_bytes, uint32_t layout) {
