@@ -61,9 +61,10 @@ def load_peaks():
 
 # DRAM bytes per algorithmic flop of the config-5 forward GEMM launch, from one
 # ncu capture of `python bench.py --config c5gemm --steps 1 --warmup 3`
-# (dram__bytes_read.sum + dram__bytes_write.sum = 1.252e9 + 0.238e9 B over
-# 2.749e11 flop); `roofline.traffic` is this times the flops of one launch.
-GEMM_TRAFFIC_BYTES_PER_FLOP = 5.42e-3
+# (dram__bytes_read.sum + dram__bytes_write.sum = 1.385e9 + 0.443e9 B over
+# 2.749e11 flop, segmented accumulation on); `roofline.traffic` is this times
+# the flops of one launch.
+GEMM_TRAFFIC_BYTES_PER_FLOP = 6.65e-3
 # A timed region shorter than this runs at the burst clock; longer ones settle
 # at the sustained (power-capped) clock.
 SUSTAINED_AFTER_S = 2.0
@@ -379,7 +380,8 @@ def our_arm(args):
                        f"rate) / 3 (3xTF32 issues three MMAs per product); {peak_key} because the "
                        f"timed region lasts {region_s:.3f} s (burst below {SUSTAINED_AFTER_S} s)"),
         "traffic_basis": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the config-5 forward "
-                          "GEMM launch per algorithmic flop (5.42e-3 B/flop) x the flops of one launch"),
+                          f"GEMM launch per algorithmic flop ({GEMM_TRAFFIC_BYTES_PER_FLOP:.3g} B/flop, "
+                          "profiles/gemm3x_c5_shapes_ncu.md) x the flops of one launch"),
         "frac_of_tf32_issue": ((3 * achieved) / tf32_peak) if achieved else None,
         "tf32_tflops_measured": tf32_measured,
         "frac_vs_measured_tf32": ((3 * achieved) / tf32_measured) if achieved and tf32_measured
