@@ -41,9 +41,10 @@ constexpr int UMMA_K = 8;   // K of one kind::tf32 MMA
 constexpr int kThreads = 192;
 
 // BK: fp32 elements per k-block.  32 is one 128-byte swizzle row per K-major
-// operand row; 16 (64-byte swizzle) halves a stage, so the same shared
-// memory holds twice the stages and more operand bytes are in flight while
-// the tensor cores consume one stage (FG_GEMM_BK selects; 32 by default).
+// operand row; 16 (64-byte swizzle) and 8 (32-byte swizzle) shrink a stage,
+// so the same shared memory holds 2x / 4x the stages and more operand bytes
+// are in flight while the tensor cores consume one stage (FG_GEMM_BK
+// selects).
 template <int BN, int BK>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 4;
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // a K row is 128 bytes (32 elements of M or N), the next 8 K rows are
       // +1024 bytes, SBO = 4 rows = 512 bytes, LBO = BK*128 bytes between the
       // 32-element MN chunks that TMA wrote as separate boxes.
-      constexpr uint32_t kmaj_lay = BK == 32 ? kLayoutSw128 : kLayoutSw64;
+      constexpr uint32_t kmaj_lay = BK == 32 ? kLayoutSw128 : BK == 16 ? kLayoutSw64 : kLayoutSw32;
       constexpr uint32_t a_kstep = A_MN ? 1024 : 32;
       constexpr uint32_t b_kstep = B_MN ? 1024 : 32;
       constexpr uint32_t a_lbo = A_MN ? BK * 128 : 16, a_sbo = A_MN ? 512 : 8 * BK * 4;
@@ -518,7 +519,8 @@ static int make_map(CUtensorMap *map, const float *ptr, int inner, int outer, in
                   CU_TENSOR_MAP_INTERLEAVE_NONE,
                   mn_major  ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
                   : bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B
-                             : CU_TENSOR_MAP_SWIZZLE_64B,
+                  : bk == 16 ? CU_TENSOR_MAP_SWIZZLE_64B
+                             : CU_TENSOR_MAP_SWIZZLE_32B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(FG_ERR_CUDA,
@@ -678,7 +680,8 @@ int make_plan(int M, int N, int K, const float *a, const float *a_lo, int lda, c
   const int bn = (N >= 256) ? 256 : 128;
   static const int bk = [] {
     const char *e = getenv("FG_GEMM_BK");
-    return e && *e && atoi(e) == 16 ? 16 : 32;
+    const int v = e && *e ? atoi(e) : 16;
+    return v == 8 || v == 32 ? v : 16;
   }();
   int rc;
   // A: [M,K] K-major (box 32 x BM rows) or [K,M] MN-major (box 32 x 32)
@@ -799,6 +802,7 @@ static int run_plan_bk(const GemmPlan &pl, cudaStream_t st) {
 }
 
 int run_plan(const GemmPlan &pl, cudaStream_t st) {
+  if (pl.bk == 8) return run_plan_bk<8>(pl, st);
   return pl.bk == 16 ? run_plan_bk<16>(pl, st) : run_plan_bk<32>(pl, st);
 }
 

@@ -44,7 +44,7 @@ struct GemmPlan {
   CUtensorMap a, alo, b, blo;
   GemmParams p;
   int bn;
-  int bk;  // 16 or 32 fp32 elements per k-block (FG_GEMM_BK)
+  int bk;  // 8, 16 or 32 fp32 elements per k-block (FG_GEMM_BK, default 16)
   bool a_mn, b_mn;
   int max_ctas;  // persistent grid cap (0: one CTA per SM); leaves SMs to a concurrent collective
   // Stream-K workspace (null: whole tiles only).  Launches that share one

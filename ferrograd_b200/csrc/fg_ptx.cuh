@@ -160,6 +160,9 @@ constexpr uint32_t kLayoutSw128Base32 = 1;
 //   kLayoutSw64        (4): 64-byte swizzle of 16-byte chunks, 8-row atoms of
 //                           64-byte rows (K-major operands with 16-deep k-blocks)
 constexpr uint32_t kLayoutSw64 = 4;
+//   kLayoutSw32        (6): 32-byte swizzle of 16-byte chunks, 8-row atoms of
+//                           32-byte rows (K-major operands with 8-deep k-blocks)
+constexpr uint32_t kLayoutSw32 = 6;
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
                                               uint32_t sbo_bytes, uint32_t layout) {
