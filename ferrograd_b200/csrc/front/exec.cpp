@@ -1053,6 +1053,7 @@ bool try_gemm_bias(const ScheduleItem &item) {
       run_contraction(*c, c->a, c->b, item.output);
     } else {
       run_contraction(*c, c->a, c->b, item.output, FG_EPI_BIAS, fptr(bv->buf, bv->offset));
+      g_stats.gemm_bias++;
     }
     return true;
   }
@@ -1086,6 +1087,7 @@ bool try_gemm_relu_mask(const ScheduleItem &item) {
   if (c->M != v->shape[0] || c->N != v->shape[1]) return false;
   run_contraction(*c, c->a, c->b, item.output, FG_EPI_RELU_MASK, nullptr,
                   fptr(zv->buf, zv->offset), (int)v->shape[1]);
+  g_stats.gemm_mask++;
   return true;
 }
 

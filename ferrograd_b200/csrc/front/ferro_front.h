@@ -326,6 +326,8 @@ struct Stats {
   uint64_t xent = 0;         // fused cross-entropy passes (fg_xent_fwd_bwd)
   uint64_t xent_reused = 0;  // losses taken from an earlier XentGrad pass
   uint64_t sgd = 0;          // parameter stores run on the fused SGD kernel
+  uint64_t gemm_bias = 0;    // GEMMs with the bias epilogue (Linear::forward)
+  uint64_t gemm_mask = 0;    // GEMMs with the ReLU-mask epilogue (relu's gradient)
   uint64_t rendered = 0;     // launches of NVRTC-rendered kernels
   uint64_t compiled = 0;     // NVRTC compilations (program cache misses)
   uint64_t cache_hits = 0;

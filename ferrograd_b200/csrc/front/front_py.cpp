@@ -262,6 +262,8 @@ PYBIND11_MODULE(_front, m) {
     d["xent"] = s.xent;
     d["xent_reused"] = s.xent_reused;
     d["sgd"] = s.sgd;
+    d["gemm_bias"] = s.gemm_bias;
+    d["gemm_mask"] = s.gemm_mask;
     d["rendered"] = s.rendered;
     d["compiled"] = s.compiled;
     d["cache_hits"] = s.cache_hits;

@@ -63,6 +63,8 @@ def main(src, dst):
     out["gemm"] = np.array(st["gemm"])
     out["hand_reduce"] = np.array(st["hand_reduce"])
     out["schedule_hits"] = np.array(st["schedule_hits"])
+    for k in ("xent", "xent_reused", "sgd", "gemm_bias", "gemm_mask"):
+        out[k] = np.array(st[k])
     np.savez(dst, **out)
 
 

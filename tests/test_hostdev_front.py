@@ -129,6 +129,11 @@ def test_host_routed_step_matches_oracle_within_tolerance(oracle, hostdev, tmp_p
     dims, batch = (512, 256, 256, 10), 64
     x, t, r = run(hostdev, tmp_path, dims, batch, steps=1, routed=True)
     assert int(r["gemm"]) >= 4  # both forward contractions, both dW, the dX of layer 1
+    # the fused routes: one cross-entropy pass whose loss to_vec() reuses,
+    # SGD stores for the routed dW, the ReLU-masked dX as a GEMM epilogue
+    # (a zero-initialised bias takes the plain product on the first step)
+    assert int(r["xent"]) == 1 and int(r["xent_reused"]) == 1
+    assert int(r["sgd"]) >= 2 and int(r["gemm_mask"]) == 1
     nl = len(dims) - 1
     ws = [r[f"w0_{i}"] for i in range(nl)]
     bs = [r[f"b0_{i}"] for i in range(nl)]
@@ -147,6 +152,8 @@ def test_host_routed_steps_track_oracle(oracle, hostdev, tmp_path):
     stale residual would drift from the oracle here."""
     dims, batch = (512, 256, 256, 10), 64
     x, t, r = run(hostdev, tmp_path, dims, batch, steps=3, routed=True, seeds=(7, 8))
+    # steps 2 and 3 add the updated biases in the forward GEMMs' epilogue
+    assert int(r["gemm_bias"]) >= 4 and int(r["schedule_hits"]) >= 4
     ws = [r[f"w0_{i}"] for i in range(3)]
     bs = [r[f"b0_{i}"] for i in range(3)]
     w0 = [w.copy() for w in ws]
