@@ -169,6 +169,19 @@ int fg_device_open(int ordinal, fg_device **out) {
              ordinal, n);
   FG_CUDA_TRY(cudaSetDevice(ordinal));
   if (!fg::ctx_current()) return fg::set_error(FG_ERR_CUDA, "device context init failed");
+  // Buffers come from the device's stream-ordered pool (cudaMallocAsync).
+  // With the pool's default release threshold (0) every synchronisation
+  // hands freed memory back to the driver, and the next allocation maps it
+  // again; keeping it in this process's pool makes a training loop's
+  // per-step allocations cheap.  (A pool attribute of this process only.)
+  {
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, ordinal) == cudaSuccess) {
+      uint64_t keep = UINT64_MAX;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    cudaGetLastError();
+  }
   fg_device *d = new fg_device;
   d->ordinal = ordinal;
   cudaError_t e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
