@@ -61,10 +61,10 @@ def load_peaks():
 
 # DRAM bytes per algorithmic flop of the config-5 forward GEMM launch, from one
 # ncu capture of `python bench.py --config c5gemm --steps 1 --warmup 3`
-# (dram__bytes_read.sum + dram__bytes_write.sum = 1.385e9 + 0.443e9 B over
-# 2.749e11 flop, segmented accumulation on); `roofline.traffic` is this times
-# the flops of one launch.
-GEMM_TRAFFIC_BYTES_PER_FLOP = 6.65e-3
+# (dram__bytes_read.sum + dram__bytes_write.sum = 1.469e9 + 0.486e9 B over
+# 2.749e11 flop; 16-deep k-blocks, segmented accumulation on);
+# `roofline.traffic` is this times the flops of one launch.
+GEMM_TRAFFIC_BYTES_PER_FLOP = 7.11e-3
 # A timed region shorter than this runs at the burst clock; longer ones settle
 # at the sustained (power-capped) clock.
 SUSTAINED_AFTER_S = 2.0
