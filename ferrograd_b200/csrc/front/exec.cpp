@@ -974,7 +974,9 @@ void run_xent(const ScheduleItem &item, const UOp *node) {
     if (keyed) {
       done.push_back({vl->buf, vt->buf, vl->offset, vt->offset, vl->buf->version,
                       vt->buf->version, loss});
-      if (done.size() > 8) done.erase(done.begin());
+      // bounded: an entry keeps its logits and targets alive until its loss
+      // is read or it is evicted
+      if (done.size() > 4) done.erase(done.begin());
     }
   }
   g_stats.xent++;
