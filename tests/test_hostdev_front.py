@@ -274,3 +274,42 @@ def test_schedule_cache_replays_the_same_kernels(hostdev, tmp_path, routed, monk
     for k in off:
         if k not in ("schedule_hits",):
             assert np.array_equal(off[k], on[k]), k
+
+
+def test_host_fused_route_edge_cases(hostdev, tmp_path):
+    """Default mode's fused routes on their edges (tests/hostdev/run_front_edges.py):
+    targets needing a gradient keep the reference's decomposed graph; a loss
+    read before its gradient costs a second fused pass but gives the same
+    values; a scaled loss scales the fused gradient; graphs of alternating
+    shapes miss and hit the schedule cache correctly; an SGD store whose
+    gradient is not contiguous falls back to a rendered kernel."""
+    runner = os.path.join(os.path.dirname(hostdev), "run_front_edges.py")
+    dst = tmp_path / "edges.npz"
+    subprocess.run([sys.executable, runner, str(dst)], check=True, timeout=600)
+    r = dict(np.load(dst))
+    x, t, soft = (r[k].astype(np.float64) for k in ("x", "t", "soft"))
+    B = x.shape[0]
+    lse = np.log(np.exp(x - x.max(1, keepdims=True)).sum(1, keepdims=True)) + x.max(1, keepdims=True)
+    logp = x - lse
+    p = np.exp(logp)
+
+    def near(got, ref, tol=1e-5):
+        got, ref = np.asarray(got, np.float64).ravel(), np.asarray(ref, np.float64).ravel()
+        assert np.max(np.abs(got - ref)) <= tol * max(np.max(np.abs(ref)), 1e-30), (got, ref)
+
+    assert int(r["dec_xent"]) == 0
+    near(r["dec_loss"], -(soft * logp).sum() / B)
+    near(r["dec_dl"], (p * soft.sum(1, keepdims=True) - soft) / B)
+    near(r["dec_dt"], -logp / B)
+    assert int(r["first_xent"]) == 2 and int(r["first_reused"]) == 0
+    near(r["first_loss"], -(t * logp).sum() / B)
+    dl = (p * t.sum(1, keepdims=True) - t) / B
+    near(r["first_dl"], dl)
+    near(r["scaled_dl"], 3.0 * dl)
+    for i in range(4):
+        assert np.array_equal(r[f"alt{i}"], np.full(5 if i % 2 == 0 else 6, 8.0 * (i + 1) ** 2))
+    assert int(r["alt_hits"]) >= 2
+    w0 = r["w0"].astype(np.float64)
+    grad = np.arange(24, dtype=np.float64).reshape(4, 6).T
+    assert np.array_equal(r["w1"], (w0 - 0.5 * grad).astype(np.float32))
+    assert int(r["sgd_count"]) == 0
