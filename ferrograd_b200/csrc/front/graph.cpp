@@ -180,9 +180,17 @@ UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, std::vector<int64_t> arg = 
   const uint64_t h = node_hash(op, dt, rop, vbits, buf.get(), srcs, arg);
   auto &m = interner();
   auto range = m.equal_range(h);
-  for (auto it = range.first; it != range.second; ++it)
-    if (auto live = it->second.lock())
+  // Entries of nodes that died are dropped as the lookup meets them: a
+  // training loop re-creates the same nodes every step, and their stale
+  // entries would otherwise pile up under one hash until the next sweep.
+  for (auto it = range.first; it != range.second;) {
+    if (auto live = it->second.lock()) {
       if (same_node(*live, op, dt, rop, vbits, buf.get(), srcs, arg)) return live;
+      ++it;
+    } else {
+      it = m.erase(it);
+    }
+  }
   auto u = std::make_shared<UOp>();
   u->op = op;
   u->dtype = dt;
