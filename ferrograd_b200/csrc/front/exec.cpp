@@ -529,10 +529,9 @@ std::string spec_key(const RenderSpec &spec, const ParamSlots &ps,
   for (int64_t d : spec.domain) k.put(d);
   k.put((int64_t)spec.value_ctx.size());
   for (auto &c : spec.value_ctx) k.put_str(c);
-  std::unordered_map<const UOp *, int64_t> pos;
-  pos.reserve(order.size());
+  int64_t next = 0;
   for (auto &n : order) {
-    pos[n.get()] = (int64_t)pos.size();
+    n->topo_pos = next++;  // sources come first in `order`
     k.put((int64_t)n->op);
     k.put((int64_t)n->dtype);
     k.put((int64_t)n->reduce_op);
@@ -544,7 +543,7 @@ std::string spec_key(const RenderSpec &spec, const ParamSlots &ps,
     k.put((int64_t)n->arg.size());
     for (int64_t a : n->arg) k.put(a);
     k.put((int64_t)n->src.size());
-    for (auto &src : n->src) k.put(pos.at(src.get()));
+    for (auto &src : n->src) k.put(src->topo_pos);
     if (n->op == Op::Buffer) {
       k.put(ps.buffer_slot.at(n->buf.get()));
       k.put((int64_t)n->buf->count);

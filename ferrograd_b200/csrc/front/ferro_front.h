@@ -127,8 +127,9 @@ struct UOp {
   // Graph walks mark a node visited by stamping their own walk number here
   // (toposort); the front end is single-threaded, so no two walks overlap.
   mutable uint64_t walk_mark = 0;
-  // Scratch for the schedule cache: the node's position in the toposort of
-  // the graph being keyed (valid only inside that computation).
+  // Scratch for the structural keys (schedule cache, program lookup): the
+  // node's position in the toposort of the graph being keyed (valid only
+  // inside that computation).
   mutable int64_t topo_pos = -1;
 };
 
