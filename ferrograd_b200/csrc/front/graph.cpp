@@ -708,6 +708,10 @@ UOpP substitute_materialized(const UOpP &root, const ReplMap &repl) {
 
 UOpP substitute_with_map(const UOpP &root, const std::unordered_map<const UOp *, UOpP> &repl,
                          std::unordered_map<const UOp *, UOpP> &memo) {
+  // a replaced or already rewritten root needs no walk of what lies below it
+  // (a parameter's After(target, Store) after Sgd::step's realize)
+  if (auto r = repl.find(root.get()); r != repl.end()) return r->second;
+  if (auto m = memo.find(root.get()); m != memo.end()) return m->second;
   auto order = toposort_until(
       root, [&](const UOp *n) { return repl.count(n) > 0 || memo.count(n) > 0; });
   for (auto &node : order) {
