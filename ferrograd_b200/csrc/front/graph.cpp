@@ -173,7 +173,9 @@ void infer_shape(UOp &u) {
   }
 }
 
-UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, std::vector<int64_t> arg = {},
+const std::vector<int64_t> kNoArg;
+
+UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, const std::vector<int64_t> &arg = kNoArg,
             Op rop = Op::Add, double value = 0.0, const BufferP &buf = nullptr) {
   uint64_t vbits;
   std::memcpy(&vbits, &value, sizeof(double));
@@ -195,7 +197,7 @@ UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, std::vector<int64_t> arg = 
   u->op = op;
   u->dtype = dt;
   u->src = std::move(srcs);
-  u->arg = std::move(arg);
+  u->arg = arg;
   u->reduce_op = op == Op::ReduceAxis ? rop : Op::Add;
   u->value = value;
   u->buf = buf;
@@ -850,13 +852,28 @@ SchedulePlan schedule_many(const std::vector<UOpP> &exprs, bool with_inputs) {
 // ---- structural schedule cache ----------------------------------------------
 namespace {
 
-// A schedule whose leaves (buffers, literals) are placeholders: `leaves`
-// gives, per toposort position of the keyed graph, the template node that
-// stands for that position's leaf; item outputs are placeholder buffers too.
+// A schedule whose leaves (buffers, literals) are placeholders, stored as a
+// flat program: the template's nodes in toposort order (sources first), each
+// with what an instance puts in its place -- the keyed graph's leaf at a
+// toposort position, an item's fresh output buffer, or the template node
+// rebuilt over its sources' instances (the node itself when none changed).
+// An instance is then one pass over a vector, with no hash lookups.
 struct CachedSchedule {
-  std::vector<std::pair<size_t, UOpP>> leaves;
-  std::vector<ScheduleItem> items;
-  std::vector<std::pair<size_t, UOpP>> repl;  // (position of the replaced node, template)
+  enum Kind : uint8_t { Interior, Leaf, Output };
+  struct Node {
+    UOpP t;
+    Kind kind = Interior;
+    int64_t ref = 0;           // Leaf: toposort position; Output: item index
+    std::vector<int32_t> src;  // Interior: node indices of t's sources
+  };
+  struct Item {
+    Shape out_shape;
+    BufferP output;  // placeholder (dtype and count) or null for in-place items
+    int32_t value = -1, store_dest = -1;
+  };
+  std::vector<Node> nodes;
+  std::vector<Item> items;
+  std::vector<std::pair<size_t, int32_t>> repl;  // (position of the replaced node, node)
 };
 
 std::unordered_map<std::string, CachedSchedule> &schedule_cache() {
@@ -905,27 +922,46 @@ SchedulePlan schedule_cached(const std::vector<UOpP> &roots) {
   auto hit = cache.find(key);
   if (hit != cache.end()) {
     const CachedSchedule &cs = hit->second;
-    std::unordered_map<const UOp *, UOpP> m, memo;
-    for (auto &[pos, tleaf] : cs.leaves)
-      if (order[pos] != tleaf) m[tleaf.get()] = order[pos];
     SchedulePlan plan;
-    plan.items.reserve(cs.items.size());
-    for (const ScheduleItem &t : cs.items) {
-      ScheduleItem it;
-      it.out_shape = t.out_shape;
-      if (t.output) {
-        it.output = std::make_shared<DeviceBuffer>(t.output->dtype, t.output->count);
-        m[make_buffer(t.output).get()] = make_buffer(it.output);
+    plan.items.resize(cs.items.size());
+    for (size_t i = 0; i < cs.items.size(); i++) {
+      plan.items[i].out_shape = cs.items[i].out_shape;
+      if (const BufferP &o = cs.items[i].output)
+        plan.items[i].output = std::make_shared<DeviceBuffer>(o->dtype, o->count);
+    }
+    std::vector<UOpP> inst(cs.nodes.size());
+    for (size_t i = 0; i < cs.nodes.size(); i++) {
+      const CachedSchedule::Node &nd = cs.nodes[i];
+      switch (nd.kind) {
+        case CachedSchedule::Leaf:
+          inst[i] = order[(size_t)nd.ref];
+          break;
+        case CachedSchedule::Output:
+          inst[i] = make_buffer(plan.items[(size_t)nd.ref].output);
+          break;
+        case CachedSchedule::Interior: {
+          const UOp &t = *nd.t;
+          bool changed = false;
+          std::vector<UOpP> srcs;
+          srcs.reserve(nd.src.size());
+          for (size_t j = 0; j < nd.src.size(); j++) {
+            const UOpP &s = inst[(size_t)nd.src[j]];
+            changed |= s != t.src[j];
+            srcs.push_back(s);
+          }
+          inst[i] = changed ? intern(t.op, t.dtype, std::move(srcs), t.arg, t.reduce_op, t.value,
+                                     t.buf)
+                            : nd.t;
+          break;
+        }
       }
-      plan.items.push_back(std::move(it));
     }
     for (size_t i = 0; i < cs.items.size(); i++) {
-      const ScheduleItem &t = cs.items[i];
-      plan.items[i].value = substitute_with_map(t.value, m, memo);
-      if (t.store_dest) plan.items[i].store_dest = substitute_with_map(t.store_dest, m, memo);
+      plan.items[i].value = inst[(size_t)cs.items[i].value];
+      if (cs.items[i].store_dest >= 0)
+        plan.items[i].store_dest = inst[(size_t)cs.items[i].store_dest];
     }
-    for (auto &[pos, trep] : cs.repl)
-      plan.replacements[order[pos].get()] = substitute_with_map(trep, m, memo);
+    for (auto &[pos, idx] : cs.repl) plan.replacements[order[pos].get()] = inst[(size_t)idx];
     plan.keep = std::move(order);
     stats().schedule_hits++;
     return plan;
@@ -933,32 +969,69 @@ SchedulePlan schedule_cached(const std::vector<UOpP> &roots) {
   SchedulePlan plan = schedule_many(roots, false);
   // Template: every leaf and item output replaced by a placeholder that owns
   // no device memory, so the cache keeps no tensor alive.
-  CachedSchedule cs;
   std::unordered_map<const UOp *, UOpP> m, memo;
+  std::unordered_map<const UOp *, std::pair<CachedSchedule::Kind, int64_t>> role;
   for (size_t i = 0; i < order.size(); i++) {
     const UOpP &n = order[i];
     if (n->op == Op::Buffer) {
       UOpP ph = make_buffer(std::make_shared<DeviceBuffer>(n->buf->dtype, n->buf->count));
       m[n.get()] = ph;
-      cs.leaves.emplace_back(i, ph);
+      role[ph.get()] = {CachedSchedule::Leaf, (int64_t)i};
     } else if (n->op == Op::Const) {
-      cs.leaves.emplace_back(i, n);
+      role[n.get()] = {CachedSchedule::Leaf, (int64_t)i};
     }
   }
-  for (const ScheduleItem &it : plan.items)
-    if (it.output)
-      m[make_buffer(it.output).get()] =
-          make_buffer(std::make_shared<DeviceBuffer>(it.output->dtype, it.output->count));
+  std::vector<BufferP> outputs;
+  for (size_t i = 0; i < plan.items.size(); i++) {
+    const ScheduleItem &it = plan.items[i];
+    if (!it.output) {
+      outputs.push_back(nullptr);
+      continue;
+    }
+    outputs.push_back(std::make_shared<DeviceBuffer>(it.output->dtype, it.output->count));
+    UOpP ph = make_buffer(outputs.back());
+    m[make_buffer(it.output).get()] = ph;
+    role[ph.get()] = {CachedSchedule::Output, (int64_t)i};
+  }
+  std::vector<UOpP> troots;
+  std::vector<std::pair<UOpP, UOpP>> titems;
   for (const ScheduleItem &it : plan.items) {
-    ScheduleItem t;
-    t.out_shape = it.out_shape;
-    t.value = substitute_with_map(it.value, m, memo);
-    if (it.store_dest) t.store_dest = substitute_with_map(it.store_dest, m, memo);
-    if (it.output) t.output = m.at(make_buffer(it.output).get())->buf;
+    UOpP v = substitute_with_map(it.value, m, memo);
+    UOpP d = it.store_dest ? substitute_with_map(it.store_dest, m, memo) : nullptr;
+    troots.push_back(v);
+    if (d) troots.push_back(d);
+    titems.emplace_back(v, d);
+  }
+  std::vector<std::pair<size_t, UOpP>> trepl;
+  for (auto &[node, rep] : plan.replacements) {
+    trepl.emplace_back((size_t)node->topo_pos, substitute_with_map(rep, m, memo));
+    troots.push_back(trepl.back().second);
+  }
+  CachedSchedule cs;
+  std::unordered_map<const UOp *, int32_t> index;
+  std::vector<UOpP> torder = toposort(make_sink(troots));
+  torder.pop_back();  // the sink
+  for (const UOpP &n : torder) {
+    CachedSchedule::Node nd;
+    nd.t = n;
+    if (auto r = role.find(n.get()); r != role.end()) {
+      nd.kind = r->second.first;
+      nd.ref = r->second.second;
+    } else {
+      for (const UOpP &s : n->src) nd.src.push_back(index.at(s.get()));
+    }
+    index[n.get()] = (int32_t)cs.nodes.size();
+    cs.nodes.push_back(std::move(nd));
+  }
+  for (size_t i = 0; i < plan.items.size(); i++) {
+    CachedSchedule::Item t;
+    t.out_shape = plan.items[i].out_shape;
+    t.output = outputs[i];
+    t.value = index.at(titems[i].first.get());
+    if (titems[i].second) t.store_dest = index.at(titems[i].second.get());
     cs.items.push_back(std::move(t));
   }
-  for (auto &[node, rep] : plan.replacements)
-    cs.repl.emplace_back((size_t)node->topo_pos, substitute_with_map(rep, m, memo));
+  for (auto &[pos, rep] : trepl) cs.repl.emplace_back(pos, index.at(rep.get()));
   if (cache.size() >= 32) cache.clear();
   cache.emplace(std::move(key), std::move(cs));
   return plan;
