@@ -61,8 +61,11 @@ bool exact_mode() {
 }
 
 int debug_level() {
-  const char *e = std::getenv("DEBUG");
-  return e ? std::atoi(e) : 0;
+  static const int level = [] {
+    const char *e = std::getenv("DEBUG");
+    return e ? std::atoi(e) : 0;
+  }();
+  return level;
 }
 
 // DEBUG >= 2 prints each launch's execution time (src/tensor.rs:1017-1028,
@@ -507,18 +510,28 @@ void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelIn
 // but not which buffers fill the slots.  Encoding it costs a walk of the
 // expression; rendering costs ~60 us per kernel, so steady-state steps look
 // programs up by this key and render only on a miss.
+// Words collected in a vector (an inlined push_back each) and turned into
+// the string key with one copy at the end.
 struct KeyBuf {
-  std::string s;
-  void put(int64_t v) { s.append(reinterpret_cast<const char *>(&v), sizeof(v)); }
+  std::vector<int64_t> w;
+  void put(int64_t v) { w.push_back(v); }
   void put_str(const std::string &t) {
     put((int64_t)t.size());
-    s.append(t);
+    for (size_t i = 0; i < t.size(); i += 8) {
+      int64_t v = 0;
+      std::memcpy(&v, t.data() + i, std::min<size_t>(8, t.size() - i));
+      put(v);
+    }
+  }
+  std::string str() const {
+    return std::string(reinterpret_cast<const char *>(w.data()), w.size() * sizeof(int64_t));
   }
 };
 
 std::string spec_key(const RenderSpec &spec, const ParamSlots &ps,
                      const std::vector<UOpP> &order) {
   KeyBuf k;
+  k.w.reserve(16 + order.size() * 12);
   k.put((int64_t)spec.store);
   k.put(spec.pitch);
   k.put((int64_t)spec.out_dtype);
@@ -553,7 +566,7 @@ std::string spec_key(const RenderSpec &spec, const ParamSlots &ps,
     }
   }
   k.put(spec.store == RenderSpec::View ? 1 : 0);
-  return k.s;
+  return k.str();
 }
 
 struct CachedKernel {
@@ -1192,9 +1205,12 @@ void run_item(const ScheduleItem &item) {
       const bool is_root = !item.store_dest && root_reduce(item.value) == n.get();
       BufferP out = is_root ? item.output : temp_buffer(n->dtype, numel(n->shape));
       if (c) {
-        std::unordered_map<const UOp *, UOpP> memo_a, memo_b;
-        UOpP a = repl.empty() ? c->a : substitute_with_map(c->a, repl, memo_a);
-        UOpP b = repl.empty() ? c->b : substitute_with_map(c->b, repl, memo_b);
+        UOpP a = c->a, b = c->b;
+        if (!repl.empty()) {
+          Rewriter rewrite(repl);
+          a = rewrite(c->a);
+          b = rewrite(c->b);
+        }
         run_contraction(*c, a, b, out);
       } else {
         run_hand_reduce(*h, out);
@@ -1205,8 +1221,7 @@ void run_item(const ScheduleItem &item) {
       repl[n.get()] = sub;
     }
     if (!repl.empty()) {
-      std::unordered_map<const UOp *, UOpP> memo;
-      value = substitute_with_map(item.value, repl, memo);
+      value = Rewriter(repl)(item.value);
     }
   }
   bool wrote_lo = false;

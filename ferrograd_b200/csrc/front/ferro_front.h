@@ -131,6 +131,10 @@ struct UOp {
   // node's position in the toposort of the graph being keyed (valid only
   // inside that computation).
   mutable int64_t topo_pos = -1;
+  // A Rewriter's memo: the node's rewritten form is slot memo_slot of the
+  // rewriter whose number is memo_mark (one rewriter is live at a time).
+  mutable uint64_t memo_mark = 0;
+  mutable uint32_t memo_slot = 0;
 };
 
 // Interned constructors (src/uop.rs:536-760, 926-1040): structurally equal

@@ -41,8 +41,37 @@ struct View {
 std::optional<View> try_view(const UOp *n);
 
 UOpP substitute_materialized(const UOpP &root, const std::map<const UOp *, UOpP> &repl);
-UOpP substitute_with_map(const UOpP &root, const std::unordered_map<const UOp *, UOpP> &repl,
-                         std::unordered_map<const UOp *, UOpP> &memo);
+
+// Rewrites graphs under one replacement map: every node at or above a
+// replaced node is rebuilt (interned) over its sources' rewritten forms, and
+// the rest come back unchanged.  Each node's result is remembered in the node
+// itself (UOp::memo_mark / memo_slot) instead of a hash map, so the subgraphs
+// shared by all graphs given to one Rewriter are rewritten once.  Only one
+// Rewriter may be live at a time (a second one throws).
+class Rewriter {
+ public:
+  template <typename Map>
+  explicit Rewriter(const Map &repl) : Rewriter() {
+    for (auto &[node, with] : repl) remember(node, with);
+  }
+  ~Rewriter();
+  Rewriter(const Rewriter &) = delete;
+  Rewriter &operator=(const Rewriter &) = delete;
+  // Adds a replacement (for a node this rewriter has not met yet).
+  void replace(const UOp *node, const UOpP &with) { remember(node, with); }
+  UOpP operator()(const UOpP &root);
+
+ private:
+  Rewriter();
+  bool done(const UOp *n) const { return n->memo_mark == mark_; }
+  void remember(const UOp *n, UOpP v) {
+    n->memo_mark = mark_;
+    n->memo_slot = (uint32_t)vals_.size();
+    vals_.push_back(std::move(v));
+  }
+  uint64_t mark_;
+  std::vector<UOpP> vals_;
+};
 
 // ---- CUDA C renderer (render.cpp) -----------------------------------------
 // One rendered kernel: thread t of the grid evaluates `value` at the domain

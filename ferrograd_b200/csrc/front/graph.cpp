@@ -708,35 +708,48 @@ UOpP substitute_materialized(const UOpP &root, const ReplMap &repl) {
   return sub[root.get()];
 }
 
-UOpP substitute_with_map(const UOpP &root, const std::unordered_map<const UOp *, UOpP> &repl,
-                         std::unordered_map<const UOp *, UOpP> &memo) {
-  // a replaced or already rewritten root needs no walk of what lies below it
-  // (a parameter's After(target, Store) after Sgd::step's realize)
-  if (auto r = repl.find(root.get()); r != repl.end()) return r->second;
-  if (auto m = memo.find(root.get()); m != memo.end()) return m->second;
-  auto order = toposort_until(
-      root, [&](const UOp *n) { return repl.count(n) > 0 || memo.count(n) > 0; });
-  for (auto &node : order) {
-    if (memo.count(node.get())) continue;
-    auto r = repl.find(node.get());
-    if (r != repl.end()) {
-      memo[node.get()] = r->second;
+namespace {
+bool g_rewriter_live = false;
+}  // namespace
+
+Rewriter::Rewriter() {
+  if (g_rewriter_live) throw Panic("Rewriter: another rewriter is live");
+  g_rewriter_live = true;
+  static uint64_t rewriters = 0;
+  mark_ = ++rewriters;
+}
+
+Rewriter::~Rewriter() { g_rewriter_live = false; }
+
+UOpP Rewriter::operator()(const UOpP &root) {
+  // Iterative post-order DFS that stops at nodes already rewritten (or
+  // replaced); a node is rebuilt once all its sources are done.
+  if (done(root.get())) return vals_[root->memo_slot];
+  std::vector<std::pair<const UOpP *, bool>> stack{{&root, false}};
+  while (!stack.empty()) {
+    auto [hp, processed] = stack.back();
+    stack.pop_back();
+    const UOp *node = hp->get();
+    if (done(node)) continue;
+    if (!processed) {
+      stack.push_back({hp, true});
+      for (auto it = node->src.rbegin(); it != node->src.rend(); ++it)
+        if (!done(it->get())) stack.push_back({&*it, false});
       continue;
     }
     bool changed = false;
+    for (const UOpP &s : node->src) changed |= vals_[s->memo_slot] != s;
+    if (!changed) {
+      remember(node, *hp);
+      continue;
+    }
     std::vector<UOpP> srcs;
     srcs.reserve(node->src.size());
-    for (auto &s : node->src) {
-      UOpP ns = memo.at(s.get());
-      changed |= ns != s;
-      srcs.push_back(ns);
-    }
-    memo[node.get()] =
-        changed ? intern(node->op, node->dtype, std::move(srcs), node->arg, node->reduce_op,
-                         node->value, node->buf)
-                : node;
+    for (const UOpP &s : node->src) srcs.push_back(vals_[s->memo_slot]);
+    remember(node, intern(node->op, node->dtype, std::move(srcs), node->arg, node->reduce_op,
+                          node->value, node->buf));
   }
-  return memo.at(root.get());
+  return vals_[root->memo_slot];
 }
 
 ParamSlots collect_params(const UOpP &root, int slot_offset) {
@@ -893,9 +906,9 @@ bool schedule_cache_on() {
 // order its op, dtype, reduce op, args and source positions, a buffer's
 // dtype and size; and the mode (exact mode schedules differently).
 std::string structure_key(const std::vector<UOpP> &order) {
-  std::string k;
-  k.reserve(order.size() * 48);
-  auto put = [&k](int64_t v) { k.append(reinterpret_cast<const char *>(&v), sizeof(v)); };
+  std::vector<int64_t> k;
+  k.reserve(2 + order.size() * 8);
+  auto put = [&k](int64_t v) { k.push_back(v); };
   put(exact_mode() ? 1 : 0);
   put((int64_t)order.size());
   for (size_t i = 0; i < order.size(); i++) {
@@ -908,7 +921,7 @@ std::string structure_key(const std::vector<UOpP> &order) {
     for (auto &s : n->src) put(s->topo_pos);
     if (n->op == Op::Buffer) put((int64_t)n->buf->count);
   }
-  return k;
+  return std::string(reinterpret_cast<const char *>(k.data()), k.size() * sizeof(int64_t));
 }
 
 }  // namespace
@@ -969,7 +982,7 @@ SchedulePlan schedule_cached(const std::vector<UOpP> &roots) {
   SchedulePlan plan = schedule_many(roots, false);
   // Template: every leaf and item output replaced by a placeholder that owns
   // no device memory, so the cache keeps no tensor alive.
-  std::unordered_map<const UOp *, UOpP> m, memo;
+  std::unordered_map<const UOp *, UOpP> m;
   std::unordered_map<const UOp *, std::pair<CachedSchedule::Kind, int64_t>> role;
   for (size_t i = 0; i < order.size(); i++) {
     const UOpP &n = order[i];
@@ -995,16 +1008,17 @@ SchedulePlan schedule_cached(const std::vector<UOpP> &roots) {
   }
   std::vector<UOpP> troots;
   std::vector<std::pair<UOpP, UOpP>> titems;
+  Rewriter rewrite(m);
   for (const ScheduleItem &it : plan.items) {
-    UOpP v = substitute_with_map(it.value, m, memo);
-    UOpP d = it.store_dest ? substitute_with_map(it.store_dest, m, memo) : nullptr;
+    UOpP v = rewrite(it.value);
+    UOpP d = it.store_dest ? rewrite(it.store_dest) : nullptr;
     troots.push_back(v);
     if (d) troots.push_back(d);
     titems.emplace_back(v, d);
   }
   std::vector<std::pair<size_t, UOpP>> trepl;
   for (auto &[node, rep] : plan.replacements) {
-    trepl.emplace_back((size_t)node->topo_pos, substitute_with_map(rep, m, memo));
+    trepl.emplace_back((size_t)node->topo_pos, rewrite(rep));
     troots.push_back(trepl.back().second);
   }
   CachedSchedule cs;

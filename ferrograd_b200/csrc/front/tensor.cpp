@@ -104,13 +104,12 @@ std::vector<Tensor> Tensor::live_tensors() {
 void Tensor::apply_map_to_tensors(const std::map<const UOp *, UOpP> &replacements) {
   // src/tensor.rs:222-252: one combined substitution over all affected roots.
   if (replacements.empty()) return;
-  std::unordered_map<const UOp *, UOpP> repl(replacements.begin(), replacements.end());
-  std::unordered_map<const UOp *, UOpP> memo;
   // One memoised rewrite over all live tensors: shared subgraphs are walked
   // once, and a graph that reaches no replaced node comes back unchanged.
+  Rewriter rewrite(replacements);
   for (Tensor &t : live_tensors()) {
     UOpP cur = t.uop();
-    UOpP rewritten = substitute_with_map(cur, repl, memo);
+    UOpP rewritten = rewrite(cur);
     if (rewritten != cur) t.set_uop(rewritten);
   }
 }
