@@ -354,56 +354,90 @@ std::optional<View> try_view(const UOp *n) {
 
 namespace {
 
-// Which axes of a node's value vary (used to classify contraction operands).
-std::vector<bool> deps(const UOp *n) {
-  const size_t r = n->has_shape ? n->shape.size() : 0;
-  std::vector<bool> d(r, false);
+// Which axes of a node's value vary (used to classify contraction operands):
+// bit a of `bits` for axis a; `all` marks every axis (set conservatively for
+// an axis past 63, which no contraction operand has).
+struct AxisSet {
+  size_t rank = 0;
+  uint64_t bits = 0;
+  bool all = false;
+  bool test(size_t a) const { return all || (a < 64 && ((bits >> a) & 1)); }
+  void set(size_t a) {
+    if (a < 64)
+      bits |= uint64_t(1) << a;
+    else
+      all = true;
+  }
+  bool any() const { return all || bits != 0; }
+};
+
+AxisSet deps(const UOp *n) {
+  AxisSet d;
+  d.rank = n->has_shape ? n->shape.size() : 0;
+  const size_t r = d.rank;
   switch (n->op) {
     case Op::Const:
       return d;
     case Op::Buffer:
-      if (r && n->buf->count > 1) d[0] = true;
+      if (r && n->buf->count > 1) d.set(0);
       return d;
     case Op::Reshape: {
-      auto sd = deps(n->src[0].get());
+      const AxisSet sd = deps(n->src[0].get());
       const Shape &ss = n->src[0]->shape, &ds = n->shape;
-      std::vector<size_t> dn, sn;
+      // the non-unit axes of both shapes, paired in order when they agree
+      size_t dn[64], sn[64], nd = 0, ns = 0;
+      bool same = true;
       for (size_t a = 0; a < ds.size(); a++)
-        if (ds[a] != 1) dn.push_back(a);
-      for (size_t a = 0; a < ss.size(); a++)
-        if (ss[a] != 1) sn.push_back(a);
-      bool same = dn.size() == sn.size();
-      for (size_t i = 0; same && i < dn.size(); i++) same = ds[dn[i]] == ss[sn[i]];
+        if (ds[a] != 1) {
+          if (nd == 64) { same = false; break; }
+          dn[nd++] = a;
+        }
+      for (size_t a = 0; same && a < ss.size(); a++)
+        if (ss[a] != 1) {
+          if (ns == 64) { same = false; break; }
+          sn[ns++] = a;
+        }
+      same = same && nd == ns;
+      for (size_t i = 0; same && i < nd; i++) same = ds[dn[i]] == ss[sn[i]];
       if (same) {
-        for (size_t i = 0; i < dn.size(); i++) d[dn[i]] = sd[sn[i]];
-      } else if (std::any_of(sd.begin(), sd.end(), [](bool b) { return b; })) {
-        for (size_t i : dn) d[i] = true;
+        for (size_t i = 0; i < nd; i++)
+          if (sd.test(sn[i])) d.set(dn[i]);
+      } else if (sd.any()) {
+        for (size_t a = 0; a < ds.size(); a++)
+          if (ds[a] != 1) d.set(a);
       }
       return d;
     }
     case Op::Permute: {
-      auto sd = deps(n->src[0].get());
-      for (size_t i = 0; i < r; i++) d[i] = sd[(size_t)n->arg[i]];
+      const AxisSet sd = deps(n->src[0].get());
+      for (size_t i = 0; i < r; i++)
+        if (sd.test((size_t)n->arg[i])) d.set(i);
       return d;
     }
     case Op::Expand:
     case Op::Shrink: {
-      auto sd = deps(n->src[0].get());
-      for (size_t a = 0; a < r && a < sd.size(); a++) d[a] = sd[a] && n->shape[a] != 1;
+      const AxisSet sd = deps(n->src[0].get());
+      for (size_t a = 0; a < r && a < sd.rank; a++)
+        if (sd.test(a) && n->shape[a] != 1) d.set(a);
       return d;
     }
     case Op::ReduceAxis: {
-      auto sd = deps(n->src[0].get());
-      for (size_t a = 0; a < r; a++) d[a] = sd[a];
-      for (int64_t a : n->arg) d[(size_t)a] = false;
+      const AxisSet sd = deps(n->src[0].get());
+      for (size_t a = 0; a < r; a++)
+        if (sd.test(a) && std::find(n->arg.begin(), n->arg.end(), (int64_t)a) == n->arg.end())
+          d.set(a);
       return d;
     }
     default: {
       for (auto &s : n->src) {
         if (s->op == Op::Const) continue;
-        auto sd = deps(s.get());
-        if (sd.size() != r) return std::vector<bool>(r, true);
-        for (size_t a = 0; a < r; a++) d[a] = d[a] || sd[a];
+        const AxisSet sd = deps(s.get());
+        if (sd.rank != r) {
+          d.all = true;
+          return d;
+        }
+        d.bits |= sd.bits;
+        d.all = d.all || sd.all;
       }
       return d;
     }
@@ -634,17 +668,23 @@ std::optional<Contraction> match_contraction(const UOp *n) {
   if (m->op != Op::Mul || !m->has_shape || m->shape.size() != 3) return {};
   const size_t r = (size_t)n->arg[0];
   size_t i = r == 0 ? 1 : 0, j = r == 2 ? 1 : 2;
-  auto dp = deps(m->src[0].get()), dq = deps(m->src[1].get());
-  if (dp.size() != 3 || dq.size() != 3) return {};
+  const Shape &s = m->shape;
+  if (s[i] * s[j] * s[r] < kGemmMinWork) return {};
+  // Shorter than one 32-deep k-block, a contraction is an HBM pass over its
+  // output (the 10-class layer's dX: K = 10); the tensor-core tile pipeline
+  // only adds overhead there, so it is rendered (~7x faster measured).
+  if (s[r] < 32) return {};
+  const AxisSet dp = deps(m->src[0].get()), dq = deps(m->src[1].get());
+  if (dp.rank != 3 || dq.rank != 3) return {};
   Contraction c;
   c.reduce = n;
   c.r = r;
-  if (!dp[j] && !dq[i] && (dp[i] || dq[j])) {
+  if (!dp.test(j) && !dq.test(i) && (dp.test(i) || dq.test(j))) {
     c.a = m->src[0];
     c.b = m->src[1];
     c.ai = i;
     c.bj = j;
-  } else if (!dq[j] && !dp[i] && (dq[i] || dp[j])) {
+  } else if (!dq.test(j) && !dp.test(i) && (dq.test(i) || dp.test(j))) {
     c.a = m->src[1];
     c.b = m->src[0];
     c.ai = i;
@@ -652,15 +692,9 @@ std::optional<Contraction> match_contraction(const UOp *n) {
   } else {
     return {};
   }
-  const Shape &s = m->shape;
   c.M = s[i];
   c.N = s[j];
   c.K = s[r];
-  if (c.M * c.N * c.K < kGemmMinWork) return {};
-  // Shorter than one 32-deep k-block, a contraction is an HBM pass over its
-  // output (the 10-class layer's dX: K = 10); the tensor-core tile pipeline
-  // only adds overhead there, so it is rendered (~7x faster measured).
-  if (c.K < 32) return {};
   return c;
 }
 

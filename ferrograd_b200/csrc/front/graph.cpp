@@ -441,47 +441,49 @@ std::vector<UOpP> gradient_for_op(const UOpP &nodep, const UOpP &grad) {
 
 std::map<const UOp *, UOpP> compute_gradient(const UOpP &root, const UOpP &root_grad,
                                              const std::vector<UOpP> &targets) {
+  // Per-node state lives in vectors indexed by toposort position
+  // (UOp::topo_pos), so the walk does no hash lookups.
   auto order = toposort(root);
-  auto consumers = consumer_map(order);
-  // needed_nodes (src/gradient.rs:64-81): nodes on a path from a target up
-  // to the root, found by walking consumers.
-  std::unordered_set<const UOp *> needed;
-  std::vector<const UOp *> stack;
-  for (auto &t : targets) stack.push_back(t.get());
-  while (!stack.empty()) {
-    const UOp *n = stack.back();
-    stack.pop_back();
-    if (!needed.insert(n).second) continue;
-    auto it = consumers.find(n);
-    if (it != consumers.end())
-      for (const UOp *c : it->second) stack.push_back(c);
+  const size_t n = order.size();
+  if (n == 0) throw Panic("compute_gradient: empty graph");
+  for (size_t i = 0; i < n; i++) order[i]->topo_pos = (int64_t)i;
+  auto pos_of = [&](const UOp *u) -> int64_t {
+    const int64_t p = u->topo_pos;
+    return p >= 0 && (size_t)p < n && order[(size_t)p].get() == u ? p : -1;
+  };
+  // needed_nodes (src/gradient.rs:64-81): the nodes on a path from a target
+  // up to the root -- a node is needed when it is a target or one of its
+  // sources is needed, decided in one pass in toposort order.
+  std::vector<char> needed(n, 0);
+  for (auto &t : targets)
+    if (int64_t p = pos_of(t.get()); p >= 0) needed[(size_t)p] = 1;
+  for (size_t i = 0; i < n; i++) {
+    if (needed[i]) continue;
+    for (const UOpP &s : order[i]->src)
+      if (needed[(size_t)s->topo_pos]) {
+        needed[i] = 1;
+        break;
+      }
   }
-  needed.insert(root.get());
+  needed[n - 1] = 1;  // the root
 
-  std::unordered_map<const UOp *, UOpP> grads;
-  grads[root.get()] = root_grad;
-  for (auto it = order.rbegin(); it != order.rend(); ++it) {
-    const UOpP &node = *it;
-    if (!needed.count(node.get())) continue;
-    auto g = grads.find(node.get());
-    if (g == grads.end()) continue;
-    UOpP grad = g->second;
-    auto local = gradient_for_op(node, grad);
+  std::vector<UOpP> grads(n);
+  grads[n - 1] = root_grad;
+  for (size_t k = n; k-- > 0;) {
+    const UOpP &node = order[k];
+    if (!needed[k] || !grads[k]) continue;
+    auto local = gradient_for_op(node, grads[k]);
     for (size_t i = 0; i < node->src.size() && i < local.size(); i++) {
       if (!local[i]) continue;
-      const UOp *s = node->src[i].get();
-      if (!needed.count(s)) continue;
-      auto e = grads.find(s);
-      if (e == grads.end())
-        grads[s] = local[i];
-      else
-        e->second = make_add(e->second, local[i]);
+      const size_t sp = (size_t)node->src[i]->topo_pos;
+      if (!needed[sp]) continue;
+      grads[sp] = grads[sp] ? make_add(grads[sp], local[i]) : local[i];
     }
   }
   std::map<const UOp *, UOpP> result;
   for (auto &t : targets) {
-    auto g = grads.find(t.get());
-    result[t.get()] = g != grads.end() ? g->second : zero_like(t.get());
+    const int64_t p = pos_of(t.get());
+    result[t.get()] = p >= 0 && grads[(size_t)p] ? grads[(size_t)p] : zero_like(t.get());
   }
   return result;
 }

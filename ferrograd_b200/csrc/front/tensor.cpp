@@ -438,11 +438,15 @@ std::vector<Tensor> Tensor::gradient(const std::vector<Tensor> &targets) const {
 void Tensor::backward() const {
   // src/tensor.rs:973-998.
   require(numel() == 1, "backward requires a scalar loss");
-  std::unordered_set<const UOp *> all;
-  for (auto &n : toposort(uop())) all.insert(n.get());
+  // graph membership by toposort position (UOp::topo_pos), not a hash set
+  const std::vector<UOpP> all = toposort(uop());
+  for (size_t i = 0; i < all.size(); i++) all[i]->topo_pos = (int64_t)i;
+  auto in_graph = [&all](const UOp *u) {
+    return u->topo_pos >= 0 && (size_t)u->topo_pos < all.size() && all[(size_t)u->topo_pos].get() == u;
+  };
   std::vector<Tensor> targets;
   for (Tensor &t : live_tensors())
-    if (t.requires_grad() && all.count(t.uop().get())) targets.push_back(t);
+    if (t.requires_grad() && in_graph(t.uop().get())) targets.push_back(t);
   if (targets.empty()) return;
   std::vector<UOpP> tu;
   for (auto &t : targets) tu.push_back(t.uop());
