@@ -287,7 +287,11 @@ std::vector<UOpP> toposort(const UOpP &root) {
   const uint64_t mark = new_walk();
   auto visited = [mark](const UOp *n) { return n->walk_mark == mark; };
   std::vector<UOpP> out;
-  std::vector<std::pair<const UOpP *, bool>> stack{{&root, false}};
+  out.reserve(64);
+  // the stack's storage is kept across calls (no walk runs inside another)
+  static std::vector<std::pair<const UOpP *, bool>> stack;
+  stack.clear();
+  stack.push_back({&root, false});
   while (!stack.empty()) {
     auto [hp, processed] = stack.back();
     stack.pop_back();
