@@ -271,6 +271,11 @@ class Tensor {
   void backward() const;
 
   UOpP uop() const;
+  // Tensor::apply_map_to_tensors (src/tensor.rs:222-252): every live
+  // tensor's graph rewritten with a schedule's replacements (realized nodes
+  // -> their buffers).  Public so that another executor of a SchedulePlan
+  // (the restated CPU lowering under tests/lowering) can finish a realize.
+  static void apply_map_to_tensors(const std::map<const UOp *, UOpP> &repl);
 
  private:
   explicit Tensor(std::shared_ptr<TensorInner> p) : p_(std::move(p)) {}
@@ -282,7 +287,6 @@ class Tensor {
   Tensor binary(const Tensor &o, Op op, DType out) const;
   Tensor broadcasted(const Tensor &o, Op op, DType out) const;
   static std::vector<Tensor> live_tensors();
-  static void apply_map_to_tensors(const std::map<const UOp *, UOpP> &repl);
   std::shared_ptr<TensorInner> p_;
 };
 

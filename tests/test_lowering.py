@@ -1,0 +1,158 @@
+"""The reference's CPU lowering restated (tests/lowering/) as a second oracle:
+rangeify -> upcast / unroll / symbolic -> late expand -> devectorize ->
+linearize -> the clang renderer, applied to the front end's scheduled
+proto-kernels, the emitted C compiled by gcc and run on the host test device
+(tests/hostdev), where device buffers are host memory.
+
+Pinned three ways: the reference's own unit tests of those passes, restated
+(tests/lowering/cases.cpp); whole exact-mode training steps whose every
+kernel is the reference's C, bit-identical to the C oracle; and two probes of
+the upcast path, where the passes as written give other values than their
+evident intent (kir.h lists the three behaviours) -- reproduced here as
+read, and removed by the repairs, after which the values are exact again.
+"""
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from ferrograd_b200 import data
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LOWERING = os.path.join(HERE, "lowering")
+
+
+@pytest.fixture(scope="module")
+def lowering():
+    spec = importlib.util.spec_from_file_location("lowering_build",
+                                                  os.path.join(LOWERING, "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.build()
+    return LOWERING
+
+
+@pytest.fixture(scope="module")
+def cases(lowering):
+    env = dict(os.environ)
+    env.pop("OPT", None)
+    out = subprocess.run([sys.executable, os.path.join(lowering, "run_cases.py")], check=True,
+                         timeout=900, env=env, capture_output=True, text=True).stdout
+    return json.loads(out)
+
+
+def test_reference_unit_tests_of_the_lowering_passes(cases):
+    """rangeify.rs, upcast.rs, unroll.rs, symbolic.rs, expand.rs,
+    devectorize.rs, linearize.rs and clang.rs tests, restated over the kernel
+    IR with the reference's assertions (the clang ones compile and run the
+    emitted C)."""
+    failed = {k: v for k, v in cases["cases"].items() if v != "ok"}
+    assert not failed, failed
+    assert len(cases["cases"]) >= 30
+    prefixes = {k.split("::")[0] for k in cases["cases"]}
+    assert prefixes == {"rangeify", "upcast", "unroll", "symbolic", "expand", "devectorize",
+                        "linearize", "clang"}
+
+
+def test_upcast_path_as_written_and_repaired(cases):
+    """Column sum of a [16, 8] integer matrix: upcast splits output axis 1,
+    unroll splits reduced axis 0, and the lane groups formed as
+    src/devectorize.rs:171 forms them sum across output columns -- values
+    wrong as written, exact with the lanes grouped by axis.  A contraction
+    stored into a [16, 16] output: its four lane accumulators lose their tags
+    when linearize rebuilds the nested range and collapse into one -- one
+    `acc` declared as written, four and exact values repaired."""
+    col = cases["column_sum"]
+    assert col["reference"]["values"] != col["reference"]["expect"]
+    assert col["repaired"]["values"] == col["repaired"]["expect"]
+    nest = cases["nested_contraction"]
+    ref_src, rep_src = nest["reference"]["source"], nest["repaired"]["source"]
+    assert ref_src.count("float acc") == 1 and rep_src.count("float acc") == 4
+    assert nest["reference"]["values"] != nest["reference"]["expect"]
+    assert nest["repaired"]["values"] == nest["repaired"]["expect"]
+    for src in (ref_src, rep_src):  # the reference's naming and loop form
+        assert src.startswith("#include <math.h>\nvoid kernel_")
+        assert "float* restrict data0" in src and "for (int idx0 = 0; idx0 < 16; idx0++) {" in src
+        assert "for (int ridx" in src and "uidx" not in src  # upcast lanes are unrolled away
+
+
+def run_step(tmp_path, dims, batch, steps, opt, repair=False, sources=False):
+    x, t = data.mlp_batch(batch, dims[0], dims[-1], 1, 2)
+    src, dst = tmp_path / "in.npz", tmp_path / "out.npz"
+    np.savez(src, x=x, t=t, dims=np.array(dims), lr=np.array(0.01), steps=np.array(steps))
+    env = dict(os.environ)
+    env.pop("OPT", None)
+    if opt is not None:
+        env["OPT"] = opt
+    env["FG_LOWERING_REPAIR"] = "1" if repair else "0"
+    argv = [sys.executable, os.path.join(LOWERING, "run_step.py"), str(src), str(dst)]
+    if sources:
+        argv.append(str(tmp_path / "kernels.c"))
+    subprocess.run(argv, check=True, timeout=900, env=env)
+    return x, t, dict(np.load(dst))
+
+
+def check_step(oracle, x, t, r, dims, unroll):
+    nl = len(dims) - 1
+    ws = [r[f"w0_{i}"] for i in range(nl)]
+    bs = [r[f"b0_{i}"] for i in range(nl)]
+    oracle.set_unroll(unroll)
+    try:
+        oloss, ow, ob, odw, odb, _ = oracle.mlp_step(ws, bs, x, t, 0.01)
+    finally:
+        oracle.set_unroll(True)
+    assert np.float32(r["loss"][0]) == np.float32(oloss)
+    for i in range(nl):
+        assert np.array_equal(r[f"dw_{i}"], odw[i]), i
+        assert np.array_equal(r[f"db_{i}"], odb[i]), i
+        assert np.array_equal(r[f"w_{i}"], ow[i]) and np.array_equal(r[f"b_{i}"], ob[i]), i
+
+
+@pytest.mark.parametrize("opt,unroll", [("symbolic,unroll", True), ("unroll", True),
+                                        ("symbolic", False), ("0", False)])
+@pytest.mark.parametrize("dims,batch", [((64, 32, 10), 32), ((48, 40, 24, 10), 16)])
+def test_step_as_the_references_c_matches_oracle_bitwise(oracle, lowering, tmp_path, dims, batch,
+                                                         opt, unroll):
+    """Every kernel of a training step (forward, cross_entropy, backward,
+    Sgd::step, the loss read, the gradients read back) lowered as the
+    reference lowers it and run as its C: bit-identical to the C oracle with
+    the same reduction order, for every OPT setting without the upcast pass."""
+    x, t, r = run_step(tmp_path, dims, batch, 1, opt)
+    check_step(oracle, x, t, r, dims, unroll)
+    assert int(r["front_kernels"]) == 0  # nothing ran through the front end's own executor
+    assert int(r["launches"]) > 10
+
+
+@pytest.mark.parametrize("dims,batch", [((64, 32, 10), 32), ((48, 40, 24, 10), 16)])
+def test_step_with_every_pass_repaired_matches_oracle_bitwise(oracle, lowering, tmp_path, dims,
+                                                              batch):
+    """Default OPT (upcast too): with the three upcast-path behaviours of
+    kir.h repaired, the step is again bit-identical to the oracle -- they
+    are the only differences between the passes and the oracle's (and the
+    front end's exact mode's) arithmetic."""
+    x, t, r = run_step(tmp_path, dims, batch, 1, None, repair=True)
+    check_step(oracle, x, t, r, dims, True)
+
+
+def test_steps_track_oracle_and_emit_the_references_c(oracle, lowering, tmp_path):
+    dims, batch, steps = (32, 16, 10), 16, 3
+    x, t, r = run_step(tmp_path, dims, batch, steps, "symbolic,unroll", sources=True)
+    ws = [r["w0_0"], r["w0_1"]]
+    bs = [r["b0_0"], r["b0_1"]]
+    for s in range(steps):
+        oloss, ws, bs, _, _, _ = oracle.mlp_step(ws, bs, x, t, 0.01)
+        assert np.float32(r["loss"][s]) == np.float32(oloss), s
+    for i in range(2):
+        assert np.array_equal(r[f"w_{i}"], ws[i]) and np.array_equal(r[f"b_{i}"], bs[i])
+    src = (tmp_path / "kernels.c").read_text()
+    kernels = src.count("#include <math.h>\nvoid kernel_")
+    assert kernels >= 5  # Sgd::step's realize: forward, loss, backward, updates
+    # the clang renderer's vocabulary (src/codegen/clang.rs:12-281); the
+    # gradient kernels have the softmax's exp2, the loss alone its log2
+    for token in ("float* restrict data0", "float val0 = *(", "float acc", "exp2(",
+                  "for (int ridx", "(1/"):
+        assert token in src, token
