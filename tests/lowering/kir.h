@@ -143,9 +143,17 @@ std::vector<U> ended_ranges(const U &node);
 //    axes (numbered over the stored value's shape) and reduce axes (over the
 //    reduced source's shape) are numbered independently, so an upcast lane
 //    and an unroll lane can carry the same id and be merged as one.
-// set_repair(true) keeps tags across rebuilds, groups lanes by their axes
-// and gives upcast lanes ids of their own (not the reference; used to show
-// that these are the only differences).
+// And one that needs no upcast: a reduction whose value does not depend on
+// its reduce range (a constant broadcast and summed, as a gradient of sum
+// builds) gets an update that the linearizer is free to hoist out of the
+// loop (src/devectorize.rs:274-330 with src/linearize.rs:79-100 priorities),
+// so it is applied once; with the range unrolled the Contract of a
+// lane-invariant value is never lowered and rendering stops
+// (src/devectorize.rs:147-150, src/codegen/clang.rs:260).
+// set_repair(true) keeps tags across rebuilds, groups lanes by their axes,
+// gives upcast lanes ids of their own, makes the update depend on the reduce
+// ranges and expands a lane-invariant contracted value to its lanes (not
+// the reference; used to show that these are the only differences).
 void set_repair(bool on);
 bool repair();
 std::optional<uint64_t> rebuilt_tag(const Node &n);

@@ -490,7 +490,16 @@ bool reduce_lane_groups(const U &value, std::vector<std::vector<U>> *groups, Lan
     const Lanes &contract = value->arg.lanes;
     U vec;
     Lanes full;
-    if (!unwrap_unroll(value->src[0], &vec, &full)) return false;
+    if (!unwrap_unroll(value->src[0], &vec, &full)) {
+      if (!repair()) return false;
+      // a lane-invariant value (a constant reduced over an unrolled axis):
+      // each unrolled lane contributes it once
+      size_t csize = 1;
+      for (auto &c : contract) csize *= (size_t)c.second;
+      *groups = {std::vector<U>(csize, value->src[0])};
+      meta->clear();
+      return true;
+    }
     Lanes remaining;
     for (auto &l : full)
       if (std::none_of(contract.begin(), contract.end(),
@@ -580,7 +589,12 @@ U lower_reduce(const U &node) {
     asrc.insert(asrc.end(), outer.begin(), outer.end());
     U acc = make(Op::DefineAcc, node->dtype, std::move(asrc), Arg::none(), tag << 32);
     U red = horizontal_reduce(groups[i], rop);
-    U upd = make(rop, node->dtype, {acc, red});
+    std::vector<U> usrc{acc, red};
+    // repair: the update depends on the reduce ranges even when the reduced
+    // value does not (a constant), so the linearizer keeps it in the loop
+    // (the renderer reads only the first two sources of an ALU node)
+    if (repair()) usrc.insert(usrc.end(), rranges.begin(), rranges.end());
+    U upd = make(rop, node->dtype, std::move(usrc));
     assigns.push_back(make(Op::Assign, node->dtype, {acc, upd}, Arg::none(), (tag << 32) | 1));
     accs.push_back(acc);
   }

@@ -6,10 +6,11 @@ proto-kernels, the emitted C compiled by gcc and run on the host test device
 
 Pinned three ways: the reference's own unit tests of those passes, restated
 (tests/lowering/cases.cpp); whole exact-mode training steps whose every
-kernel is the reference's C, bit-identical to the C oracle; and two probes of
-the upcast path, where the passes as written give other values than their
-evident intent (kir.h lists the three behaviours) -- reproduced here as
-read, and removed by the repairs, after which the values are exact again.
+kernel is the reference's C, bit-identical to the C oracle; two probes of
+the upcast path and a zoo of Tensor-API graphs compared with the front end's
+exact mode, where the passes as written give other values than their
+evident intent (kir.h lists the behaviours) -- reproduced here as read, and
+removed by the repairs, after which the values are exact again.
 """
 import importlib.util
 import json
@@ -130,8 +131,7 @@ def test_step_as_the_references_c_matches_oracle_bitwise(oracle, lowering, tmp_p
 @pytest.mark.parametrize("dims,batch", [((64, 32, 10), 32), ((48, 40, 24, 10), 16)])
 def test_step_with_every_pass_repaired_matches_oracle_bitwise(oracle, lowering, tmp_path, dims,
                                                               batch):
-    """Default OPT (upcast too): with the three upcast-path behaviours of
-    kir.h repaired, the step is again bit-identical to the oracle -- they
+    """Default OPT (upcast too): with the behaviours of kir.h repaired, the step is again bit-identical to the oracle -- they
     are the only differences between the passes and the oracle's (and the
     front end's exact mode's) arithmetic."""
     x, t, r = run_step(tmp_path, dims, batch, 1, None, repair=True)
@@ -156,3 +156,45 @@ def test_steps_track_oracle_and_emit_the_references_c(oracle, lowering, tmp_path
     for token in ("float* restrict data0", "float val0 = *(", "float acc", "exp2(",
                   "for (int ridx", "(1/"):
         assert token in src, token
+
+
+ZOO_AS_WRITTEN = {
+    # rangeify pushes one flat index into a 2-D reduction source and stops
+    # (src/schedule/indexing.rs:151-155, the reshape of a keepdim sum)
+    "reshape_chain": "error",
+}
+
+
+@pytest.mark.parametrize("env,differs", [
+    # without upcast, as written: the gradient of log_softmax sums a
+    # broadcast constant; its update is hoisted out of the reduce loop
+    # (OPT=0), or, unrolled, its Contract is never lowered (kir.h)
+    ({"OPT": "0"}, {**ZOO_AS_WRITTEN, "grad_log_softmax": "values"}),
+    ({"OPT": "symbolic,unroll"}, {**ZOO_AS_WRITTEN, "grad_log_softmax": "error"}),
+    # every pass, as written: the upcast-path behaviours of kir.h as well
+    ({}, {**ZOO_AS_WRITTEN, "grad_log_softmax": "error", "col_sum": "values",
+          "col_max": "values", "sum_3d_middle": "values", "i32_col_sum": "values",
+          "grad_matmul": "values"}),
+    # every pass, repaired: only the graph rangeify rejects is left
+    ({"FG_LOWERING_REPAIR": "1"}, ZOO_AS_WRITTEN),
+    ({"FG_LOWERING_REPAIR": "1", "OPT": "0"}, ZOO_AS_WRITTEN),
+])
+def test_graph_zoo_against_the_front_ends_exact_mode(lowering, env, differs):
+    """25 Tensor-API graphs (broadcast chains, unary math, row / column / 3-D
+    / i32 reductions, max, permute + contiguous, narrow, matmul, log_softmax,
+    cross_entropy, and the gradients of max with ties, matmul + relu,
+    cross_entropy and log_softmax), each realized by the front end's exact
+    mode and as the reference's C: bit-identical wherever the reference's
+    passes compute what they intend; the exceptions are exactly those the
+    passes as read produce."""
+    e = dict(os.environ)
+    e.pop("OPT", None)
+    e.update(env)
+    out = subprocess.run([sys.executable, os.path.join(lowering, "run_zoo.py")], check=True,
+                         timeout=900, env=e, capture_output=True, text=True).stdout
+    res = json.loads(out)
+    assert len(res) == 25
+    got = {k: ("error" if "error" in v else "values") for k, v in res.items()
+           if not v.get("equal")}
+    assert got == differs
+    assert all(v["kernels"] >= 1 for v in res.values() if "kernels" in v)
