@@ -198,3 +198,27 @@ def test_graph_zoo_against_the_front_ends_exact_mode(lowering, env, differs):
            if not v.get("equal")}
     assert got == differs
     assert all(v["kernels"] >= 1 for v in res.values() if "kernels" in v)
+
+
+def test_routed_paths_against_the_references_c(lowering):
+    """SURVEY's purpose for this oracle: the default mode's pattern router
+    checked on graphs other than the MLP step.  Each graph realized through
+    the routes (3xTF32 GEMM with and without the bias epilogue, HBM row /
+    column sum and max, fused cross-entropy forward and gradient, the SGD
+    update -- their host restatements on the host test device) and as the
+    reference's C (repaired) agrees to 1e-5 of the output's scale."""
+    e = dict(os.environ)
+    e.pop("OPT", None)
+    out = subprocess.run([sys.executable, os.path.join(lowering, "run_routed.py")], check=True,
+                         timeout=1200, env=e, capture_output=True, text=True).stdout
+    res = json.loads(out)
+    for name, r in res.items():
+        assert r["max_rel"] < 1e-5, (name, r)
+    routes = lambda name: res[name]["routes"]  # noqa: E731
+    assert routes("matmul")["gemm"] == 1
+    assert routes("linear_bias")["gemm_bias"] == 1 and routes("linear_bias_relu")["gemm_bias"] == 1
+    assert all(routes(n)["hand_reduce"] == 1 for n in ("row_sum", "col_sum", "row_max"))
+    assert routes("cross_entropy")["xent"] == 1 and routes("grad_cross_entropy")["xent"] == 1
+    assert routes("grad_relu_layer_dx")["gemm"] >= 1 and routes("grad_relu_layer_dw")["gemm"] >= 1
+    assert routes("matmul_chain")["gemm"] == 2
+    assert routes("sgd_update")["sgd"] == 1
