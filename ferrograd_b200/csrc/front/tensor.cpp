@@ -177,11 +177,16 @@ Tensor Tensor::ones(const Shape &shape, DType dt) {
 }
 
 Tensor Tensor::scalar(float value) {
-  Tensor t = from_f32(&value, {1});
-  const BufferP &b = t.uop()->src[0]->buf;  // Reshape(Buffer)
-  b->has_host_scalar = true;
-  b->host_scalar = value;
-  return t;
+  // The value stays on the host until a kernel reads the buffer (the upload
+  // is then part of its allocation, DeviceBuffer::ensure_allocated): the
+  // routes that take it by value (the SGD step's lr) never allocate or copy
+  // it, which saves Sgd::step one host-to-device copy per parameter.
+  auto buf = std::make_shared<DeviceBuffer>(DType::F32, 1);
+  const uint8_t *p = reinterpret_cast<const uint8_t *>(&value);
+  buf->pending.assign(p, p + sizeof(float));
+  buf->has_host_scalar = true;
+  buf->host_scalar = value;
+  return from_uop(make_reshape(make_buffer(buf), {1}), false);
 }
 
 Shape Tensor::shape() const {
