@@ -13,6 +13,7 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include <chrono>
 #include <stdexcept>
 
 #include "../../ferrograd_b200/csrc/front/ferro_front.h"
@@ -137,15 +138,37 @@ kir::OptimizeConfig opt_config() {
 }
 
 uint64_t g_kernels = 0, g_launches = 0;
-std::vector<std::pair<std::string, std::vector<uint8_t>>> g_trace;  // (C source, output bytes)
+struct Traced {
+  std::string code;
+  std::vector<uint8_t> out;  // allocating kernels' output bytes
+  double seconds;            // the C function's run time
+};
+std::vector<Traced> g_trace;
 bool g_tracing = false;
+double g_kernel_seconds = 0;  // time inside the kernels' C functions (and first compiles)
 
-std::string lower_to_c(const kir::U &sink, const std::string &name) {
+kir::U lower(const kir::U &sink) {
   kir::U r = kir::rangeify(sink);
   kir::U o = kir::optimize(r, opt_config());
   kir::U e = kir::late_expand(o);
-  kir::U d = kir::devectorize(e);
-  return kir::render_c(kir::linearize(d), name);
+  return kir::devectorize(e);
+}
+
+std::string lower_to_c(const kir::U &sink, const std::string &name) {
+  return kir::render_c(kir::linearize(lower(sink)), name);
+}
+
+// Programs by lowered sink, as the reference's backend caches them
+// (cached_program / insert_program, src/tensor.rs:838-890): the entry holds
+// the sink, so an identical kernel of a later step interns to the same node;
+// a hit skips linearize, render and compile and keeps the first name.
+struct Program {
+  kir::U sink;
+  std::string code, name;
+};
+std::unordered_map<const kir::Node *, Program> &programs() {
+  static std::unordered_map<const kir::Node *, Program> p;
+  return p;
 }
 
 // Tensor::realize_many (src/tensor.rs:781-821) with every kernel lowered and
@@ -158,8 +181,17 @@ void realize(const std::vector<ferro::Tensor> &ts) {
   ferro::SchedulePlan plan = ferro::schedule_many(roots, true);
   for (const ferro::ScheduleItem &item : plan.items) {
     Proto p = to_proto(item);
-    const std::string name = "kernel_" + std::to_string(g_kernels++);
-    const std::string code = lower_to_c(p.sink, name);
+    kir::U lowered = lower(p.sink);
+    auto hit = programs().find(lowered.get());
+    if (hit == programs().end()) {
+      const std::string nm = "kernel_" + std::to_string(g_kernels++);
+      hit = programs()
+                .emplace(lowered.get(),
+                         Program{lowered, kir::render_c(kir::linearize(lowered), nm), nm})
+                .first;
+    }
+    const std::string &name = hit->second.name;
+    const std::string &code = hit->second.code;
     std::vector<int32_t> i32(p.inputs.size() + 1);
     std::vector<float> f32(p.inputs.size() + 1);
     std::vector<uint8_t> b8(p.inputs.size() + 1);
@@ -174,9 +206,22 @@ void realize(const std::vector<ferro::Tensor> &ts) {
         case ferro::KernelInput::Bool: b8[i] = (uint8_t)in.i; args.push_back(&b8[i]); break;
       }
     }
-    kir::run_c(code, name, args);
+    const auto k0 = std::chrono::steady_clock::now();
+    kir::run_c(code, name, args);  // compiles on first use
+    g_kernel_seconds +=
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - k0).count();
+    double secs = 0;
+    if (g_tracing) {  // a second, timed run (kernels are idempotent for their outputs
+                      // unless in place; in-place ones are timed on the first run)
+      if (!item.store_dest) {
+        const auto t0 = std::chrono::steady_clock::now();
+        kir::run_c(code, name, args);
+        secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      }
+    }
     g_launches++;
-    if (g_tracing && item.output) g_trace.push_back({code, item.output->to_host()});
+    if (g_tracing)
+      g_trace.push_back({code, item.output ? item.output->to_host() : std::vector<uint8_t>{}, secs});
     if (item.store_dest) {
       const ferro::UOp *d = item.store_dest.get();
       while (d->op != ferro::Op::Buffer && !d->src.empty()) d = d->src[0].get();
@@ -217,10 +262,17 @@ PYBIND11_MODULE(_lowering, m) {
         "Record each allocating kernel's C and output bytes from now on.");
   m.def("traced", []() {
     py::list l;
-    for (auto &[code, bytes] : g_trace)
-      l.append(py::make_tuple(code, py::bytes((const char *)bytes.data(), bytes.size())));
+    for (auto &t : g_trace)
+      l.append(py::make_tuple(t.code, py::bytes((const char *)t.out.data(), t.out.size()),
+                              t.seconds));
     return l;
   });
+  m.def("kernel_seconds", [](bool reset) {
+          const double s = g_kernel_seconds;
+          if (reset) g_kernel_seconds = 0;
+          return s;
+        }, py::arg("reset"),
+        "Seconds spent in run_c (the kernels' C, and compiles on first use) since the last reset.");
   m.def("stats", []() {
     py::dict d;
     d["kernels"] = g_kernels;

@@ -62,7 +62,8 @@ using Entry = void (*)(void **);
 
 Entry compile(const std::string &code, const std::string &name) {
   static std::unordered_map<std::string, Entry> programs;
-  const std::string src = code + trampoline(code, name);
+  const char *cf = std::getenv("FG_LOWERING_CFLAGS");
+  const std::string src = code + trampoline(code, name) + "// " + (cf ? cf : "") + "\n";
   auto it = programs.find(src);
   if (it != programs.end()) return it->second;
   const std::string dir = cache_dir();
@@ -74,7 +75,11 @@ Entry compile(const std::string &code, const std::string &name) {
     std::ofstream f(stem + ".c");
     f << src;
   }
-  const std::string cmd = "gcc -O2 -ffp-contract=off -fPIC -shared -o " + stem + ".so " + stem +
+  // FG_LOWERING_CFLAGS replaces the optimisation flags (the reference builds
+  // with clang -O3 -march=native; -ffp-contract=off stays, so no product is
+  // fused into an FMA under any setting)
+  const std::string flags = std::string(cf && *cf ? cf : "-O2") + " -ffp-contract=off";
+  const std::string cmd = "gcc " + flags + " -fPIC -shared -o " + stem + ".so " + stem +
                           ".c -lm 2> " + stem + ".log";
   if (std::system(cmd.c_str()) != 0) {
     std::ifstream l(stem + ".log");
