@@ -23,28 +23,32 @@ def _stale(target, deps):
                                              for d in deps)
 
 
-def build() -> str:
+def build(noexec: bool = False) -> str:
+    """noexec: a variant under _build_noexec whose compute entry points
+    return without computing (FG_HOSTDEV_NOEXEC), for timing host work."""
     import pybind11
-    os.makedirs(OUT, exist_ok=True)
-    dev = os.path.join(OUT, "libferro_cuda.so")
+    out = OUT + "_noexec" if noexec else OUT
+    os.makedirs(out, exist_ok=True)
+    dev = os.path.join(out, "libferro_cuda.so")
     dev_src = [os.path.join(HERE, "hostdev.cpp"),
                os.path.join(ROOT, "ferrograd_b200", "csrc", "fg_init.cpp")]
+    defs = ["-DFG_HOSTDEV_NOEXEC"] if noexec else []
     if _stale(dev, dev_src + [os.path.join(ROOT, "include", "ferro_cuda.h")]):
-        subprocess.run(["g++", *FLAGS, "-shared", *dev_src, "-ldl", "-o", dev], check=True)
+        subprocess.run(["g++", *FLAGS, *defs, "-shared", *dev_src, "-ldl", "-o", dev], check=True)
     front_src = [os.path.join(FRONT, f) for f in ("graph.cpp", "render.cpp", "exec.cpp", "tensor.cpp")]
     headers = [os.path.join(FRONT, f) for f in os.listdir(FRONT) if f.endswith(".h")]
-    lib = os.path.join(OUT, "libferro_front.so")
+    lib = os.path.join(out, "libferro_front.so")
     if _stale(lib, front_src + headers + [dev]):
-        subprocess.run(["g++", *FLAGS, "-shared", *front_src, "-L" + OUT, "-lferro_cuda",
+        subprocess.run(["g++", *FLAGS, "-shared", *front_src, "-L" + out, "-lferro_cuda",
                         "-Wl,-rpath,$ORIGIN", "-o", lib], check=True)
-    mod = os.path.join(OUT, "_front" + sysconfig.get_config_var("EXT_SUFFIX"))
+    mod = os.path.join(out, "_front" + sysconfig.get_config_var("EXT_SUFFIX"))
     py_src = os.path.join(FRONT, "front_py.cpp")
     if _stale(mod, [py_src, lib] + headers):
         subprocess.run(["g++", *FLAGS, "-shared", f"-I{pybind11.get_include()}",
-                        f"-I{sysconfig.get_paths()['include']}", py_src, "-L" + OUT,
+                        f"-I{sysconfig.get_paths()['include']}", py_src, "-L" + out,
                         "-lferro_front", "-lferro_cuda", "-Wl,-rpath,$ORIGIN", "-o", mod],
                        check=True)
-    return OUT
+    return out
 
 
 if __name__ == "__main__":

@@ -29,6 +29,15 @@
 #include <string>
 #include <vector>
 
+// FG_HOSTDEV_NOEXEC: every compute entry point returns before computing, so
+// the front end's host work (graph building, scheduling, routing, launch
+// preparation) can be timed alone (tests/hostdev/host_time.py).
+#ifdef FG_HOSTDEV_NOEXEC
+#define FG_HOSTDEV_SKIP_COMPUTE() return FG_OK
+#else
+#define FG_HOSTDEV_SKIP_COMPUTE() (void)0
+#endif
+
 #include "ferro_cuda.h"
 
 namespace fg {
@@ -312,7 +321,9 @@ int fg_execute(fg_program *prog, const fg_kernel_arg *args, int nargs) {
         break;
     }
   }
+#ifndef FG_HOSTDEV_NOEXEC
   prog->launch(slots.data(), prog->grid, prog->block);
+#endif
   for (int i = 0; i < nargs; i++)
     if (args[i].kind == FG_ARG_BUFFER && !guard_ok(args[i].v.buffer))
       return fg::set_error(FG_ERR_DEVICE,
@@ -341,6 +352,7 @@ static float tf32_hi(float v) {
 int fg_gemm_3xtf32(int M, int N, int K, const float *a, const float *a_lo, int lda, const float *b,
                    const float *b_lo, int ldb, float *c, float *c_lo, int ldc, int flags,
                    int epilogue, const float *bias, const float *mask, int ldmask, void *) {
+  FG_HOSTDEV_SKIP_COMPUTE();
   if (M <= 0 || N <= 0 || K <= 0)
     return fg::set_error(FG_ERR_INVALID, "gemm: M, N, K must be positive (got %d, %d, %d)", M, N, K);
   if (!a || !b || !c) return fg::set_error(FG_ERR_INVALID, "gemm: null operand");
@@ -372,6 +384,7 @@ int fg_gemm_3xtf32(int M, int N, int K, const float *a, const float *a_lo, int l
 }
 
 int fg_split_lo(const float *x, float *lo, size_t n, void *) {
+  FG_HOSTDEV_SKIP_COMPUTE();
   for (size_t i = 0; i < n; i++) lo[i] = x[i] - tf32_hi(x[i]);
   return FG_OK;
 }
@@ -400,6 +413,7 @@ static int host_reduce(int op, const T *x, T *out, size_t outer, size_t extent, 
 extern "C" {
 
 int fg_reduce_rows(int dtype, int op, const void *x, void *out, size_t rows, size_t cols, void *) {
+  FG_HOSTDEV_SKIP_COMPUTE();
   if (dtype == FG_F32)
     return host_reduce(op, (const float *)x, (float *)out, rows, cols, 1);
   if (dtype == FG_I32)
@@ -408,6 +422,7 @@ int fg_reduce_rows(int dtype, int op, const void *x, void *out, size_t rows, siz
 }
 
 int fg_reduce_cols(int dtype, int op, const void *x, void *out, size_t rows, size_t cols, void *) {
+  FG_HOSTDEV_SKIP_COMPUTE();
   if (dtype == FG_F32)
     return host_reduce(op, (const float *)x, (float *)out, 1, rows, cols);
   if (dtype == FG_I32)
@@ -427,6 +442,7 @@ int fg_u8_to_f32_div(const uint8_t *src, float *dst, size_t n, float divisor, vo
 // one rounding per op, as the reference's store, plus the new residual.
 int fg_xent_fwd_bwd(const float *x, const float *t, size_t rows, size_t cols, float *loss,
                     float *dx, float grad_scale, void *) {
+  FG_HOSTDEV_SKIP_COMPUTE();
   if (!x || !t || !loss) return fg::set_error(FG_ERR_INVALID, "fg_xent_fwd_bwd: null pointer");
   double total = 0.0;
   for (size_t r = 0; r < rows; r++) {
@@ -450,6 +466,7 @@ int fg_xent_fwd_bwd(const float *x, const float *t, size_t rows, size_t cols, fl
 }
 
 int fg_sgd(float *p, const float *g, size_t n, float lr, float *lo, void *) {
+  FG_HOSTDEV_SKIP_COMPUTE();
   for (size_t i = 0; i < n; i++) {
     const float d = g[i] * lr;
     p[i] = p[i] + (-d);
