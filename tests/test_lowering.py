@@ -222,3 +222,24 @@ def test_routed_paths_against_the_references_c(lowering):
     assert routes("grad_relu_layer_dx")["gemm"] >= 1 and routes("grad_relu_layer_dw")["gemm"] >= 1
     assert routes("matmul_chain")["gemm"] == 2
     assert routes("sgd_update")["sgd"] == 1
+
+
+@pytest.mark.parametrize("opt", [None, "0"])
+def test_reference_known_answers_through_its_own_lowering(lowering, opt):
+    """The reference's end-to-end unit tests (log_softmax, cross_entropy
+    0.12692805, sum over axis 0, relu, max, the narrow + matmul gradient, the
+    product's gradient, the SGD step, assignment in place;
+    tests/golden/known_answers.json) realized as the reference's C, as
+    written (no repairs): the restated passes give the answers the
+    reference's own tests assert."""
+    e = dict(os.environ)
+    e.pop("OPT", None)
+    e.pop("FG_LOWERING_REPAIR", None)
+    if opt is not None:
+        e["OPT"] = opt
+    out = subprocess.run([sys.executable, os.path.join(lowering, "run_known.py")], check=True,
+                         timeout=900, env=e, capture_output=True, text=True).stdout
+    res = json.loads(out)
+    assert len(res) == 9
+    for name, r in res.items():
+        assert np.allclose(r["got"], r["expected"], rtol=0, atol=r["tol"]), (name, r)
