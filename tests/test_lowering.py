@@ -243,3 +243,16 @@ def test_reference_known_answers_through_its_own_lowering(lowering, opt):
     assert len(res) == 9
     for name, r in res.items():
         assert np.allclose(r["got"], r["expected"], rtol=0, atol=r["tol"]), (name, r)
+
+
+def test_config1_step_as_the_references_c(oracle, lowering, tmp_path):
+    """Config 1 at its own shapes (784-128-10, batch 256), every pass on:
+    repaired, the reference's C is bit-identical to the oracle; as written,
+    the 128-wide hidden layer's matmul sits in a nested loop with upcast
+    lanes, its accumulators collapse (kir.h), and the first loss is far from
+    the intended one."""
+    dims, batch = (784, 128, 10), 256
+    x, t, r = run_step(tmp_path, dims, batch, 1, None, repair=True)
+    check_step(oracle, x, t, r, dims, True)
+    _, _, w = run_step(tmp_path, dims, batch, 1, None, repair=False)
+    assert abs(float(w["loss"][0]) - float(r["loss"][0])) > 0.1
