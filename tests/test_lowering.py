@@ -256,3 +256,19 @@ def test_config1_step_as_the_references_c(oracle, lowering, tmp_path):
     check_step(oracle, x, t, r, dims, True)
     _, _, w = run_step(tmp_path, dims, batch, 1, None, repair=False)
     assert abs(float(w["loss"][0]) - float(r["loss"][0])) > 0.1
+
+
+def test_config1_kernels_match_the_committed_reference_c(lowering):
+    """Regression pin of the restated passes: the C they emit, as written and
+    with every OPT pass on, for the 23 kernels of a config-1 Sgd::step
+    realize equals tests/golden/c1_step_reference_c.txt (made by
+    tests/golden/make_lowering_golden.py)."""
+    spec = importlib.util.spec_from_file_location(
+        "make_lowering_golden", os.path.join(HERE, "golden", "make_lowering_golden.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    fresh = mod.emit()
+    with open(mod.OUT) as f:
+        committed = f.read()
+    assert fresh.count("#include <math.h>\nvoid kernel_") == 23
+    assert fresh == committed
