@@ -128,8 +128,10 @@ int debug_level();
 // read once per process: "0"/"off"/"none" disables every pass, "1"/"on"/
 // "all" or unset enables every pass, otherwise a comma list of "symbolic",
 // "upcast", "unroll".  unroll decides the reduction order (4-lane blocks)
-// and symbolic the constant folds of rendered kernels; upcast only changes
-// the reference's loop structure, never a value.
+// and symbolic the constant folds of rendered kernels; upcast, as the
+// reference's passes intend it, only changes the loop structure (as they are
+// written it also changes values in some kernels -- the restated lowering in
+// tests/lowering/kir.h lists where -- which the front end does not copy).
 struct OptimizeConfig {
   bool symbolic = true, upcast = true, unroll = true;
 };
