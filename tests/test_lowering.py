@@ -201,8 +201,8 @@ def test_graph_zoo_against_the_front_ends_exact_mode(lowering, env, differs):
 
 
 def test_routed_paths_against_the_references_c(lowering):
-    """SURVEY's purpose for this oracle: the default mode's pattern router
-    checked on graphs other than the MLP step.  Each graph realized through
+    """The default mode's pattern router checked against the reference's C
+    on graphs other than the MLP step.  Each graph realized through
     the routes (3xTF32 GEMM with and without the bias epilogue, HBM row /
     column sum and max, fused cross-entropy forward and gradient, the SGD
     update -- their host restatements on the host test device) and as the
