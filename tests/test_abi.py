@@ -87,3 +87,39 @@ def test_python_constants_match_the_header():
     defs = dict(re.findall(r"#define\s+(FG_[A-Z0-9_]+)\s+(\d+)", text))
     assert int(defs["FG_UNIQUE_ID_BYTES"]) == _lib.UNIQUE_ID_BYTES
     assert int(defs["FG_PEER_HANDLE_BYTES"]) == _lib.PEER_HANDLE_BYTES
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """No CPU fallback: without libferro_cuda.so the package refuses to load,
+    naming the file and the build command; without the front-end extension
+    the Tensor API refuses to import."""
+    import subprocess
+    import sys
+    code = (
+        "import ferrograd_b200._lib as L\n"
+        f"L.LIB_PATH = {str(tmp_path / 'absent.so')!r}\n"
+        "L._lib = None\n"
+        "try:\n"
+        "    L.lib()\n"
+        "except L.FerroError as e:\n"
+        "    assert 'absent.so is missing' in str(e) and 'ferrograd_b200.build' in str(e), e\n"
+        "    print('ok')\n")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=120, cwd=ROOT)
+    assert out.stdout.strip() == "ok", out.stderr
+    code = (
+        "import sys, builtins\n"
+        "real = builtins.__import__\n"
+        "def fake(name, *a, **k):\n"
+        "    if name.endswith('_front') or (a and a[2] and '_front' in a[2]):\n"
+        "        raise ImportError('no _front')\n"
+        "    return real(name, *a, **k)\n"
+        "builtins.__import__ = fake\n"
+        "try:\n"
+        "    import ferrograd_b200.front\n"
+        "except ImportError as e:\n"
+        "    assert 'not built' in str(e), e\n"
+        "    print('ok')\n")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=120, cwd=ROOT)
+    assert out.stdout.strip() == "ok", out.stderr
