@@ -55,10 +55,18 @@ std::unordered_map<std::string, fg_program *> &program_cache() {
 
 }  // namespace
 
-bool exact_mode() {
+namespace {
+bool exact_env() {
   const char *e = std::getenv("FG_FRONT_EXACT");
   return e && *e && std::strcmp(e, "0") != 0;
 }
+int g_exact_scope = -1;  // the flag as read at the current realize's start
+}  // namespace
+
+bool exact_mode() { return g_exact_scope >= 0 ? g_exact_scope != 0 : exact_env(); }
+
+ExactModeScope::ExactModeScope() : prev(g_exact_scope) { g_exact_scope = exact_env() ? 1 : 0; }
+ExactModeScope::~ExactModeScope() { g_exact_scope = prev; }
 
 int debug_level() {
   static const int level = [] {
@@ -544,11 +552,15 @@ void launch_args(fg_program *prog, bool has_out_slot, const std::vector<KernelIn
 // but not which buffers fill the slots.  Encoding it costs a walk of the
 // expression; rendering costs ~60 us per kernel, so steady-state steps look
 // programs up by this key and render only on a miss.
-// Words collected in a vector (an inlined push_back each) and turned into
-// the string key with one copy at the end.
+// Words collected in a vector (an inlined push_back each) and hashed as
+// they are added; the vector itself is the map key (moved in, not copied).
 struct KeyBuf {
   std::vector<int64_t> w;
-  void put(int64_t v) { w.push_back(v); }
+  uint64_t h = 1469598103934665603ULL;
+  void put(int64_t v) {
+    w.push_back(v);
+    h = (h ^ (uint64_t)v) * 1099511628211ULL;
+  }
   void put_str(const std::string &t) {
     put((int64_t)t.size());
     for (size_t i = 0; i < t.size(); i += 8) {
@@ -557,13 +569,15 @@ struct KeyBuf {
       put(v);
     }
   }
-  std::string str() const {
-    return std::string(reinterpret_cast<const char *>(w.data()), w.size() * sizeof(int64_t));
-  }
+  bool operator==(const KeyBuf &o) const { return h == o.h && w == o.w; }
 };
 
-std::string spec_key(const RenderSpec &spec, const ParamSlots &ps,
-                     const std::vector<UOpP> &order) {
+struct KeyBufHash {
+  size_t operator()(const KeyBuf &k) const { return (size_t)(k.h ^ (k.h >> 29)); }
+};
+
+KeyBuf spec_key(const RenderSpec &spec, const ParamSlots &ps,
+                     const std::vector<const UOp *> &order) {
   KeyBuf k;
   k.w.reserve(16 + order.size() * 12);
   k.put((int64_t)spec.store);
@@ -596,11 +610,11 @@ std::string spec_key(const RenderSpec &spec, const ParamSlots &ps,
       k.put((int64_t)n->buf->count);
       k.put(n->buf->known_zero() ? 1 : 0);
     } else if (n->op == Op::Shrink) {
-      for (int sl : ps.shrink_slots.at(n.get())) k.put(sl);
+      for (int sl : ps.shrink_slots.at(n)) k.put(sl);
     }
   }
   k.put(spec.store == RenderSpec::View ? 1 : 0);
-  return k.str();
+  return k;
 }
 
 struct CachedKernel {
@@ -608,8 +622,8 @@ struct CachedKernel {
   bool has_out_slot;
 };
 
-std::unordered_map<std::string, CachedKernel> &spec_cache() {
-  static std::unordered_map<std::string, CachedKernel> c;
+std::unordered_map<KeyBuf, CachedKernel, KeyBufHash> &spec_cache() {
+  static std::unordered_map<KeyBuf, CachedKernel, KeyBufHash> c;
   return c;
 }
 
@@ -624,16 +638,18 @@ void launch_spec(const RenderSpec &spec, const BufferP &out, const BufferP &lo_o
   }
   // one walk of the kernel's graph gives both its parameter slots and its
   // structural key
-  const std::vector<UOpP> order = toposort(view ? make_store(spec.dest, spec.value) : spec.value);
+  const UOpP root = view ? make_store(spec.dest, spec.value) : spec.value;
+  const std::vector<const UOp *> order = toposort_nodes(root.get());
   ParamSlots ps = collect_params_from(order, view ? 0 : 1);
-  std::string key = spec_key(spec, ps, order);
+  KeyBuf key = spec_key(spec, ps, order);
   auto &cache = spec_cache();
   auto it = cache.find(key);
   if (it == cache.end()) {
     RenderedKernel rk = render_kernel(spec);
     launch_rendered(rk, out, written, lo_out);
     auto pit = program_cache().find(rk.source);
-    if (pit != program_cache().end()) cache.emplace(key, CachedKernel{pit->second, rk.has_out_slot});
+    if (pit != program_cache().end())
+      cache.emplace(std::move(key), CachedKernel{pit->second, rk.has_out_slot});
     return;
   }
   g_stats.cache_hits++;
@@ -824,7 +840,7 @@ Operand prepare_operand(const UOpP &x, size_t row_axis, size_t red_axis, size_t 
     spec.with_lo = true;
     launch_spec(spec, st.hold, st.lo);
     st.keep = x;
-    for (auto &n : toposort(x))
+    for (const UOp *n : toposort_nodes(x.get()))
       if (n->op == Op::Buffer) st.reads.emplace_back(n->buf, n->buf->version);
     sit = stage.insert_or_assign(key, std::move(st)).first;
   }
@@ -1171,16 +1187,16 @@ RoutePlan plan_route(const ScheduleItem &item) {
             }
   }
   bool root_handled = false;
-  for (auto &n : toposort(item.value)) {
-    if (auto c = match_contraction(n.get())) {
+  for (const UOp *n : toposort_nodes(item.value.get())) {
+    if (auto c = match_contraction(n)) {
       char buf[128];
       snprintf(buf, sizeof(buf), "gemm %lldx%lldx%lld", (long long)c->M, (long long)c->N,
                (long long)c->K);
       p.steps.push_back(buf);
-      if (!item.store_dest && root_reduce(item.value) == n.get()) root_handled = true;
-    } else if (auto h = match_hand_reduce(n.get())) {
+      if (!item.store_dest && root_reduce(item.value) == n) root_handled = true;
+    } else if (auto h = match_hand_reduce(n)) {
       p.steps.push_back(h->rows ? "reduce_rows" : "reduce_cols");
-      if (!item.store_dest && root_reduce(item.value) == n.get()) root_handled = true;
+      if (!item.store_dest && root_reduce(item.value) == n) root_handled = true;
     }
   }
   if (root_handled && p.steps.size() == 1)
@@ -1230,13 +1246,13 @@ void run_item(const ScheduleItem &item) {
     // Extract routed reductions bottom-up, substituting each result.
     std::unordered_map<const UOp *, UOpP> repl;
     std::vector<UOpP> hold;
-    for (auto &n : toposort(item.value)) {
+    for (const UOp *n : toposort_nodes(item.value.get())) {
       if (n->op != Op::ReduceAxis) continue;
-      auto c = match_contraction(n.get());
+      auto c = match_contraction(n);
       std::optional<HandReduce> h;
-      if (!c) h = match_hand_reduce(n.get());
+      if (!c) h = match_hand_reduce(n);
       if (!c && !h) continue;
-      const bool is_root = !item.store_dest && root_reduce(item.value) == n.get();
+      const bool is_root = !item.store_dest && root_reduce(item.value) == n;
       BufferP out = is_root ? item.output : temp_buffer(n->dtype, numel(n->shape));
       if (c) {
         UOpP a = c->a, b = c->b;
@@ -1252,7 +1268,7 @@ void run_item(const ScheduleItem &item) {
       if (is_root) return;
       UOpP sub = make_reshape(make_buffer(out), n->shape);
       hold.push_back(sub);
-      repl[n.get()] = sub;
+      repl[n] = sub;
     }
     if (!repl.empty()) {
       value = Rewriter(repl)(item.value);

@@ -112,7 +112,7 @@ using BufferP = std::shared_ptr<DeviceBuffer>;
 struct UOp;
 using UOpP = std::shared_ptr<const UOp>;
 
-struct UOp {
+struct UOp : std::enable_shared_from_this<UOp> {
   Op op;
   DType dtype;
   std::vector<UOpP> src;
@@ -135,6 +135,14 @@ struct UOp {
   // rewriter whose number is memo_mark (one rewriter is live at a time).
   mutable uint64_t memo_mark = 0;
   mutable uint32_t memo_slot = 0;
+  // The interner's entry: the node's structural hash; the node leaves the
+  // table when it is destroyed.
+  uint64_t intern_hash = 0;
+  bool interned = false;
+  UOp() = default;
+  UOp(const UOp &) = delete;
+  UOp &operator=(const UOp &) = delete;
+  ~UOp();
 };
 
 // Interned constructors (src/uop.rs:536-760, 926-1040): structurally equal
@@ -164,6 +172,8 @@ UOpP make_full(const Shape &shape, DType dt, double value);
 
 bool has_buffer_identity(const UOp *u);  // src/uop.rs:870-877
 std::vector<UOpP> toposort(const UOpP &root);  // src/uop.rs:1044-1074
+// The same order as plain node pointers, for walks that only read the nodes.
+std::vector<const UOp *> toposort_nodes(const UOp *root);
 std::string dump(const UOpP &root);
 size_t interner_size();
 

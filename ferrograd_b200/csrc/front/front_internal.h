@@ -26,7 +26,7 @@ struct ParamSlots {
 };
 ParamSlots collect_params(const UOpP &root, int slot_offset);
 // The same over an existing toposort of the kernel's root.
-ParamSlots collect_params_from(const std::vector<UOpP> &order, int slot_offset);
+ParamSlots collect_params_from(const std::vector<const UOp *> &order, int slot_offset);
 
 // A node's value as a strided view of one buffer: element (c0..cn) of the
 // node is buf[offset + sum_a c_a * strides[a]].
@@ -123,6 +123,13 @@ std::string float_literal(double v);
 // Environment flag: FG_FRONT_EXACT=1 renders every kernel (no GEMM or
 // hand-written reductions), reproducing the reference's arithmetic order.
 bool exact_mode();
+// Inside a realize the flag is read once, at its start: every kernel of one
+// realize runs in the same mode, and the per-kernel lookups cost nothing.
+struct ExactModeScope {
+  ExactModeScope();
+  ~ExactModeScope();
+  int prev;
+};
 int debug_level();
 // The reference's OPT environment variable (src/optimize/mod.rs:80-112),
 // read once per process: "0"/"off"/"none" disables every pass, "1"/"on"/

@@ -63,12 +63,13 @@ bool is_movement(Op op) {
 
 // ---------------------------------------------------------------------------
 // Interning (src/uop.rs:536-570): a node is looked up by (op, dtype, source
-// identities, arg, literal, buffer identity).  The table maps the hash of
-// those fields to weak references of the nodes that have it; a lookup
-// compares the candidates' own fields, so it allocates nothing.  Sources of
-// a live node are alive (the node owns them), so comparing source pointers
-// of a live candidate is sound; expired entries are swept when the table
-// has doubled.
+// identities, arg, literal, buffer identity).  The table is an open-addressing
+// set of live nodes (linear probing, power-of-two size, at most half full)
+// keyed by the hash of those fields; a lookup compares the candidates' own
+// fields, so it allocates nothing.  A node leaves the table in its destructor
+// (backward-shift deletion, no tombstones), so the table holds live nodes
+// only and its entries need no reference counts.  Sources of a live node are
+// alive (the node owns them), so comparing source pointers is sound.
 namespace {
 
 uint64_t node_hash(Op op, DType dt, Op rop, uint64_t vbits, const DeviceBuffer *buf,
@@ -82,7 +83,7 @@ uint64_t node_hash(Op op, DType dt, Op rop, uint64_t vbits, const DeviceBuffer *
   mix((uint64_t)(uintptr_t)buf);
   for (auto &p : srcs) mix((uint64_t)(uintptr_t)p.get());
   for (auto a : arg) mix((uint64_t)a);
-  return h;
+  return h ^ (h >> 31);
 }
 
 bool same_node(const UOp &u, Op op, DType dt, Op rop, uint64_t vbits, const DeviceBuffer *buf,
@@ -98,23 +99,60 @@ bool same_node(const UOp &u, Op op, DType dt, Op rop, uint64_t vbits, const Devi
   return u.arg == arg;
 }
 
-std::unordered_multimap<uint64_t, std::weak_ptr<const UOp>> &interner() {
-  static std::unordered_multimap<uint64_t, std::weak_ptr<const UOp>> m;
-  return m;
-}
-size_t g_sweep_at = 4096;
-uint64_t g_uid = 0;
+struct InternTable {
+  struct Slot {
+    uint64_t h;
+    UOp *p;  // null: empty
+  };
+  std::vector<Slot> slots = std::vector<Slot>(1024, Slot{0, nullptr});
+  size_t count = 0;
 
-void sweep_interner() {
-  auto &m = interner();
-  for (auto it = m.begin(); it != m.end();) {
-    if (it->second.expired())
-      it = m.erase(it);
-    else
-      ++it;
+  size_t mask() const { return slots.size() - 1; }
+  void place(uint64_t h, UOp *p) {
+    size_t i = h & mask();
+    while (slots[i].p) i = (i + 1) & mask();
+    slots[i] = {h, p};
   }
-  g_sweep_at = std::max<size_t>(4096, m.size() * 2);
+  void insert(uint64_t h, UOp *p) {
+    if (2 * (count + 1) > slots.size()) {
+      std::vector<Slot> old(slots.size() * 2, Slot{0, nullptr});
+      old.swap(slots);
+      for (const Slot &s : old)
+        if (s.p) place(s.h, s.p);
+    }
+    place(h, p);
+    count++;
+  }
+  void erase(uint64_t h, const UOp *p) {
+    size_t i = h & mask();
+    while (slots[i].p != p) {
+      if (!slots[i].p) return;
+      i = (i + 1) & mask();
+    }
+    // backward shift: move later entries of the probe run into the hole
+    // unless their home slot lies cyclically in (hole, entry]
+    size_t j = i;
+    for (;;) {
+      j = (j + 1) & mask();
+      if (!slots[j].p) break;
+      const size_t k = slots[j].h & mask();
+      const bool stays = i <= j ? (i < k && k <= j) : (i < k || k <= j);
+      if (stays) continue;
+      slots[i] = slots[j];
+      i = j;
+    }
+    slots[i] = Slot{0, nullptr};
+    count--;
+  }
+};
+
+// Never destroyed: nodes held by other static objects may be destroyed
+// after this file's statics at exit, and their destructors still use it.
+InternTable &interner() {
+  static InternTable *t = new InternTable;
+  return *t;
 }
+uint64_t g_uid = 0;
 
 void infer_shape(UOp &u) {
   switch (u.op) {
@@ -180,19 +218,10 @@ UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, const std::vector<int64_t> 
   uint64_t vbits;
   std::memcpy(&vbits, &value, sizeof(double));
   const uint64_t h = node_hash(op, dt, rop, vbits, buf.get(), srcs, arg);
-  auto &m = interner();
-  auto range = m.equal_range(h);
-  // Entries of nodes that died are dropped as the lookup meets them: a
-  // training loop re-creates the same nodes every step, and their stale
-  // entries would otherwise pile up under one hash until the next sweep.
-  for (auto it = range.first; it != range.second;) {
-    if (auto live = it->second.lock()) {
-      if (same_node(*live, op, dt, rop, vbits, buf.get(), srcs, arg)) return live;
-      ++it;
-    } else {
-      it = m.erase(it);
-    }
-  }
+  InternTable &t = interner();
+  for (size_t i = h & t.mask(); t.slots[i].p; i = (i + 1) & t.mask())
+    if (t.slots[i].h == h && same_node(*t.slots[i].p, op, dt, rop, vbits, buf.get(), srcs, arg))
+      return t.slots[i].p->shared_from_this();
   auto u = std::make_shared<UOp>();
   u->op = op;
   u->dtype = dt;
@@ -203,18 +232,19 @@ UOpP intern(Op op, DType dt, std::vector<UOpP> srcs, const std::vector<int64_t> 
   u->buf = buf;
   u->uid = g_uid++;
   infer_shape(*u);
-  UOpP out = u;
-  m.emplace(h, out);
-  if (m.size() > g_sweep_at) sweep_interner();
-  return out;
+  u->intern_hash = h;
+  u->interned = true;
+  t.insert(h, u.get());
+  return u;
 }
 
 }  // namespace
 
-size_t interner_size() {
-  sweep_interner();
-  return interner().size();
+UOp::~UOp() {
+  if (interned) interner().erase(intern_hash, this);
 }
+
+size_t interner_size() { return interner().count; }
 
 UOpP make_buffer(const BufferP &b) { return intern(Op::Buffer, b->dtype, {}, {}, Op::Add, 0.0, b); }
 UOpP make_const(double v, DType dt) { return intern(Op::Const, dt, {}, {}, Op::Add, v); }
@@ -309,6 +339,36 @@ std::vector<UOpP> toposort(const UOpP &root) {
     } else {
       for (auto it = node->src.rbegin(); it != node->src.rend(); ++it)
         if (!visited(it->get())) stack.push_back({&*it, false});
+    }
+  }
+  return out;
+}
+
+std::vector<const UOp *> toposort_nodes(const UOp *root) {
+  // The same walk and order as toposort, over plain pointers: for walkers
+  // that only read the nodes (no handle copies, no reference counting).
+  const uint64_t mark = new_walk();
+  std::vector<const UOp *> out;
+  out.reserve(64);
+  static std::vector<std::pair<const UOp *, bool>> stack;
+  const size_t base = stack.size();  // callers may walk inside a walk's loop
+  stack.push_back({root, false});
+  while (stack.size() > base) {
+    auto [node, processed] = stack.back();
+    stack.pop_back();
+    if (node->walk_mark == mark) continue;
+    if (processed) {
+      node->walk_mark = mark;
+      out.push_back(node);
+      continue;
+    }
+    stack.push_back({node, true});
+    if (node->op == Op::After) {
+      for (auto &s : node->src)
+        if (s->walk_mark != mark) stack.push_back({s.get(), false});
+    } else {
+      for (auto it = node->src.rbegin(); it != node->src.rend(); ++it)
+        if ((*it)->walk_mark != mark) stack.push_back({it->get(), false});
     }
   }
   return out;
@@ -447,13 +507,13 @@ std::map<const UOp *, UOpP> compute_gradient(const UOpP &root, const UOpP &root_
                                              const std::vector<UOpP> &targets) {
   // Per-node state lives in vectors indexed by toposort position
   // (UOp::topo_pos), so the walk does no hash lookups.
-  auto order = toposort(root);
+  const std::vector<const UOp *> order = toposort_nodes(root.get());
   const size_t n = order.size();
   if (n == 0) throw Panic("compute_gradient: empty graph");
   for (size_t i = 0; i < n; i++) order[i]->topo_pos = (int64_t)i;
   auto pos_of = [&](const UOp *u) -> int64_t {
     const int64_t p = u->topo_pos;
-    return p >= 0 && (size_t)p < n && order[(size_t)p].get() == u ? p : -1;
+    return p >= 0 && (size_t)p < n && order[(size_t)p] == u ? p : -1;
   };
   // needed_nodes (src/gradient.rs:64-81): the nodes on a path from a target
   // up to the root -- a node is needed when it is a target or one of its
@@ -474,8 +534,8 @@ std::map<const UOp *, UOpP> compute_gradient(const UOpP &root, const UOpP &root_
   std::vector<UOpP> grads(n);
   grads[n - 1] = root_grad;
   for (size_t k = n; k-- > 0;) {
-    const UOpP &node = order[k];
     if (!needed[k] || !grads[k]) continue;
+    const UOpP node = order[k]->shared_from_this();
     auto local = gradient_for_op(node, grads[k]);
     for (size_t i = 0; i < node->src.size() && i < local.size(); i++) {
       if (!local[i]) continue;
@@ -759,10 +819,10 @@ UOpP Rewriter::operator()(const UOpP &root) {
 }
 
 ParamSlots collect_params(const UOpP &root, int slot_offset) {
-  return collect_params_from(toposort(root), slot_offset);
+  return collect_params_from(toposort_nodes(root.get()), slot_offset);
 }
 
-ParamSlots collect_params_from(const std::vector<UOpP> &order, int slot_offset) {
+ParamSlots collect_params_from(const std::vector<const UOp *> &order, int slot_offset) {
   // parameterize_inputs (src/schedule.rs:176-245): buffers by first
   // appearance, one scalar per parameterised Shrink start.
   ParamSlots ps;
@@ -785,7 +845,7 @@ ParamSlots collect_params_from(const std::vector<UOpP> &order, int slot_offset) 
           ps.inputs.push_back(in);
         }
       }
-      ps.shrink_slots[node.get()] = slots;
+      ps.shrink_slots[node] = slots;
     }
   }
   return ps;
@@ -911,14 +971,14 @@ bool schedule_cache_on() {
 // Everything schedule_many's decisions depend on: per node in toposort
 // order its op, dtype, reduce op, args and source positions, a buffer's
 // dtype and size; and the mode (exact mode schedules differently).
-std::string structure_key(const std::vector<UOpP> &order) {
+std::string structure_key(const std::vector<const UOp *> &order) {
   std::vector<int64_t> k;
   k.reserve(2 + order.size() * 8);
   auto put = [&k](int64_t v) { k.push_back(v); };
   put(exact_mode() ? 1 : 0);
   put((int64_t)order.size());
   for (size_t i = 0; i < order.size(); i++) {
-    const UOp *n = order[i].get();
+    const UOp *n = order[i];
     n->topo_pos = (int64_t)i;
     put((int64_t)n->op | ((int64_t)n->dtype << 8) | ((int64_t)n->reduce_op << 16));
     put((int64_t)n->arg.size());
@@ -935,7 +995,9 @@ std::string structure_key(const std::vector<UOpP> &order) {
 SchedulePlan schedule_cached(const std::vector<UOpP> &roots) {
   if (!schedule_cache_on()) return schedule_many(roots, false);
   if (roots.empty()) throw Panic("schedule_many requires at least one root");
-  std::vector<UOpP> order = toposort(make_sink(roots));
+  // the sink holds the whole graph; the walk's order is plain pointers
+  UOpP sink = make_sink(roots);
+  const std::vector<const UOp *> order = toposort_nodes(sink.get());
   std::string key = structure_key(order);
   auto &cache = schedule_cache();
   auto hit = cache.find(key);
@@ -953,7 +1015,7 @@ SchedulePlan schedule_cached(const std::vector<UOpP> &roots) {
       const CachedSchedule::Node &nd = cs.nodes[i];
       switch (nd.kind) {
         case CachedSchedule::Leaf:
-          inst[i] = order[(size_t)nd.ref];
+          inst[i] = order[(size_t)nd.ref]->shared_from_this();
           break;
         case CachedSchedule::Output:
           inst[i] = make_buffer(plan.items[(size_t)nd.ref].output);
@@ -980,8 +1042,8 @@ SchedulePlan schedule_cached(const std::vector<UOpP> &roots) {
       if (cs.items[i].store_dest >= 0)
         plan.items[i].store_dest = inst[(size_t)cs.items[i].store_dest];
     }
-    for (auto &[pos, idx] : cs.repl) plan.replacements[order[pos].get()] = inst[(size_t)idx];
-    plan.keep = std::move(order);
+    for (auto &[pos, idx] : cs.repl) plan.replacements[order[pos]] = inst[(size_t)idx];
+    plan.keep.push_back(std::move(sink));
     stats().schedule_hits++;
     return plan;
   }
@@ -991,13 +1053,13 @@ SchedulePlan schedule_cached(const std::vector<UOpP> &roots) {
   std::unordered_map<const UOp *, UOpP> m;
   std::unordered_map<const UOp *, std::pair<CachedSchedule::Kind, int64_t>> role;
   for (size_t i = 0; i < order.size(); i++) {
-    const UOpP &n = order[i];
+    const UOp *n = order[i];
     if (n->op == Op::Buffer) {
       UOpP ph = make_buffer(std::make_shared<DeviceBuffer>(n->buf->dtype, n->buf->count));
-      m[n.get()] = ph;
+      m[n] = ph;
       role[ph.get()] = {CachedSchedule::Leaf, (int64_t)i};
     } else if (n->op == Op::Const) {
-      role[n.get()] = {CachedSchedule::Leaf, (int64_t)i};
+      role[n] = {CachedSchedule::Leaf, (int64_t)i};
     }
   }
   std::vector<BufferP> outputs;

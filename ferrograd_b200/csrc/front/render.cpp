@@ -652,7 +652,7 @@ Val Emitter::value(const UOp *n, const std::vector<std::string> &ctx) {
 }
 
 bool contains_reduce(const UOpP &root) {
-  for (auto &n : toposort(root))
+  for (const UOp *n : toposort_nodes(root.get()))
     if (n->op == Op::ReduceAxis) return true;
   return false;
 }
@@ -752,8 +752,8 @@ void choose_thread_mapping(RenderSpec &spec) {
   int64_t best = 0;
   bool inner = false;
   int reduces = 0;
-  auto order = toposort(spec.value);
-  for (auto &n : order) {
+  const auto order = toposort_nodes(spec.value.get());
+  for (const UOp *n : order) {
     if (n->op != Op::ReduceAxis) continue;
     reduces++;
     if (n->dtype == DType::Bool) return;
@@ -772,9 +772,9 @@ void choose_thread_mapping(RenderSpec &spec) {
   // A reduction inside another's source (the scheduler materialises those;
   // kept as a guard) stays on the sequential mapping.
   if (reduces > 1)
-    for (auto &n : order)
+    for (const UOp *n : order)
       if (n->op == Op::ReduceAxis)
-        for (auto &m : toposort(n->src[0]))
+        for (const UOp *m : toposort_nodes(n->src[0].get()))
           if (m->op == Op::ReduceAxis) return;
   if (best < 32) return;
   if (inner)

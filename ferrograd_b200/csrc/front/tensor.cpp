@@ -384,6 +384,7 @@ void Tensor::realize_many(const std::vector<Tensor> &ts) {
     if (seen.insert(r.get()).second) roots.push_back(r);
   }
   if (roots.empty()) return;
+  ExactModeScope mode;
   using clk = std::chrono::steady_clock;
   auto secs = [](clk::time_point a, clk::time_point b) {
     return std::chrono::duration<double>(b - a).count();
@@ -444,10 +445,11 @@ void Tensor::backward() const {
   // src/tensor.rs:973-998.
   require(numel() == 1, "backward requires a scalar loss");
   // graph membership by toposort position (UOp::topo_pos), not a hash set
-  const std::vector<UOpP> all = toposort(uop());
+  const UOpP root = uop();
+  const std::vector<const UOp *> all = toposort_nodes(root.get());
   for (size_t i = 0; i < all.size(); i++) all[i]->topo_pos = (int64_t)i;
   auto in_graph = [&all](const UOp *u) {
-    return u->topo_pos >= 0 && (size_t)u->topo_pos < all.size() && all[(size_t)u->topo_pos].get() == u;
+    return u->topo_pos >= 0 && (size_t)u->topo_pos < all.size() && all[(size_t)u->topo_pos] == u;
   };
   std::vector<Tensor> targets;
   for (Tensor &t : live_tensors())
