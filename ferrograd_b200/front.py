@@ -41,10 +41,11 @@ stats = _front.stats
 reset_stats = _front.reset_stats
 last_source = _front.last_source
 exact_mode = _front.exact_mode
+interner_size = _front.interner_size
 
 __all__ = ["Tensor", "Linear", "Sgd", "UOp", "Mlp", "reset_init_seed", "init_seed",
            "set_device", "synchronize", "stream", "schedule", "schedule_uops", "stats", "reset_stats",
-           "last_source", "exact_mode", "tensor", "one_hot"]
+           "last_source", "exact_mode", "interner_size", "tensor", "one_hot"]
 
 
 def tensor(data, dtype=None) -> "Tensor":

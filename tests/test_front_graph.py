@@ -89,6 +89,26 @@ def test_interning_makes_equal_graphs_identical():
     assert not U.add(a, a).same(U.mul(a, a))
 
 
+def test_interner_holds_live_nodes_only():
+    """The interning table grows past its initial size, finds every live node
+    again (also after entries around it were deleted), and a node leaves it
+    when the node dies."""
+    base = F.interner_size()
+    a = U.buffer([4])
+    nodes = [U.add(a, U.const_int(i)) for i in range(5000)]
+    grown = F.interner_size()
+    assert grown >= base + 2 * 5000  # each sum and its literal
+    # drop every other node: their deletions shift the probe runs of the rest
+    kept = nodes[1::2]
+    del nodes
+    assert F.interner_size() <= grown - 2 * 2500
+    found = all(n.same(U.add(a, U.const_int(2 * j + 1))) for j, n in enumerate(kept))
+    other = kept[0].same(U.add(a, U.const_int(0)))
+    assert found and not other
+    del kept
+    assert F.interner_size() == base + 2  # a: its buffer and reshape
+
+
 # --------------------------------------------------------------- tensor API
 def test_add_is_lazy_and_shapes_infer():
     a = F.tensor([1.0, 2.0])
