@@ -292,6 +292,10 @@ class Tensor {
   static Tensor from_uop(UOpP u, bool requires_grad);
   static Tensor from_host(DType dt, const void *data, size_t bytes, const Shape &shape);
   void set_uop(UOpP u) const;
+  // The node and its shape without copying the handle or the shape (valid
+  // until the tensor's node is replaced).
+  const UOp &node() const;
+  const Shape &shape_ref() const;
   UOpP target_uop() const;
   Tensor unary(Op op) const;
   Tensor binary(const Tensor &o, Op op, DType out) const;

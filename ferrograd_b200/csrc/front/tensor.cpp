@@ -189,18 +189,23 @@ Tensor Tensor::scalar(float value) {
   return from_uop(make_reshape(make_buffer(buf), {1}), false);
 }
 
-Shape Tensor::shape() const {
-  UOpP u = uop();
-  require(u->has_shape, "tensor must have shape");
-  return u->shape;
+const UOp &Tensor::node() const {
+  require((bool)p_, "use of an undefined tensor");
+  return *p_->uop;
 }
-DType Tensor::dtype() const { return uop()->dtype; }
-int64_t Tensor::numel() const { return ferro::numel(shape()); }
-int64_t Tensor::ndim() const { return (int64_t)shape().size(); }
+const Shape &Tensor::shape_ref() const {
+  const UOp &u = node();
+  require(u.has_shape, "tensor must have shape");
+  return u.shape;
+}
+Shape Tensor::shape() const { return shape_ref(); }
+DType Tensor::dtype() const { return node().dtype; }
+int64_t Tensor::numel() const { return ferro::numel(shape_ref()); }
+int64_t Tensor::ndim() const { return (int64_t)shape_ref().size(); }
 
 bool Tensor::is_realized() const {
-  UOpP u = uop();
-  return u->op == Op::Buffer || (u->op == Op::Reshape && u->src[0]->op == Op::Buffer);
+  const UOp &u = node();
+  return u.op == Op::Buffer || (u.op == Op::Reshape && u.src[0]->op == Op::Buffer);
 }
 
 bool Tensor::requires_grad() const { return p_->requires_grad; }
@@ -236,17 +241,17 @@ Tensor Tensor::unary(Op op) const {
 }
 
 Tensor Tensor::binary(const Tensor &o, Op op, DType out) const {
-  require(shape() == o.shape(), std::string("shape mismatch for ") + op_name(op));
+  require(shape_ref() == o.shape_ref(), std::string("shape mismatch for ") + op_name(op));
   return from_uop(make_alu(op, out, {uop(), o.uop()}), requires_grad() || o.requires_grad());
 }
 
 Tensor Tensor::broadcasted(const Tensor &o, Op op, DType out) const {
-  if (shape() == o.shape()) return binary(o, op, out);
+  if (shape_ref() == o.shape_ref()) return binary(o, op, out);
   Shape target;
-  require(broadcast_shape(shape(), o.shape(), &target),
+  require(broadcast_shape(shape_ref(), o.shape_ref(), &target),
           "broadcast: incompatible dims for " + shape_str(shape()) + " vs " + shape_str(o.shape()));
-  Tensor l = reshape(pad_left(shape(), target.size())).expand(target);
-  Tensor r = o.reshape(pad_left(o.shape(), target.size())).expand(target);
+  Tensor l = reshape(pad_left(shape_ref(), target.size())).expand(target);
+  Tensor r = o.reshape(pad_left(o.shape_ref(), target.size())).expand(target);
   return l.binary(r, op, out);
 }
 
@@ -261,13 +266,13 @@ Tensor Tensor::sqrt() const { return unary(Op::Sqrt); }
 
 Tensor Tensor::relu() const {
   // where(0 < x, x, zeros) with a real zero buffer (src/tensor.rs:519-531).
-  Tensor zero = zeros(shape(), dtype());
+  Tensor zero = zeros(shape_ref(), dtype());
   Tensor cond = zero.binary(*this, Op::CmpLt, DType::Bool);
   return from_uop(make_alu(Op::Where, dtype(), {cond.uop(), uop(), zero.uop()}), requires_grad());
 }
 
 Tensor Tensor::reshape(const Shape &s) const {
-  if (shape() == s) return *this;
+  if (shape_ref() == s) return *this;
   require(numel() == ferro::numel(s),
           "reshape: numel mismatch for " + shape_str(shape()) + " -> " + shape_str(s));
   return from_uop(make_reshape(uop(), s), requires_grad());
@@ -308,7 +313,7 @@ Tensor Tensor::contiguous() const {
 }
 
 Tensor Tensor::expand(const Shape &s) const {
-  Shape src = shape();
+  const Shape &src = shape_ref();
   if (src == s) return *this;
   require(src.size() == s.size(),
           "expand: rank mismatch for " + shape_str(src) + " -> " + shape_str(s));
