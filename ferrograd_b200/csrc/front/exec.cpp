@@ -1225,6 +1225,15 @@ std::string render_item_source(const ScheduleItem &item) {
 
 void end_realize() { staged_cache().clear(); }
 
+void all_reduce_mean_buffer(const BufferP &buf, fg_comm *comm) {
+  if (buf->dtype != DType::F32) throw Panic("all_reduce_mean: f32 buffers only");
+  if (debug_level() >= 1)
+    fprintf(stderr, "*** CUDA %4llu  all-reduce mean %zu\n", (unsigned long long)g_kernel_count++,
+            buf->count);
+  check(fg_allreduce_mean_f32(comm, fptr(buf), buf->count, stream()), "all-reduce");
+  buf->version++;
+}
+
 void run_item(const ScheduleItem &item) {
   g_stats.kernels++;
   // DEBUG >= 3 dumps each kernel's graph (src/tensor.rs:855-869,900-904);

@@ -279,6 +279,10 @@ class Tensor {
   std::vector<uint8_t> to_bytes() const;  // raw bytes of the realized buffer
   std::vector<Tensor> gradient(const std::vector<Tensor> &targets) const;
   void backward() const;
+  // In place, on the device stream: realizes this f32 tensor and replaces
+  // its contents by their mean over the communicator's ranks (every rank
+  // calls it, in the same order).  No reference counterpart.
+  void all_reduce_mean(fg_comm *comm) const;
 
   UOpP uop() const;
   // Tensor::apply_map_to_tensors (src/tensor.rs:222-252): every live
@@ -320,6 +324,13 @@ uint64_t init_seed();
 struct Sgd {
   std::vector<Tensor> params;
   float lr;
+  // Data parallelism (no reference counterpart: the reference is
+  // single-device): with a communicator attached, step() first realizes every
+  // parameter's gradient and replaces it by its mean over the ranks
+  // (Tensor::all_reduce_mean), then applies the update as always.  Every rank
+  // runs the same step on its own shard of the batch from the same
+  // parameters, so the parameters stay identical across ranks.
+  fg_comm *comm = nullptr;
   Sgd(const std::vector<Tensor> &params, float lr);
   void zero_grad() const;
   void step() const;
@@ -333,6 +344,10 @@ bool device_is_open();
 void synchronize();
 // Drops per-realize caches (staged GEMM operands); called after a realize.
 void end_realize();
+// fg_allreduce_mean_f32 over a whole f32 buffer on the device stream; the
+// buffer's contents change, so its version moves on (cached residuals and
+// cross-entropy losses of the old contents are not reused).
+void all_reduce_mean_buffer(const std::shared_ptr<DeviceBuffer> &buf, fg_comm *comm);
 
 // Per-kernel routing decision for an item, without running it.
 struct RoutePlan {

@@ -188,6 +188,10 @@ PYBIND11_MODULE(_front, m) {
       .def("to_vec", &Tensor::to_vec)
       .def("numpy", &tensor_to_numpy)
       .def("backward", &Tensor::backward)
+      .def(
+          "all_reduce_mean",
+          [](const Tensor &t, uintptr_t comm) { t.all_reduce_mean(reinterpret_cast<fg_comm *>(comm)); },
+          py::arg("comm"), "In place: realize, then the mean over the communicator's ranks.")
       .def("gradient", &Tensor::gradient)
       .def("_graph", [](const Tensor &t) { return dump(t.uop()); })
       .def("__repr__", [](const Tensor &t) {
@@ -214,7 +218,14 @@ PYBIND11_MODULE(_front, m) {
       .def_readonly("params", &Sgd::params)
       .def_readonly("lr", &Sgd::lr)
       .def("zero_grad", &Sgd::zero_grad)
-      .def("step", &Sgd::step);
+      .def("step", &Sgd::step)
+      .def(
+          "set_comm",
+          [](Sgd &s, uintptr_t comm) { s.comm = reinterpret_cast<fg_comm *>(comm); },
+          py::arg("comm"),
+          "Attach an fg_comm handle (0 detaches): step() then averages the gradients over "
+          "the ranks first.")
+      .def_property_readonly("comm", [](const Sgd &s) { return (uintptr_t)s.comm; });
 
   m.def("reset_init_seed", &reset_init_seed, py::arg("seed") = 42);
   m.def("init_seed", &init_seed);

@@ -523,7 +523,28 @@ void Sgd::zero_grad() const {
   for (const Tensor &p : params) p.clear_grad();
 }
 
+void Tensor::all_reduce_mean(fg_comm *comm) const {
+  require(comm != nullptr, "all_reduce_mean: no communicator");
+  require(dtype() == DType::F32, "all_reduce_mean: f32 tensors only");
+  realize();
+  // a realized tensor is its buffer, or a reshape of all of it
+  const UOp &u = node();
+  const UOp *b = u.op == Op::Reshape ? u.src[0].get() : &u;
+  require(b->op == Op::Buffer, "all_reduce_mean: tensor is not a whole buffer");
+  all_reduce_mean_buffer(b->buf, comm);
+}
+
 void Sgd::step() const {
+  if (comm) {
+    std::vector<Tensor> grads;
+    for (const Tensor &p : params) {
+      Tensor g = p.grad();
+      if (!g.defined()) throw Panic("optimizer step requires parameter gradients");
+      grads.push_back(g);
+    }
+    Tensor::realize_many(grads);
+    for (const Tensor &g : grads) g.all_reduce_mean(comm);
+  }
   for (const Tensor &p : params) {
     Tensor lr_t = Tensor::scalar(lr);
     Tensor g = p.grad();

@@ -65,6 +65,14 @@ class Communicator:
         call("fg_comm_unique_id", buf)
         return buf.raw
 
+    @property
+    def handle(self) -> int:
+        """The fg_comm pointer, for the front end (``Sgd.set_comm``,
+        ``Tensor.all_reduce_mean``)."""
+        if not self._h:
+            raise RuntimeError("communicator is closed")
+        return int(self._h)
+
     def allreduce_mean_(self, ptr: int, count: int, stream: int) -> None:
         call("fg_allreduce_mean_f32", self._h, ptr, int(count), stream)
 

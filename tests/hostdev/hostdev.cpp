@@ -481,4 +481,42 @@ int fg_one_hot_u8(const uint8_t *labels, float *out, size_t n, int classes, void
   return FG_OK;
 }
 
+// Communicator: the ranks are processes on this machine, and the transport
+// is a callback the test registers (fg_hostdev_set_allreduce), which sums a
+// host buffer over the ranks in place -- a gloo all-reduce in the tests.  The
+// mean is that sum times 1/nranks; NCCL's order of additions differs, so
+// results through it are held to a tolerance, not to bits.
+}  // extern "C"
+struct fg_comm {
+  int rank, nranks;
+};
+static int (*g_allreduce_sum)(float *, size_t) = nullptr;
+extern "C" {
+void fg_hostdev_set_allreduce(int (*fn)(float *, size_t)) { g_allreduce_sum = fn; }
+int fg_comm_unique_id(char out[FG_UNIQUE_ID_BYTES]) {
+  memset(out, 0, FG_UNIQUE_ID_BYTES);
+  return FG_OK;
+}
+int fg_comm_init(int rank, int nranks, const char *, int, fg_comm **out) {
+  if (nranks < 1 || rank < 0 || rank >= nranks)
+    return fg::set_error(FG_ERR_INVALID, "fg_comm_init: bad rank %d of %d", rank, nranks);
+  *out = new fg_comm{rank, nranks};
+  return FG_OK;
+}
+int fg_comm_destroy(fg_comm *comm) {
+  delete comm;
+  return FG_OK;
+}
+int fg_comm_abort(fg_comm *comm) { return fg_comm_destroy(comm); }
+int fg_allreduce_mean_f32(fg_comm *comm, float *buf, size_t count, void *) {
+  if (!comm || (count && !buf)) return fg::set_error(FG_ERR_INVALID, "fg_allreduce_mean_f32: null argument");
+  FG_HOSTDEV_SKIP_COMPUTE();
+  if (comm->nranks == 1 || count == 0) return FG_OK;
+  if (!g_allreduce_sum) return fg::set_error(FG_ERR_INVALID, "hostdev: no all-reduce transport registered");
+  if (g_allreduce_sum(buf, count)) return fg::set_error(FG_ERR_NCCL, "hostdev: all-reduce transport failed");
+  const float inv = 1.0f / (float)comm->nranks;
+  for (size_t i = 0; i < count; i++) buf[i] *= inv;
+  return FG_OK;
+}
+
 }  // extern "C"
