@@ -272,3 +272,19 @@ def test_config1_kernels_match_the_committed_reference_c(lowering):
         committed = f.read()
     assert fresh.count("#include <math.h>\nvoid kernel_") == 23
     assert fresh == committed
+
+
+def test_random_graphs_through_the_references_lowering(lowering):
+    """Random Tensor-API graphs (tests/lowering/run_fuzz.py, every pass,
+    repaired): each graph the passes lower gives the front end's exact-mode
+    bits; the ones they reject are rejected for the two reasons the
+    reference's source gives (a flat index pushed into a multi-axis source,
+    an index declared inside a size-1 loop), never another."""
+    e = dict(os.environ)
+    e.pop("OPT", None)
+    e["FG_LOWERING_REPAIR"] = "1"
+    out = subprocess.run([sys.executable, os.path.join(lowering, "run_fuzz.py"), "21", "60"],
+                         check=True, timeout=1200, env=e, capture_output=True, text=True).stdout
+    res = json.loads(out)
+    assert res["differ"] == [] and res["other"] == []
+    assert res["checked"] >= 40
