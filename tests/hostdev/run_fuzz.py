@@ -13,8 +13,10 @@ graph times a random weight, backward to every leaf) compare the default
 mode's gradients with exact mode's at the same tolerance, NaN where the
 other mode has NaN (sqrt of 0 and the like); a gradient the reference does
 not define (Shrink, src/gradient.rs:203) must raise in both modes.
+Integer graphs (i32 leaves in -1000..1000; add, mul, neg, relu, sum, max and
+the movement ops) must give the int64 result exactly in both modes.
 
-argv: seed count fwd|grad output.npz
+argv: seed count fwd|grad|i32 output.npz
 """
 import os
 import sys
@@ -43,30 +45,40 @@ class Node:
         return self.ref.shape
 
 
-def leaf(rng, shape):
+I32_OPS = ["add", "mul", "neg", "relu", "sum", "max", "permute", "reshape", "expand", "narrow",
+           "contig"]
+
+
+def leaf(rng, shape, i32=False):
+    if i32:
+        a = rng.integers(-1000, 1001, shape).astype(np.int32)
+        return Node(lambda env, a=a: env.leaf(a), a.astype(np.int64))
     a = rng.standard_normal(shape).astype(np.float32)
     return Node(lambda env, a=a: env.leaf(a), a.astype(np.float64))
 
 
-def rand_graph(rng, depth=0):
+def rand_graph(rng, depth=0, i32=False):
+    """A random graph over f32 leaves, or over i32 leaves with the integer
+    ops (its float64 / int64 value alongside)."""
     if depth > 3 or rng.random() < 0.25:
         shape = tuple(int(rng.choice(SIZES)) for _ in range(int(rng.integers(1, 4))))
         if np.prod(shape) > 200000:
             shape = shape[:1]
-        return leaf(rng, shape)
-    op = rng.choice(OPS)
-    x = rand_graph(rng, depth + 1)
+        return leaf(rng, shape, i32)
+    op = rng.choice(I32_OPS if i32 else OPS)
+    x = rand_graph(rng, depth + 1, i32)
     s = x.shape
     if op in ("add", "mul"):
         y = leaf(rng, s if rng.random() < 0.5 else
-                 tuple(d if rng.random() < 0.5 else 1 for d in s))
+                 tuple(d if rng.random() < 0.5 else 1 for d in s), i32)
         if op == "add":
             return Node(lambda env, x=x, y=y: x.build(env).add(y.build(env)), x.ref + y.ref)
         return Node(lambda env, x=x, y=y: x.build(env).mul(y.build(env)), x.ref * y.ref)
     if op == "neg":
         return Node(lambda env, x=x: x.build(env).neg(), -x.ref)
     if op == "relu":
-        return Node(lambda env, x=x: x.build(env).relu(), np.where(x.ref > 0, x.ref, 0.0))
+        return Node(lambda env, x=x: x.build(env).relu(),
+                    np.where(x.ref > 0, x.ref, np.zeros_like(x.ref)))
     if op == "chain":
         return Node(lambda env, x=x: x.build(env).mul(x.build(env)).add(x.build(env)).relu(),
                     np.maximum(x.ref * x.ref + x.ref, 0.0))
@@ -156,12 +168,18 @@ def realize(node, mode, grad, wv):
     return [None if g is None else g.numpy() for g in grads]
 
 
+def fits_i32(node):
+    return node.ref.size == 0 or np.max(np.abs(node.ref)) < 2**31
+
+
 def main(seed, count, kind, dst):
-    grad = kind == "grad"
+    grad, i32 = kind == "grad", kind == "i32"
     failures, checked, undefined = [], 0, 0
     for i in range(count):
         rng = np.random.default_rng(seed * 100000 + i)
-        node = rand_graph(rng)
+        node = rand_graph(rng, i32=i32)
+        if i32 and not fits_i32(node):
+            continue  # the int64 reference left the i32 range (a product of sums)
         wv = rng.standard_normal(node.shape).astype(np.float32)
         outs, errors = {}, {}
         for mode in ("1", "0"):
@@ -186,6 +204,11 @@ def main(seed, count, kind, dst):
                 e = scale_err(b, a.astype(np.float64))
                 if not e <= 1e-4:
                     failures.append(f"{i}: leaf {j} {a.shape}: default vs exact {e:.2e}")
+        elif i32:
+            for mode in ("1", "0"):
+                got = outs[mode][0]
+                if got.dtype != np.int32 or not np.array_equal(got.astype(np.int64), node.ref):
+                    failures.append(f"{i}: mode {mode} {node.shape}: i32 result differs")
         else:
             for mode in ("1", "0"):
                 e = scale_err(outs[mode][0], node.ref)

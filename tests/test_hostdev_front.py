@@ -315,12 +315,12 @@ def test_host_fused_route_edge_cases(hostdev, tmp_path):
     assert int(r["sgd_count"]) == 0
 
 
-@pytest.mark.parametrize("kind", ["fwd", "grad"])
+@pytest.mark.parametrize("kind", ["fwd", "grad", "i32"])
 def test_random_graphs_agree_across_modes(hostdev, tmp_path, kind):
     """Random Tensor-API graphs (tests/hostdev/run_fuzz.py): forward values of
     exact and default mode within 1e-4 of float64, gradients of the default
     mode within 1e-4 of exact mode's; gradients the reference leaves
-    undefined raise in both modes."""
+    undefined raise in both modes; integer graphs exact in both modes."""
     runner = os.path.join(os.path.dirname(hostdev), "run_fuzz.py")
     dst = tmp_path / f"fuzz_{kind}.npz"
     subprocess.run([sys.executable, runner, "3", "30", kind, str(dst)], check=True, timeout=900)
