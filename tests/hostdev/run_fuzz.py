@@ -8,7 +8,8 @@ contiguous, matmul -- over f32 leaves of ragged shapes (1 to 257 per axis,
 up to rank 3).  Forward graphs are realized in exact mode (every kernel
 rendered in the reference's order) and in the default mode (routed GEMMs and
 reductions, warp/block reductions, 128-bit accesses) and both are held to
-1e-4 of scale against float64 numpy.  Gradient graphs (loss = sum of the
+float64 numpy within 1e-4 of the magnitude of the terms that make each
+element (a sum's terms, not its possibly cancelled result).  Gradient graphs (loss = sum of the
 graph times a random weight, backward to every leaf) compare the default
 mode's gradients with exact mode's at the same tolerance, NaN where the
 other mode has NaN (sqrt of 0 and the like); a gradient the reference does
@@ -35,10 +36,14 @@ OPS = ["add", "mul", "neg", "relu", "sum", "max", "permute", "reshape", "expand"
 
 
 class Node:
-    """A graph: build(env) makes its Tensor, ref is its float64 value."""
+    """A graph: build(env) makes its Tensor, ref is its float64 value and
+    mag a bound on the magnitude of the terms that make each element (the
+    graph over absolute values: a sum's terms, not its cancelled result), the
+    scale its rounding error is measured against."""
 
-    def __init__(self, build, ref):
+    def __init__(self, build, ref, mag=None):
         self.build, self.ref = build, ref
+        self.mag = np.abs(ref) if mag is None else mag
 
     @property
     def shape(self):
@@ -72,37 +77,42 @@ def rand_graph(rng, depth=0, i32=False):
         y = leaf(rng, s if rng.random() < 0.5 else
                  tuple(d if rng.random() < 0.5 else 1 for d in s), i32)
         if op == "add":
-            return Node(lambda env, x=x, y=y: x.build(env).add(y.build(env)), x.ref + y.ref)
-        return Node(lambda env, x=x, y=y: x.build(env).mul(y.build(env)), x.ref * y.ref)
+            return Node(lambda env, x=x, y=y: x.build(env).add(y.build(env)), x.ref + y.ref,
+                        x.mag + y.mag)
+        return Node(lambda env, x=x, y=y: x.build(env).mul(y.build(env)), x.ref * y.ref,
+                    x.mag * y.mag)
     if op == "neg":
-        return Node(lambda env, x=x: x.build(env).neg(), -x.ref)
+        return Node(lambda env, x=x: x.build(env).neg(), -x.ref, x.mag)
     if op == "relu":
         return Node(lambda env, x=x: x.build(env).relu(),
-                    np.where(x.ref > 0, x.ref, np.zeros_like(x.ref)))
+                    np.where(x.ref > 0, x.ref, np.zeros_like(x.ref)), x.mag)
     if op == "chain":
         return Node(lambda env, x=x: x.build(env).mul(x.build(env)).add(x.build(env)).relu(),
-                    np.maximum(x.ref * x.ref + x.ref, 0.0))
+                    np.maximum(x.ref * x.ref + x.ref, 0.0), x.mag * x.mag + x.mag)
     if op in ("sum", "max"):
         axes = sorted(rng.choice(len(s), int(rng.integers(1, len(s) + 1)), replace=False).tolist())
         if op == "sum":
             return Node(lambda env, x=x, a=axes: x.build(env).sum(a),
-                        x.ref.sum(axis=tuple(axes), keepdims=True))
+                        x.ref.sum(axis=tuple(axes), keepdims=True),
+                        x.mag.sum(axis=tuple(axes), keepdims=True))
         return Node(lambda env, x=x, a=axes: x.build(env).max(a),
-                    x.ref.max(axis=tuple(axes), keepdims=True))
+                    x.ref.max(axis=tuple(axes), keepdims=True),
+                    x.mag.max(axis=tuple(axes), keepdims=True))
     if op == "permute":
         order = rng.permutation(len(s)).tolist()
-        return Node(lambda env, x=x, o=order: x.build(env).permute(o), np.transpose(x.ref, order))
+        return Node(lambda env, x=x, o=order: x.build(env).permute(o), np.transpose(x.ref, order),
+                    np.transpose(x.mag, order))
     if op == "reshape":
         n = int(np.prod(s))
         d0 = int(rng.choice([d for d in range(1, n + 1) if n % d == 0]))
         return Node(lambda env, x=x, sh=[d0, n // d0]: x.build(env).reshape(sh),
-                    x.ref.reshape(d0, n // d0))
+                    x.ref.reshape(d0, n // d0), x.mag.reshape(d0, n // d0))
     if op == "expand":
         shape = tuple(int(rng.choice([2, 5, 32])) if d == 1 else d for d in s)
         if 1 not in s or np.prod(shape) > 300000:
             return x
         return Node(lambda env, x=x, sh=list(shape): x.build(env).expand(sh),
-                    np.broadcast_to(x.ref, shape))
+                    np.broadcast_to(x.ref, shape), np.broadcast_to(x.mag, shape))
     if op == "narrow":
         dim = int(rng.integers(0, len(s)))
         if s[dim] < 2:
@@ -111,25 +121,27 @@ def rand_graph(rng, depth=0, i32=False):
         ln = int(rng.integers(1, s[dim] - start + 1))
         sl = [slice(None)] * len(s)
         sl[dim] = slice(start, start + ln)
-        return Node(lambda env, x=x, a=(dim, start, ln): x.build(env).narrow(*a), x.ref[tuple(sl)])
+        return Node(lambda env, x=x, a=(dim, start, ln): x.build(env).narrow(*a), x.ref[tuple(sl)],
+                    x.mag[tuple(sl)])
     if op == "contig":
-        return Node(lambda env, x=x: x.build(env).contiguous(), x.ref)
+        return Node(lambda env, x=x: x.build(env).contiguous(), x.ref, x.mag)
     if op == "matmul":
         if len(s) != 2:
             return x
         w = leaf(rng, (s[1], int(rng.choice([1, 5, 16, 40, 128]))))
-        return Node(lambda env, x=x, w=w: x.build(env).matmul(w.build(env)), x.ref @ w.ref)
+        return Node(lambda env, x=x, w=w: x.build(env).matmul(w.build(env)), x.ref @ w.ref,
+                    x.mag @ w.mag)
     sq = lambda env, x: x.build(env).mul(x.build(env))  # noqa: E731
     if op == "exp":
         return Node(lambda env, x=x: x.build(env).mul(F.Tensor.scalar(0.25)).exp(),
-                    np.exp(x.ref * 0.25))
+                    np.exp(x.ref * 0.25), np.exp(x.mag * 0.25) * (1.0 + 0.25 * x.mag))
     if op == "log":
         return Node(lambda env, x=x: sq(env, x).add(F.Tensor.scalar(1.0)).log(),
-                    np.log(x.ref * x.ref + 1.0))
+                    np.log(x.ref * x.ref + 1.0), np.log(x.mag * x.mag + 1.0) + x.mag * x.mag)
     if op == "recip":
         return Node(lambda env, x=x: sq(env, x).add(F.Tensor.scalar(1.0)).reciprocal(),
-                    1.0 / (x.ref * x.ref + 1.0))
-    return Node(lambda env, x=x: sq(env, x).sqrt(), np.abs(x.ref))  # sqrt
+                    1.0 / (x.ref * x.ref + 1.0), 1.0 + x.mag * x.mag)
+    return Node(lambda env, x=x: sq(env, x).sqrt(), np.abs(x.ref), x.mag)  # sqrt
 
 
 class Env:
@@ -145,7 +157,9 @@ class Env:
         return self.tensors[id(a)]
 
 
-def scale_err(got, ref):
+def scale_err(got, ref, mag=None):
+    """Largest |got - ref| over the scale max(mag) (max |ref| by default);
+    NaN must sit where ref has NaN."""
     if ref.size == 0:
         return 0.0
     both_nan = np.isnan(got) & np.isnan(ref)
@@ -153,7 +167,8 @@ def scale_err(got, ref):
         return float("inf")
     ref = np.where(both_nan, 0.0, ref)
     got = np.where(both_nan, 0.0, got.astype(np.float64))
-    return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-3))
+    scale = np.abs(ref) if mag is None else np.where(both_nan, 0.0, mag)
+    return float(np.max(np.abs(got - ref)) / max(np.max(scale), 1e-3))
 
 
 def realize(node, mode, grad, wv):
@@ -211,7 +226,7 @@ def main(seed, count, kind, dst):
                     failures.append(f"{i}: mode {mode} {node.shape}: i32 result differs")
         else:
             for mode in ("1", "0"):
-                e = scale_err(outs[mode][0], node.ref)
+                e = scale_err(outs[mode][0], node.ref, node.mag)
                 if not e <= 1e-4:
                     failures.append(f"{i}: mode {mode} {node.shape}: vs float64 {e:.2e}")
     np.savez(dst, failures=np.array(failures, dtype=str), checked=np.array(checked),

@@ -318,7 +318,8 @@ def test_host_fused_route_edge_cases(hostdev, tmp_path):
 @pytest.mark.parametrize("kind", ["fwd", "grad", "i32"])
 def test_random_graphs_agree_across_modes(hostdev, tmp_path, kind):
     """Random Tensor-API graphs (tests/hostdev/run_fuzz.py): forward values of
-    exact and default mode within 1e-4 of float64, gradients of the default
+    exact and default mode within 1e-4 of float64 (relative to the magnitude
+    of the terms that make each element), gradients of the default
     mode within 1e-4 of exact mode's; gradients the reference leaves
     undefined raise in both modes; integer graphs exact in both modes."""
     runner = os.path.join(os.path.dirname(hostdev), "run_fuzz.py")
