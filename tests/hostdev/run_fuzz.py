@@ -4,8 +4,8 @@ in a subprocess by tests/test_hostdev_front.py).
 Each graph is drawn from the ops the training path uses -- broadcast add and
 mul, neg, relu, the fused chain relu(x*x+x), exp, log, reciprocal, sqrt,
 sum / max over random axis sets, permute, reshape, expand, narrow,
-contiguous, matmul -- over f32 leaves of ragged shapes (1 to 257 per axis,
-up to rank 3).  Forward graphs are realized in exact mode (every kernel
+contiguous, matmul -- over f32 leaves of ragged shapes (0 to 257 per axis,
+up to rank 3; a max over an empty axis is -inf, the reference's identity).  Forward graphs are realized in exact mode (every kernel
 rendered in the reference's order) and in the default mode (routed GEMMs and
 reductions, warp/block reductions, 128-bit accesses) and both are held to
 float64 numpy within 1e-4 of the magnitude of the terms that make each
@@ -30,7 +30,7 @@ os.makedirs(os.environ["FG_HOSTDEV_CACHE"], exist_ok=True)
 sys.path.insert(0, _BUILD)
 import _front as F  # noqa: E402
 
-SIZES = [1, 3, 4, 7, 8, 16, 33, 40, 64, 100, 128, 257]
+SIZES = [0, 1, 3, 4, 7, 8, 16, 33, 40, 64, 100, 128, 257]
 OPS = ["add", "mul", "neg", "relu", "sum", "max", "permute", "reshape", "expand", "narrow",
        "contig", "matmul", "exp", "log", "recip", "sqrt", "chain"]
 
@@ -95,15 +95,19 @@ def rand_graph(rng, depth=0, i32=False):
             return Node(lambda env, x=x, a=axes: x.build(env).sum(a),
                         x.ref.sum(axis=tuple(axes), keepdims=True),
                         x.mag.sum(axis=tuple(axes), keepdims=True))
+        ident = -np.inf if x.ref.dtype.kind == "f" else -(2**31)  # max over nothing
         return Node(lambda env, x=x, a=axes: x.build(env).max(a),
-                    x.ref.max(axis=tuple(axes), keepdims=True),
-                    x.mag.max(axis=tuple(axes), keepdims=True))
+                    x.ref.max(axis=tuple(axes), keepdims=True, initial=ident),
+                    x.mag.max(axis=tuple(axes), keepdims=True, initial=0))
     if op == "permute":
         order = rng.permutation(len(s)).tolist()
         return Node(lambda env, x=x, o=order: x.build(env).permute(o), np.transpose(x.ref, order),
                     np.transpose(x.mag, order))
     if op == "reshape":
         n = int(np.prod(s))
+        if n == 0:
+            return Node(lambda env, x=x: x.build(env).reshape([0, 3]), x.ref.reshape(0, 3),
+                        x.mag.reshape(0, 3))
         d0 = int(rng.choice([d for d in range(1, n + 1) if n % d == 0]))
         return Node(lambda env, x=x, sh=[d0, n // d0]: x.build(env).reshape(sh),
                     x.ref.reshape(d0, n // d0), x.mag.reshape(d0, n // d0))
@@ -167,8 +171,13 @@ def scale_err(got, ref, mag=None):
         return float("inf")
     ref = np.where(both_nan, 0.0, ref)
     got = np.where(both_nan, 0.0, got.astype(np.float64))
+    same = got == ref  # equal infinities too (a max over an empty axis is -inf)
+    if np.any(~np.isfinite(ref) & ~same):
+        return float("inf")
+    diff = np.where(same, 0.0, np.abs(got - np.where(same, 0.0, ref)))
     scale = np.abs(ref) if mag is None else np.where(both_nan, 0.0, mag)
-    return float(np.max(np.abs(got - ref)) / max(np.max(scale), 1e-3))
+    scale = np.where(np.isfinite(scale), scale, 0.0)
+    return float(np.max(diff) / max(np.max(scale), 1e-3))
 
 
 def realize(node, mode, grad, wv):
@@ -184,7 +193,7 @@ def realize(node, mode, grad, wv):
 
 
 def fits_i32(node):
-    return node.ref.size == 0 or np.max(np.abs(node.ref)) < 2**31
+    return node.ref.size == 0 or np.max(np.abs(node.ref)) <= 2**31
 
 
 def main(seed, count, kind, dst):
