@@ -249,6 +249,10 @@ size_t interner_size() { return interner().count; }
 UOpP make_buffer(const BufferP &b) { return intern(Op::Buffer, b->dtype, {}, {}, Op::Add, 0.0, b); }
 UOpP make_const(double v, DType dt) { return intern(Op::Const, dt, {}, {}, Op::Add, v); }
 UOpP make_reshape(const UOpP &s, const Shape &shape) {
+  // A reshape views the same elements: a count that differs would make every
+  // kernel that reads the node index past its source.
+  if (s->has_shape && numel(s->shape) != numel(shape))
+    throw Panic("reshape: numel mismatch for " + shape_str(s->shape) + " -> " + shape_str(shape));
   return intern(Op::Reshape, s->dtype, {s}, shape);
 }
 UOpP make_permute(const UOpP &s, const std::vector<int64_t> &order) {
@@ -460,10 +464,16 @@ std::vector<UOpP> gradient_for_op(const UOpP &nodep, const UOpP &grad) {
       return {make_permute(grad, inv)};
     }
     case Op::Expand: {
+      // Summed over the broadcast axes (src/gradient.rs:165-176).  The
+      // reference's axis test (src/shape.rs:93-101) takes dst > 1; an axis of
+      // 1 expanded to 0 is reduced here too (its gradient is the sum over
+      // nothing, 0), because left out it would hand the Reshape rule below a
+      // gradient with 0 elements to view as the source's shape, a kernel that
+      // reads past the end of its buffer.
       const Shape &src = node->src[0]->shape;
       std::vector<int64_t> axes;
       for (size_t a = 0; a < src.size(); a++)
-        if (src[a] == 1 && node->arg[a] > 1) axes.push_back((int64_t)a);
+        if (src[a] == 1 && node->arg[a] != 1) axes.push_back((int64_t)a);
       if (axes.empty()) return {grad};
       return {make_reduce(grad, Op::Add, axes)};
     }

@@ -74,6 +74,11 @@ def main(dst):
     opt.step()
     out["w0"], out["w1"] = w0, w.numpy()
     out["sgd_count"] = np.array(F.stats()["sgd"])
+
+    # 6. an axis of 1 expanded to 0: its gradient is the sum over nothing
+    z = T(rng.standard_normal((1, 64)).astype(np.float32)).with_requires_grad(True)
+    z.expand([0, 64]).relu().sum([0, 1]).backward()
+    out["zero_expand_grad"] = z.grad().numpy()
     np.savez(dst, **out)
 
 

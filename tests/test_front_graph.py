@@ -174,6 +174,23 @@ def test_backward_targets_live_tensors_that_require_grad():
     assert "Add" in x.grad()._graph().splitlines()[-1]
 
 
+def test_gradient_of_an_axis_expanded_to_zero_keeps_the_source_shape():
+    """An axis of 1 expanded to 0 gets the sum over nothing as its gradient:
+    reduced back to 1, never a 0-element gradient viewed as the source's
+    shape (which would read past the end of the buffer)."""
+    x = F.Tensor.empty([1, 64]).with_requires_grad(True)
+    loss = x.expand([0, 64]).relu().sum([0, 1])
+    loss.backward()
+    g = x.grad()
+    assert g.shape == (1, 64)
+    assert "ReduceAxis" in g._graph()
+
+
+def test_internal_reshape_keeps_the_element_count():
+    with pytest.raises(RuntimeError, match="numel mismatch"):
+        U.reshape(U.buffer([4]), [3])
+
+
 def test_gradient_of_untracked_target_is_zeros():
     x = F.Tensor.empty([2, 2])
     w = F.Tensor.empty([2, 1]).with_requires_grad(True)

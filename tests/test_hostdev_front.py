@@ -282,7 +282,8 @@ def test_host_fused_route_edge_cases(hostdev, tmp_path):
     read before its gradient costs a second fused pass but gives the same
     values; a scaled loss scales the fused gradient; graphs of alternating
     shapes miss and hit the schedule cache correctly; an SGD store whose
-    gradient is not contiguous falls back to a rendered kernel."""
+    gradient is not contiguous falls back to a rendered kernel; an axis
+    expanded from 1 to 0 gets a zero gradient of the source's shape."""
     runner = os.path.join(os.path.dirname(hostdev), "run_front_edges.py")
     dst = tmp_path / "edges.npz"
     subprocess.run([sys.executable, runner, str(dst)], check=True, timeout=600)
@@ -313,6 +314,7 @@ def test_host_fused_route_edge_cases(hostdev, tmp_path):
     grad = np.arange(24, dtype=np.float64).reshape(4, 6).T
     assert np.array_equal(r["w1"], (w0 - 0.5 * grad).astype(np.float32))
     assert int(r["sgd_count"]) == 0
+    assert np.array_equal(r["zero_expand_grad"], np.zeros((1, 64), np.float32))
 
 
 @pytest.mark.parametrize("kind", ["fwd", "grad", "i32"])
