@@ -356,9 +356,10 @@ Tensor Tensor::cross_entropy(const Tensor &targets) const {
   const int64_t classes_axis = ndim() != 1 ? 1 : 0;
   // Default mode: one fused op, run as a single fg_xent_fwd_bwd pass that
   // also yields d loss / d logits for backward().  Exact mode (and targets
-  // that need a gradient, or other ranks/dtypes) build the reference graph.
+  // that need a gradient, other ranks/dtypes, or empty logits, which the
+  // fused kernel rejects) build the reference graph.
   if (!exact_mode() && (ndim() == 1 || ndim() == 2) && dtype() == DType::F32 &&
-      targets.dtype() == DType::F32 && !targets.requires_grad())
+      targets.dtype() == DType::F32 && !targets.requires_grad() && numel() > 0)
     return from_uop(make_xent_loss(uop(), targets.uop()), requires_grad());
   Tensor log_probs = log_softmax(classes_axis);
   Tensor per_sample = targets.mul(log_probs).sum({classes_axis}).neg();

@@ -443,6 +443,7 @@ int fg_u8_to_f32_div(const uint8_t *src, float *dst, size_t n, float divisor, vo
 int fg_xent_fwd_bwd(const float *x, const float *t, size_t rows, size_t cols, float *loss,
                     float *dx, float grad_scale, void *) {
   FG_HOSTDEV_SKIP_COMPUTE();
+  if (rows == 0 || cols == 0) return fg::set_error(FG_ERR_INVALID, "cross_entropy: empty logits");
   if (!x || !t || !loss) return fg::set_error(FG_ERR_INVALID, "fg_xent_fwd_bwd: null pointer");
   double total = 0.0;
   for (size_t r = 0; r < rows; r++) {

@@ -4,16 +4,18 @@ in a subprocess by tests/test_hostdev_front.py).
 Each graph is drawn from the ops the training path uses -- broadcast add and
 mul, neg, relu, the fused chain relu(x*x+x), exp, log, reciprocal, sqrt,
 sum / max over random axis sets, permute, reshape, expand, narrow,
-contiguous, matmul -- over f32 leaves of ragged shapes (0 to 257 per axis,
-up to rank 3; a max over an empty axis is -inf, the reference's identity).  Forward graphs are realized in exact mode (every kernel
-rendered in the reference's order) and in the default mode (routed GEMMs and
-reductions, warp/block reductions, 128-bit accesses) and both are held to
-float64 numpy within 1e-4 of the magnitude of the terms that make each
-element (a sum's terms, not its possibly cancelled result).  Gradient graphs (loss = sum of the
-graph times a random weight, backward to every leaf) compare the default
-mode's gradients with exact mode's at the same tolerance, NaN where the
-other mode has NaN (sqrt of 0 and the like); a gradient the reference does
-not define (Shrink, src/gradient.rs:203) must raise in both modes.
+contiguous, matmul, log_softmax, cross_entropy against one-hot targets --
+over f32 leaves of ragged shapes (0 to 257 per axis, up to rank 3; a max
+over an empty axis is -inf, the reference's identity).  Forward graphs are
+realized in exact mode (every kernel rendered in the reference's order) and
+in the default mode (routed GEMMs and reductions, warp/block reductions,
+128-bit accesses, the fused cross-entropy) and both are held to float64
+numpy within 1e-4 of the magnitude of the terms that make each element (a
+sum's terms, not its possibly cancelled result).  Gradient graphs (loss =
+sum of the graph times a random weight, backward to every leaf) compare the
+default mode's gradients with exact mode's at the same tolerance, NaN where
+the other mode has NaN (sqrt of 0 and the like); a gradient the reference
+does not define (Shrink, src/gradient.rs:203) must raise in both modes.
 Integer graphs (i32 leaves in -1000..1000; add, mul, neg, relu, sum, max and
 the movement ops) must give the int64 result exactly in both modes.
 
@@ -32,7 +34,7 @@ import _front as F  # noqa: E402
 
 SIZES = [0, 1, 3, 4, 7, 8, 16, 33, 40, 64, 100, 128, 257]
 OPS = ["add", "mul", "neg", "relu", "sum", "max", "permute", "reshape", "expand", "narrow",
-       "contig", "matmul", "exp", "log", "recip", "sqrt", "chain"]
+       "contig", "matmul", "exp", "log", "recip", "sqrt", "chain", "logsm", "xent"]
 
 
 class Node:
@@ -135,6 +137,24 @@ def rand_graph(rng, depth=0, i32=False):
         w = leaf(rng, (s[1], int(rng.choice([1, 5, 16, 40, 128]))))
         return Node(lambda env, x=x, w=w: x.build(env).matmul(w.build(env)), x.ref @ w.ref,
                     x.mag @ w.mag)
+    if op == "logsm":
+        axis = int(rng.integers(0, len(s)))
+        m = x.ref.max(axis=axis, keepdims=True, initial=-np.inf)
+        m = np.where(np.isfinite(m), m, 0.0)
+        lse = np.log(np.exp(x.ref - m).sum(axis=axis, keepdims=True)) + m
+        return Node(lambda env, x=x, a=axis: x.build(env).log_softmax(a), x.ref - lse,
+                    np.abs(x.ref - lse) + 2 * x.mag.max(axis=axis, keepdims=True, initial=0))
+    if op == "xent":
+        if len(s) != 2 or s[0] == 0 or s[1] == 0:
+            return x
+        t = np.zeros(s, np.float32)
+        t[np.arange(s[0]), rng.integers(0, s[1], s[0])] = 1
+        m = x.ref.max(axis=1, keepdims=True)
+        logp = x.ref - (np.log(np.exp(x.ref - m).sum(axis=1, keepdims=True)) + m)
+        loss = -(t * logp).sum(keepdims=True) / s[0]
+        mag = (np.abs(logp) + 2 * x.mag.max(axis=1, keepdims=True)).max(keepdims=True)
+        return Node(lambda env, x=x, t=t: x.build(env).cross_entropy(F.Tensor.new(t)),
+                    loss.reshape(1, 1), mag.reshape(1, 1))
     sq = lambda env, x: x.build(env).mul(x.build(env))  # noqa: E731
     if op == "exp":
         return Node(lambda env, x=x: x.build(env).mul(F.Tensor.scalar(0.25)).exp(),

@@ -186,6 +186,15 @@ def test_gradient_of_an_axis_expanded_to_zero_keeps_the_source_shape():
     assert "ReduceAxis" in g._graph()
 
 
+def test_cross_entropy_of_empty_logits_keeps_the_reference_graph(monkeypatch):
+    """The fused cross-entropy kernel rejects empty logits, so the default
+    mode builds the reference's decomposed graph for them."""
+    monkeypatch.delenv("FG_FRONT_EXACT", raising=False)
+    t = F.Tensor.zeros([0, 10])
+    assert "XentLoss" not in F.Tensor.empty([0, 10]).cross_entropy(t)._graph()
+    assert "XentLoss" in F.Tensor.empty([4, 10]).cross_entropy(F.Tensor.zeros([4, 10]))._graph()
+
+
 def test_internal_reshape_keeps_the_element_count():
     with pytest.raises(RuntimeError, match="numel mismatch"):
         U.reshape(U.buffer([4]), [3])
